@@ -1,0 +1,93 @@
+"""ctypes binding of ``libspa_b200.so`` (declared in include/spa_b200.h).
+
+The library is the product path: there is no fallback.  Importing this module
+without the built library raises immediately with the command that builds it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("SPA_B200_LIB", _PKG / "libspa_b200.so"))
+
+SPA_OK, SPA_ERR_INVALID, SPA_ERR_UNSUPPORTED, SPA_ERR_CUDA, SPA_ERR_WORKSPACE, SPA_ERR_TIMEOUT = range(6)
+STATUS_NAMES = {
+    SPA_ERR_INVALID: "invalid argument",
+    SPA_ERR_UNSUPPORTED: "unsupported configuration",
+    SPA_ERR_CUDA: "CUDA error",
+    SPA_ERR_WORKSPACE: "workspace missing or too small",
+    SPA_ERR_TIMEOUT: "bounded device wait gave up",
+}
+SPA_F32, SPA_F16, SPA_BF16 = 0, 1, 2
+
+
+class KvLayout(ctypes.Structure):
+    """Mirror of ``spa_kv_layout``."""
+
+    _fields_ = [
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("total_rows", ctypes.c_int64),
+        ("batch_stride_rows", ctypes.c_int64),
+        ("page_stride_rows", ctypes.c_int64),
+        ("head_stride_rows", ctypes.c_int64),
+        ("page_table", ctypes.c_void_p),
+        ("table_stride", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+    ]
+
+
+_vp, _i, _i64, _d, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_double, ctypes.c_size_t
+_KV = ctypes.POINTER(KvLayout)
+
+# name -> (restype, argtypes); keep in the order of include/spa_b200.h
+PROTOTYPES = {
+    "spa_version": (ctypes.c_char_p, []),
+    "spa_device_error": (_i, [ctypes.POINTER(ctypes.c_uint32)]),
+    "spa_summaries_build": (_i, [_KV, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp]),
+    "spa_router_topm": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _d, _i, _vp, _vp, _vp]),
+    "spa_router_tree_topm": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _vp, _i, _i, _i, _d, _i, _vp, _vp]),
+    "spa_decode_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "spa_paged_decode": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp, _sz, _vp]),
+    "spa_kv_append": (_i, [_KV, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "spa_local_prefill": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),
+    "spa_promotion_update": (_i, [_vp, _vp, _i, _i, _vp, _i, _i, _i, _vp]),
+}
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"attention_b200: CUDA library {LIB_PATH} is not built "
+            "(run `python -m attention_b200.build`); there is no CPU fallback"
+        )
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in PROTOTYPES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+class SpaError(RuntimeError):
+    pass
+
+
+def check(rc: int, what: str) -> None:
+    if rc != SPA_OK:
+        if rc == SPA_ERR_INVALID:
+            raise ValueError(f"{what}: {STATUS_NAMES[rc]}")
+        raise SpaError(f"{what}: {STATUS_NAMES.get(rc, rc)} (status {rc})")
+
+
+def device_error_flags() -> int:
+    """Reads and clears the library's device error word (synchronises the device)."""
+    v = ctypes.c_uint32(0)
+    check(lib.spa_device_error(ctypes.byref(v)), "spa_device_error")
+    return int(v.value)

@@ -1,0 +1,104 @@
+// KV append and the promotion-cache table update.
+#pragma once
+
+#include "common.cuh"
+
+namespace spa {
+
+// grid (B, Hkv), block = head_dim threads (<= 256).  Writes token positions[b].
+// Reference: the tail K/V overwrite of page_decode (triton_kvcache_transformer_decode.py:51-55).
+template <typename T>
+__global__ void kv_append_kernel(T* __restrict__ k, T* __restrict__ v, KvAddr addr, int head_dim,
+                                 const T* __restrict__ k_new, const T* __restrict__ v_new,
+                                 const int32_t* __restrict__ positions) {
+  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int pos = positions[b];
+  if (pos < 0 || d >= head_dim) return;
+  const int64_t row = addr.row(b, h, pos);
+  if (row < 0 || row >= addr.total_rows) {
+    if (d == 0) spa_raise(SPA_DEVERR_BAD_PAGE);
+    return;
+  }
+  const int64_t src = (static_cast<int64_t>(b) * gridDim.y + h) * head_dim + d;
+  k[row * head_dim + d] = k_new[src];
+  v[row * head_dim + d] = v_new[src];
+}
+
+// One thread per table row.  Policy: hits refresh last_hit, then entries idle for
+// >= ttl steps are freed, then new pages fill the lowest free slot or evict the
+// least recently hit entry (ties: smallest page id).  Reference policy: fixed-TTL
+// refresh of promoted ids, evaluate_promotion_ttl.py:134-135; promoted-id reuse,
+// triton_promotion_cache_benchmark.py:53-60.
+__global__ void promotion_update_kernel(int32_t* __restrict__ pages, int32_t* __restrict__ last_hit, int rows,
+                                        int slots, const int64_t* __restrict__ selected, int top_m, int step,
+                                        int ttl) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  int32_t* pg = pages + static_cast<int64_t>(r) * slots;
+  int32_t* lh = last_hit + static_cast<int64_t>(r) * slots;
+  const int64_t* sel = selected + static_cast<int64_t>(r) * top_m;
+  for (int j = 0; j < top_m; ++j) {
+    const int64_t id = sel[j];
+    if (id < 0) continue;
+    for (int i = 0; i < slots; ++i)
+      if (pg[i] == static_cast<int32_t>(id)) lh[i] = step;
+  }
+  for (int i = 0; i < slots; ++i)
+    if (pg[i] >= 0 && step - lh[i] >= ttl) pg[i] = -1;
+  for (int j = 0; j < top_m; ++j) {
+    const int64_t id64 = sel[j];
+    if (id64 < 0 || id64 > 0x7fffffff) continue;
+    const int32_t id = static_cast<int32_t>(id64);
+    bool present = false;
+    for (int i = 0; i < slots; ++i) present |= (pg[i] == id);
+    if (present) continue;
+    int slot = -1;
+    for (int i = 0; i < slots && slot < 0; ++i)
+      if (pg[i] < 0) slot = i;
+    if (slot < 0) {
+      slot = 0;
+      for (int i = 1; i < slots; ++i)
+        if (lh[i] < lh[slot] || (lh[i] == lh[slot] && pg[i] < pg[slot])) slot = i;
+    }
+    pg[slot] = id;
+    lh[slot] = step;
+  }
+}
+
+}  // namespace spa
+
+extern "C" int spa_kv_append(const spa_kv_layout* kv, int dtype, int batch, int kv_heads, int head_dim,
+                             const void* k_new, const void* v_new, const int32_t* positions, spa_stream_t stream) {
+  if (!kv || !kv->k || !kv->v || !k_new || !v_new || !positions || !dtype_ok(dtype)) return SPA_ERR_INVALID;
+  if (batch <= 0 || kv_heads <= 0 || head_dim <= 0 || head_dim > 256 || kv->page_size <= 0) return SPA_ERR_INVALID;
+  if (kv->page_table && kv->table_stride <= 0) return SPA_ERR_INVALID;
+  const KvAddr addr = make_kv_addr(*kv);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid(batch, kv_heads);
+  if (dtype == SPA_F32)
+    spa::kv_append_kernel<float><<<grid, head_dim, 0, st>>>(
+        static_cast<float*>(const_cast<void*>(kv->k)), static_cast<float*>(const_cast<void*>(kv->v)), addr,
+        head_dim, static_cast<const float*>(k_new), static_cast<const float*>(v_new), positions);
+  else if (dtype == SPA_F16)
+    spa::kv_append_kernel<__half><<<grid, head_dim, 0, st>>>(
+        static_cast<__half*>(const_cast<void*>(kv->k)), static_cast<__half*>(const_cast<void*>(kv->v)), addr,
+        head_dim, static_cast<const __half*>(k_new), static_cast<const __half*>(v_new), positions);
+  else
+    spa::kv_append_kernel<__nv_bfloat16><<<grid, head_dim, 0, st>>>(
+        static_cast<__nv_bfloat16*>(const_cast<void*>(kv->k)), static_cast<__nv_bfloat16*>(const_cast<void*>(kv->v)),
+        addr, head_dim, static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new),
+        positions);
+  SPA_CHECK_CUDA(cudaGetLastError());
+  return SPA_OK;
+}
+
+extern "C" int spa_promotion_update(int32_t* pages, int32_t* last_hit, int rows, int slots, const int64_t* selected,
+                                    int top_m, int step, int ttl, spa_stream_t stream) {
+  if (!pages || !last_hit || !selected || rows <= 0 || slots <= 0 || top_m <= 0 || top_m > slots || ttl <= 0)
+    return SPA_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  spa::promotion_update_kernel<<<(rows + 127) / 128, 128, 0, st>>>(pages, last_hit, rows, slots, selected, top_m,
+                                                                   step, ttl);
+  SPA_CHECK_CUDA(cudaGetLastError());
+  return SPA_OK;
+}

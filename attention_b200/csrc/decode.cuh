@@ -1,0 +1,569 @@
+// Split-K paged decode attention (dense over a context, or local window + selected pages).
+//
+// Reference kernels: paged_decode_attention_kernel (triton_paged_attention.py:20-53) and
+// paged_gather_decode_attention_kernel (:84-136).  Both stream candidates through one
+// online softmax per (b, h); candidate c of the gather kernel is token ctx-W+c for c < W,
+// else sel[b,(c-W)//P]*P + (c-W)%P (:111-122).  Here the candidates are cut into chunks of
+// 64 tokens that never straddle a page, every (b, kv head) is split over `nsplit` CTAs,
+// and each CTA serves all `group` query heads that share the kv head (GQA packing).
+//
+// Fast path (bf16/fp16, D in {64,128}): one producer warp streams K and V chunks with
+// 2D TMA loads (128-byte swizzle) into a STAGES-deep mbarrier ring; four consumer warps
+// each take 16 tokens of a chunk and run QK^T and PV on mma.sync m16n8k16 with the
+// query heads as the (zero-padded) M dimension.  Partials (normalised O, log2-sum-exp)
+// go to the workspace and a small kernel merges the splits.
+#pragma once
+
+#include "common.cuh"
+
+namespace spa {
+
+struct DecodeArgs {
+  const void* q;
+  void* out;
+  int B, Hq, Hkv, group, D;
+  KvAddr addr;
+  const int32_t* ctx_lens;
+  int local_window;
+  const int64_t* selected;
+  int top_m;
+  int nsplit;
+  float scale_log2;  // softmax scale * log2(e)
+  float scale;
+  float* part_o;    // [B*Hq, nsplit, D]
+  float* part_lse;  // [B*Hq, nsplit] (log2 domain)
+};
+
+struct ChunkPlan {
+  int lo, hi, seg_a, n_seg, cpp, n_total, ctx;
+};
+
+__device__ __forceinline__ ChunkPlan make_plan(const DecodeArgs& a, int b, int chunk) {
+  ChunkPlan p;
+  const int ctx = a.ctx_lens[b];
+  p.ctx = ctx;
+  int lo = 0;
+  if (a.selected || a.local_window > 0) lo = max(0, ctx - max(a.local_window, 0));
+  p.lo = lo;
+  p.hi = ctx;
+  p.seg_a = (lo / chunk) * chunk;
+  p.n_seg = ctx > lo ? (ctx - p.seg_a + chunk - 1) / chunk : 0;
+  p.cpp = a.selected ? (a.addr.page_size + chunk - 1) / chunk : 0;
+  p.n_total = p.n_seg + (a.selected ? a.top_m * p.cpp : 0);
+  return p;
+}
+
+struct ChunkInfo {
+  int t0, vlo, vhi;  // tokens [t0, t0+chunk) are loaded; [vlo, vhi) are candidates
+};
+
+__device__ __forceinline__ ChunkInfo chunk_info(const DecodeArgs& a, const ChunkPlan& p, int b, int k,
+                                                int chunk) {
+  ChunkInfo c;
+  if (k < p.n_seg) {
+    c.t0 = p.seg_a + k * chunk;
+    c.vlo = max(c.t0, p.lo);
+    c.vhi = min(c.t0 + chunk, p.hi);
+  } else {
+    const int kk = k - p.n_seg;
+    const int j = kk / p.cpp, ci = kk - j * p.cpp;
+    const int64_t lp = a.selected[static_cast<int64_t>(b) * a.top_m + j];
+    const int P = a.addr.page_size;
+    if (lp < 0 || lp * P >= p.ctx) {
+      // -1 marks an unfilled slot; anything else past the context is an input error
+      if (lp >= 0) spa_raise(SPA_DEVERR_BAD_PAGE);
+      c.t0 = 0;
+      c.vlo = c.vhi = 0;
+    } else {
+      c.t0 = static_cast<int>(lp) * P + ci * chunk;
+      c.vlo = c.t0;
+      c.vhi = min(min(c.t0 + chunk, static_cast<int>(lp + 1) * P), p.ctx);
+    }
+  }
+  return c;
+}
+
+// ---------------------------------------------------------------------------
+// Fast path
+constexpr int kChunk = 64;
+constexpr int kConsumerWarps = 4;
+constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
+
+template <int D, int STAGES>
+struct DecodeSmem {
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kBoxBytes = kChunk * 128;
+  static constexpr int kKvBytes = kBoxes * kBoxBytes;
+  static constexpr int kStageBytes = 2 * kKvBytes;
+  static constexpr int kRingBytes = STAGES * kStageBytes;
+  static constexpr int kBytes = kRingBytes + STAGES * 16 + STAGES * 16 + 1024;  // + barriers, info, align
+};
+
+template <int D>
+__device__ __forceinline__ uint32_t swz_addr(uint32_t base, int row, int c16) {
+  // 16-byte chunk c16 of token row `row` in a [kChunk rows x 128 B] box array with SWIZZLE_128B
+  constexpr int kBoxBytes = kChunk * 128;
+  return base + (c16 >> 3) * kBoxBytes + row * 128 + (((c16 & 7) ^ (row & 7)) << 4);
+}
+
+template <typename T, int D, int STAGES>
+__global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                                     const __grid_constant__ CUtensorMap vmap,
+                                                                     const DecodeArgs a) {
+  using S = DecodeSmem<D, STAGES>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kRingBytes);
+  uint64_t* empty = full + STAGES;
+  int4* info = reinterpret_cast<int4*>(empty + STAGES);
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const ChunkPlan plan = make_plan(a, b, kChunk);
+  const int k0 = static_cast<int>(static_cast<int64_t>(plan.n_total) * split / a.nsplit);
+  const int k1 = static_cast<int>(static_cast<int64_t>(plan.n_total) * (split + 1) / a.nsplit);
+  const int nk = k1 - k0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+    }
+    const uint64_t policy = l2_policy_evict_first();
+    bool ok = true;
+    for (int base = 0; base < nk && ok; base += 32) {
+      ChunkInfo ci{0, 0, 0};
+      long long row = -1;
+      if (base + lane < nk) {
+        ci = chunk_info(a, plan, b, k0 + base + lane, kChunk);
+        if (ci.vlo < ci.vhi) {
+          row = a.addr.row(b, kvh, ci.t0);
+          if (row < 0 || row >= a.addr.total_rows) {
+            spa_raise(SPA_DEVERR_BAD_PAGE);
+            row = -1;
+          }
+        }
+      }
+      const int cnt = min(32, nk - base);
+      for (int j = 0; j < cnt; ++j) {
+        const int i = base + j;
+        const int t0 = __shfl_sync(0xffffffffu, ci.t0, j);
+        const int vlo = __shfl_sync(0xffffffffu, ci.vlo, j);
+        const int vhi = __shfl_sync(0xffffffffu, ci.vhi, j);
+        const long long r = __shfl_sync(0xffffffffu, row, j);
+        if (lane == 0) {
+          const int stage = i % STAGES;
+          if (i >= STAGES && !mbar_wait_bounded(&empty[stage], ((i / STAGES) - 1) & 1)) ok = false;
+          if (ok) {
+            info[stage] = make_int4(t0, r >= 0 ? vlo : 0, r >= 0 ? vhi : 0, 0);
+            uint64_t* bar = &full[stage];
+            if (r >= 0) {
+              mbar_arrive_expect_tx(bar, S::kStageBytes);
+              unsigned char* dst = smem + stage * S::kStageBytes;
+#pragma unroll
+              for (int bx = 0; bx < S::kBoxes; ++bx) {
+                tma_load_2d_hint(dst + bx * S::kBoxBytes, &kmap, bar, bx * 64, static_cast<int>(r), policy);
+                tma_load_2d_hint(dst + S::kKvBytes + bx * S::kBoxBytes, &vmap, bar, bx * 64, static_cast<int>(r),
+                                 policy);
+              }
+            } else {
+              mbar_arrive(bar);
+            }
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  using Mma = MmaOp<T>;
+  const int group = a.group;
+  const int g0 = lane >> 2, tig = lane & 3;
+  uint32_t qa[D / 16][4];
+  {
+    const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(b) * a.Hq + kvh * group) * D;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const int col = ks * 16 + tig * 2;
+      qa[ks][0] = g0 < group ? *reinterpret_cast<const uint32_t*>(qb + g0 * D + col) : 0u;
+      qa[ks][1] = g0 + 8 < group ? *reinterpret_cast<const uint32_t*>(qb + (g0 + 8) * D + col) : 0u;
+      qa[ks][2] = g0 < group ? *reinterpret_cast<const uint32_t*>(qb + g0 * D + col + 8) : 0u;
+      qa[ks][3] = g0 + 8 < group ? *reinterpret_cast<const uint32_t*>(qb + (g0 + 8) * D + col + 8) : 0u;
+    }
+  }
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float acc[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+
+  const int rbase = warp * 16;
+  const int mi = lane >> 3, mr = lane & 7;
+  bool ok = true;
+  for (int i = 0; i < nk; ++i) {
+    const int stage = i % STAGES;
+    if (!mbar_wait_bounded(&full[stage], (i / STAGES) & 1)) {
+      ok = false;
+      break;
+    }
+    const int4 ci = info[stage];
+    const int tw0 = ci.x + rbase;
+    const bool any = ci.y < ci.z && tw0 < ci.z && tw0 + 16 > ci.y;
+    if (any) {
+      const uint32_t sk = smem_u32(smem + stage * S::kStageBytes);
+      const uint32_t sv = sk + S::kKvBytes;
+      const bool partial = tw0 < ci.y || tw0 + 16 > ci.z;
+      if (partial) {
+        // zero the V rows of non-candidate tokens so 0 * (stale bits) cannot make NaN
+        unsigned char* vrow = smem + stage * S::kStageBytes + S::kKvBytes;
+        for (int e = lane; e < 16 * S::kBoxes * 8; e += 32) {
+          const int r = e / (S::kBoxes * 8), rem = e - r * (S::kBoxes * 8);
+          const int bx = rem >> 3, c = rem & 7;
+          const int tok = tw0 + r;
+          if (tok < ci.y || tok >= ci.z)
+            *reinterpret_cast<int4*>(vrow + bx * S::kBoxBytes + (rbase + r) * 128 + c * 16) = make_int4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+      float s[2][4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        uint32_t kb[4];
+        ldmatrix_x4(kb, swz_addr<D>(sk, rbase + (mi >> 1) * 8 + mr, 2 * ks + (mi & 1)));
+        Mma::run(s[0], qa[ks], kb[0], kb[1]);
+        Mma::run(s[1], qa[ks], kb[2], kb[3]);
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int tok = tw0 + j * 8 + tig * 2 + (e & 1);
+          s[j][e] = (tok >= ci.y && tok < ci.z) ? s[j][e] * a.scale_log2 : -INFINITY;
+        }
+      float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+      float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float mu0 = mn0 == -INFINITY ? 0.f : mn0, mu1 = mn1 == -INFINITY ? 0.f : mn1;
+      const float al0 = fast_exp2(m0 - mu0), al1 = fast_exp2(m1 - mu1);
+      float p[2][4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        p[j][0] = fast_exp2(s[j][0] - mu0);
+        p[j][1] = fast_exp2(s[j][1] - mu0);
+        p[j][2] = fast_exp2(s[j][2] - mu1);
+        p[j][3] = fast_exp2(s[j][3] - mu1);
+      }
+      l0 = l0 * al0 + (p[0][0] + p[0][1] + p[1][0] + p[1][1]);
+      l1 = l1 * al1 + (p[0][2] + p[0][3] + p[1][2] + p[1][3]);
+      m0 = mn0;
+      m1 = mn1;
+#pragma unroll
+      for (int n = 0; n < D / 8; ++n) {
+        acc[n][0] *= al0;
+        acc[n][1] *= al0;
+        acc[n][2] *= al1;
+        acc[n][3] *= al1;
+      }
+      uint32_t pa[4];
+      pa[0] = Mma::pack(p[0][0], p[0][1]);
+      pa[1] = Mma::pack(p[0][2], p[0][3]);
+      pa[2] = Mma::pack(p[1][0], p[1][1]);
+      pa[3] = Mma::pack(p[1][2], p[1][3]);
+#pragma unroll
+      for (int nd = 0; nd < D / 16; ++nd) {
+        uint32_t vb[4];
+        ldmatrix_x4_trans(vb, swz_addr<D>(sv, rbase + (mi & 1) * 8 + mr, 2 * nd + (mi >> 1)));
+        Mma::run(acc[2 * nd], pa, vb[0], vb[1]);
+        Mma::run(acc[2 * nd + 1], pa, vb[2], vb[3]);
+      }
+      if (partial) fence_proxy_async_smem();
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+  }
+  if (!ok) return;  // error word already raised; outputs of this split are undefined
+
+  // ------------------------------------------------ merge the four warps
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+  float* red = reinterpret_cast<float*>(smem);               // [4][16][D]
+  float* ml = red + kConsumerWarps * 16 * D;                 // [4][16][2]
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) {
+    const int col = n * 8 + tig * 2;
+    red[(warp * 16 + g0) * D + col] = acc[n][0];
+    red[(warp * 16 + g0) * D + col + 1] = acc[n][1];
+    red[(warp * 16 + g0 + 8) * D + col] = acc[n][2];
+    red[(warp * 16 + g0 + 8) * D + col + 1] = acc[n][3];
+  }
+  if (tig == 0) {
+    ml[(warp * 16 + g0) * 2] = m0;
+    ml[(warp * 16 + g0) * 2 + 1] = l0;
+    ml[(warp * 16 + g0 + 8) * 2] = m1;
+    ml[(warp * 16 + g0 + 8) * 2 + 1] = l1;
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+  for (int idx = threadIdx.x; idx < group * D; idx += kConsumerWarps * 32) {
+    const int row = idx / D, col = idx - row * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ml[(w * 16 + row) * 2]);
+    const float Mu = M == -INFINITY ? 0.f : M;
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float f = fast_exp2(ml[(w * 16 + row) * 2] - Mu);
+      L += ml[(w * 16 + row) * 2 + 1] * f;
+      O += red[(w * 16 + row) * D + col] * f;
+    }
+    const int h = kvh * group + row;
+    const float o = L > 0.f ? O / L : 0.f;
+    if (a.nsplit == 1) {
+      static_cast<T*>(a.out)[(static_cast<int64_t>(b) * a.Hq + h) * D + col] = from_f32<T>(o);
+    } else {
+      const int64_t bh = static_cast<int64_t>(b) * a.Hq + h;
+      a.part_o[(bh * a.nsplit + split) * D + col] = o;
+      if (col == 0) a.part_lse[bh * a.nsplit + split] = L > 0.f ? M + __log2f(L) : -INFINITY;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Generic path: one warp per (b, q head, split); any dtype, head_dim <= 256,
+// any page size.  fp32 math with accurate expf.
+constexpr int kGenericChunk = 16;
+
+template <typename T>
+__global__ void __launch_bounds__(32) decode_generic_kernel(const T* __restrict__ k, const T* __restrict__ v,
+                                                            const DecodeArgs a) {
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z, lane = threadIdx.x;
+  const int kvh = h / a.group, D = a.D;
+  const ChunkPlan plan = make_plan(a, b, kGenericChunk);
+  const int k0 = static_cast<int>(static_cast<int64_t>(plan.n_total) * split / a.nsplit);
+  const int k1 = static_cast<int>(static_cast<int64_t>(plan.n_total) * (split + 1) / a.nsplit);
+  float qv[8], acc[8];
+  const T* qp = static_cast<const T*>(a.q) + (static_cast<int64_t>(b) * a.Hq + h) * D;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int d = lane + 32 * e;
+    qv[e] = d < D ? to_f32(qp[d]) : 0.f;
+    acc[e] = 0.f;
+  }
+  float m = -INFINITY, l = 0.f;
+  for (int kk = k0; kk < k1; ++kk) {
+    const ChunkInfo ci = chunk_info(a, plan, b, kk, kGenericChunk);
+    for (int t = ci.vlo; t < ci.vhi; ++t) {
+      const int64_t row = a.addr.row(b, kvh, t);
+      if (row < 0 || row >= a.addr.total_rows) {
+        if (lane == 0) spa_raise(SPA_DEVERR_BAD_PAGE);
+        continue;
+      }
+      const T* kr = k + row * D;
+      const T* vr = v + row * D;
+      float dot = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int d = lane + 32 * e;
+        if (d < D) dot = fmaf(qv[e], to_f32(kr[d]), dot);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+      const float sc = dot * a.scale;
+      const float mn = fmaxf(m, sc);
+      const float alpha = expf(m - mn);  // m = -inf -> 0
+      const float p = expf(sc - mn);
+      l = l * alpha + p;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int d = lane + 32 * e;
+        acc[e] = acc[e] * alpha + (d < D ? p * to_f32(vr[d]) : 0.f);
+      }
+      m = mn;
+    }
+  }
+  const int64_t bh = static_cast<int64_t>(b) * a.Hq + h;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int d = lane + 32 * e;
+    if (d >= D) continue;
+    const float o = l > 0.f ? acc[e] / l : 0.f;
+    if (a.nsplit == 1)
+      static_cast<T*>(a.out)[bh * D + d] = from_f32<T>(o);
+    else
+      a.part_o[(bh * a.nsplit + split) * D + d] = o;
+  }
+  if (a.nsplit > 1 && lane == 0)
+    a.part_lse[bh * a.nsplit + split] = l > 0.f ? m * 1.4426950408889634f + log2f(l) : -INFINITY;
+}
+
+// ---------------------------------------------------------------------------
+// Split merge: grid (B*Hq), block 128.
+template <typename T>
+__global__ void __launch_bounds__(128) decode_combine_kernel(const float* __restrict__ part_o,
+                                                             const float* __restrict__ part_lse, int nsplit,
+                                                             int D, T* __restrict__ out) {
+  const int64_t bh = blockIdx.x;
+  const float* lse = part_lse + bh * nsplit;
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, lse[s]);
+  const float Mu = M == -INFINITY ? 0.f : M;
+  float W = 0.f;
+  for (int s = 0; s < nsplit; ++s) W += exp2f(lse[s] - Mu);
+  const float inv = W > 0.f ? 1.f / W : 0.f;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float o = 0.f;
+    for (int s = 0; s < nsplit; ++s) o += part_o[(bh * nsplit + s) * D + d] * exp2f(lse[s] - Mu);
+    out[bh * D + d] = from_f32<T>(o * inv);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host planning
+inline int device_sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// Splits per (b, kv head): fill ~2 CTAs per SM, keep >= 2 chunks per split.
+inline int decode_nsplit(int batch, int kv_heads, int max_candidates) {
+  const int pairs = batch * kv_heads;
+  const int slots = device_sm_count() * 2;
+  const int chunks = max_candidates / kChunk + 2;
+  int ns = pairs >= slots ? 1 : slots / pairs;
+  const int cap = chunks / 2 > 1 ? chunks / 2 : 1;
+  if (ns > cap) ns = cap;
+  if (ns > 256) ns = 256;
+  return ns < 1 ? 1 : ns;
+}
+
+constexpr int kDecodeStages = 3;
+
+template <typename T, int D>
+int launch_decode_mma(const spa_kv_layout& kv, int dtype, const DecodeArgs& a, cudaStream_t st) {
+  using S = DecodeSmem<D, kDecodeStages>;
+  CUtensorMap kmap, vmap;
+  if (!spa_make_tensor_map_2d(&kmap, kv.k, dtype, kv.total_rows, D, kChunk, 64, true)) return SPA_ERR_INVALID;
+  if (!spa_make_tensor_map_2d(&vmap, kv.v, dtype, kv.total_rows, D, kChunk, 64, true)) return SPA_ERR_INVALID;
+  auto kern = decode_mma_kernel<T, D, kDecodeStages>;
+  SPA_CHECK_CUDA(spa_set_smem_once(kern, S::kBytes));
+  kern<<<dim3(a.nsplit, a.Hkv, a.B), kDecodeThreads, S::kBytes, st>>>(kmap, vmap, a);
+  SPA_CHECK_CUDA(cudaGetLastError());
+  return SPA_OK;
+}
+
+template <typename T>
+int launch_decode(const spa_kv_layout& kv, int dtype, DecodeArgs a, bool fast, cudaStream_t st) {
+  int rc = SPA_OK;
+  if (fast) {
+    rc = a.D == 128 ? launch_decode_mma<T, 128>(kv, dtype, a, st) : launch_decode_mma<T, 64>(kv, dtype, a, st);
+    if (rc) return rc;
+  } else {
+    decode_generic_kernel<T><<<dim3(a.nsplit, a.Hq, a.B), 32, 0, st>>>(static_cast<const T*>(kv.k),
+                                                                        static_cast<const T*>(kv.v), a);
+    SPA_CHECK_CUDA(cudaGetLastError());
+  }
+  if (a.nsplit > 1) {
+    decode_combine_kernel<T><<<a.B * a.Hq, 128, 0, st>>>(a.part_o, a.part_lse, a.nsplit, a.D,
+                                                          static_cast<T*>(a.out));
+    SPA_CHECK_CUDA(cudaGetLastError());
+  }
+  return SPA_OK;
+}
+
+template <>
+int launch_decode<float>(const spa_kv_layout& kv, int dtype, DecodeArgs a, bool, cudaStream_t st) {
+  (void)dtype;
+  decode_generic_kernel<float><<<dim3(a.nsplit, a.Hq, a.B), 32, 0, st>>>(static_cast<const float*>(kv.k),
+                                                                          static_cast<const float*>(kv.v), a);
+  SPA_CHECK_CUDA(cudaGetLastError());
+  if (a.nsplit > 1) {
+    decode_combine_kernel<float><<<a.B * a.Hq, 128, 0, st>>>(a.part_o, a.part_lse, a.nsplit, a.D,
+                                                              static_cast<float*>(a.out));
+    SPA_CHECK_CUDA(cudaGetLastError());
+  }
+  return SPA_OK;
+}
+
+}  // namespace spa
+
+// ---------------------------------------------------------------------------
+// C ABI
+extern "C" size_t spa_decode_workspace_size(int batch, int q_heads, int kv_heads, int head_dim,
+                                            int max_candidates) {
+  if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || max_candidates < 0) return 0;
+  const int ns = spa::decode_nsplit(batch, kv_heads, max_candidates);
+  if (ns <= 1) return 0;
+  return static_cast<size_t>(batch) * q_heads * ns * (head_dim + 1) * sizeof(float);
+}
+
+extern "C" int spa_paged_decode(const void* q, int dtype, int batch, int q_heads, int kv_heads, int head_dim,
+                                const spa_kv_layout* kv, const int32_t* context_lens, int local_window,
+                                const int64_t* selected, int top_m, int max_candidates, double scale, void* out,
+                                void* workspace, size_t workspace_bytes, spa_stream_t stream) {
+  if (!q || !out || !kv || !kv->k || !kv->v || !context_lens) return SPA_ERR_INVALID;
+  if (!dtype_ok(dtype) || batch <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads) return SPA_ERR_INVALID;
+  if (head_dim <= 0 || head_dim > 256 || kv->page_size <= 0 || kv->total_rows <= 0) return SPA_ERR_INVALID;
+  if (local_window < 0 || max_candidates < 0 || (selected && top_m <= 0)) return SPA_ERR_INVALID;
+  if (kv->page_table && kv->table_stride <= 0) return SPA_ERR_INVALID;
+  spa::DecodeArgs a;
+  a.q = q;
+  a.out = out;
+  a.B = batch;
+  a.Hq = q_heads;
+  a.Hkv = kv_heads;
+  a.group = q_heads / kv_heads;
+  a.D = head_dim;
+  a.addr = make_kv_addr(*kv);
+  a.ctx_lens = context_lens;
+  a.local_window = local_window;
+  a.selected = selected;
+  a.top_m = selected ? top_m : 0;
+  a.nsplit = spa::decode_nsplit(batch, kv_heads, max_candidates);
+  a.scale = static_cast<float>(scale);
+  a.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  a.part_o = nullptr;
+  a.part_lse = nullptr;
+  if (a.nsplit > 1) {
+    const size_t need = spa_decode_workspace_size(batch, q_heads, kv_heads, head_dim, max_candidates);
+    if (!workspace || workspace_bytes < need) return SPA_ERR_WORKSPACE;
+    a.part_o = static_cast<float*>(workspace);
+    a.part_lse = a.part_o + static_cast<size_t>(batch) * q_heads * a.nsplit * head_dim;
+  }
+  const bool linear_rows = !kv->page_table && kv->page_stride_rows == kv->page_size;
+  const bool fast = dtype != SPA_F32 && (head_dim == 64 || head_dim == 128) && a.group <= 16 &&
+                    (kv->page_size % spa::kChunk == 0 || linear_rows) && kv->total_rows < (1ll << 31) &&
+                    reinterpret_cast<uintptr_t>(kv->k) % 16 == 0 && reinterpret_cast<uintptr_t>(kv->v) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(q) % 4 == 0;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SPA_F32:
+      return spa::launch_decode<float>(*kv, dtype, a, false, st);
+    case SPA_F16:
+      return spa::launch_decode<__half>(*kv, dtype, a, fast, st);
+    default:
+      return spa::launch_decode<__nv_bfloat16>(*kv, dtype, a, fast, st);
+  }
+}

@@ -1,0 +1,101 @@
+// Library runtime: device error word, version string, TMA descriptor encoding
+// (through the driver entry point, so the library needs no -lcuda) with a small
+// host-side cache keyed by (base, shape, box, dtype).
+#pragma once
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+extern "C" const char* spa_version(void) {
+  return "spa_b200 0.1 (sm_100a; tcgen05 prefill, TMA+mma.sync paged decode, fp64 router)";
+}
+
+extern "C" int spa_device_error(uint32_t* out_flags) {
+  if (!out_flags) return SPA_ERR_INVALID;
+  SPA_CHECK_CUDA(cudaDeviceSynchronize());
+  uint32_t v = 0, zero = 0;
+  SPA_CHECK_CUDA(cudaMemcpyFromSymbol(&v, g_spa_error_flags, sizeof(v)));
+  SPA_CHECK_CUDA(cudaMemcpyToSymbol(g_spa_error_flags, &zero, sizeof(zero)));
+  *out_flags = v;
+  return SPA_OK;
+}
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+struct MapKey {
+  uintptr_t base;
+  uint64_t rows, cols;
+  uint32_t box_rows, box_cols;
+  int dtype, swz, dev;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && rows == o.rows && cols == o.cols && box_rows == o.box_rows &&
+           box_cols == o.box_cols && dtype == o.dtype && swz == o.swz && dev == o.dev;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = k.base * 1000003u;
+    h ^= k.rows + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+    h ^= k.cols * 31 + k.box_rows * 131 + k.box_cols * 7 + k.dtype * 3 + k.swz + k.dev * 977;
+    return h;
+  }
+};
+
+}  // namespace
+
+bool spa_make_tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols,
+                            uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, box_rows, box_cols, dtype, swizzle128 ? 1 : 0, dev};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return false;
+  const size_t es = dtype_size(dtype);
+  if ((cols * es) % 16 != 0) return false;
+  CUtensorMapDataType dt = dtype == SPA_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                           : dtype == SPA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * es};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(out, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, *out);
+  return true;
+}

@@ -1,0 +1,185 @@
+/*
+ * spa_b200.h -- C ABI of the B200 (sm_100a) sparse paged-attention library.
+ *
+ * Every entry point takes raw device pointers, sizes and a cudaStream_t, enqueues
+ * its work on that stream and returns immediately (no host synchronisation).  No
+ * function allocates device memory; callers pass a workspace when one is needed
+ * and query its size first.  Return value: SPA_OK (0) or a spa_status code.
+ *
+ * The reference (divagr18/attention) is Python + Triton; each function below names
+ * the reference function or Triton launch it replaces.
+ */
+#ifndef SPA_B200_H
+#define SPA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* spa_stream_t; /* same type as cudaStream_t */
+
+typedef enum {
+  SPA_OK = 0,
+  SPA_ERR_INVALID = 1,     /* bad shape, pointer, alignment or argument */
+  SPA_ERR_UNSUPPORTED = 2, /* valid request this build does not implement */
+  SPA_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed */
+  SPA_ERR_WORKSPACE = 4,   /* workspace pointer missing or too small */
+  SPA_ERR_TIMEOUT = 5      /* a bounded device-side wait gave up */
+} spa_status;
+
+typedef enum { SPA_F32 = 0, SPA_F16 = 1, SPA_BF16 = 2 } spa_dtype;
+
+/*
+ * Where the K/V rows of a (sequence b, kv head h, token t) live.  A "row" is the
+ * head_dim contiguous elements of one token of one head.  Row index:
+ *
+ *   page = page_table ? page_table[b * table_stride + t / page_size] : t / page_size
+ *   row  = b * batch_stride_rows + page * page_stride_rows
+ *        + h * head_stride_rows + t % page_size
+ *
+ * Shared page pool [num_pages, Hkv, P, D]:   batch_stride_rows = 0,
+ *     page_stride_rows = Hkv * P, head_stride_rows = P, page_table = [B, max_pages].
+ * Reference contiguous layout [B, H, L, D] (triton_paged_attention.py:56,139):
+ *     batch_stride_rows = H * L, page_stride_rows = P, head_stride_rows = L,
+ *     page_table = NULL.
+ * k and v share the layout.  total_rows bounds every row the kernels may touch.
+ */
+typedef struct {
+  const void* k;
+  const void* v;
+  int64_t total_rows;
+  int64_t batch_stride_rows;
+  int64_t page_stride_rows;
+  int64_t head_stride_rows;
+  const int32_t* page_table;
+  int32_t table_stride;
+  int32_t page_size;
+} spa_kv_layout;
+
+/* Library version and build information (NUL-terminated, static storage). */
+const char* spa_version(void);
+
+/* Reads and clears the library's device-side error word on the current device
+ * (nonzero after a bounded wait gave up or a kernel saw an invalid page id).
+ * Synchronises the current device.  Returns SPA_OK or SPA_ERR_CUDA. */
+int spa_device_error(uint32_t* out_flags);
+
+/*
+ * Page summaries: summary[b, h, g, :] = mean of K rows of logical page g of
+ * sequence b, kv head h, for g < n_pages (the routable, historical pages).
+ * Accumulated in fp64 in token order, stored fp32.  Optional superblock
+ * summaries: super[b, h, s, :] = mean of K over pages [s*superblock,
+ * min((s+1)*superblock, n_pages)), accumulated in fp64 from the page sums.
+ * Replaces: keys[:, :, :hist].view(B,H,hist/P,P,D).mean(3)
+ *   (triton_paged_gather_decode_benchmark.py:61, triton_paged_decode_benchmark.py:71).
+ * page_sums64: workspace of B*Hkv*n_pages*D doubles (required when super != NULL).
+ */
+int spa_summaries_build(const spa_kv_layout* kv, int batch, int kv_heads,
+                        int head_dim, int dtype, int n_pages, float* summaries,
+                        int superblock, float* super_summaries,
+                        double* page_sums64, spa_stream_t stream);
+
+/*
+ * Router: score[b, g] = scale * mean_h (q[b, h, :] . summary[b, h / group, g, :])
+ * in fp64, then the top_m pages by descending score, ties to the lower page
+ * index, written as int64 [B, top_m] in descending-score order.  Optional
+ * scores_out: fp64 [B, n_pages].
+ * Replaces: select_blocks (triton_paged_gather_decode_benchmark.py:16-17,
+ *   triton_promotion_cache_benchmark.py:16-17) and the routing half of
+ *   paged_candidates (triton_paged_decode_benchmark.py:29-30).
+ */
+int spa_router_topm(const void* q, int q_dtype, int batch, int q_heads,
+                    int kv_heads, int head_dim, const float* summaries,
+                    int n_pages, double scale, int top_m, int64_t* selected,
+                    double* scores_out, spa_stream_t stream);
+
+/*
+ * Two-level (tree) router: score superblocks with super_summaries, keep the
+ * top_super, then score only the pages inside them with page summaries and keep
+ * top_m.  Same scoring, ordering and tie rule as spa_router_topm.
+ * Replaces the block->token hierarchy of hierarchical_retrieval
+ *   (benchmark_decode_attention.py:58-67) with superblock->page levels.
+ */
+int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q_heads,
+                         int kv_heads, int head_dim,
+                         const float* super_summaries, int n_super,
+                         const float* summaries, int n_pages, int superblock,
+                         int top_super, double scale, int top_m,
+                         int64_t* selected, spa_stream_t stream);
+
+/*
+ * Split-K paged decode attention.  For each sequence b and query head h
+ * (kv head h / (q_heads / kv_heads)):
+ *   out[b,h] = softmax(q . K_C^T * scale) V_C
+ * over the candidate token set C (one softmax over all of it):
+ *   selected == NULL:  C = [lo_b, ctx_b) where ctx_b = context_lens[b] and
+ *                      lo_b = max(0, ctx_b - local_window) (local_window <= 0:
+ *                      the whole context).
+ *   selected != NULL:  C = [ctx_b - local_window, ctx_b) followed by the
+ *                      top_m logical pages selected[b, :] (int64), each
+ *                      page_size tokens.
+ * q: [B, Hq, D]; out: [B, Hq, D] (same dtype as q).
+ * Replaces: paged_decode_attention_kernel launch (triton_paged_attention.py:56-81)
+ *   and paged_gather_decode_attention_kernel launch (:139-168).
+ * workspace: spa_decode_workspace_size() bytes of device memory (may be NULL
+ *   when that size is 0).
+ */
+size_t spa_decode_workspace_size(int batch, int q_heads, int kv_heads,
+                                 int head_dim, int max_candidates);
+int spa_paged_decode(const void* q, int dtype, int batch, int q_heads,
+                     int kv_heads, int head_dim, const spa_kv_layout* kv,
+                     const int32_t* context_lens, int local_window,
+                     const int64_t* selected, int top_m, int max_candidates,
+                     double scale, void* out, void* workspace,
+                     size_t workspace_bytes, spa_stream_t stream);
+
+/*
+ * KV append: writes k_new/v_new [B, Hkv, D] at token positions[b] of sequence b
+ * (the row given by the layout).  Replaces the tail overwrite of
+ * page_decode (triton_kvcache_transformer_decode.py:51-55).
+ */
+int spa_kv_append(const spa_kv_layout* kv, int dtype, int batch, int kv_heads,
+                  int head_dim, const void* k_new, const void* v_new,
+                  const int32_t* positions, spa_stream_t stream);
+
+/*
+ * Causal sliding-window local prefill, q/k/v/out [B, H, S, D] contiguous:
+ *   out[b,h,i] = softmax_{j in [i-W+1, i]} (q_i . k_j * D^-1/2) v_j
+ * Optional halo (sequence-parallel chunk): k_halo/v_halo [B, H, halo_len, D]
+ * hold the halo_len keys that precede this chunk; query i then sees keys
+ * i+halo_len-W+1 .. i+halo_len of the concatenation [halo ; k].
+ * Only query rows [row_begin, row_end) are computed (row_end <= 0: seq_len), so
+ * rows that need no halo can run while the halo is still in flight.
+ * Replaces: local_causal_prefill_kernel launch (triton_local_prefill.py:61-81).
+ */
+int spa_local_prefill(const void* q, const void* k, const void* v, int dtype,
+                      int batch, int heads, int seq_len, int head_dim,
+                      int window, const void* k_halo, const void* v_halo,
+                      int halo_len, int row_begin, int row_end, void* out,
+                      spa_stream_t stream);
+
+/*
+ * Promotion cache update (one table of `slots` entries per row r < rows):
+ * page[r, i] (int32, -1 = free) and last_hit[r, i] (int32).  With the row's
+ * selected pages sel[r, 0..top_m) at decode step `step`:
+ *   1. a selected page already present gets last_hit = step;
+ *   2. entries with step - last_hit >= ttl are freed (page = -1);
+ *   3. each new selected page (in selection order) takes the free slot with
+ *      the lowest index, else evicts the entry with the smallest last_hit,
+ *      ties to the smallest page id.
+ * Requires top_m <= slots; duplicate ids in one selection count once.
+ * Replaces the host-side promoted-id swap of triton_promotion_cache_benchmark.py:53-60
+ *   with a fixed-TTL policy (evaluate_promotion_ttl.py:134-135).
+ */
+int spa_promotion_update(int32_t* pages, int32_t* last_hit, int rows,
+                         int slots, const int64_t* selected, int top_m,
+                         int step, int ttl, spa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPA_B200_H */

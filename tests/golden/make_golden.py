@@ -1,0 +1,116 @@
+"""Generates tests/golden/*.npz by running the reference's own PyTorch functions.
+
+Run where the reference checkout is importable (it is not needed anywhere else):
+
+    python tests/golden/make_golden.py /path/to/divagr18-attention
+
+Every fixture stores the seed and shapes that regenerate its inputs with
+torch.manual_seed + torch.randn on CPU (the reference's own draw order), input
+checksums to prove the regeneration, and the reference's outputs:
+
+* cfg1_sparse_decode  -- batch 1, 8 heads, head_dim 64, fp32, 4096 tokens in 32
+  pages of 128, seed 0, draws K, V, q; select_blocks top-4 over the 31 historical
+  pages, make_candidates + reference_attention over 640 tokens, and the dense
+  masked attention over the same token set.
+* gather_small        -- seed 7 (reference main() order q, K, V): select_blocks,
+  make_candidates + reference_attention, paged_candidates equality.
+* dense_small         -- seed 7: reference_attention over the whole buffer.
+* prefill_small       -- seed 7: local_reference (masked causal window).
+* periodic_router     -- seed 7: periodic_router indices with -1 padding.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+def main(ref_root: str) -> None:
+    sys.path.insert(0, str(Path(ref_root) / "experiments"))
+    import triton_local_prefill as tlp  # noqa: E402
+    import triton_paged_attention as tpa  # noqa: E402
+    import triton_paged_decode_benchmark as tpd  # noqa: E402
+    import triton_paged_gather_decode_benchmark as tpg  # noqa: E402
+    import triton_prefill_router_overhead as tpr  # noqa: E402
+
+    # ---- configuration 1
+    torch.manual_seed(0)
+    b, h, length, d, page, win, m = 1, 8, 4096, 64, 128, 128, 4
+    keys = torch.randn(b, h, length, d)
+    values = torch.randn(b, h, length, d)
+    query = torch.randn(b, h, d)
+    hist = length - win
+    summaries = keys[:, :, :hist].view(b, h, hist // page, page, d).mean(3).contiguous()
+    sel = tpg.select_blocks(query, summaries, m)
+    ck, cv = tpg.make_candidates(keys, values, sel, win, page)
+    out = tpa.reference_attention(query, ck, cv)
+    allowed = torch.zeros(b, length, dtype=torch.bool)
+    allowed[:, hist:] = True
+    for bb in range(b):
+        for p in sel[bb].tolist():
+            allowed[bb, p * page:(p + 1) * page] = True
+    scores = torch.einsum("bhd,bhld->bhl", query, keys) / d ** 0.5
+    dense_masked = torch.einsum("bhl,bhld->bhd", scores.masked_fill(~allowed[:, None], float("-inf")).softmax(-1),
+                                values)
+    np.savez(HERE / "cfg1_sparse_decode.npz", seed=0, shape=np.array([b, h, length, d, page, win, m]),
+             k_sum=keys.double().sum().item(), v_sum=values.double().sum().item(), q_sum=query.double().sum().item(),
+             selected=sel.numpy(), out=out.numpy(), dense_masked=dense_masked.numpy(),
+             summaries=summaries.numpy())
+
+    # ---- gather (reference main() draw order: q, K, V)
+    torch.manual_seed(7)
+    b, h, length, d, page, win, m = 2, 4, 2048, 32, 256, 256, 3
+    query = torch.randn(b, h, d)
+    keys = torch.randn(b, h, length, d)
+    values = torch.randn_like(keys)
+    hist = length - win
+    summaries = keys[:, :, :hist].view(b, h, hist // page, page, d).mean(3).contiguous()
+    sel = tpg.select_blocks(query, summaries, m)
+    ck, cv = tpg.make_candidates(keys, values, sel, win, page)
+    out = tpa.reference_attention(query, ck, cv)
+    pk, pv = tpd.paged_candidates(query, keys, values, summaries, local_window=win, block_size=page, top_blocks=m)
+    assert torch.equal(pk, ck) and torch.equal(pv, cv)
+    np.savez(HERE / "gather_small.npz", seed=7, shape=np.array([b, h, length, d, page, win, m]),
+             k_sum=keys.double().sum().item(), v_sum=values.double().sum().item(), q_sum=query.double().sum().item(),
+             selected=sel.numpy(), out=out.numpy())
+
+    # ---- dense candidate buffer
+    torch.manual_seed(7)
+    b, h, length, d = 2, 4, 1280, 16
+    query = torch.randn(b, h, d)
+    keys = torch.randn(b, h, length, d)
+    values = torch.randn_like(keys)
+    out = tpa.reference_attention(query, keys, values)
+    np.savez(HERE / "dense_small.npz", seed=7, shape=np.array([b, h, length, d]),
+             k_sum=keys.double().sum().item(), v_sum=values.double().sum().item(), q_sum=query.double().sum().item(),
+             out=out.numpy())
+
+    # ---- prefill
+    torch.manual_seed(7)
+    b, h, s, d, w = 1, 2, 300, 16, 64
+    query = torch.randn(b, h, s, d)
+    keys = torch.randn_like(query)
+    values = torch.randn_like(query)
+    out = tlp.local_reference(query, keys, values, w)
+    np.savez(HERE / "prefill_small.npz", seed=7, shape=np.array([b, h, s, d, w]),
+             k_sum=keys.double().sum().item(), v_sum=values.double().sum().item(), q_sum=query.double().sum().item(),
+             out=out.numpy())
+
+    # ---- periodic causal router
+    torch.manual_seed(7)
+    b, h, ctx, d, page, stride, m = 1, 2, 1024, 16, 128, 128, 3
+    query = torch.randn(b, h, ctx, d)
+    keys = torch.randn_like(query)
+    sel = tpr.periodic_router(query, keys, block_size=page, router_stride=stride, top_blocks=m)
+    np.savez(HERE / "periodic_router.npz", seed=7, shape=np.array([b, h, ctx, d, page, stride, m]),
+             k_sum=keys.double().sum().item(), q_sum=query.double().sum().item(), selected=sel.numpy())
+    print("wrote fixtures to", HERE)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
