@@ -217,21 +217,16 @@ inline KvAddr make_kv_addr(const spa_kv_layout& kv) {
 inline size_t dtype_size(int dtype) { return dtype == SPA_F32 ? 4 : 2; }
 inline bool dtype_ok(int dtype) { return dtype == SPA_F32 || dtype == SPA_F16 || dtype == SPA_BF16; }
 
-// Host: sets a kernel's dynamic shared memory limit once per device.
+// Host: sets a kernel's dynamic shared memory limit once per (kernel, device).
+cudaError_t spa_set_smem_limit(const void* kernel, int bytes);
 template <typename K>
 inline cudaError_t spa_set_smem_once(K kernel, int bytes) {
-  static uint64_t done_mask = 0;  // one bit per device ordinal < 64
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
-  if (bit && (__atomic_load_n(&done_mask, __ATOMIC_ACQUIRE) & bit)) return cudaSuccess;
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess && bit) __atomic_fetch_or(&done_mask, bit, __ATOMIC_ACQ_REL);
-  return e;
+  return spa_set_smem_limit(reinterpret_cast<const void*>(kernel), bytes);
 }
 
 // Host: builds (and caches) a 2D tiled TMA descriptor over a [rows, cols] row-major
 // buffer with box [box_rows, box_cols] and 128-byte swizzle.  Returns false on failure.
 bool spa_make_tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols,
                             uint32_t box_rows, uint32_t box_cols, bool swizzle128);
+// Host: 3D view [bh, rows, d] of a contiguous [B, H, rows, D] tensor, box [1, 128, 64], 128-byte swizzle.
+bool spa_make_tensor_map_3d(CUtensorMap* out, const void* base, int dtype, uint64_t d, uint64_t rows, uint64_t bh);

@@ -1,16 +1,496 @@
 // Causal sliding-window prefill on the sm_100a tensor cores (tcgen05 + TMEM).
-// Placeholder dispatch until the tensor-core kernel lands: no shape is routed here.
+//
+// Reference: local_causal_prefill_kernel (triton_local_prefill.py:17-58), one program
+// per query row scanning keys [i-W+1, i] with an online softmax.  Here one CTA owns two
+// 128-row query tiles of one (b, h) and streams the 128-key tiles that intersect their
+// windows (W/128 + 2 tiles for W a multiple of 128):
+//
+//   warp 0      TMA producer: Q tiles once, then K/V tiles into a STAGES-deep ring
+//   warp 1      MMA issuer (one thread): S_t = Q_t K^T (SS form, both operands in
+//               shared memory, K-major), O_t += P_t V (TS form: P read from TMEM,
+//               V from shared memory, MN-major)
+//   warps 4-7   softmax of query tile 0 (thread = row = TMEM lane)
+//   warps 8-11  softmax of query tile 1
+//
+// TMEM (512 columns): S_0 [0,128), S_1 [128,256), O_0 [256,256+D), O_1 [384,384+D).
+// P_t (bf16 pairs) overwrites the first 64 columns of S_t once S_t is in registers.
+// The MMA warp interleaves O_0(j), S_0(j+1), O_1(j), S_1(j+1) so each softmax warp
+// group overlaps the other tile's tensor-core work.  The running max is only moved
+// (and O rescaled in TMEM) when a tile's max exceeds it by more than 2^8.
+//
+// Keys are indexed in the concatenation [halo ; keys] (halo_len a multiple of 128):
+// query i sits at position i + halo_len and sees positions (i+halo-W, i+halo].
 #pragma once
 
 #include "prefill_generic.cuh"
 
 namespace spa {
 
-inline bool prefill_sm100_supported(const PrefillArgs&, int) { return false; }
+constexpr int kPfTile = 128;
+constexpr int kPfStages = 2;
+constexpr int kPfThreads = 384;
+constexpr float kPfRescaleThreshold = 8.0f;  // log2 units
+
+struct PfTcArgs {
+  void* out;
+  int S, W, halo, row0, row1, H, n_pairs;
+  float scale_log2;
+};
+
+template <int D>
+struct PfSmem {
+  static constexpr int kBoxBytes = kPfTile * 128;  // [128 rows x 64 elements] bf16
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kTileBytes = kBoxes * kBoxBytes;
+  static constexpr int kQ0 = 0;
+  static constexpr int kQ1 = kTileBytes;
+  static constexpr int kK = 2 * kTileBytes;
+  static constexpr int kV = kK + kPfStages * kTileBytes;
+  static constexpr int kBar = kV + kPfStages * kTileBytes;
+  // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_final[2], mma_done; + tmem slot
+  static constexpr int kNumBars = 1 + 2 * kPfStages + 2 + 2 + 2 + 1;
+  static constexpr int kBytes = kBar + kNumBars * 8 + 16 + 1024;
+};
+
+// ---- tcgen05 wrappers
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// D[tmem] (+)= A[smem desc] * B[smem desc]
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+#define SPA_TMEM_LD32(taddr, r)                                                                                  \
+  asm volatile(                                                                                                  \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"   \
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                                        \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),         \
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),  \
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), \
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])  \
+      : "r"(taddr))
+
+#define SPA_TMEM_ST32(taddr, r)                                                                                  \
+  asm volatile(                                                                                                  \
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"   \
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),                         \
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),        \
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),           \
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),          \
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])                      \
+      : "memory")
+
+#define SPA_TMEM_ST16(taddr, r)                                                                                  \
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14," \
+               "%15,%16};" ::"r"(taddr),                                                                        \
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),          \
+               "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])     \
+               : "memory")
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (SWIZZLE_128B, sm_100 version field = 1).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= 1ull << 46;  // version
+  d |= 2ull << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: fp32 accumulate, A/B 16-bit (fmt 0 = f16, 1 = bf16).
+__host__ __device__ constexpr uint32_t instr_desc_f16(int fmt, int m, int n, int a_mn_major, int b_mn_major) {
+  return (1u << 4) | (static_cast<uint32_t>(fmt) << 7) | (static_cast<uint32_t>(fmt) << 10) |
+         (static_cast<uint32_t>(a_mn_major) << 15) | (static_cast<uint32_t>(b_mn_major) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
+                                            int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 
 template <typename T>
-int launch_prefill_sm100(const PrefillArgs& a, int, cudaStream_t st) {
-  return launch_prefill_generic<T>(a, st);
+struct PfFmt;
+template <>
+struct PfFmt<__nv_bfloat16> {
+  static constexpr int kFmt = 1;
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+template <>
+struct PfFmt<__half> {
+  static constexpr int kFmt = 0;
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+
+// Key-tile range [lo, hi] (concatenated coordinates) of query tile qt; empty if lo > hi.
+__device__ __forceinline__ void pf_tile_range(const PfTcArgs& a, int qt, int& lo, int& hi) {
+  const int qc0 = qt * kPfTile + a.halo;                          // first query position
+  const int qlast = min(qt * kPfTile + kPfTile, a.S) - 1 + a.halo;  // last real query position
+  const int first_key = qc0 - a.W + 1;
+  lo = first_key <= 0 ? 0 : first_key / kPfTile;
+  hi = qlast / kPfTile;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap khmap,
+                      const __grid_constant__ CUtensorMap vhmap, const PfTcArgs a) {
+  using L = PfSmem<D>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + kPfStages;
+  uint64_t* s_full = kv_empty + kPfStages;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_final = p_full + 2;
+  uint64_t* mma_done = o_final + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int qt0 = a.row0 / kPfTile + 2 * blockIdx.x;
+  const int last_tile = (a.row1 - 1) / kPfTile;
+  bool act[2];
+  int lo[2], hi[2];
+  for (int t = 0; t < 2; ++t) {
+    act[t] = qt0 + t <= last_tile;
+    pf_tile_range(a, qt0 + t, lo[t], hi[t]);
+    if (lo[t] > hi[t]) act[t] = false;
+  }
+  const int J0 = act[0] ? lo[0] : lo[1];
+  const int J1 = act[1] ? hi[1] : hi[0];
+  const int halo_tiles = a.halo / kPfTile;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_final[t], 1);
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0 && (act[0] || act[1])) {
+      tma_prefetch_desc(&qmap);
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+      const int nq = (act[0] ? 1 : 0) + (act[1] ? 1 : 0);
+      mbar_arrive_expect_tx(q_full, nq * L::kTileBytes);
+      for (int t = 0; t < 2; ++t) {
+        if (!act[t]) continue;
+        for (int bx = 0; bx < L::kBoxes; ++bx)
+          tma_load_3d(smem + (t ? L::kQ1 : L::kQ0) + bx * L::kBoxBytes, &qmap, q_full, bx * 64,
+                      (qt0 + t) * kPfTile, bh);
+      }
+      for (int j = J0; j <= J1; ++j) {
+        const int i = j - J0, s = i % kPfStages;
+        if (i >= kPfStages && !mbar_wait_bounded(&kv_empty[s], ((i / kPfStages) - 1) & 1)) break;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * L::kTileBytes);
+        const bool from_halo = j < halo_tiles;
+        const CUtensorMap* km = from_halo ? &khmap : &kmap;
+        const CUtensorMap* vm = from_halo ? &vhmap : &vmap;
+        const int y = from_halo ? j * kPfTile : (j - halo_tiles) * kPfTile;
+        for (int bx = 0; bx < L::kBoxes; ++bx) {
+          tma_load_3d(smem + L::kK + s * L::kTileBytes + bx * L::kBoxBytes, km, &kv_full[s], bx * 64, y, bh);
+          tma_load_3d(smem + L::kV + s * L::kTileBytes + bx * L::kBoxBytes, vm, &kv_full[s], bx * 64, y, bh);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0 && (act[0] || act[1])) {
+      constexpr uint32_t kIdQK = instr_desc_f16(PfFmt<T>::kFmt, kPfTile, kPfTile, 0, 0);
+      constexpr uint32_t kIdPV = instr_desc_f16(PfFmt<T>::kFmt, kPfTile, D, 0, 1);
+      const uint32_t q_addr[2] = {smem_u32(smem + L::kQ0), smem_u32(smem + L::kQ1)};
+      const uint32_t k_addr = smem_u32(smem + L::kK), v_addr = smem_u32(smem + L::kV);
+      const uint32_t s_col[2] = {0u, 128u}, o_col[2] = {256u, 384u};
+      bool ok = mbar_wait_bounded(q_full, 0);
+      int it[2] = {0, 0};
+      int kv_ready = J0 - 1;  // last key tile whose kv_full has been waited on
+      auto wait_kv = [&](int j) -> bool {
+        if (j <= kv_ready) return true;
+        const int i = j - J0;
+        if (!mbar_wait_bounded(&kv_full[i % kPfStages], (i / kPfStages) & 1)) return false;
+        kv_ready = j;
+        tc_fence_after();
+        return true;
+      };
+      auto issue_s = [&](int t, int j) {
+        const uint32_t kb = k_addr + ((j - J0) % kPfStages) * L::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kBoxBytes + (kk & 3) * 32;
+          mma_ss(tmem + s_col[t], smem_desc(q_addr[t] + off, 16, 1024), smem_desc(kb + off, 16, 1024), kIdQK,
+                 kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[t]);
+      };
+      // prologue: S_t(J0)
+      if (ok && wait_kv(J0)) {
+        for (int t = 0; t < 2; ++t)
+          if (act[t] && lo[t] <= J0 && J0 <= hi[t]) issue_s(t, J0);
+      } else {
+        ok = false;
+      }
+      for (int j = J0; ok && j <= J1; ++j) {
+        const uint32_t vb = v_addr + ((j - J0) % kPfStages) * L::kTileBytes;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (act[t] && lo[t] <= j && j <= hi[t]) {
+            if (!mbar_wait_bounded(&p_full[t], it[t] & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kPfTile / 16; ++kk)
+              mma_ts(tmem + o_col[t], tmem + s_col[t] + kk * 8,
+                     smem_desc(vb + kk * 16 * 128, L::kBoxBytes, 1024), kIdPV, (it[t] > 0 || kk > 0) ? 1u : 0u);
+            ++it[t];
+            if (j == hi[t]) tc_commit(&o_final[t]);
+          }
+          if (act[t] && lo[t] <= j + 1 && j + 1 <= hi[t]) {
+            if (!wait_kv(j + 1)) {
+              ok = false;
+              break;
+            }
+            issue_s(t, j + 1);
+          }
+        }
+        tc_commit(&kv_empty[(j - J0) % kPfStages]);
+      }
+      // every issued MMA completes before TMEM is released
+      tc_commit(mma_done);
+      mbar_wait_bounded(mma_done, 0);
+    }
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- softmax
+    const int t = (warp - 4) >> 2;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // row within the tile == TMEM lane
+    if (act[t]) {
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+      const uint32_t s_addr = lane_base + (t ? 128u : 0u);
+      const uint32_t o_addr = lane_base + (t ? 384u : 256u);
+      const int qc = (qt0 + t) * kPfTile + r + a.halo;  // this row's query position
+      float m_run = -INFINITY, l_run = 0.f;
+      bool ok = true;
+      const int n = hi[t] - lo[t] + 1;
+      for (int it = 0; it < n; ++it) {
+        const int j = lo[t] + it;
+        if (!mbar_wait_bounded(&s_full[t], it & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int kc0 = j * kPfTile;
+        const int tile_q0 = (qt0 + t) * kPfTile + a.halo;
+        const bool full_tile =
+            kc0 + kPfTile - 1 <= tile_q0 && kc0 > tile_q0 + kPfTile - 1 - a.W && kc0 + kPfTile <= a.halo + a.S;
+        const int kmax = full_tile ? 127 : min(qc, a.halo + a.S - 1) - kc0;  // last valid column
+        const int kmin = full_tile ? 0 : qc - a.W + 1 - kc0;                 // first valid column
+        // pass 1: row max of the scaled, masked scores (S stays in TMEM)
+        float mt = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t u[32];
+          SPA_TMEM_LD32(s_addr + 32 * c, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int col = 32 * c + e;
+            const float x = __uint_as_float(u[e]) * a.scale_log2;
+            mt = (col >= kmin && col <= kmax) ? fmaxf(mt, x) : mt;
+          }
+        }
+        if (mt > m_run + kPfRescaleThreshold || (m_run == -INFINITY && mt > -INFINITY)) {
+          // move the running max; rescale O (complete: S_t(j) was issued after O_t(j-1))
+          const float alpha = fast_exp2(m_run - mt);  // 0 when m_run = -inf
+          if (it > 0 && m_run > -INFINITY) {
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t o[32];
+              SPA_TMEM_LD32(o_addr + 32 * c, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              SPA_TMEM_ST32(o_addr + 32 * c, o);
+            }
+          }
+          l_run *= alpha;
+          m_run = mt;
+        }
+        const float mu = m_run == -INFINITY ? 0.f : m_run;
+        // pass 2: P = exp2(s - m) as 16-bit pairs into the first 64 columns of S_t.  Chunk c
+        // reads columns [32c, 32c+32) and writes [16c, 16c+16): never ahead of the reads.
+        float lsum = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t u[32];
+          SPA_TMEM_LD32(s_addr + 32 * c, u);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int col = 32 * c + 2 * e;
+            const float x0 = __uint_as_float(u[2 * e]) * a.scale_log2;
+            const float x1 = __uint_as_float(u[2 * e + 1]) * a.scale_log2;
+            const float p0 = (col >= kmin && col <= kmax) ? fast_exp2(x0 - mu) : 0.f;
+            const float p1 = (col + 1 >= kmin && col + 1 <= kmax) ? fast_exp2(x1 - mu) : 0.f;
+            lsum += p0 + p1;
+            pk[e] = PfFmt<T>::pack(p0, p1);
+          }
+          SPA_TMEM_ST16(s_addr + 16 * c, pk);
+        }
+        l_run += lsum;
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+      }
+      // epilogue: O / l -> global
+      if (ok && mbar_wait_bounded(&o_final[t], 0)) {
+        tc_fence_after();
+        const int q = (qt0 + t) * kPfTile + r;
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        T* orow = static_cast<T*>(a.out) + (static_cast<int64_t>(bh) * a.S + q) * D;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          SPA_TMEM_LD32(o_addr + 32 * c, o);
+          tmem_wait_ld();
+          if (q < a.row1) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              pk[e] = PfFmt<T>::pack(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+            uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+inline bool prefill_sm100_supported(const PrefillArgs& a, int dtype) {
+  if (dtype != SPA_BF16 && dtype != SPA_F16) return false;
+  if (a.D != 128 && a.D != 64) return false;
+  if (a.halo % kPfTile != 0 || a.row0 % kPfTile != 0) return false;
+  if (static_cast<int64_t>(a.B) * a.H > 65535) return false;
+  const uintptr_t m = reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
+                      reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.out) |
+                      reinterpret_cast<uintptr_t>(a.k_halo) | reinterpret_cast<uintptr_t>(a.v_halo);
+  return (m & 15) == 0;
+}
+
+template <typename T>
+int launch_prefill_sm100(const PrefillArgs& a, int dtype, cudaStream_t st) {
+  CUtensorMap qm, km, vm, khm, vhm;
+  const uint64_t bh = static_cast<uint64_t>(a.B) * a.H;
+  if (!spa_make_tensor_map_3d(&qm, a.q, dtype, a.D, a.S, bh) || !spa_make_tensor_map_3d(&km, a.k, dtype, a.D, a.S, bh) ||
+      !spa_make_tensor_map_3d(&vm, a.v, dtype, a.D, a.S, bh))
+    return SPA_ERR_INVALID;
+  if (a.halo > 0) {
+    if (!spa_make_tensor_map_3d(&khm, a.k_halo, dtype, a.D, a.halo, bh) ||
+        !spa_make_tensor_map_3d(&vhm, a.v_halo, dtype, a.D, a.halo, bh))
+      return SPA_ERR_INVALID;
+  } else {
+    khm = km;
+    vhm = vm;
+  }
+  PfTcArgs t;
+  t.out = a.out;
+  t.S = a.S;
+  t.W = a.W;
+  t.halo = a.halo;
+  t.row0 = a.row0;
+  t.row1 = a.row1;
+  t.H = a.H;
+  const int tiles = (a.row1 - 1) / kPfTile - a.row0 / kPfTile + 1;
+  t.n_pairs = (tiles + 1) / 2;
+  t.scale_log2 = a.scale * 1.4426950408889634f;
+  if (a.D == 128) {
+    auto kern = prefill_tc_kernel<T, 128>;
+    SPA_CHECK_CUDA(spa_set_smem_once(kern, PfSmem<128>::kBytes));
+    kern<<<dim3(t.n_pairs, static_cast<unsigned>(bh)), kPfThreads, PfSmem<128>::kBytes, st>>>(qm, km, vm, khm, vhm, t);
+  } else {
+    auto kern = prefill_tc_kernel<T, 64>;
+    SPA_CHECK_CUDA(spa_set_smem_once(kern, PfSmem<64>::kBytes));
+    kern<<<dim3(t.n_pairs, static_cast<unsigned>(bh)), kPfThreads, PfSmem<64>::kBytes, st>>>(qm, km, vm, khm, vhm, t);
+  }
+  SPA_CHECK_CUDA(cudaGetLastError());
+  return SPA_OK;
 }
 
 }  // namespace spa

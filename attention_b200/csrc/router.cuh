@@ -313,8 +313,7 @@ extern "C" int spa_router_topm(const void* q, int q_dtype, int batch, int q_head
 #define SPA_LAUNCH_ROUTER(T)                                                                               \
   do {                                                                                                     \
     if (smem > 48 * 1024)                                                                                  \
-      SPA_CHECK_CUDA(cudaFuncSetAttribute(spa::router_topm_kernel<T>,                                      \
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));        \
+      SPA_CHECK_CUDA(spa_set_smem_once(spa::router_topm_kernel<T>, (int)smem));                          \
     spa::router_topm_kernel<T><<<batch, 256, smem, st>>>(static_cast<const T*>(q), q_heads, kv_heads,     \
                                                          head_dim, summaries, n_pages, scale, top_m,      \
                                                          selected, scores_out);                            \
@@ -351,8 +350,7 @@ extern "C" int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q
 #define SPA_LAUNCH_TREE(T)                                                                                  \
   do {                                                                                                      \
     if (smem > 48 * 1024)                                                                                   \
-      SPA_CHECK_CUDA(cudaFuncSetAttribute(spa::router_tree_kernel<T>,                                       \
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));         \
+      SPA_CHECK_CUDA(spa_set_smem_once(spa::router_tree_kernel<T>, (int)smem));                           \
     spa::router_tree_kernel<T><<<batch, 256, smem, st>>>(static_cast<const T*>(q), q_heads, kv_heads,      \
                                                          head_dim, super_summaries, n_super, summaries,    \
                                                          n_pages, superblock, top_super, scale, top_m,     \

@@ -44,11 +44,11 @@ EncodeTiledFn get_encode_fn() {
 
 struct MapKey {
   uintptr_t base;
-  uint64_t rows, cols;
+  uint64_t rows, cols, depth;
   uint32_t box_rows, box_cols;
   int dtype, swz, dev;
   bool operator==(const MapKey& o) const {
-    return base == o.base && rows == o.rows && cols == o.cols && box_rows == o.box_rows &&
+    return base == o.base && rows == o.rows && cols == o.cols && depth == o.depth && box_rows == o.box_rows &&
            box_cols == o.box_cols && dtype == o.dtype && swz == o.swz && dev == o.dev;
   }
 };
@@ -56,20 +56,38 @@ struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     size_t h = k.base * 1000003u;
     h ^= k.rows + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
-    h ^= k.cols * 31 + k.box_rows * 131 + k.box_cols * 7 + k.dtype * 3 + k.swz + k.dev * 977;
+    h ^= k.cols * 31 + k.depth * 65599 + k.box_rows * 131 + k.box_cols * 7 + k.dtype * 3 + k.swz + k.dev * 977;
     return h;
   }
 };
 
 }  // namespace
 
-bool spa_make_tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols,
-                            uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
+cudaError_t spa_set_smem_limit(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, int> done;  // (kernel, device) -> bytes set
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t key = (reinterpret_cast<uint64_t>(kernel) << 8) ^ static_cast<uint64_t>(dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[key] = bytes;
+  return e;
+}
+
+namespace {
+// depth == 0: 2D [rows, cols]; depth > 0: 3D [depth, rows, cols] with box depth 1.
+bool make_tensor_map(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols, uint64_t depth,
+                     uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
   static std::mutex mu;
   static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, box_rows, box_cols, dtype, swizzle128 ? 1 : 0, dev};
+  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, depth, box_rows, box_cols, dtype, swizzle128 ? 1 : 0,
+             dev};
   {
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
@@ -86,11 +104,12 @@ bool spa_make_tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint6
   CUtensorMapDataType dt = dtype == SPA_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                            : dtype == SPA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                               : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols * es};
-  cuuint32_t box[2] = {box_cols, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(out, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  const cuuint32_t rank = depth ? 3 : 2;
+  cuuint64_t dims[3] = {cols, rows, depth};
+  cuuint64_t strides[2] = {cols * es, rows * cols * es};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(out, dt, rank, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
@@ -98,4 +117,14 @@ bool spa_make_tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint6
   if (cache.size() > 4096) cache.clear();
   cache.emplace(key, *out);
   return true;
+}
+}  // namespace
+
+bool spa_make_tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols,
+                            uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
+  return make_tensor_map(out, base, dtype, rows, cols, 0, box_rows, box_cols, swizzle128);
+}
+
+bool spa_make_tensor_map_3d(CUtensorMap* out, const void* base, int dtype, uint64_t d, uint64_t rows, uint64_t bh) {
+  return make_tensor_map(out, base, dtype, rows, d, bh, 128, 64, true);
 }
