@@ -1,0 +1,54 @@
+// Allocation-free variant of spa_paged_decode.
+//
+// Some callers cannot allocate device memory at the point where they decode: a
+// serving engine that owns every byte of HBM through its own pool, or a plugin
+// host whose interface has no way to hand the plugin a workspace.  This entry
+// point takes the split-K partials from a fixed scratch array compiled into the
+// library instead of a caller workspace.  The array lives in device memory of
+// every GPU that loads the library, for the life of the process.
+#pragma once
+
+#include <mutex>
+
+#include "decode.cuh"
+
+namespace spa {
+
+// The scratch itself.  Host code must never pass this name to a kernel: on the host
+// it is only a stand-in, and the device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_decode_scratch[SPA_DECODE_STATIC_SCRATCH_BYTES];
+
+// Device address of g_decode_scratch on the current device, looked up once per
+// device (with that device current) and cached.  Returns nullptr on failure.
+inline void* decode_scratch_ptr() {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static void* ptrs[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess) return nullptr;
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+
+}  // namespace spa
+
+extern "C" int spa_paged_decode_noalloc(const void* q, int dtype, int batch, int q_heads, int kv_heads,
+                                        int head_dim, const spa_kv_layout* kv, const int32_t* context_lens,
+                                        int local_window, const int64_t* selected, int top_m, int max_candidates,
+                                        double scale, void* out, spa_stream_t stream) {
+  if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || max_candidates < 0) return SPA_ERR_INVALID;
+  const size_t need = spa_decode_workspace_size(batch, q_heads, kv_heads, head_dim, max_candidates);
+  if (need > SPA_DECODE_STATIC_SCRATCH_BYTES) return SPA_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  if (need > 0) {
+    scratch = spa::decode_scratch_ptr();
+    if (!scratch) return SPA_ERR_CUDA;
+  }
+  return spa_paged_decode(q, dtype, batch, q_heads, kv_heads, head_dim, kv, context_lens, local_window, selected,
+                          top_m, max_candidates, scale, out, scratch, need, stream);
+}

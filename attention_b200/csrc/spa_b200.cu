@@ -4,6 +4,7 @@
 #include "runtime.cuh"
 #include "router.cuh"
 #include "decode.cuh"
+#include "decode_noalloc.cuh"
 #include "cache.cuh"
 #include "prefill_generic.cuh"
 #include "prefill_sm100.cuh"

@@ -137,6 +137,32 @@ int spa_paged_decode(const void* q, int dtype, int batch, int q_heads,
                      size_t workspace_bytes, spa_stream_t stream);
 
 /*
+ * Allocation-free spa_paged_decode, for callers that cannot allocate device
+ * memory or pass a workspace (a serving engine that owns all of HBM through its
+ * own pool, a plugin interface with no workspace argument).  No counterpart in
+ * the reference, which allocates through PyTorch.
+ * Same arguments and results as spa_paged_decode, minus the workspace: the
+ * split-K partials go to a scratch array of SPA_DECODE_STATIC_SCRATCH_BYTES
+ * compiled into the library (held in device memory of every GPU that loads it
+ * until the process exits).  Returns SPA_ERR_WORKSPACE when
+ * spa_decode_workspace_size() of the request exceeds that size.
+ * Allocates nothing.  The first call on a device looks up the scratch's device
+ * address (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture.  All calls on a device share the one array: calls
+ * whose kernels can overlap on the GPU (different streams, no ordering) race and
+ * must be serialised by the caller.  Nothing in the array needs clearing: every
+ * split writes its slot before the merge reads it.
+ */
+#define SPA_DECODE_STATIC_SCRATCH_BYTES (4u << 20)
+int spa_paged_decode_noalloc(const void* q, int dtype, int batch, int q_heads,
+                             int kv_heads, int head_dim,
+                             const spa_kv_layout* kv,
+                             const int32_t* context_lens, int local_window,
+                             const int64_t* selected, int top_m,
+                             int max_candidates, double scale, void* out,
+                             spa_stream_t stream);
+
+/*
  * KV append: writes k_new/v_new [B, Hkv, D] at token positions[b] of sequence b
  * (the row given by the layout).  Replaces the tail overwrite of
  * page_decode (triton_kvcache_transformer_decode.py:51-55).
