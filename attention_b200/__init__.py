@@ -10,6 +10,7 @@ from .cache import PagedKVCache, PromotionCache, kv_append
 from .paged_attention import paged_decode_attention, paged_gather_decode_attention
 from .prefill import local_causal_prefill
 from .router import page_summaries, select_blocks, select_blocks_tree
+from .step import sparse_decode_step
 
 __all__ = [
     "LIB_PATH",
@@ -24,4 +25,5 @@ __all__ = [
     "page_summaries",
     "select_blocks",
     "select_blocks_tree",
+    "sparse_decode_step",
 ]

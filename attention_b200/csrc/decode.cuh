@@ -14,6 +14,8 @@
 // go to the workspace and a small kernel merges the splits.
 #pragma once
 
+#include <utility>
+
 #include "common.cuh"
 
 namespace spa {
@@ -30,9 +32,29 @@ struct DecodeArgs {
   int nsplit;
   float scale_log2;  // softmax scale * log2(e)
   float scale;
-  float* part_o;    // [B*Hq, nsplit, D]
-  float* part_lse;  // [B*Hq, nsplit] (log2 domain)
+  float* part_o;    // [B*Hq, nsplit, D]       (global-merge path)
+  float* part_lse;  // [B*Hq, nsplit] log2-sum-exp
+  int cluster_merge;  // splits of a pair form one cluster and merge through DSMEM
+  // Launched right after the router (programmatic dependent launch) with every input
+  // except `selected` already complete: local-window chunks may stream before the
+  // router finishes.  Otherwise the kernel waits for its predecessor before any read.
+  int early_local;
 };
+
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Barrier over the consumer threads of every CTA in the cluster (the producer warps have
+// exited; barrier.cluster counts the threads that are still running).
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_dsmem(const float* local_ptr, int rank) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+__device__ __forceinline__ void pdl_block() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 struct ChunkPlan {
   int lo, hi, seg_a, n_seg, cpp, n_total, ctx;
@@ -96,7 +118,8 @@ struct DecodeSmem {
   static constexpr int kKvBytes = kBoxes * kBoxBytes;
   static constexpr int kStageBytes = 2 * kKvBytes;
   static constexpr int kRingBytes = STAGES * kStageBytes;
-  static constexpr int kBytes = kRingBytes + STAGES * 16 + STAGES * 16 + 1024;  // + barriers, info, align
+  static constexpr int kTabCap = 2048;  // page-table entries prefetched into shared memory
+  static constexpr int kBytes = kRingBytes + STAGES * 16 + STAGES * 16 + kTabCap * 4 + 1024;  // + bars, info, table
 };
 
 template <int D>
@@ -117,14 +140,11 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kRingBytes);
   uint64_t* empty = full + STAGES;
   int4* info = reinterpret_cast<int4*>(empty + STAGES);
+  int32_t* tab = reinterpret_cast<int32_t*>(info + STAGES);
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const ChunkPlan plan = make_plan(a, b, kChunk);
-  const int k0 = static_cast<int>(static_cast<int64_t>(plan.n_total) * split / a.nsplit);
-  const int k1 = static_cast<int>(static_cast<int64_t>(plan.n_total) * (split + 1) / a.nsplit);
-  const int nk = k1 - k0;
-
+  pdl_trigger();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -132,6 +152,11 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     }
     fence_mbar_init();
   }
+  if (!a.early_local) pdl_block();
+  const ChunkPlan plan = make_plan(a, b, kChunk);
+  const int k0 = static_cast<int>(static_cast<int64_t>(plan.n_total) * split / a.nsplit);
+  const int k1 = static_cast<int>(static_cast<int64_t>(plan.n_total) * (split + 1) / a.nsplit);
+  const int nk = k1 - k0;
   __syncthreads();
 
   if (warp == kConsumerWarps) {
@@ -142,49 +167,85 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     }
     const uint64_t policy = l2_policy_evict_first();
     bool ok = true;
-    for (int base = 0; base < nk && ok; base += 32) {
-      ChunkInfo ci{0, 0, 0};
-      long long row = -1;
-      if (base + lane < nk) {
-        ci = chunk_info(a, plan, b, k0 + base + lane, kChunk);
-        if (ci.vlo < ci.vhi) {
-          row = a.addr.row(b, kvh, ci.t0);
-          if (row < 0 || row >= a.addr.total_rows) {
-            spa_raise(SPA_DEVERR_BAD_PAGE);
-            row = -1;
-          }
-        }
-      }
-      const int cnt = min(32, nk - base);
-      for (int j = 0; j < cnt; ++j) {
-        const int i = base + j;
-        const int t0 = __shfl_sync(0xffffffffu, ci.t0, j);
-        const int vlo = __shfl_sync(0xffffffffu, ci.vlo, j);
-        const int vhi = __shfl_sync(0xffffffffu, ci.vhi, j);
-        const long long r = __shfl_sync(0xffffffffu, row, j);
-        if (lane == 0) {
-          const int stage = i % STAGES;
-          if (i >= STAGES && !mbar_wait_bounded(&empty[stage], ((i / STAGES) - 1) & 1)) ok = false;
-          if (ok) {
-            info[stage] = make_int4(t0, r >= 0 ? vlo : 0, r >= 0 ? vhi : 0, 0);
-            uint64_t* bar = &full[stage];
-            if (r >= 0) {
-              mbar_arrive_expect_tx(bar, S::kStageBytes);
-              unsigned char* dst = smem + stage * S::kStageBytes;
+    // the sequence's page-table row, prefetched with independent loads (one round trip)
+    const int tstride = a.addr.table_stride;
+    const bool use_tab = a.addr.page_table != nullptr && tstride <= S::kTabCap;
+    if (use_tab) {
+      const int32_t* src = a.addr.page_table + static_cast<int64_t>(b) * tstride;
+      for (int e0 = lane; e0 < tstride; e0 += 32 * 16) {
+        int32_t r[16];
 #pragma unroll
-              for (int bx = 0; bx < S::kBoxes; ++bx) {
-                tma_load_2d_hint(dst + bx * S::kBoxBytes, &kmap, bar, bx * 64, static_cast<int>(r), policy);
-                tma_load_2d_hint(dst + S::kKvBytes + bx * S::kBoxBytes, &vmap, bar, bx * 64, static_cast<int>(r),
-                                 policy);
-              }
-            } else {
-              mbar_arrive(bar);
+        for (int u = 0; u < 16; ++u) r[u] = e0 + 32 * u < tstride ? __ldg(src + e0 + 32 * u) : -1;
+#pragma unroll
+        for (int u = 0; u < 16; ++u)
+          if (e0 + 32 * u < tstride) tab[e0 + 32 * u] = r[u];
+      }
+      __syncwarp();
+    }
+    auto row_of = [&](int t) -> long long {
+      if (!use_tab) return a.addr.row(b, kvh, t);
+      const int lp = t / a.addr.page_size;
+      if (lp < 0 || lp >= tstride) return -1;
+      const int32_t pg = tab[lp];
+      if (pg < 0) return -1;
+      return b * a.addr.batch_stride_rows + static_cast<long long>(pg) * a.addr.page_stride_rows +
+             kvh * a.addr.head_stride_rows + (t - lp * a.addr.page_size);
+    };
+    // chunks [0, n_local) of this split are local-window chunks (no router output needed);
+    // with early_local they are issued before waiting for the router.
+    const int n_local = max(0, min(k1, plan.n_seg) - k0);
+    for (int part = 0; part < 2 && ok; ++part) {
+      const int lo = part ? n_local : 0, hi = part ? nk : n_local;
+      if (part == 1 && a.early_local) pdl_block();
+      for (int base = lo; base < hi && ok; base += 32) {
+        ChunkInfo ci{0, 0, 0};
+        long long row = -1;
+        if (base + lane < hi) {
+          ci = chunk_info(a, plan, b, k0 + base + lane, kChunk);
+          if (ci.vlo < ci.vhi) {
+            row = row_of(ci.t0);
+            if (row < 0 || row >= a.addr.total_rows) {
+              spa_raise(SPA_DEVERR_BAD_PAGE);
+              row = -1;
             }
           }
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
+        const int cnt = min(32, hi - base);
+        for (int j = 0; j < cnt; ++j) {
+          const int i = base + j;
+          const int t0 = __shfl_sync(0xffffffffu, ci.t0, j);
+          const int vlo = __shfl_sync(0xffffffffu, ci.vlo, j);
+          const int vhi = __shfl_sync(0xffffffffu, ci.vhi, j);
+          const long long r = __shfl_sync(0xffffffffu, row, j);
+          if (lane == 0) {
+            const int stage = i % STAGES;
+            if (i >= STAGES && !mbar_wait_bounded(&empty[stage], ((i / STAGES) - 1) & 1)) ok = false;
+            if (ok) {
+              info[stage] = make_int4(t0, r >= 0 ? vlo : 0, r >= 0 ? vhi : 0, 0);
+              uint64_t* bar = &full[stage];
+              if (r >= 0) {
+                mbar_arrive_expect_tx(bar, S::kStageBytes);
+                unsigned char* dst = smem + stage * S::kStageBytes;
+#pragma unroll
+                for (int bx = 0; bx < S::kBoxes; ++bx) {
+                  tma_load_2d_hint(dst + bx * S::kBoxBytes, &kmap, bar, bx * 64, static_cast<int>(r), policy);
+                  tma_load_2d_hint(dst + S::kKvBytes + bx * S::kBoxBytes, &vmap, bar, bx * 64, static_cast<int>(r),
+                                   policy);
+                }
+              } else {
+                mbar_arrive(bar);
+              }
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+        }
       }
+    }
+    // every thread of every CTA in a merging cluster reaches both cluster barriers
+    if (a.cluster_merge && a.nsplit > 1) {
+      cluster_barrier();
+      cluster_barrier();
     }
     return;
   }
@@ -215,7 +276,8 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   bool ok = true;
   for (int i = 0; i < nk; ++i) {
     const int stage = i % STAGES;
-    if (!mbar_wait_bounded(&full[stage], (i / STAGES) & 1)) {
+    // warp-uniform outcome: lanes must agree before any aligned barrier below
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[stage], (i / STAGES) & 1))) {
       ok = false;
       break;
     }
@@ -300,54 +362,99 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);
   }
-  if (!ok) return;  // error word already raised; outputs of this split are undefined
+  if (!ok) {  // error word already raised; outputs of this split are undefined
+    if (a.cluster_merge && a.nsplit > 1) {
+      cluster_barrier();
+      cluster_barrier();
+    }
+    return;
+  }
 
-  // ------------------------------------------------ merge the four warps
+  // ------------------------------------------------ merge the four warps (shared memory)
+  // Each consumer warp holds (m, l, O) of its 16 token rows for every query head.  The
+  // real rows go to padded shared-memory rows (conflict-free float2 stores) and the
+  // CTA combines them into one normalised partial (O, log2-sum-exp) per head.
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-  float* red = reinterpret_cast<float*>(smem);               // [4][16][D]
-  float* ml = red + kConsumerWarps * 16 * D;                 // [4][16][2]
+  constexpr int LD = D + 8;
+  float* red = reinterpret_cast<float*>(smem);                 // [warp][group][LD]
+  float* ml = red + kConsumerWarps * group * LD;               // [warp][group][2]
+  float* cta_o = ml + kConsumerWarps * group * 2;              // [group][D]  this CTA's partial
+  float* cta_lse = cta_o + group * D;                          // [group]
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");  // ring reads done
 #pragma unroll
-  for (int n = 0; n < D / 8; ++n) {
-    const int col = n * 8 + tig * 2;
-    red[(warp * 16 + g0) * D + col] = acc[n][0];
-    red[(warp * 16 + g0) * D + col + 1] = acc[n][1];
-    red[(warp * 16 + g0 + 8) * D + col] = acc[n][2];
-    red[(warp * 16 + g0 + 8) * D + col + 1] = acc[n][3];
-  }
-  if (tig == 0) {
-    ml[(warp * 16 + g0) * 2] = m0;
-    ml[(warp * 16 + g0) * 2 + 1] = l0;
-    ml[(warp * 16 + g0 + 8) * 2] = m1;
-    ml[(warp * 16 + g0 + 8) * 2 + 1] = l1;
+  for (int half = 0; half < 2; ++half) {
+    const int row = g0 + 8 * half;
+    if (row >= group) continue;
+    float* dst = red + (warp * group + row) * LD + tig * 2;
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n)
+      *reinterpret_cast<float2*>(dst + n * 8) = make_float2(acc[n][2 * half], acc[n][2 * half + 1]);
+    if (tig == 0) {
+      ml[(warp * group + row) * 2] = half ? m1 : m0;
+      ml[(warp * group + row) * 2 + 1] = half ? l1 : l0;
+    }
   }
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+  const int64_t bh0 = static_cast<int64_t>(b) * a.Hq + kvh * group;
   for (int idx = threadIdx.x; idx < group * D; idx += kConsumerWarps * 32) {
     const int row = idx / D, col = idx - row * D;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ml[(w * 16 + row) * 2]);
+    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ml[(w * group + row) * 2]);
     const float Mu = M == -INFINITY ? 0.f : M;
     float L = 0.f, O = 0.f;
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) {
-      const float f = fast_exp2(ml[(w * 16 + row) * 2] - Mu);
-      L += ml[(w * 16 + row) * 2 + 1] * f;
-      O += red[(w * 16 + row) * D + col] * f;
+      const float f = fast_exp2(ml[(w * group + row) * 2] - Mu);
+      L += ml[(w * group + row) * 2 + 1] * f;
+      O += red[(w * group + row) * LD + col] * f;
     }
-    const int h = kvh * group + row;
     const float o = L > 0.f ? O / L : 0.f;
+    const float lse = L > 0.f ? M + __log2f(L) : -INFINITY;
     if (a.nsplit == 1) {
-      static_cast<T*>(a.out)[(static_cast<int64_t>(b) * a.Hq + h) * D + col] = from_f32<T>(o);
+      static_cast<T*>(a.out)[(bh0 + row) * D + col] = from_f32<T>(o);
+    } else if (a.cluster_merge) {
+      cta_o[row * D + col] = o;
+      if (col == 0) cta_lse[row] = lse;
     } else {
-      const int64_t bh = static_cast<int64_t>(b) * a.Hq + h;
-      a.part_o[(bh * a.nsplit + split) * D + col] = o;
-      if (col == 0) a.part_lse[bh * a.nsplit + split] = L > 0.f ? M + __log2f(L) : -INFINITY;
+      a.part_o[((bh0 + row) * a.nsplit + split) * D + col] = o;
+      if (col == 0) a.part_lse[(bh0 + row) * a.nsplit + split] = lse;
     }
   }
+  if (a.nsplit == 1 || !a.cluster_merge) return;
+
+  // ------------------------------------------------ cluster merge of the pair's splits
+  // The nsplit CTAs of this (b, kv head) form one cluster; after a cluster barrier,
+  // rank r merges output columns [r*D/nsplit, (r+1)*D/nsplit) of every head from the
+  // peers' shared memory, and a second barrier keeps that memory alive until all read.
+  cluster_barrier();
+  const int ns = a.nsplit;
+  const int c0 = split * D / ns, c1 = (split + 1) * D / ns;
+  for (int idx = threadIdx.x; idx < group * (c1 - c0); idx += kConsumerWarps * 32) {
+    const int row = idx / (c1 - c0), col = c0 + (idx - row * (c1 - c0));
+    float lse[16], ov[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      lse[r] = r < ns ? ld_dsmem(cta_lse + row, r) : -INFINITY;
+      ov[r] = r < ns ? ld_dsmem(cta_o + row * D + col, r) : 0.f;
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) M = fmaxf(M, lse[r]);
+    const float Mu = M == -INFINITY ? 0.f : M;
+    float W = 0.f, O = 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const float f = r < ns ? fast_exp2(lse[r] - Mu) : 0.f;
+      W += f;
+      O += ov[r] * f;
+    }
+    static_cast<T*>(a.out)[(bh0 + row) * D + col] = from_f32<T>(W > 0.f ? O / W : 0.f);
+  }
+  cluster_barrier();
 }
 
 // ---------------------------------------------------------------------------
@@ -359,6 +466,8 @@ template <typename T>
 __global__ void __launch_bounds__(32) decode_generic_kernel(const T* __restrict__ k, const T* __restrict__ v,
                                                             const DecodeArgs a) {
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z, lane = threadIdx.x;
+  pdl_trigger();
+  pdl_block();
   const int kvh = h / a.group, D = a.D;
   const ChunkPlan plan = make_plan(a, b, kGenericChunk);
   const int k0 = static_cast<int>(static_cast<int64_t>(plan.n_total) * split / a.nsplit);
@@ -419,23 +528,67 @@ __global__ void __launch_bounds__(32) decode_generic_kernel(const T* __restrict_
 }
 
 // ---------------------------------------------------------------------------
-// Split merge: grid (B*Hq), block 128.
+// Split merge: grid (B*Hq), block kMergeThreads.  Thread t owns column t % D of slot
+// group t / D; the slot groups' weighted sums are added in shared memory.
+constexpr int kMergeThreads = 512;
+constexpr int kMergeMaxSlots = 1024;
+
 template <typename T>
-__global__ void __launch_bounds__(128) decode_combine_kernel(const float* __restrict__ part_o,
-                                                             const float* __restrict__ part_lse, int nsplit,
-                                                             int D, T* __restrict__ out) {
+__global__ void __launch_bounds__(kMergeThreads) decode_combine_kernel(const float* __restrict__ part_o,
+                                                                       const float* __restrict__ part_lse,
+                                                                       int nslots, int D, T* __restrict__ out) {
+  constexpr int kRegSlots = 16;  // partials a thread holds in registers per batch
+  pdl_block();
+  __shared__ float w[kMergeMaxSlots];
+  __shared__ float red[kMergeThreads];
+  __shared__ float s_max, s_inv;
   const int64_t bh = blockIdx.x;
-  const float* lse = part_lse + bh * nsplit;
-  float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, lse[s]);
-  const float Mu = M == -INFINITY ? 0.f : M;
-  float W = 0.f;
-  for (int s = 0; s < nsplit; ++s) W += exp2f(lse[s] - Mu);
-  const float inv = W > 0.f ? 1.f / W : 0.f;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float o = 0.f;
-    for (int s = 0; s < nsplit; ++s) o += part_o[(bh * nsplit + s) * D + d] * exp2f(lse[s] - Mu);
-    out[bh * D + d] = from_f32<T>(o * inv);
+  const int groups = max(1, static_cast<int>(blockDim.x) / D);
+  const int d = threadIdx.x % D, g = threadIdx.x / D;
+  const float* base = part_o + bh * nslots * static_cast<int64_t>(D) + d;
+  // issue this thread's first batch of partial loads before the weights are known
+  float v[kRegSlots];
+#pragma unroll
+  for (int u = 0; u < kRegSlots; ++u) {
+    const int s = g + u * groups;
+    v[u] = (g < groups && s < nslots) ? __ldcg(base + static_cast<int64_t>(s) * D) : 0.f;
+  }
+  const float* lse = part_lse + bh * nslots;
+  for (int s = threadIdx.x; s < nslots; s += blockDim.x) w[s] = __ldcg(lse + s);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float M = -INFINITY;
+    for (int s = threadIdx.x; s < nslots; s += 32) M = fmaxf(M, w[s]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    const float Mu = M == -INFINITY ? 0.f : M;
+    float W = 0.f;
+    for (int s = threadIdx.x; s < nslots; s += 32) W += exp2f(w[s] - Mu);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) W += __shfl_xor_sync(0xffffffffu, W, off);
+    if (threadIdx.x == 0) {
+      s_max = Mu;
+      s_inv = W > 0.f ? 1.f / W : 0.f;
+    }
+  }
+  __syncthreads();
+  const float mx = s_max;
+  float o = 0.f;
+  if (g < groups) {
+#pragma unroll
+    for (int u = 0; u < kRegSlots; ++u) {
+      const int s = g + u * groups;
+      if (s < nslots) o += v[u] * exp2f(w[s] - mx);
+    }
+    for (int s = g + kRegSlots * groups; s < nslots; s += groups)
+      o += __ldcg(base + static_cast<int64_t>(s) * D) * exp2f(w[s] - mx);
+  }
+  red[threadIdx.x] = o;
+  __syncthreads();
+  if (threadIdx.x < D) {
+    float t = 0.f;
+    for (int gg = 0; gg < groups; ++gg) t += red[gg * D + threadIdx.x];
+    out[bh * D + threadIdx.x] = from_f32<T>(t * s_inv);
   }
 }
 
@@ -447,19 +600,71 @@ inline int device_sm_count() {
   return n > 0 ? n : 148;
 }
 
-// Splits per (b, kv head): fill ~2 CTAs per SM, keep >= 2 chunks per split.
-inline int decode_nsplit(int batch, int kv_heads, int max_candidates) {
+// Split plan per (b, kv head).  Target ~2 CTAs per SM with >= 2 chunks per split.  Up to
+// kMaxClusterSplits splits form a thread-block cluster that merges through distributed
+// shared memory; pairs too few to fill the GPU that way use more splits with global
+// partials and a merge kernel.
+constexpr int kMaxClusterSplits = 8;
+struct SplitPlan {
+  int nsplit;
+  bool cluster;
+};
+inline SplitPlan decode_plan(int batch, int q_heads, int kv_heads, int max_candidates) {
   const int pairs = batch * kv_heads;
+  const int group = q_heads / kv_heads;
   const int slots = device_sm_count() * 2;
   const int chunks = max_candidates / kChunk + 2;
   int ns = pairs >= slots ? 1 : slots / pairs;
   const int cap = chunks / 2 > 1 ? chunks / 2 : 1;
   if (ns > cap) ns = cap;
   if (ns > 256) ns = 256;
-  return ns < 1 ? 1 : ns;
+  if (ns < 1) ns = 1;
+  if (ns <= kMaxClusterSplits) return {ns, ns > 1};
+  // 8-CTA clusters still give every SM at least one CTA: prefer them
+  if (static_cast<int64_t>(pairs) * kMaxClusterSplits >= device_sm_count()) return {kMaxClusterSplits, true};
+  (void)group;
+  return {ns, false};
+}
+inline int decode_nsplit(int batch, int q_heads, int kv_heads, int max_candidates) {
+  return decode_plan(batch, q_heads, kv_heads, max_candidates).nsplit;
 }
 
 constexpr int kDecodeStages = 3;
+
+// Launch with programmatic stream serialization (when pdl: the kernel may start before its
+// predecessor in the stream completes and orders its reads with griddepcontrol.wait) and,
+// when cluster_x > 1, thread-block clusters of cluster_x CTAs along x.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                      int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                       Args&&... args) {
+  return launch_ex(kern, grid, block, smem, st, pdl, 1, std::forward<Args>(args)...);
+}
 
 template <typename T, int D>
 int launch_decode_mma(const spa_kv_layout& kv, int dtype, const DecodeArgs& a, cudaStream_t st) {
@@ -469,27 +674,25 @@ int launch_decode_mma(const spa_kv_layout& kv, int dtype, const DecodeArgs& a, c
   if (!spa_make_tensor_map_2d(&vmap, kv.v, dtype, kv.total_rows, D, kChunk, 64, true)) return SPA_ERR_INVALID;
   auto kern = decode_mma_kernel<T, D, kDecodeStages>;
   SPA_CHECK_CUDA(spa_set_smem_once(kern, S::kBytes));
-  kern<<<dim3(a.nsplit, a.Hkv, a.B), kDecodeThreads, S::kBytes, st>>>(kmap, vmap, a);
-  SPA_CHECK_CUDA(cudaGetLastError());
+  SPA_CHECK_CUDA(launch_ex(kern, dim3(a.nsplit, a.Hkv, a.B), dim3(kDecodeThreads), S::kBytes, st, a.early_local != 0,
+                           a.cluster_merge ? a.nsplit : 1, kmap, vmap, a));
   return SPA_OK;
 }
 
 template <typename T>
 int launch_decode(const spa_kv_layout& kv, int dtype, DecodeArgs a, bool fast, cudaStream_t st) {
-  int rc = SPA_OK;
+  const int nslots = a.nsplit;
   if (fast) {
-    rc = a.D == 128 ? launch_decode_mma<T, 128>(kv, dtype, a, st) : launch_decode_mma<T, 64>(kv, dtype, a, st);
-    if (rc) return rc;
+    const int rc = a.D == 128 ? launch_decode_mma<T, 128>(kv, dtype, a, st) : launch_decode_mma<T, 64>(kv, dtype, a, st);
+    if (rc || a.cluster_merge || nslots <= 1) return rc;
   } else {
     decode_generic_kernel<T><<<dim3(a.nsplit, a.Hq, a.B), 32, 0, st>>>(static_cast<const T*>(kv.k),
                                                                         static_cast<const T*>(kv.v), a);
     SPA_CHECK_CUDA(cudaGetLastError());
   }
-  if (a.nsplit > 1) {
-    decode_combine_kernel<T><<<a.B * a.Hq, 128, 0, st>>>(a.part_o, a.part_lse, a.nsplit, a.D,
-                                                          static_cast<T*>(a.out));
-    SPA_CHECK_CUDA(cudaGetLastError());
-  }
+  if (nslots > 1)
+    SPA_CHECK_CUDA(launch_pdl(decode_combine_kernel<T>, dim3(a.B * a.Hq), dim3(kMergeThreads), 0, st, true,
+                              a.part_o, a.part_lse, nslots, a.D, static_cast<T*>(a.out)));
   return SPA_OK;
 }
 
@@ -500,8 +703,8 @@ int launch_decode<float>(const spa_kv_layout& kv, int dtype, DecodeArgs a, bool,
                                                                           static_cast<const float*>(kv.v), a);
   SPA_CHECK_CUDA(cudaGetLastError());
   if (a.nsplit > 1) {
-    decode_combine_kernel<float><<<a.B * a.Hq, 128, 0, st>>>(a.part_o, a.part_lse, a.nsplit, a.D,
-                                                              static_cast<float*>(a.out));
+    decode_combine_kernel<float><<<a.B * a.Hq, kMergeThreads, 0, st>>>(a.part_o, a.part_lse, a.nsplit, a.D,
+                                                                        static_cast<float*>(a.out));
     SPA_CHECK_CUDA(cudaGetLastError());
   }
   return SPA_OK;
@@ -514,9 +717,11 @@ int launch_decode<float>(const spa_kv_layout& kv, int dtype, DecodeArgs a, bool,
 extern "C" size_t spa_decode_workspace_size(int batch, int q_heads, int kv_heads, int head_dim,
                                             int max_candidates) {
   if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || max_candidates < 0) return 0;
-  const int ns = spa::decode_nsplit(batch, kv_heads, max_candidates);
-  if (ns <= 1) return 0;
-  return static_cast<size_t>(batch) * q_heads * ns * (head_dim + 1) * sizeof(float);
+  // one partial slot per split per head on the global-merge path; clusters merge on chip,
+  // but the generic (CUDA-core) kernel always uses global partials
+  const int slots = spa::decode_nsplit(batch, q_heads, kv_heads, max_candidates);
+  if (slots <= 1) return 0;
+  return static_cast<size_t>(batch) * q_heads * slots * (head_dim + 1) * sizeof(float);
 }
 
 extern "C" int spa_paged_decode(const void* q, int dtype, int batch, int q_heads, int kv_heads, int head_dim,
@@ -541,22 +746,25 @@ extern "C" int spa_paged_decode(const void* q, int dtype, int batch, int q_heads
   a.local_window = local_window;
   a.selected = selected;
   a.top_m = selected ? top_m : 0;
-  a.nsplit = spa::decode_nsplit(batch, kv_heads, max_candidates);
+  const spa::SplitPlan plan = spa::decode_plan(batch, q_heads, kv_heads, max_candidates);
+  a.nsplit = plan.nsplit;
   a.scale = static_cast<float>(scale);
   a.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   a.part_o = nullptr;
   a.part_lse = nullptr;
-  if (a.nsplit > 1) {
+  a.early_local = 0;
+  {
     const size_t need = spa_decode_workspace_size(batch, q_heads, kv_heads, head_dim, max_candidates);
-    if (!workspace || workspace_bytes < need) return SPA_ERR_WORKSPACE;
+    if (need && (!workspace || workspace_bytes < need)) return SPA_ERR_WORKSPACE;
     a.part_o = static_cast<float*>(workspace);
-    a.part_lse = a.part_o + static_cast<size_t>(batch) * q_heads * a.nsplit * head_dim;
+    a.part_lse = need ? a.part_o + static_cast<size_t>(batch) * q_heads * a.nsplit * head_dim : nullptr;
   }
   const bool linear_rows = !kv->page_table && kv->page_stride_rows == kv->page_size;
   const bool fast = dtype != SPA_F32 && (head_dim == 64 || head_dim == 128) && a.group <= 16 &&
                     (kv->page_size % spa::kChunk == 0 || linear_rows) && kv->total_rows < (1ll << 31) &&
                     reinterpret_cast<uintptr_t>(kv->k) % 16 == 0 && reinterpret_cast<uintptr_t>(kv->v) % 16 == 0 &&
                     reinterpret_cast<uintptr_t>(q) % 4 == 0;
+  a.cluster_merge = fast && plan.cluster;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case SPA_F32:

@@ -351,20 +351,32 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             kc0 + kPfTile - 1 <= tile_q0 && kc0 > tile_q0 + kPfTile - 1 - a.W && kc0 + kPfTile <= a.halo + a.S;
         const int kmax = full_tile ? 127 : min(qc, a.halo + a.S - 1) - kc0;  // last valid column
         const int kmin = full_tile ? 0 : qc - a.W + 1 - kc0;                 // first valid column
-        // pass 1: row max of the scaled, masked scores (S stays in TMEM)
-        float mt = -INFINITY;
+        // pass 1: row max of the raw scores (scale > 0 commutes with max); S stays in TMEM
+        float raw_max = -INFINITY;
+        if (full_tile) {
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t u[32];
-          SPA_TMEM_LD32(s_addr + 32 * c, u);
-          tmem_wait_ld();
+          for (int c = 0; c < 4; c += 2) {
+            uint32_t u[32], w[32];
+            SPA_TMEM_LD32(s_addr + 32 * c, u);
+            SPA_TMEM_LD32(s_addr + 32 * c + 32, w);
+            tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int col = 32 * c + e;
-            const float x = __uint_as_float(u[e]) * a.scale_log2;
-            mt = (col >= kmin && col <= kmax) ? fmaxf(mt, x) : mt;
+            for (int e = 0; e < 32; ++e) raw_max = fmaxf(raw_max, fmaxf(__uint_as_float(u[e]), __uint_as_float(w[e])));
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t u[32];
+            SPA_TMEM_LD32(s_addr + 32 * c, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int col = 32 * c + e;
+              raw_max = (col >= kmin && col <= kmax) ? fmaxf(raw_max, __uint_as_float(u[e])) : raw_max;
+            }
           }
         }
+        const float mt = raw_max * a.scale_log2;
         if (mt > m_run + kPfRescaleThreshold || (m_run == -INFINITY && mt > -INFINITY)) {
           // move the running max; rescale O (complete: S_t(j) was issued after O_t(j-1))
           const float alpha = fast_exp2(m_run - mt);  // 0 when m_run = -inf
@@ -382,27 +394,53 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           l_run *= alpha;
           m_run = mt;
         }
-        const float mu = m_run == -INFINITY ? 0.f : m_run;
-        // pass 2: P = exp2(s - m) as 16-bit pairs into the first 64 columns of S_t.  Chunk c
-        // reads columns [32c, 32c+32) and writes [16c, 16c+16): never ahead of the reads.
+        const float neg_mu = m_run == -INFINITY ? 0.f : -m_run;
+        const float sc = a.scale_log2;
+        // pass 2: P = exp2(s*scale - m) as 16-bit pairs into the first 64 columns of S_t.
+        // Chunk pair (c, c+1) reads columns [32c, 32c+64) and writes [16c, 16c+32), which
+        // were read by earlier chunks (or by this one): writes never overtake reads.
         float lsum = 0.f;
+        if (full_tile) {
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t u[32];
-          SPA_TMEM_LD32(s_addr + 32 * c, u);
-          tmem_wait_ld();
-          uint32_t pk[16];
+          for (int c = 0; c < 4; c += 2) {
+            uint32_t u[32], w[32];
+            SPA_TMEM_LD32(s_addr + 32 * c, u);
+            SPA_TMEM_LD32(s_addr + 32 * c + 32, w);
+            tmem_wait_ld();
+            uint32_t pk[16], pw[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int col = 32 * c + 2 * e;
-            const float x0 = __uint_as_float(u[2 * e]) * a.scale_log2;
-            const float x1 = __uint_as_float(u[2 * e + 1]) * a.scale_log2;
-            const float p0 = (col >= kmin && col <= kmax) ? fast_exp2(x0 - mu) : 0.f;
-            const float p1 = (col + 1 >= kmin && col + 1 <= kmax) ? fast_exp2(x1 - mu) : 0.f;
-            lsum += p0 + p1;
-            pk[e] = PfFmt<T>::pack(p0, p1);
+            for (int e = 0; e < 16; ++e) {
+              const float p0 = fast_exp2(fmaf(__uint_as_float(u[2 * e]), sc, neg_mu));
+              const float p1 = fast_exp2(fmaf(__uint_as_float(u[2 * e + 1]), sc, neg_mu));
+              const float q0 = fast_exp2(fmaf(__uint_as_float(w[2 * e]), sc, neg_mu));
+              const float q1 = fast_exp2(fmaf(__uint_as_float(w[2 * e + 1]), sc, neg_mu));
+              lsum += (p0 + p1) + (q0 + q1);
+              pk[e] = PfFmt<T>::pack(p0, p1);
+              pw[e] = PfFmt<T>::pack(q0, q1);
+            }
+            SPA_TMEM_ST16(s_addr + 16 * c, pk);
+            SPA_TMEM_ST16(s_addr + 16 * c + 16, pw);
           }
-          SPA_TMEM_ST16(s_addr + 16 * c, pk);
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t u[32];
+            SPA_TMEM_LD32(s_addr + 32 * c, u);
+            tmem_wait_ld();
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int col = 32 * c + 2 * e;
+              const float p0 =
+                  (col >= kmin && col <= kmax) ? fast_exp2(fmaf(__uint_as_float(u[2 * e]), sc, neg_mu)) : 0.f;
+              const float p1 = (col + 1 >= kmin && col + 1 <= kmax)
+                                   ? fast_exp2(fmaf(__uint_as_float(u[2 * e + 1]), sc, neg_mu))
+                                   : 0.f;
+              lsum += p0 + p1;
+              pk[e] = PfFmt<T>::pack(p0, p1);
+            }
+            SPA_TMEM_ST16(s_addr + 16 * c, pk);
+          }
         }
         l_run += lsum;
         tmem_wait_st();

@@ -6,12 +6,13 @@
 //   summary    = fp32(S / page_size)                              (fp64 divide)
 //   super sum  = ((S[g0] + S[g0+1]) + ...) over the superblock's pages in order
 //   super      = fp32(super sum / (pages_in_super * page_size))
-//   qg[kvh,d]  = ((q[h0,d] + q[h0+1,d]) + ...) over the kv head's query heads, fp64
+//   qg[kvh,d]  = ((q[h0,d] + q[h0+1,d]) + ...) over the kv head's query heads, fp32
 //   dot_kvh    = per lane l: sum_k qg[kvh, l+32k] * summ[kvh, l+32k]  (k ascending,
-//                separate multiply and add), then xor-butterfly over lanes with
+//                fp32, separate multiply and add), then xor-butterfly over lanes with
 //                offsets 16, 8, 4, 2, 1
-//   score      = ((dot_0 + dot_1) + ...) over kv heads, / q_heads, * scale
-// Selection: descending score, ties to the lower page index.
+//   score      = ((dot_0 + dot_1) + ...) over kv heads, / q_heads, * fp32(scale), fp32
+// Selection: descending score, ties to the lower page index.  Scores are fp32, the
+// precision of the reference's own einsum router.
 //
 // Reference: select_blocks (triton_paged_gather_decode_benchmark.py:16-17) computes
 // einsum("bhd,bhgd->bhg").mean(1).topk(m); summaries at :61.  Grouping the q heads
@@ -63,53 +64,19 @@ __global__ void super_summaries_kernel(const double* __restrict__ sums64, int he
 constexpr int kRouterMaxHeadDim = 256;
 constexpr int kRouterMaxKvHeads = 64;
 
-// qg (fp64, [Hkv][D]) into shared memory; group sums in head order.
-template <typename T>
-__device__ void load_group_query(const T* __restrict__ q, int b, int q_heads, int kv_heads, int head_dim,
-                                 double* __restrict__ qg) {
-  const int group = q_heads / kv_heads;
-  for (int i = threadIdx.x; i < kv_heads * head_dim; i += blockDim.x) {
-    const int kvh = i / head_dim, d = i - kvh * head_dim;
-    const T* qp = q + (static_cast<int64_t>(b) * q_heads + kvh * group) * head_dim + d;
-    double acc = 0.0;
-    for (int j = 0; j < group; ++j) acc = __dadd_rn(acc, to_f64(qp[static_cast<int64_t>(j) * head_dim]));
-    qg[i] = acc;
-  }
-}
-
-// Score of one page by one warp (all lanes return the same value).
-// summ points at summary[b, 0, g, 0]; kv_stride = elements between kv heads.
-__device__ __forceinline__ double warp_page_score(const double* __restrict__ qg, const float* __restrict__ summ,
-                                                  int64_t kv_stride, int kv_heads, int head_dim, int q_heads,
-                                                  double scale) {
-  const int lane = threadIdx.x & 31;
-  double total = 0.0;
-  for (int kvh = 0; kvh < kv_heads; ++kvh) {
-    const float* s = summ + kvh * kv_stride;
-    const double* qq = qg + kvh * head_dim;
-    double part = 0.0;
-    for (int d = lane; d < head_dim; d += 32)
-      part = __dadd_rn(part, __dmul_rn(qq[d], static_cast<double>(__ldg(s + d))));
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) part = __dadd_rn(part, __shfl_xor_sync(0xffffffffu, part, off));
-    total = __dadd_rn(total, part);
-  }
-  return __dmul_rn(__ddiv_rn(total, static_cast<double>(q_heads)), scale);
-}
-
 // (score, index) ordering: a beats b when its score is larger, or equal with a lower index.
-__device__ __forceinline__ bool beats(double sa, int ia, double sb, int ib) {
+__device__ __forceinline__ bool beats(float sa, int ia, float sb, int ib) {
   return sa > sb || (sa == sb && ia < ib);
 }
 
 // Block-wide top-m over cand_score[0..n) (indices cand_idx[0..n)), written in
 // descending order to out[0..m).  Chosen entries are overwritten with -inf and
 // index INT_MAX.  Uses red_s / red_i scratch of blockDim.x/32 entries.
-__device__ void block_topm(double* cand_score, int* cand_idx, int n, int m, int64_t* out, double* red_s,
+__device__ void block_topm(float* cand_score, int* cand_idx, int n, int m, int64_t* out, float* red_s,
                            int* red_i, int* chosen_pos) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   for (int r = 0; r < m; ++r) {
-    double bs = -INFINITY;
+    float bs = -INFINITY;
     int bi = 0x7fffffff, bp = -1;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
       if (cand_idx[i] != 0x7fffffff && (bp < 0 || beats(cand_score[i], cand_idx[i], bs, bi))) {
@@ -120,7 +87,7 @@ __device__ void block_topm(double* cand_score, int* cand_idx, int n, int m, int6
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
-      const double os = __shfl_xor_sync(0xffffffffu, bs, off);
+      const float os = __shfl_xor_sync(0xffffffffu, bs, off);
       const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
       const int op = __shfl_xor_sync(0xffffffffu, bp, off);
       if (op >= 0 && (bp < 0 || beats(os, oi, bs, bi))) {
@@ -150,109 +117,337 @@ __device__ void block_topm(double* cand_score, int* cand_idx, int n, int m, int6
 }
 
 // ---------------------------------------------------------------------------
-// single-level router: grid (B), block 256; dynamic smem: qg + scores + idx
-template <typename T>
-__global__ void __launch_bounds__(256) router_topm_kernel(const T* __restrict__ q, int q_heads, int kv_heads,
-                                                          int head_dim, const float* __restrict__ summaries,
-                                                          int n_pages, double scale, int top_m,
-                                                          int64_t* __restrict__ selected,
-                                                          double* __restrict__ scores_out) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  double* qg = reinterpret_cast<double*>(smem_raw);
-  double* sc = qg + kv_heads * head_dim;
-  int* ix = reinterpret_cast<int*>(sc + n_pages);
-  __shared__ double red_s[8];
-  __shared__ int red_i[8];
-  __shared__ int chosen;
-  const int b = blockIdx.x;
-  load_group_query(q, b, q_heads, kv_heads, head_dim, qg);
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  const int64_t kv_stride = static_cast<int64_t>(n_pages) * head_dim;
-  const float* base = summaries + static_cast<int64_t>(b) * kv_heads * kv_stride;
-  for (int g = warp; g < n_pages; g += nwarps) {
-    const double s = warp_page_score(qg, base + static_cast<int64_t>(g) * head_dim, kv_stride, kv_heads,
-                                     head_dim, q_heads, scale);
-    if (lane == 0) {
-      sc[g] = s;
-      ix[g] = g;
-      if (scores_out) scores_out[static_cast<int64_t>(b) * n_pages + g] = s;
-    }
-  }
-  __syncthreads();
-  block_topm(sc, ix, n_pages, top_m, selected + static_cast<int64_t>(b) * top_m, red_s, red_i, &chosen);
+// Cluster router.  One cluster of kRouterCluster CTAs per batch row; candidate c is
+// owned by CTA rank c % kRouterCluster and scored by one warp: each lane loads its
+// lane-strided slice of the candidate's summary rows for every kv head (independent
+// loads, one memory round trip), forms the lane partials, and the kv heads' butterflies
+// run interleaved.  The cluster exchanges scores through distributed shared memory.
+// Tree mode: level 1 over superblocks (every CTA selects the top_super -- identical
+// inputs, identical result), level 2 over the pages of the chosen superblocks; rank 0
+// selects the final top_m.
+constexpr int kRouterCluster = 8;
+constexpr int kRouterThreads = 256;
+constexpr int kRouterKvBatch = 8;   // kv heads per register batch
+constexpr int kRouterMaxSlices = 8; // head_dim / 32 (head_dim <= 256)
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_dsmem_f32(const float* local_ptr, uint32_t rank) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// ---------------------------------------------------------------------------
-// tree router: grid (B), block 256.  Level 1 over n_super superblocks, level 2
-// over the pages of the top_super chosen superblocks.
+struct RouterArgs {
+  const void* q;
+  int q_heads, kv_heads, head_dim;
+  const float* supers;     // [B, Hkv, n_super, D] (tree mode) or nullptr
+  const float* summaries;  // [B, Hkv, n_pages, D]
+  int n_super, n_pages, superblock, top_super, top_m, max_cand;
+  float scale;
+  int64_t* selected;  // [B, top_m]
+  float* scores_out;  // [B, n_pages] (single-level mode) or nullptr
+};
+
+// qg (fp32, [Hkv][D]) for batch row b, summed over each kv head's query heads in
+// order.  The raw query row [Hq, D] is first copied to shared memory with 16-byte
+// loads that are all issued before any is consumed (one memory round trip).
 template <typename T>
-__global__ void __launch_bounds__(256) router_tree_kernel(const T* __restrict__ q, int q_heads, int kv_heads,
-                                                          int head_dim, const float* __restrict__ supers,
-                                                          int n_super, const float* __restrict__ summaries,
-                                                          int n_pages, int superblock, int top_super,
-                                                          double scale, int top_m,
-                                                          int64_t* __restrict__ selected) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  double* qg = reinterpret_cast<double*>(smem_raw);
-  const int cand_cap = max(n_super, top_super * superblock);
-  double* sc = qg + kv_heads * head_dim;
-  int* ix = reinterpret_cast<int*>(sc + cand_cap);
-  int64_t* chosen_super = reinterpret_cast<int64_t*>(ix + cand_cap + (cand_cap & 1));
-  __shared__ double red_s[8];
-  __shared__ int red_i[8];
-  __shared__ int chosen;
-  const int b = blockIdx.x;
-  load_group_query(q, b, q_heads, kv_heads, head_dim, qg);
+__device__ void load_group_query(const T* __restrict__ q, int b, int q_heads, int kv_heads, int head_dim,
+                                 T* __restrict__ qraw, float* __restrict__ qg) {
+  const int n = q_heads * head_dim;
+  const int nvec = n * static_cast<int>(sizeof(T)) / 16;
+  const uint4* src = reinterpret_cast<const uint4*>(q + static_cast<int64_t>(b) * n);
+  constexpr int U = 8;
+  for (int v0 = threadIdx.x; v0 < nvec; v0 += U * blockDim.x) {
+    uint4 r[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (v0 + u * static_cast<int>(blockDim.x) < nvec) r[u] = __ldg(src + v0 + u * blockDim.x);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (v0 + u * static_cast<int>(blockDim.x) < nvec) reinterpret_cast<uint4*>(qraw)[v0 + u * blockDim.x] = r[u];
+  }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  // level 1
-  {
-    const int64_t kv_stride = static_cast<int64_t>(n_super) * head_dim;
-    const float* base = supers + static_cast<int64_t>(b) * kv_heads * kv_stride;
-    for (int s = warp; s < n_super; s += nwarps) {
-      const double v = warp_page_score(qg, base + static_cast<int64_t>(s) * head_dim, kv_stride, kv_heads,
-                                       head_dim, q_heads, scale);
-      if (lane == 0) {
-        sc[s] = v;
-        ix[s] = s;
-      }
+  const int group = q_heads / kv_heads;
+  for (int i = threadIdx.x; i < kv_heads * head_dim; i += blockDim.x) {
+    const int kvh = i / head_dim, d = i - kvh * head_dim;
+    float acc = 0.f;
+    for (int j = 0; j < group; ++j) acc = __fadd_rn(acc, to_f32(qraw[(kvh * group + j) * head_dim + d]));
+    qg[i] = acc;
+  }
+}
+
+// One warp's view of a candidate: its lane-strided summary values for up to
+// kRouterKvBatch kv heads (registers), loaded with independent loads.
+struct CandRows {
+  float v[kRouterKvBatch][kRouterMaxSlices];
+};
+
+template <typename RowPtr>
+__device__ __forceinline__ void load_cand_rows(CandRows& r, int k0, int kv_heads, int head_dim, RowPtr rowp) {
+  const int lane = threadIdx.x & 31;
+  const int nk = min(kRouterKvBatch, kv_heads - k0);
+#pragma unroll
+  for (int u = 0; u < kRouterKvBatch; ++u) {
+    const float* row = rowp(k0 + (u < nk ? u : 0));
+#pragma unroll
+    for (int k = 0; k < kRouterMaxSlices; ++k) {
+      const int d = lane + 32 * k;
+      r.v[u][k] = (u < nk && d < head_dim) ? __ldg(row + d) : 0.f;
+    }
+  }
+}
+
+// Adds the kv heads [k0, k0+kRouterKvBatch) of one candidate to `total` in the canonical
+// order: lane partials over the lane's slice, xor butterflies, kv heads in order.
+__device__ __forceinline__ float accumulate_cand(const CandRows& r, const float* qg, int k0, int kv_heads,
+                                                 int head_dim, float total) {
+  const int lane = threadIdx.x & 31;
+  const int nk = min(kRouterKvBatch, kv_heads - k0);
+  float part[kRouterKvBatch];
+#pragma unroll
+  for (int u = 0; u < kRouterKvBatch; ++u) {
+    const float* qq = qg + (k0 + (u < nk ? u : 0)) * head_dim;
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < kRouterMaxSlices; ++k) {
+      const int d = lane + 32 * k;
+      if (d < head_dim) acc = __fadd_rn(acc, __fmul_rn(qq[d], r.v[u][k]));
+    }
+    part[u] = acc;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int u = 0; u < kRouterKvBatch; ++u) part[u] = __fadd_rn(part[u], __shfl_xor_sync(0xffffffffu, part[u], off));
+#pragma unroll
+  for (int u = 0; u < kRouterKvBatch; ++u)
+    if (u < nk) total = __fadd_rn(total, part[u]);
+  return total;
+}
+
+// Score of one candidate by one warp (all lanes return the same value).
+template <typename RowPtr>
+__device__ __forceinline__ float warp_candidate_score(const float* qg, int kv_heads, int head_dim, int q_heads,
+                                                      float scale, RowPtr rowp) {
+  float total = 0.f;
+  for (int k0 = 0; k0 < kv_heads; k0 += kRouterKvBatch) {
+    CandRows r;
+    load_cand_rows(r, k0, kv_heads, head_dim, rowp);
+    total = accumulate_cand(r, qg, k0, kv_heads, head_dim, total);
+  }
+  return __fmul_rn(__fdiv_rn(total, static_cast<float>(q_heads)), scale);
+}
+
+// T threads (a power of two dividing 32) share one candidate's rank count: candidate i
+// goes to out[rank_i], rank_i = number of candidates that beat it.  One pass, one barrier.
+__device__ void block_topm_rank(const float* sc, const int* id, int n, int m, int64_t* out) {
+  int T = 1;
+  while (T < 32 && T * 2 * n <= static_cast<int>(blockDim.x)) T *= 2;
+  const int per_round = static_cast<int>(blockDim.x) / T;
+  for (int base = 0; base < n; base += per_round) {
+    const int i = base + static_cast<int>(threadIdx.x) / T, part = static_cast<int>(threadIdx.x) % T;
+    int r = 0;
+    float si = 0.f;
+    int ii = 0;
+    if (i < n) {
+      si = sc[i];
+      ii = id[i];
+      for (int j = part; j < n; j += T) r += beats(sc[j], id[j], si, ii) ? 1 : 0;
+    }
+    for (int off = T / 2; off > 0; off >>= 1) r += __shfl_xor_sync(0xffffffffu, r, off);
+    if (i < n && part == 0 && r < m) out[r] = ii;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void select_top(float* sc, int* id, int n, int m, int64_t* out, float* red_s, int* red_i,
+                                           int* pos) {
+  if (n <= 2048)
+    block_topm_rank(sc, id, n, m, out);
+  else
+    block_topm(sc, id, n, m, out, red_s, red_i, pos);
+}
+
+// Dynamic shared memory of router_cluster_kernel.
+__host__ __device__ inline size_t router_smem_bytes(int kv_heads, int head_dim, int max_cand, int top_super,
+                                                    size_t q_row_bytes) {
+  const size_t loc_cap = (max_cand + kRouterCluster - 1) / kRouterCluster;
+  const size_t base = sizeof(float) * (static_cast<size_t>(kv_heads) * head_dim + 2 * loc_cap + max_cand) +
+                      sizeof(int64_t) * (top_super > 0 ? top_super : 1) + sizeof(int) * (max_cand + 4);
+  return ((base + 15) & ~size_t(15)) + q_row_bytes + 16;
+}
+
+// grid (kRouterCluster, B), cluster (kRouterCluster, 1, 1), block kRouterThreads.
+template <typename T>
+__global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const RouterArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int hkv = a.kv_heads, D = a.head_dim;
+  const int loc_cap = (a.max_cand + kRouterCluster - 1) / kRouterCluster;
+  int64_t* chosen = reinterpret_cast<int64_t*>(smem_raw);                       // [top_super]
+  float* qg = reinterpret_cast<float*>(chosen + (a.top_super > 0 ? a.top_super : 1));  // [Hkv*D]
+  float* score1 = qg + hkv * D;                                                 // [loc_cap] level 1 (own)
+  float* score2 = score1 + loc_cap;                                             // [loc_cap] level 2 (own)
+  float* all_score = score2 + loc_cap;                                          // [max_cand]
+  int* all_id = reinterpret_cast<int*>(all_score + a.max_cand);                 // [max_cand]
+  T* qraw = reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(all_id + a.max_cand + 4) + 15) & ~uintptr_t(15));
+  __shared__ float red_s[kRouterThreads / 32];
+  __shared__ int red_i[kRouterThreads / 32];
+  __shared__ int chosen_pos;
+  __shared__ int cand_start[65];
+
+  pdl_launch_dependents();
+  const int b = blockIdx.y;
+  const uint32_t rank = cluster_rank();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kRouterThreads / 32;
+  // first level's rows (the warp's first owned candidate, first kv-head batch) are
+  // requested before the query row so both loads are in flight together
+  CandRows first;
+  const float* sup_tab0 = a.supers ? a.supers + static_cast<int64_t>(b) * hkv * a.n_super * D : nullptr;
+  const float* page_tab0 = a.summaries + static_cast<int64_t>(b) * hkv * a.n_pages * D;
+  const int n_first = a.supers ? a.n_super : a.n_pages;
+  const int64_t first_stride = static_cast<int64_t>(n_first) * D;
+  const float* first_tab = a.supers ? sup_tab0 : page_tab0;
+  const int c_first = static_cast<int>(rank) + warp * kRouterCluster;
+  if (c_first < n_first)
+    load_cand_rows(first, 0, hkv, D, [&](int kvh) { return first_tab + kvh * first_stride + static_cast<int64_t>(c_first) * D; });
+  load_group_query(static_cast<const T*>(a.q), b, a.q_heads, hkv, D, qraw, qg);
+  __syncthreads();
+  // first-level score of the warp's first candidate from the prefetched rows
+  auto first_score = [&](int c) {
+    float total = accumulate_cand(first, qg, 0, hkv, D, 0.f);
+    for (int k0 = kRouterKvBatch; k0 < hkv; k0 += kRouterKvBatch) {
+      CandRows r;
+      load_cand_rows(r, k0, hkv, D, [&](int kvh) { return first_tab + kvh * first_stride + static_cast<int64_t>(c) * D; });
+      total = accumulate_cand(r, qg, k0, hkv, D, total);
+    }
+    return __fmul_rn(__fdiv_rn(total, static_cast<float>(a.q_heads)), a.scale);
+  };
+
+  const float* page_tab = a.summaries + static_cast<int64_t>(b) * hkv * a.n_pages * D;
+  const int64_t page_kv_stride = static_cast<int64_t>(a.n_pages) * D;
+  int n_cand = a.n_pages;
+  auto n_local_of = [&](int n) {
+    return n > static_cast<int>(rank) ? (n - 1 - static_cast<int>(rank)) / kRouterCluster + 1 : 0;
+  };
+  if (a.supers) {
+    // ---- level 1: superblocks
+    const float* sup_tab = a.supers + static_cast<int64_t>(b) * hkv * a.n_super * D;
+    const int64_t sup_kv_stride = static_cast<int64_t>(a.n_super) * D;
+    const int nl = n_local_of(a.n_super);
+    for (int i = warp; i < nl; i += nwarps) {
+      const int c = static_cast<int>(rank) + i * kRouterCluster;
+      const float v = i == warp ? first_score(c)
+                                : warp_candidate_score(qg, hkv, D, a.q_heads, a.scale, [&](int kvh) {
+                                    return sup_tab + kvh * sup_kv_stride + static_cast<int64_t>(c) * D;
+                                  });
+      if (lane == 0) score1[i] = v;
+    }
+    cluster_sync_all();
+    for (int c = threadIdx.x; c < a.n_super; c += blockDim.x) {
+      all_score[c] = ld_dsmem_f32(score1 + c / kRouterCluster, static_cast<uint32_t>(c % kRouterCluster));
+      all_id[c] = c;
     }
     __syncthreads();
-    block_topm(sc, ix, n_super, top_super, chosen_super, red_s, red_i, &chosen);
-  }
-  // level 2: candidate pages listed superblock by superblock (selection order)
-  __shared__ int cand_start[64];
-  __shared__ int n_cand;
-  if (threadIdx.x == 0) {
-    int n = 0;
-    for (int j = 0; j < top_super; ++j) {
-      cand_start[j] = n;
-      const int s = static_cast<int>(chosen_super[j]);
-      const int g0 = s * superblock, g1 = min(g0 + superblock, n_pages);
-      n += max(0, g1 - g0);
+    select_top(all_score, all_id, a.n_super, a.top_super, chosen, red_s, red_i, &chosen_pos);
+    if (threadIdx.x == 0) {
+      int n = 0;
+      for (int j = 0; j < a.top_super; ++j) {
+        cand_start[j] = n;
+        const int sidx = static_cast<int>(chosen[j]);
+        const int g0 = sidx * a.superblock, g1 = min(g0 + a.superblock, a.n_pages);
+        n += max(0, g1 - g0);
+      }
+      cand_start[a.top_super] = n;
     }
-    n_cand = n;
-  }
-  __syncthreads();
-  const int nc = n_cand;
-  {
-    const int64_t kv_stride = static_cast<int64_t>(n_pages) * head_dim;
-    const float* base = summaries + static_cast<int64_t>(b) * kv_heads * kv_stride;
-    for (int c = warp; c < nc; c += nwarps) {
+    __syncthreads();
+    n_cand = cand_start[a.top_super];
+    auto page_of = [&](int c) {
       int j = 0;
-      while (j + 1 < top_super && cand_start[j + 1] <= c) ++j;
-      const int g = static_cast<int>(chosen_super[j]) * superblock + (c - cand_start[j]);
-      const double v = warp_page_score(qg, base + static_cast<int64_t>(g) * head_dim, kv_stride, kv_heads,
-                                       head_dim, q_heads, scale);
-      if (lane == 0) {
-        sc[c] = v;
-        ix[c] = g;
+      while (j + 1 < a.top_super && cand_start[j + 1] <= c) ++j;
+      return static_cast<int>(chosen[j]) * a.superblock + (c - cand_start[j]);
+    };
+    // ---- level 2: pages of the chosen superblocks, listed superblock by superblock
+    const int nl2 = n_local_of(n_cand);
+    for (int i = warp; i < nl2; i += nwarps) {
+      const int g = page_of(static_cast<int>(rank) + i * kRouterCluster);
+      const float v = warp_candidate_score(qg, hkv, D, a.q_heads, a.scale,
+                                           [&](int kvh) { return page_tab + kvh * page_kv_stride + static_cast<int64_t>(g) * D; });
+      if (lane == 0) score2[i] = v;
+    }
+    cluster_sync_all();
+    if (rank == 0) {
+      for (int c = threadIdx.x; c < n_cand; c += blockDim.x) {
+        all_score[c] = ld_dsmem_f32(score2 + c / kRouterCluster, static_cast<uint32_t>(c % kRouterCluster));
+        all_id[c] = page_of(c);
       }
     }
+    // peers keep their shared memory alive until rank 0 has read it
+    cluster_sync_all();
+    if (rank == 0)
+      select_top(all_score, all_id, n_cand, a.top_m, a.selected + static_cast<int64_t>(b) * a.top_m, red_s, red_i,
+                 &chosen_pos);
+  } else {
+    // ---- single level: every routable page is a candidate
+    const int nl = n_local_of(n_cand);
+    for (int i = warp; i < nl; i += nwarps) {
+      const int c = static_cast<int>(rank) + i * kRouterCluster;
+      const float v = i == warp ? first_score(c)
+                                : warp_candidate_score(qg, hkv, D, a.q_heads, a.scale, [&](int kvh) {
+                                    return page_tab + kvh * page_kv_stride + static_cast<int64_t>(c) * D;
+                                  });
+      if (lane == 0) {
+        score2[i] = v;
+        if (a.scores_out) a.scores_out[static_cast<int64_t>(b) * a.n_pages + c] = v;
+      }
+    }
+    cluster_sync_all();
+    if (rank == 0) {
+      for (int c = threadIdx.x; c < n_cand; c += blockDim.x) {
+        all_score[c] = ld_dsmem_f32(score2 + c / kRouterCluster, static_cast<uint32_t>(c % kRouterCluster));
+        all_id[c] = c;
+      }
+    }
+    cluster_sync_all();
+    if (rank == 0)
+      select_top(all_score, all_id, n_cand, a.top_m, a.selected + static_cast<int64_t>(b) * a.top_m, red_s, red_i,
+                 &chosen_pos);
   }
-  __syncthreads();
-  block_topm(sc, ix, nc, top_m, selected + static_cast<int64_t>(b) * top_m, red_s, red_i, &chosen);
+}
+
+template <typename T>
+int launch_router(const RouterArgs& a, int batch, cudaStream_t st) {
+  const size_t smem = router_smem_bytes(a.kv_heads, a.head_dim, a.max_cand, a.top_super,
+                                       static_cast<size_t>(a.q_heads) * a.head_dim * sizeof(T));
+  if (smem > 200 * 1024) return SPA_ERR_UNSUPPORTED;
+  auto kern = router_cluster_kernel<T>;
+  SPA_CHECK_CUDA(spa_set_smem_once(kern, static_cast<int>(smem)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kRouterCluster, batch, 1);
+  cfg.blockDim = dim3(kRouterThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kRouterCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SPA_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+  return SPA_OK;
 }
 
 }  // namespace spa
@@ -297,36 +492,40 @@ int router_common_checks(const void* q, int q_dtype, int batch, int q_heads, int
   if (!q || batch <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads) return SPA_ERR_INVALID;
   if (head_dim <= 0 || head_dim > spa::kRouterMaxHeadDim || !dtype_ok(q_dtype)) return SPA_ERR_INVALID;
   if (kv_heads > spa::kRouterMaxKvHeads) return SPA_ERR_UNSUPPORTED;
+  // the query row is staged with 16-byte loads
+  const size_t qbytes = static_cast<size_t>(q_heads) * head_dim * dtype_size(q_dtype);
+  if (reinterpret_cast<uintptr_t>(q) % 16 != 0 || qbytes % 16 != 0 || qbytes > 64 * 1024) return SPA_ERR_UNSUPPORTED;
   return SPA_OK;
 }
 }  // namespace
 
 extern "C" int spa_router_topm(const void* q, int q_dtype, int batch, int q_heads, int kv_heads, int head_dim,
                                const float* summaries, int n_pages, double scale, int top_m, int64_t* selected,
-                               double* scores_out, spa_stream_t stream) {
+                               float* scores_out, spa_stream_t stream) {
   int rc = router_common_checks(q, q_dtype, batch, q_heads, kv_heads, head_dim);
   if (rc) return rc;
   if (!summaries || !selected || n_pages <= 0 || top_m <= 0 || top_m > n_pages) return SPA_ERR_INVALID;
-  const size_t smem = sizeof(double) * (kv_heads * head_dim + n_pages) + sizeof(int) * n_pages;
-  if (smem > 200 * 1024) return SPA_ERR_UNSUPPORTED;
+  if (batch > 65535) return SPA_ERR_UNSUPPORTED;
+  spa::RouterArgs a;
+  a.q = q;
+  a.q_heads = q_heads;
+  a.kv_heads = kv_heads;
+  a.head_dim = head_dim;
+  a.supers = nullptr;
+  a.summaries = summaries;
+  a.n_super = 0;
+  a.n_pages = n_pages;
+  a.superblock = 0;
+  a.top_super = 0;
+  a.top_m = top_m;
+  a.max_cand = n_pages;
+  a.scale = static_cast<float>(scale);
+  a.selected = selected;
+  a.scores_out = scores_out;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-#define SPA_LAUNCH_ROUTER(T)                                                                               \
-  do {                                                                                                     \
-    if (smem > 48 * 1024)                                                                                  \
-      SPA_CHECK_CUDA(spa_set_smem_once(spa::router_topm_kernel<T>, (int)smem));                          \
-    spa::router_topm_kernel<T><<<batch, 256, smem, st>>>(static_cast<const T*>(q), q_heads, kv_heads,     \
-                                                         head_dim, summaries, n_pages, scale, top_m,      \
-                                                         selected, scores_out);                            \
-  } while (0)
-  if (q_dtype == SPA_F32)
-    SPA_LAUNCH_ROUTER(float);
-  else if (q_dtype == SPA_F16)
-    SPA_LAUNCH_ROUTER(__half);
-  else
-    SPA_LAUNCH_ROUTER(__nv_bfloat16);
-#undef SPA_LAUNCH_ROUTER
-  SPA_CHECK_CUDA(cudaGetLastError());
-  return SPA_OK;
+  if (q_dtype == SPA_F32) return spa::launch_router<float>(a, batch, st);
+  if (q_dtype == SPA_F16) return spa::launch_router<__half>(a, batch, st);
+  return spa::launch_router<__nv_bfloat16>(a, batch, st);
 }
 
 extern "C" int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q_heads, int kv_heads,
@@ -342,27 +541,25 @@ extern "C" int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q
   const int last = n_pages - (n_super - 1) * superblock;
   const int min_cand = (top_super - 1) * superblock + (last < superblock ? last : superblock);
   if (top_m > min_cand) return SPA_ERR_INVALID;
-  const int cand_cap = n_super > top_super * superblock ? n_super : top_super * superblock;
-  const size_t smem = sizeof(double) * (kv_heads * head_dim + cand_cap) + sizeof(int) * (cand_cap + 1) +
-                      sizeof(int64_t) * (top_super + 1);
-  if (smem > 200 * 1024) return SPA_ERR_UNSUPPORTED;
+  if (batch > 65535) return SPA_ERR_UNSUPPORTED;
+  spa::RouterArgs a;
+  a.q = q;
+  a.q_heads = q_heads;
+  a.kv_heads = kv_heads;
+  a.head_dim = head_dim;
+  a.supers = super_summaries;
+  a.summaries = summaries;
+  a.n_super = n_super;
+  a.n_pages = n_pages;
+  a.superblock = superblock;
+  a.top_super = top_super;
+  a.top_m = top_m;
+  a.max_cand = n_super > top_super * superblock ? n_super : top_super * superblock;
+  a.scale = static_cast<float>(scale);
+  a.selected = selected;
+  a.scores_out = nullptr;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-#define SPA_LAUNCH_TREE(T)                                                                                  \
-  do {                                                                                                      \
-    if (smem > 48 * 1024)                                                                                   \
-      SPA_CHECK_CUDA(spa_set_smem_once(spa::router_tree_kernel<T>, (int)smem));                           \
-    spa::router_tree_kernel<T><<<batch, 256, smem, st>>>(static_cast<const T*>(q), q_heads, kv_heads,      \
-                                                         head_dim, super_summaries, n_super, summaries,    \
-                                                         n_pages, superblock, top_super, scale, top_m,     \
-                                                         selected);                                         \
-  } while (0)
-  if (q_dtype == SPA_F32)
-    SPA_LAUNCH_TREE(float);
-  else if (q_dtype == SPA_F16)
-    SPA_LAUNCH_TREE(__half);
-  else
-    SPA_LAUNCH_TREE(__nv_bfloat16);
-#undef SPA_LAUNCH_TREE
-  SPA_CHECK_CUDA(cudaGetLastError());
-  return SPA_OK;
+  if (q_dtype == SPA_F32) return spa::launch_router<float>(a, batch, st);
+  if (q_dtype == SPA_F16) return spa::launch_router<__half>(a, batch, st);
+  return spa::launch_router<__nv_bfloat16>(a, batch, st);
 }

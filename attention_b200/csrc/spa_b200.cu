@@ -5,6 +5,7 @@
 #include "router.cuh"
 #include "decode.cuh"
 #include "decode_noalloc.cuh"
+#include "step.cuh"
 #include "cache.cuh"
 #include "prefill_generic.cuh"
 #include "prefill_sm100.cuh"

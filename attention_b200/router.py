@@ -9,8 +9,9 @@ Reference entry points:
 * ``paged_candidates`` -- triton_paged_decode_benchmark.py:16-36 (route, then
   assemble local window + selected pages into a contiguous buffer).
 
-Scores are accumulated in fp64 in one fixed order and ties resolve to the lower
-page index, so the selection is deterministic and reproducible bit-for-bit.
+Scores are computed in fp32 (the precision of the reference's einsum) in one fixed
+order and ties resolve to the lower page index, so the selection is deterministic
+and reproducible bit-for-bit.
 With grouped-query attention the q heads of one kv head score that kv head's
 summary.  ``scale`` multiplies the mean score (1/sqrt(D) gives the
 q.mean(K_page)/sqrt(D) form; the reference's select_blocks uses 1).
@@ -91,7 +92,7 @@ def select_blocks(query: torch.Tensor, summaries: torch.Tensor, top_blocks: int,
     if not 0 < top_blocks <= n_pages:
         raise ValueError("top_blocks must be in [1, pages]")
     out = torch.empty(b, top_blocks, dtype=torch.int64, device=q.device)
-    scores = torch.empty(b, n_pages, dtype=torch.float64, device=q.device) if return_scores else None
+    scores = torch.empty(b, n_pages, dtype=torch.float32, device=q.device) if return_scores else None
     rc = _lib.lib.spa_router_topm(q.data_ptr(), dtype_code(q), b, hq, hkv, d, s.data_ptr(), n_pages, float(scale),
                                   top_blocks, out.data_ptr(), scores.data_ptr() if scores is not None else None,
                                   stream_ptr(q.device))

@@ -262,16 +262,15 @@ def run_ours(args, world, rank, local):
         summ.append(s)
         sup.append(u)
     scale = cfg.head_dim ** -0.5
-    sel_buf = [None] * groups
-    out_buf = [None] * groups
+    out_buf = [torch.empty_like(wl["query"][g]) for g in range(groups)]
+    sel_buf = [torch.empty(cfg.batch, cfg.top_m, dtype=torch.int64, device=dev) for _ in range(groups)]
 
     def step(g):
-        sel = spa.select_blocks_tree(wl["query"][g], sup[g], summ[g], superblock=cfg.superblock,
-                                     top_super=cfg.top_super, top_blocks=cfg.top_m, scale=scale)
-        out = spa.paged_gather_decode_attention(wl["query"][g], k_pool, v_pool, sel, local_window=cfg.local_window,
-                                                block_size=cfg.page_size, page_table=wl["page_table"][g],
-                                                context_lens=ctx)
-        sel_buf[g], out_buf[g] = sel, out
+        spa.sparse_decode_step(wl["query"][g], k_pool, v_pool, summ[g], super_summaries=sup[g],
+                               superblock=cfg.superblock, top_super=cfg.top_super, top_blocks=cfg.top_m,
+                               local_window=cfg.local_window, block_size=cfg.page_size, router_scale=scale,
+                               page_table=wl["page_table"][g], context_lens=ctx, out=out_buf[g],
+                               selected=sel_buf[g])
 
     def attention_only(g, sel):
         spa.paged_gather_decode_attention(wl["query"][g], k_pool, v_pool, sel, local_window=cfg.local_window,
@@ -358,11 +357,11 @@ def run_ours(args, world, rank, local):
 
         def e2e_step(g):
             dq[g].copy_(host_q[g], non_blocking=True)
-            sel = spa.select_blocks_tree(dq[g], sup[g], summ[g], superblock=cfg.superblock, top_super=cfg.top_super,
-                                         top_blocks=cfg.top_m, scale=scale)
-            out = spa.paged_gather_decode_attention(dq[g], k_pool, v_pool, sel, local_window=cfg.local_window,
-                                                    block_size=cfg.page_size, page_table=wl["page_table"][g],
-                                                    context_lens=ctx)
+            out, sel = spa.sparse_decode_step(dq[g], k_pool, v_pool, summ[g], super_summaries=sup[g],
+                                              superblock=cfg.superblock, top_super=cfg.top_super,
+                                              top_blocks=cfg.top_m, local_window=cfg.local_window,
+                                              block_size=cfg.page_size, router_scale=scale,
+                                              page_table=wl["page_table"][g], context_lens=ctx)
             host_out[g].copy_(out, non_blocking=True)
             host_sel[g].copy_(sel, non_blocking=True)
 
@@ -383,7 +382,7 @@ def run_ours(args, world, rank, local):
                "us_per_step": round(e_ms * 1e3 / e2e_steps, 3), "steps": e2e_steps,
                "h2d_bytes_per_step": qbytes,
                "d2h_bytes_per_step": qbytes + cfg.batch * cfg.top_m * 8,
-               "path": "attention_b200.select_blocks_tree + paged_gather_decode_attention (C ABI), pinned host "
+               "path": "attention_b200.sparse_decode_step (C ABI spa_sparse_decode_step), pinned host "
                        "query in, output and page ids out, one synchronisation at the end"}
 
     # CPU baseline: the reference's path on the host cores, rank 0 at N=1

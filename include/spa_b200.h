@@ -84,9 +84,10 @@ int spa_summaries_build(const spa_kv_layout* kv, int batch, int kv_heads,
 
 /*
  * Router: score[b, g] = scale * mean_h (q[b, h, :] . summary[b, h / group, g, :])
- * in fp64, then the top_m pages by descending score, ties to the lower page
- * index, written as int64 [B, top_m] in descending-score order.  Optional
- * scores_out: fp64 [B, n_pages].
+ * in fp32 with one fixed summation order, then the top_m pages by descending
+ * score, ties to the lower page index, written as int64 [B, top_m] in
+ * descending-score order.  Optional scores_out: fp32 [B, n_pages].
+ * Requires q_heads / kv_heads <= 16.
  * Replaces: select_blocks (triton_paged_gather_decode_benchmark.py:16-17,
  *   triton_promotion_cache_benchmark.py:16-17) and the routing half of
  *   paged_candidates (triton_paged_decode_benchmark.py:29-30).
@@ -94,7 +95,7 @@ int spa_summaries_build(const spa_kv_layout* kv, int batch, int kv_heads,
 int spa_router_topm(const void* q, int q_dtype, int batch, int q_heads,
                     int kv_heads, int head_dim, const float* summaries,
                     int n_pages, double scale, int top_m, int64_t* selected,
-                    double* scores_out, spa_stream_t stream);
+                    float* scores_out, spa_stream_t stream);
 
 /*
  * Two-level (tree) router: score superblocks with super_summaries, keep the
@@ -124,8 +125,10 @@ int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q_heads,
  * q: [B, Hq, D]; out: [B, Hq, D] (same dtype as q).
  * Replaces: paged_decode_attention_kernel launch (triton_paged_attention.py:56-81)
  *   and paged_gather_decode_attention_kernel launch (:139-168).
- * workspace: spa_decode_workspace_size() bytes of device memory (may be NULL
- *   when that size is 0).
+ * workspace: spa_decode_workspace_size() bytes of device memory, zero-filled
+ *   before its first use (it begins with arrival counters that every call leaves
+ *   at zero; re-zero it after spa_device_error reports a failed wait).
+ *   Requires batch * kv_heads <= 65536.
  */
 size_t spa_decode_workspace_size(int batch, int q_heads, int kv_heads,
                                  int head_dim, int max_candidates);
@@ -135,6 +138,29 @@ int spa_paged_decode(const void* q, int dtype, int batch, int q_heads,
                      const int64_t* selected, int top_m, int max_candidates,
                      double scale, void* out, void* workspace,
                      size_t workspace_bytes, spa_stream_t stream);
+
+/*
+ * One routed sparse decode step: router then gather decode, enqueued as chained
+ * kernels (the decode starts while the router runs and streams the local window
+ * before it reads the page ids).  super_summaries != NULL: two-level router
+ * (spa_router_tree_topm); NULL: single level over n_pages (spa_router_topm).
+ * router_scale multiplies the router score, attn_scale the attention logits.
+ * selected: int64 [B, top_m] (written); out: [B, Hq, D]; workspace as for
+ * spa_paged_decode with max_candidates = local_window + top_m * page_size.
+ * Every input except `selected` must be complete when this call is enqueued.
+ * Replaces the timed unit paged_gather_decode_attention(q, K, V,
+ *   select_blocks(q, summaries, m), ...) of triton_paged_gather_decode_benchmark.py:69
+ *   and triton_promotion_cache_benchmark.py:59.
+ */
+int spa_sparse_decode_step(const void* q, int dtype, int batch, int q_heads,
+                           int kv_heads, int head_dim, const spa_kv_layout* kv,
+                           const int32_t* context_lens, int local_window,
+                           const float* super_summaries, int n_super,
+                           const float* summaries, int n_pages, int superblock,
+                           int top_super, int top_m, double router_scale,
+                           double attn_scale, int64_t* selected, void* out,
+                           void* workspace, size_t workspace_bytes,
+                           spa_stream_t stream);
 
 /*
  * Allocation-free spa_paged_decode, for callers that cannot allocate device

@@ -3,15 +3,14 @@
 TEST INFRASTRUCTURE ONLY (see oracle/__init__.py).  Each function cites the
 reference code it restates (paths inside divagr18/attention).
 
-Router arithmetic follows one canonical fp64 order, identical to the CUDA
-kernels', so scores -- and therefore selections, ties included -- are
-bit-identical:
-  page sum    sequential over tokens            summary = fp32(sum / P)
-  super sum   sequential over the pages' sums   super   = fp32(sum / (n_pages_in_super * P))
-  qg[kvh]     sequential over that kv head's q heads
-  dot_kvh     lane l (of 32) accumulates d = l, l+32, ... (separate multiply, add),
-              then an xor butterfly over lanes with offsets 16, 8, 4, 2, 1
-  score       sequential over kv heads, then / Hq, then * scale
+Router arithmetic follows one canonical order, identical to the CUDA kernels', so
+scores -- and therefore selections, ties included -- are bit-identical:
+  page sum    fp64, sequential over tokens      summary = fp32(sum / P)
+  super sum   fp64, sequential over page sums   super   = fp32(sum / (n_pages_in_super * P))
+  qg[kvh]     fp32, sequential over that kv head's q heads
+  dot_kvh     fp32: lane l (of 32) accumulates d = l, l+32, ... (separate multiply,
+              add), then an xor butterfly over lanes with offsets 16, 8, 4, 2, 1
+  score       fp32, sequential over kv heads, then / Hq, then * fp32(scale)
 Ranking: descending score, ties to the lower page index (a stable sort).  The
 reference's torch.topk leaves tie order unspecified; on the seeded inputs the
 two agree (tests/test_oracle_golden.py).
@@ -61,37 +60,38 @@ def super_summaries(sums64: torch.Tensor, superblock: int, page_size: int) -> to
 
 # ------------------------------------------------------------------ router
 def router_scores(query: torch.Tensor, summaries: torch.Tensor, scale: float = 1.0) -> torch.Tensor:
-    """fp64 scores [B, G] = scale * mean_h q[b,h] . summary[b, h // group, g].
+    """fp32 scores [B, G] = scale * mean_h q[b,h] . summary[b, h // group, g].
 
     Restates einsum("bhd,bhgd->bhg", q, summaries).mean(dim=1)
     (triton_paged_gather_decode_benchmark.py:17) with GQA grouping, in the
-    canonical order documented at the top of this module."""
+    canonical fp32 order documented at the top of this module."""
+    f32 = torch.float32
     b, hq, d = query.shape
     hkv, g = summaries.size(1), summaries.size(2)
     group = hq // hkv
-    qd = query.to(torch.float64).reshape(b, hkv, group, d)
-    qg = torch.zeros(b, hkv, d, dtype=torch.float64)
+    qd = query.to(f32).reshape(b, hkv, group, d)
+    qg = torch.zeros(b, hkv, d, dtype=f32)
     for j in range(group):
         qg = qg + qd[:, :, j]
     lanes = 32
     dpad = -(-d // lanes) * lanes
-    qgp = torch.zeros(b, hkv, dpad, dtype=torch.float64)
+    qgp = torch.zeros(b, hkv, dpad, dtype=f32)
     qgp[..., :d] = qg
-    sp = torch.zeros(b, hkv, g, dpad, dtype=torch.float64)
-    sp[..., :d] = summaries.to(torch.float64)
+    sp = torch.zeros(b, hkv, g, dpad, dtype=f32)
+    sp[..., :d] = summaries.to(f32)
     qgp = qgp.reshape(b, hkv, 1, dpad // lanes, lanes)
     sp = sp.reshape(b, hkv, g, dpad // lanes, lanes)
-    part = torch.zeros(b, hkv, g, lanes, dtype=torch.float64)
+    part = torch.zeros(b, hkv, g, lanes, dtype=f32)
     for kk in range(dpad // lanes):
         part = part + qgp[:, :, :, kk] * sp[:, :, :, kk]
     idx = torch.arange(lanes)
     for off in (16, 8, 4, 2, 1):
         part = part + part[..., idx ^ off]
     dots = part[..., 0]  # [B, Hkv, G]
-    total = torch.zeros(b, g, dtype=torch.float64)
+    total = torch.zeros(b, g, dtype=f32)
     for kvh in range(hkv):
         total = total + dots[:, kvh]
-    return (total / float(hq)) * float(scale)
+    return (total / torch.tensor(float(hq), dtype=f32)) * torch.tensor(scale, dtype=f32)
 
 
 def topm(scores: torch.Tensor, m: int, index: torch.Tensor | None = None) -> torch.Tensor:

@@ -1,0 +1,79 @@
+"""The fused step (router -> gather decode, chained on the device) equals the two
+separate calls bit for bit, and the oracle within tolerance."""
+
+import numpy as np
+import pytest
+import torch
+
+import attention_b200 as spa
+import oracle
+from attention_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _no_device_errors():
+    yield
+    assert spa.device_error_flags() == 0
+
+
+@pytest.mark.parametrize("m", [2, 4, 8])
+def test_tree_step_equals_separate_calls(m):
+    cfg = workloads.SparseDecodeConfig(top_m=m, pages_per_seq=64)
+    wl = workloads.sparse_decode_workload(cfg, groups=2, seed=m)
+    for g in range(2):
+        table, q = wl["page_table"][g], wl["query"][g]
+        summ, sup = spa.page_summaries(wl["k_pool"], block_size=cfg.page_size, n_pages=cfg.routable_pages,
+                                       page_table=table, superblock=cfg.superblock)
+        scale = cfg.head_dim ** -0.5
+        out, sel = spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ, super_summaries=sup,
+                                          superblock=cfg.superblock, top_super=cfg.top_super, top_blocks=m,
+                                          local_window=cfg.local_window, block_size=cfg.page_size, router_scale=scale,
+                                          page_table=table, context_lens=wl["context_lens"])
+        sel2 = spa.select_blocks_tree(q, sup, summ, superblock=cfg.superblock, top_super=cfg.top_super,
+                                      top_blocks=m, scale=scale)
+        out2 = spa.paged_gather_decode_attention(q, wl["k_pool"], wl["v_pool"], sel2, local_window=cfg.local_window,
+                                                 block_size=cfg.page_size, page_table=table,
+                                                 context_lens=wl["context_lens"])
+        assert torch.equal(sel, sel2)
+        assert torch.equal(out, out2)
+        exp = oracle.select_blocks_tree(q.cpu(), sup.cpu(), summ.cpu(), superblock=cfg.superblock,
+                                        top_super=cfg.top_super, top_blocks=m, scale=scale)
+        assert torch.equal(sel.cpu(), exp)
+
+
+def test_single_level_step_on_reference_layout(golden_dir):
+    fx = dict(np.load(golden_dir / "gather_small.npz"))
+    b, h, length, d, page, win, m = fx["shape"].tolist()
+    torch.manual_seed(int(fx["seed"]))
+    q = torch.randn(b, h, d)
+    k = torch.randn(b, h, length, d)
+    v = torch.randn_like(k)
+    kd, vd = k.to(DEV), v.to(DEV)
+    summ = spa.page_summaries(kd, block_size=page, local_window=win)
+    out, sel = spa.sparse_decode_step(q.to(DEV), kd, vd, summ, top_blocks=m, local_window=win, block_size=page)
+    assert torch.equal(sel.cpu(), torch.from_numpy(fx["selected"]))
+    ref = torch.from_numpy(fx["out"]).double()
+    assert ((out.double().cpu() - ref).abs() <= 1e-5).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_step_head_dim_64(dtype):
+    gen = torch.Generator().manual_seed(9)
+    b, hq, hkv, d, page, win, n_pages = 2, 16, 4, 64, 128, 128, 20
+    length = win + n_pages * page
+    q = (torch.randn(b, hq, d, generator=gen) * 0.5).to(dtype)
+    k = (torch.randn(b, hkv, length, d, generator=gen) * 0.5).to(dtype)
+    v = (torch.randn(b, hkv, length, d, generator=gen) * 0.5).to(dtype)
+    kd, vd = k.to(DEV), v.to(DEV)
+    summ = spa.page_summaries(kd, block_size=page, local_window=win)
+    out, sel = spa.sparse_decode_step(q.to(DEV), kd, vd, summ, top_blocks=3, local_window=win, block_size=page,
+                                      router_scale=d ** -0.5)
+    ref_summ, _ = oracle.summaries_fp64(k, page, n_pages)
+    exp_sel = oracle.select_blocks(q, ref_summ, 3, scale=d ** -0.5)
+    assert torch.equal(sel.cpu(), exp_sel)
+    ref = oracle.gather_decode(q, k, v, exp_sel, local_window=win, block_size=page)
+    o = out.double().cpu()
+    assert ((o - ref).abs() <= 2e-2 + 1e-2 * ref.abs()).all()
