@@ -477,7 +477,8 @@ def run_prefill(args, world, rank, dev, peaks):
     peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
     tf = flops / (ms * 1e-3) / 1e12
     return {"seq_len": seq, "window": window, "heads": heads, "head_dim": dim, "ms": round(ms, 4),
-            "tflops": round(tf, 1), "peak_tflops": peak, "frac": round(tf / peak, 4),
+            "tflops": round(tf, 1), "peak_tflops": peak * world, "frac": round(tf / (peak * world), 4),
+            "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst) x GPUs",
             "flops": flops, "sharding": f"{world} contiguous chunks, 2048-token K/V halo over NCCL" if world > 1
             else "single GPU", "reps": reps}
 
