@@ -7,9 +7,9 @@ Drop-in replacements for the reference's decode / prefill / router entry points
 
 from ._lib import LIB_PATH, SpaError, device_error_flags
 from .cache import PagedKVCache, PromotionCache, kv_append
-from .paged_attention import paged_decode_attention, paged_gather_decode_attention
+from .paged_attention import paged_decode_attention, paged_gather_decode_attention, span_gather_decode_attention
 from .prefill import local_causal_prefill
-from .router import page_summaries, select_blocks, select_blocks_tree
+from .router import page_summaries, periodic_router, select_blocks, select_blocks_tree
 from .step import sparse_decode_step
 
 __all__ = [
@@ -21,8 +21,10 @@ __all__ = [
     "kv_append",
     "paged_decode_attention",
     "paged_gather_decode_attention",
+    "span_gather_decode_attention",
     "local_causal_prefill",
     "page_summaries",
+    "periodic_router",
     "select_blocks",
     "select_blocks_tree",
     "sparse_decode_step",

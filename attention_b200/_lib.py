@@ -50,8 +50,10 @@ PROTOTYPES = {
     "spa_summaries_build": (_i, [_KV, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp]),
     "spa_router_topm": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _d, _i, _vp, _vp, _vp]),
     "spa_router_tree_topm": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _vp, _i, _i, _i, _d, _i, _vp, _vp]),
+    "spa_periodic_router": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _i, _i, _i, _vp, _vp]),
     "spa_decode_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "spa_paged_decode": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp, _sz, _vp]),
+    "spa_span_gather_decode": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp, _sz, _vp]),
     "spa_sparse_decode_step": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _d, _d, _vp,
                                     _vp, _vp, _sz, _vp]),
     "spa_paged_decode_noalloc": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp]),

@@ -29,6 +29,9 @@ struct DecodeArgs {
   int local_window;
   const int64_t* selected;
   int top_m;
+  // 0: selected[] are logical pages of page_size tokens.  > 0: selected[] are first
+  // tokens of spans of span_len tokens (span_gather_decode_attention).
+  int span_len;
   int nsplit;
   float scale_log2;  // softmax scale * log2(e)
   float scale;
@@ -70,7 +73,8 @@ __device__ __forceinline__ ChunkPlan make_plan(const DecodeArgs& a, int b, int c
   p.hi = ctx;
   p.seg_a = (lo / chunk) * chunk;
   p.n_seg = ctx > lo ? (ctx - p.seg_a + chunk - 1) / chunk : 0;
-  p.cpp = a.selected ? (a.addr.page_size + chunk - 1) / chunk : 0;
+  // span starts are arbitrary tokens: their chunks are chunk-aligned, so one extra chunk
+  p.cpp = !a.selected ? 0 : a.span_len > 0 ? (a.span_len + chunk - 1) / chunk + 1 : (a.addr.page_size + chunk - 1) / chunk;
   p.n_total = p.n_seg + (a.selected ? a.top_m * p.cpp : 0);
   return p;
 }
@@ -91,6 +95,21 @@ __device__ __forceinline__ ChunkInfo chunk_info(const DecodeArgs& a, const Chunk
     const int j = kk / p.cpp, ci = kk - j * p.cpp;
     const int64_t lp = a.selected[static_cast<int64_t>(b) * a.top_m + j];
     const int P = a.addr.page_size;
+    if (a.span_len > 0) {
+      // span [lp, lp + span_len) in chunk-aligned pieces, clipped to the context
+      if (lp < 0 || lp >= p.ctx) {
+        if (lp >= p.ctx) spa_raise(SPA_DEVERR_BAD_PAGE);
+        c.t0 = 0;
+        c.vlo = c.vhi = 0;
+      } else {
+        const int start = static_cast<int>(lp);
+        c.t0 = (start / chunk) * chunk + ci * chunk;
+        c.vlo = max(c.t0, start);
+        c.vhi = min(min(c.t0 + chunk, start + a.span_len), p.ctx);
+        if (c.vlo >= c.vhi) c.vlo = c.vhi = 0;
+      }
+      return c;
+    }
     if (lp < 0 || lp * P >= p.ctx) {
       // -1 marks an unfilled slot; anything else past the context is an input error
       if (lp >= 0) spa_raise(SPA_DEVERR_BAD_PAGE);
@@ -724,10 +743,35 @@ extern "C" size_t spa_decode_workspace_size(int batch, int q_heads, int kv_heads
   return static_cast<size_t>(batch) * q_heads * slots * (head_dim + 1) * sizeof(float);
 }
 
+namespace spa {
+int paged_decode_impl(const void* q, int dtype, int batch, int q_heads, int kv_heads, int head_dim,
+                      const spa_kv_layout* kv, const int32_t* context_lens, int local_window, const int64_t* selected,
+                      int top_m, int span_len, int max_candidates, double scale, void* out, void* workspace,
+                      size_t workspace_bytes, spa_stream_t stream);
+}
+
 extern "C" int spa_paged_decode(const void* q, int dtype, int batch, int q_heads, int kv_heads, int head_dim,
                                 const spa_kv_layout* kv, const int32_t* context_lens, int local_window,
                                 const int64_t* selected, int top_m, int max_candidates, double scale, void* out,
                                 void* workspace, size_t workspace_bytes, spa_stream_t stream) {
+  return spa::paged_decode_impl(q, dtype, batch, q_heads, kv_heads, head_dim, kv, context_lens, local_window,
+                                selected, top_m, 0, max_candidates, scale, out, workspace, workspace_bytes, stream);
+}
+
+extern "C" int spa_span_gather_decode(const void* q, int dtype, int batch, int q_heads, int kv_heads, int head_dim,
+                                      const spa_kv_layout* kv, const int32_t* context_lens, int local_window,
+                                      const int64_t* starts, int n_spans, int span_width, double scale, void* out,
+                                      void* workspace, size_t workspace_bytes, spa_stream_t stream) {
+  if (!starts || n_spans <= 0 || span_width <= 0) return SPA_ERR_INVALID;
+  return spa::paged_decode_impl(q, dtype, batch, q_heads, kv_heads, head_dim, kv, context_lens, local_window, starts,
+                                n_spans, span_width, local_window + n_spans * (span_width + 2 * spa::kChunk), scale,
+                                out, workspace, workspace_bytes, stream);
+}
+
+int spa::paged_decode_impl(const void* q, int dtype, int batch, int q_heads, int kv_heads, int head_dim,
+                           const spa_kv_layout* kv, const int32_t* context_lens, int local_window,
+                           const int64_t* selected, int top_m, int span_len, int max_candidates, double scale,
+                           void* out, void* workspace, size_t workspace_bytes, spa_stream_t stream) {
   if (!q || !out || !kv || !kv->k || !kv->v || !context_lens) return SPA_ERR_INVALID;
   if (!dtype_ok(dtype) || batch <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads) return SPA_ERR_INVALID;
   if (head_dim <= 0 || head_dim > 256 || kv->page_size <= 0 || kv->total_rows <= 0) return SPA_ERR_INVALID;
@@ -746,6 +790,7 @@ extern "C" int spa_paged_decode(const void* q, int dtype, int batch, int q_heads
   a.local_window = local_window;
   a.selected = selected;
   a.top_m = selected ? top_m : 0;
+  a.span_len = selected ? span_len : 0;
   const spa::SplitPlan plan = spa::decode_plan(batch, q_heads, kv_heads, max_candidates);
   a.nsplit = plan.nsplit;
   a.scale = static_cast<float>(scale);

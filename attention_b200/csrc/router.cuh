@@ -450,6 +450,54 @@ int launch_router(const RouterArgs& a, int batch, cudaStream_t st) {
   return SPA_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Periodic causal router: grid (U, H, B), block 256.  Update u routes the query at
+// position (u+1)*stride-1 of head h against that head's block summaries, over the
+// blocks that end at or before it; top-m by the canonical fp32 score of one head
+// (lane partials + butterfly), ties to the lower block, unfilled slots -1.
+// Reference: periodic_router (triton_prefill_router_overhead.py:16-34).
+template <typename T>
+__global__ void __launch_bounds__(256) periodic_router_kernel(const T* __restrict__ q, int seq_len, int head_dim,
+                                                              const float* __restrict__ summaries, int n_blocks,
+                                                              int block_size, int stride, int top_m,
+                                                              int64_t* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int u = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int H = gridDim.y, U = gridDim.x;
+  float* sc = reinterpret_cast<float*>(smem_raw);   // [n_blocks]
+  int* id = reinterpret_cast<int*>(sc + n_blocks);   // [n_blocks]
+  float* qv = reinterpret_cast<float*>(id + n_blocks);  // [head_dim]
+  const int pos = (u + 1) * stride - 1;
+  const int64_t bh = static_cast<int64_t>(b) * H + h;
+  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) qv[d] = to_f32(q[(bh * seq_len + pos) * head_dim + d]);
+  __syncthreads();
+  const int avail = min(n_blocks, (pos + 1) / block_size);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int g = warp; g < avail; g += nwarps) {
+    const float* sv = summaries + (bh * n_blocks + g) * head_dim;
+    float part = 0.f;
+    for (int d = lane; d < head_dim; d += 32) part = __fadd_rn(part, __fmul_rn(qv[d], __ldg(sv + d)));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, off));
+    if (lane == 0) {
+      sc[g] = __fadd_rn(0.f, part);
+      id[g] = g;
+    }
+  }
+  __syncthreads();
+  int64_t* o = out + (bh * U + u) * top_m;
+  const int cnt = min(top_m, avail);
+  for (int j = cnt + threadIdx.x; j < top_m; j += blockDim.x) o[j] = -1;
+  if (cnt > 0) {
+    for (int i = threadIdx.x; i < avail; i += blockDim.x) {
+      const float si = sc[i];
+      int r = 0;
+      for (int j = 0; j < avail; ++j) r += beats(sc[j], id[j], si, i) ? 1 : 0;
+      if (r < cnt) o[r] = i;
+    }
+  }
+}
+
 }  // namespace spa
 
 // ---------------------------------------------------------------------------
@@ -562,4 +610,35 @@ extern "C" int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q
   if (q_dtype == SPA_F32) return spa::launch_router<float>(a, batch, st);
   if (q_dtype == SPA_F16) return spa::launch_router<__half>(a, batch, st);
   return spa::launch_router<__nv_bfloat16>(a, batch, st);
+}
+
+extern "C" int spa_periodic_router(const void* q, int q_dtype, int batch, int heads, int seq_len, int head_dim,
+                                   const float* summaries, int n_blocks, int block_size, int router_stride,
+                                   int top_m, int64_t* out, spa_stream_t stream) {
+  if (!q || !summaries || !out || !dtype_ok(q_dtype) || batch <= 0 || heads <= 0 || seq_len <= 0) return SPA_ERR_INVALID;
+  if (head_dim <= 0 || head_dim > 256 || n_blocks <= 0 || block_size <= 0 || router_stride <= 0 || top_m <= 0)
+    return SPA_ERR_INVALID;
+  const int U = seq_len / router_stride;
+  if (U <= 0) return SPA_ERR_INVALID;
+  if (heads > 65535 || batch > 65535) return SPA_ERR_UNSUPPORTED;
+  const size_t smem = sizeof(float) * n_blocks + sizeof(int) * n_blocks + sizeof(float) * head_dim + 16;
+  if (smem > 200 * 1024) return SPA_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid(U, heads, batch);
+#define SPA_LAUNCH_PERIODIC(T)                                                                              \
+  do {                                                                                                      \
+    SPA_CHECK_CUDA(spa_set_smem_once(spa::periodic_router_kernel<T>, static_cast<int>(smem)));              \
+    spa::periodic_router_kernel<T><<<grid, 256, smem, st>>>(static_cast<const T*>(q), seq_len, head_dim,     \
+                                                            summaries, n_blocks, block_size, router_stride,  \
+                                                            top_m, out);                                      \
+  } while (0)
+  if (q_dtype == SPA_F32)
+    SPA_LAUNCH_PERIODIC(float);
+  else if (q_dtype == SPA_F16)
+    SPA_LAUNCH_PERIODIC(__half);
+  else
+    SPA_LAUNCH_PERIODIC(__nv_bfloat16);
+#undef SPA_LAUNCH_PERIODIC
+  SPA_CHECK_CUDA(cudaGetLastError());
+  return SPA_OK;
 }

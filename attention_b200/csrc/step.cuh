@@ -40,6 +40,7 @@ extern "C" int spa_sparse_decode_step(const void* q, int dtype, int batch, int q
   a.local_window = local_window;
   a.selected = selected;
   a.top_m = top_m;
+  a.span_len = 0;
   const int max_cand = local_window + top_m * kv->page_size;
   const spa::SplitPlan plan = spa::decode_plan(batch, q_heads, kv_heads, max_cand);
   a.nsplit = plan.nsplit;

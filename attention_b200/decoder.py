@@ -1,0 +1,189 @@
+"""Integrated KV-cache decoder with sparse paged attention and a promotion cache.
+
+The model follows the reference's tiny decoder block (train_tiny_transformer.py:134-190:
+pre-norm attention and a 4x GELU MLP, learned token and position embeddings) with
+RMSNorm in place of LayerNorm.  Its decode step is the reference's page_decode
+(triton_kvcache_transformer_decode.py:47-66) re-built around the paged cache:
+
+  per layer: RMSNorm -> QKV -> kv_append(new token into its page) -> router top-m over
+  the routable pages (mean-key summaries) -> fused page-gather decode over the local
+  window + selected pages -> output projection -> residual -> RMSNorm -> MLP -> residual;
+  the promotion table of the layer is updated with the step's selection
+  (fixed-TTL policy, evaluate_promotion_ttl.py:134-135).
+
+The prompt is prefilled with the causal tensor-core prefill (window = prompt length,
+i.e. full causal attention) and written into the page cache.  GEMMs run on cuBLAS;
+attention, routing, KV append and the promotion table are this library's kernels.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from .cache import PromotionCache, kv_append
+from .paged_attention import paged_gather_decode_attention
+from .prefill import local_causal_prefill
+from .router import page_summaries, select_blocks
+
+
+@dataclass
+class DecoderConfig:
+    vocab: int = 4096
+    d_model: int = 512
+    heads: int = 8
+    layers: int = 4
+    mlp_mult: int = 4
+    page_size: int = 128
+    local_window: int = 128
+    top_m: int = 8
+    promo_slots: int = 64
+    promo_ttl: int = 32
+    max_context: int = 16384 + 256
+    eps: float = 1e-6
+
+    @property
+    def head_dim(self) -> int:
+        return self.d_model // self.heads
+
+    @property
+    def max_pages(self) -> int:
+        return -(-self.max_context // self.page_size)
+
+
+def init_weights(cfg: DecoderConfig, seed: int = 0) -> dict:
+    """Seeded random init (CPU, fp32): N(0, 0.02) matrices, unit norms, zero biases."""
+    g = torch.Generator().manual_seed(seed)
+    d, v, f = cfg.d_model, cfg.vocab, cfg.mlp_mult * cfg.d_model
+
+    def n(*shape):
+        return torch.randn(*shape, generator=g) * 0.02
+
+    w = {"emb": n(v, d), "pos": n(cfg.max_context, d), "norm_f": torch.ones(d), "head": n(v, d)}
+    for i in range(cfg.layers):
+        w[f"l{i}.norm1"] = torch.ones(d)
+        w[f"l{i}.qkv.w"] = n(3 * d, d)
+        w[f"l{i}.qkv.b"] = torch.zeros(3 * d)
+        w[f"l{i}.out.w"] = n(d, d)
+        w[f"l{i}.out.b"] = torch.zeros(d)
+        w[f"l{i}.norm2"] = torch.ones(d)
+        w[f"l{i}.fc1.w"] = n(f, d)
+        w[f"l{i}.fc1.b"] = torch.zeros(f)
+        w[f"l{i}.fc2.w"] = n(d, f)
+        w[f"l{i}.fc2.b"] = torch.zeros(d)
+    return w
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * weight.float()).to(x.dtype)
+
+
+class SparseDecoder:
+    """Batch of sequences decoded with paged KV caches (one pool per layer).
+
+    Sequence b owns pages [b * max_pages, (b+1) * max_pages) of every layer's pool."""
+
+    def __init__(self, cfg: DecoderConfig, weights: dict, batch: int, *, dtype=torch.bfloat16, device="cuda"):
+        self.cfg, self.batch, self.dtype, self.device = cfg, batch, dtype, torch.device(device)
+        self.w = {k: t.to(device=self.device, dtype=dtype) for k, t in weights.items()}
+        h, p, dh = cfg.heads, cfg.page_size, cfg.head_dim
+        n_pool = batch * cfg.max_pages
+        self.k_pool = [torch.zeros(n_pool, h, p, dh, dtype=dtype, device=self.device) for _ in range(cfg.layers)]
+        self.v_pool = [torch.zeros_like(self.k_pool[0]) for _ in range(cfg.layers)]
+        self.page_table = torch.arange(n_pool, dtype=torch.int32, device=self.device).view(batch, cfg.max_pages)
+        self.ctx = 0
+        self.summaries: list[torch.Tensor | None] = [None] * cfg.layers
+        self.n_routable = 0
+        self.promotion = PromotionCache(cfg.layers * batch, slots=cfg.promo_slots, ttl=cfg.promo_ttl,
+                                        device=self.device)
+        self.step_index = 0
+
+    # ---------------------------------------------------------------- helpers
+    def _linear(self, x, name):
+        return F.linear(x, self.w[f"{name}.w"], self.w[f"{name}.b"])
+
+    def _mlp(self, x, i):
+        h = rms_norm(x, self.w[f"l{i}.norm2"], self.cfg.eps)
+        return self._linear(F.gelu(self._linear(h, f"l{i}.fc1")), f"l{i}.fc2")
+
+    def _routable_pages(self, ctx: int) -> int:
+        return max(0, (ctx - self.cfg.local_window) // self.cfg.page_size)
+
+    def _refresh_summaries(self, n: int):
+        """Summaries of pages [0, n) of every layer (recomputed when n grows: a page becomes
+        routable once all its tokens are older than the local window)."""
+        self.n_routable = n
+        for i in range(self.cfg.layers):
+            self.summaries[i] = (page_summaries(self.k_pool[i], block_size=self.cfg.page_size, n_pages=n,
+                                                page_table=self.page_table) if n > 0 else None)
+
+    # ---------------------------------------------------------------- prefill
+    @torch.no_grad()
+    def prefill(self, tokens: torch.Tensor) -> torch.Tensor:
+        """tokens [B, S] -> logits of the last position [B, vocab]."""
+        cfg = self.cfg
+        b, s = tokens.shape
+        if s % cfg.page_size:
+            raise ValueError("the prompt length must be a multiple of the page size")
+        h, dh, p = cfg.heads, cfg.head_dim, cfg.page_size
+        pos = torch.arange(s, device=self.device)
+        x = self.w["emb"][tokens] + self.w["pos"][pos]
+        for i in range(cfg.layers):
+            hid = rms_norm(x, self.w[f"l{i}.norm1"], cfg.eps)
+            qkv = self._linear(hid, f"l{i}.qkv").view(b, s, 3, h, dh).permute(2, 0, 3, 1, 4)
+            q, k, v = (t.contiguous() for t in qkv)
+            att = local_causal_prefill(q, k, v, s)  # full causal over the prompt
+            # pages of sequence j are contiguous in the pool: [n_pages, H, P, Dh]
+            npg = s // p
+            for j in range(b):
+                base = j * cfg.max_pages
+                self.k_pool[i][base:base + npg] = k[j].view(h, npg, p, dh).permute(1, 0, 2, 3)
+                self.v_pool[i][base:base + npg] = v[j].view(h, npg, p, dh).permute(1, 0, 2, 3)
+            x = x + self._linear(att.transpose(1, 2).reshape(b, s, cfg.d_model), f"l{i}.out")
+            x = x + self._mlp(x, i)
+        self.ctx = s
+        self._refresh_summaries(self._routable_pages(s + 1))
+        return F.linear(rms_norm(x[:, -1], self.w["norm_f"], cfg.eps), self.w["head"]).float()
+
+    # ---------------------------------------------------------------- decode
+    @torch.no_grad()
+    def decode_step(self, token: torch.Tensor):
+        """token [B] at position ctx -> (logits [B, vocab] fp32, selected [layers, B, m])."""
+        cfg = self.cfg
+        b = self.batch
+        h, dh = cfg.heads, cfg.head_dim
+        pos = self.ctx
+        x = self.w["emb"][token] + self.w["pos"][pos]
+        ctx_len = torch.full((b,), pos + 1, dtype=torch.int32, device=self.device)
+        positions = torch.full((b,), pos, dtype=torch.int32, device=self.device)
+        n_routable = self._routable_pages(pos + 1)
+        if n_routable != self.n_routable:
+            self._refresh_summaries(n_routable)  # its pages were all written by earlier steps
+        selected = []
+        scale = 1.0 / math.sqrt(dh)
+        for i in range(cfg.layers):
+            hid = rms_norm(x, self.w[f"l{i}.norm1"], cfg.eps)
+            qkv = self._linear(hid, f"l{i}.qkv").view(b, 3, h, dh)
+            q, k, v = qkv[:, 0].contiguous(), qkv[:, 1].contiguous(), qkv[:, 2].contiguous()
+            kv_append(self.k_pool[i], self.v_pool[i], self.page_table, k, v, positions)
+            m = min(cfg.top_m, self.n_routable)
+            if m > 0:
+                sel = select_blocks(q, self.summaries[i][:, :, : self.n_routable], m, scale=scale)
+            else:
+                sel = torch.full((b, 1), -1, dtype=torch.int64, device=self.device)
+            att = paged_gather_decode_attention(q, self.k_pool[i], self.v_pool[i], sel,
+                                                local_window=cfg.local_window, block_size=cfg.page_size,
+                                                page_table=self.page_table, context_lens=ctx_len)
+            x = x + self._linear(att.reshape(b, cfg.d_model), f"l{i}.out")
+            x = x + self._mlp(x, i)
+            selected.append(sel)
+        sel_all = torch.stack(selected)  # [layers, B, m]
+        self.promotion.update(sel_all.reshape(cfg.layers * b, -1), self.step_index)
+        self.step_index += 1
+        self.ctx = pos + 1
+        logits = F.linear(rms_norm(x, self.w["norm_f"], cfg.eps), self.w["head"]).float()
+        return logits, sel_all

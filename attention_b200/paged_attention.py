@@ -1,8 +1,9 @@
 """Paged decode attention: drop-in for the reference's fused decode entry points.
 
-``paged_decode_attention`` and ``paged_gather_decode_attention`` keep the call
-signatures, argument meaning and ValueError messages of
-experiments/triton_paged_attention.py:56-81 and :139-168.  Keyword-only
+``paged_decode_attention``, ``paged_gather_decode_attention`` and
+``span_gather_decode_attention`` keep the call signatures, argument meaning and
+ValueError messages of experiments/triton_paged_attention.py:56-81, :139-168 and
+:210-224.  Keyword-only
 extensions (defaults reproduce the reference):
 
 * ``page_table`` / ``context_lens``: K/V given as a shared page pool
@@ -151,3 +152,54 @@ def paged_gather_decode_attention(query: torch.Tensor, keys: torch.Tensor, value
         raise ValueError("page_table must be [batch, pages] and context_lens [batch]")
     layout = pool_layout(keys, values, table)
     return _decode(query, layout, keys.size(1), lens, local_window, sel, top_m, max_cand, (sel, table, lens))
+
+
+def span_gather_decode_attention(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, centers: torch.Tensor,
+                                 *, local_window: int, span_width: int, page_table: torch.Tensor | None = None,
+                                 context_lens: torch.Tensor | None = None) -> torch.Tensor:
+    """Local window plus short spans (reference: triton_paged_attention.py:210).
+
+    Candidates of sequence b: its last ``local_window`` tokens, then for every
+    ``centers[b, j]`` the ``span_width`` tokens starting there, under one softmax.
+    Negative centers are empty slots; span tokens at or past the context are dropped."""
+    batch, heads, head_dim = query.shape
+    if not (query.is_contiguous() and keys.is_contiguous() and values.is_contiguous() and centers.is_contiguous()):
+        raise ValueError("contiguous CUDA tensors are required")
+    if not (query.is_cuda and keys.is_cuda and values.is_cuda and centers.is_cuda):
+        raise ValueError("contiguous CUDA tensors are required")
+    if centers.dim() != 2 or centers.shape[0] != batch or head_dim > 256:
+        raise ValueError("invalid centers or head dimension")
+    if keys.dim() != 4 or values.shape != keys.shape or keys.size(3) != head_dim or keys.dtype != query.dtype:
+        raise ValueError("incompatible Q/K/V shapes")
+    _check_heads(query, keys.size(1))
+    if local_window < 0 or span_width <= 0:
+        raise ValueError("invalid centers or head dimension")
+    starts = as_int64(centers).contiguous()
+    n_spans = starts.size(1)
+    if page_table is None:
+        if keys.size(0) != batch:
+            raise ValueError("incompatible Q/K/V shapes")
+        length = keys.size(2)
+        layout = contiguous_layout(keys, values, length)
+        lens = const_i32(query.device, batch, length)
+        keep = (starts, lens)
+    else:
+        if context_lens is None:
+            raise ValueError("context_lens is required with page_table")
+        table = as_int32(page_table).contiguous()
+        lens = as_int32(context_lens).contiguous()
+        layout = pool_layout(keys, values, table)
+        keep = (starts, table, lens)
+    kv_heads = keys.size(1)
+    out = torch.empty_like(query)
+    dev = query.device
+    max_cand = local_window + n_spans * (span_width + 128)
+    ws_bytes = _lib.lib.spa_decode_workspace_size(batch, heads, kv_heads, head_dim, max_cand)
+    ws = workspace(dev, ws_bytes) if ws_bytes else None
+    rc = _lib.lib.spa_span_gather_decode(query.data_ptr(), dtype_code(query), batch, heads, kv_heads, head_dim,
+                                         ctypes.byref(layout), lens.data_ptr(), local_window, starts.data_ptr(),
+                                         n_spans, span_width, head_dim ** -0.5, out.data_ptr(),
+                                         ws.data_ptr() if ws is not None else None, ws_bytes, stream_ptr(dev))
+    _lib.check(rc, "spa_span_gather_decode")
+    del keep
+    return out

@@ -116,3 +116,23 @@ def select_blocks_tree(query: torch.Tensor, super_summaries: torch.Tensor, summa
                                        out.data_ptr(), stream_ptr(q.device))
     _lib.check(rc, "spa_router_tree_topm")
     return out
+
+
+def periodic_router(query: torch.Tensor, keys: torch.Tensor, *, block_size: int, router_stride: int,
+                    top_blocks: int) -> torch.Tensor:
+    """Causal routing every ``router_stride`` tokens of a prefill; int64 [B, H, U, m]
+    with -1 in unfilled slots (reference: triton_prefill_router_overhead.py:16-34).
+    One batched kernel over all update positions replaces the per-update top-k loop."""
+    require_cuda(query, keys)
+    if query.dim() != 4 or keys.shape != query.shape:
+        raise ValueError("query and keys must be [B, H, S, D]")
+    b, h, s, d = query.shape
+    if s % block_size or s % router_stride:
+        raise ValueError("context must divide evenly into block-size and router-stride")
+    summ = page_summaries(keys.contiguous(), block_size=block_size, n_pages=s // block_size)
+    q = query.contiguous()
+    out = torch.empty(b, h, s // router_stride, top_blocks, dtype=torch.int64, device=q.device)
+    rc = _lib.lib.spa_periodic_router(q.data_ptr(), dtype_code(q), b, h, s, d, summ.data_ptr(), summ.size(2),
+                                      block_size, router_stride, top_blocks, out.data_ptr(), stream_ptr(q.device))
+    _lib.check(rc, "spa_periodic_router")
+    return out

@@ -400,6 +400,9 @@ def run_ours(args, world, rank, local):
     prefill = None
     if not args.skip_prefill:
         prefill = run_prefill(args, world, rank, dev, peaks)
+    integrated = None
+    if not args.skip_integrated:
+        integrated = run_integrated(args, dev)
 
     launches_per_step = 2 + (1 if spa._lib.lib.spa_decode_workspace_size(
         cfg.batch, cfg.q_heads, cfg.kv_heads, cfg.head_dim, cfg.local_window + cfg.top_m * cfg.page_size) else 0)
@@ -434,6 +437,7 @@ def run_ours(args, world, rank, local):
         "e2e": e2e,
         "cpu_baseline": cpu,
         "prefill": prefill,
+        "integrated_decode": integrated,
         "clocks": clocks.summary(),
         "gpu_launches": steps * launches_per_step,
     }
@@ -474,13 +478,62 @@ def run_prefill(args, world, rank, dev, peaks):
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
+    # periodic causal router over the same chunk (reference: prefill + router overhead benchmark)
+    router_ms = None
+    if world == 1:
+        for _ in range(2):
+            spa.periodic_router(q, k, block_size=256, router_stride=256, top_blocks=4)
+        torch.cuda.synchronize()
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record()
+        for _ in range(5):
+            spa.periodic_router(q, k, block_size=256, router_stride=256, top_blocks=4)
+        r1.record()
+        torch.cuda.synchronize()
+        router_ms = r0.elapsed_time(r1) / 5
     peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
     tf = flops / (ms * 1e-3) / 1e12
     return {"seq_len": seq, "window": window, "heads": heads, "head_dim": dim, "ms": round(ms, 4),
             "tflops": round(tf, 1), "peak_tflops": peak * world, "frac": round(tf / (peak * world), 4),
             "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst) x GPUs",
             "flops": flops, "sharding": f"{world} contiguous chunks, 2048-token K/V halo over NCCL" if world > 1
-            else "single GPU", "reps": reps}
+            else "single GPU", "reps": reps,
+            "periodic_router_ms": round(router_ms, 4) if router_ms is not None else None,
+            "periodic_router": "block 256, stride 256, top-4, summaries included" if router_ms is not None else None}
+
+
+def run_integrated(args, dev):
+    """Integrated 4-layer decoder (d_model 512, 8 heads, vocab 4096, bf16): a 16k-token
+    prompt prefilled into 128-token pages, then greedy decode steps with router top-8 +
+    128-token local window per layer and the 64-slot TTL-32 promotion table."""
+    from attention_b200.decoder import DecoderConfig, SparseDecoder, init_weights
+
+    steps = args.integrated_steps
+    cfg = DecoderConfig(max_context=16384 + steps + 8)  # room for 3 warm-up steps
+    dec = SparseDecoder(cfg, init_weights(cfg, seed=0), 1, device=dev)
+    prompt = torch.randint(0, cfg.vocab, (1, 16384), generator=torch.Generator().manual_seed(0)).to(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    logits = dec.prefill(prompt)
+    e1.record()
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    tok = logits.argmax(-1)
+    for _ in range(3):
+        logits, _ = dec.decode_step(tok)
+        tok = logits.argmax(-1)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        logits, _ = dec.decode_step(tok)
+        tok = logits.argmax(-1)
+    e1.record()
+    torch.cuda.synchronize()
+    return {"config": "4 layers, d_model 512, 8 heads x 64, vocab 4096, bf16, prompt 16384 in 128-token pages, "
+                      "router top-8 + 128-token window, promotion 64 slots TTL 32",
+            "prefill_ms": round(prefill_ms, 3), "decode_steps": steps,
+            "decode_us_per_step": round(e0.elapsed_time(e1) * 1e3 / steps, 2),
+            "mode": "eager launches (cuBLAS GEMMs + library kernels), greedy tokens on the device"}
 
 
 # ------------------------------------------------------------------ reference arm
@@ -533,6 +586,8 @@ def main():
     ap.add_argument("--skip-prefill", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-integrated", action="store_true")
+    ap.add_argument("--integrated-steps", type=int, default=256)
     args = ap.parse_args()
     world, rank, local = init_dist()
     if world != args.gpus and rank == 0:

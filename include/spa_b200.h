@@ -112,6 +112,21 @@ int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q_heads,
                          int64_t* selected, spa_stream_t stream);
 
 /*
+ * Periodic causal router for prefill: for every update position
+ * p_u = (u+1)*router_stride - 1 (u < seq_len / router_stride) and head h, scores the
+ * blocks g with (g+1)*block_size - 1 <= p_u by q[b,h,p_u] . summary[b,h,g] (fp32,
+ * fixed order), keeps the top_m (ties to the lower block) in descending order and
+ * pads unfilled slots with -1.  q: [B, H, S, D]; summaries fp32 [B, H, n_blocks, D];
+ * out int64 [B, H, U, top_m].
+ * Replaces: periodic_router (triton_prefill_router_overhead.py:16-34), whose Python
+ *   loop issues one topk per update position.
+ */
+int spa_periodic_router(const void* q, int q_dtype, int batch, int heads,
+                        int seq_len, int head_dim, const float* summaries,
+                        int n_blocks, int block_size, int router_stride,
+                        int top_m, int64_t* out, spa_stream_t stream);
+
+/*
  * Split-K paged decode attention.  For each sequence b and query head h
  * (kv head h / (q_heads / kv_heads)):
  *   out[b,h] = softmax(q . K_C^T * scale) V_C
@@ -138,6 +153,21 @@ int spa_paged_decode(const void* q, int dtype, int batch, int q_heads,
                      const int64_t* selected, int top_m, int max_candidates,
                      double scale, void* out, void* workspace,
                      size_t workspace_bytes, spa_stream_t stream);
+
+/*
+ * Span gather decode: as spa_paged_decode with selected pages, but the candidates
+ * after the local window are n_spans spans of span_width consecutive tokens starting
+ * at token starts[b, j] (int64; negative = empty slot; tokens at or past the context
+ * are dropped).  workspace: spa_decode_workspace_size(batch, q_heads, kv_heads,
+ * head_dim, local_window + n_spans * (span_width + 128)) bytes.
+ * Replaces: span_gather_decode_attention_kernel launch (triton_paged_attention.py:210-224).
+ */
+int spa_span_gather_decode(const void* q, int dtype, int batch, int q_heads,
+                           int kv_heads, int head_dim, const spa_kv_layout* kv,
+                           const int32_t* context_lens, int local_window,
+                           const int64_t* starts, int n_spans, int span_width,
+                           double scale, void* out, void* workspace,
+                           size_t workspace_bytes, spa_stream_t stream);
 
 /*
  * One routed sparse decode step: router then gather decode, enqueued as chained

@@ -25,7 +25,7 @@ __all__ = [
     "summaries_fp64", "super_summaries", "router_scores", "topm", "select_blocks", "select_blocks_tree",
     "expand_kv", "reference_attention", "make_candidates", "candidate_tokens", "gather_decode",
     "dense_decode", "paged_to_contiguous", "local_reference", "local_reference_chunked", "promotion_update",
-    "masked_dense_attention", "periodic_router",
+    "masked_dense_attention", "periodic_router", "span_tokens", "span_decode",
 ]
 
 
@@ -172,6 +172,30 @@ def candidate_tokens(ctx: int, local_window: int, selected_row: list[int], block
             continue
         toks.extend(t for t in range(p * block_size, (p + 1) * block_size) if t < ctx)
     return toks
+
+
+def span_tokens(ctx: int, local_window: int, starts_row: list[int], span_width: int) -> list[int]:
+    """Token ids attended by the span kernel for one sequence: the last local_window
+    tokens, then span_width tokens from each start (candidate c >= W reads
+    centers[(c-W)//span] + (c-W)%span, triton_paged_attention.py:187-193); negative
+    starts skipped, tokens at or past the context dropped."""
+    toks = list(range(max(0, ctx - local_window), ctx))
+    for c in starts_row:
+        if c < 0:
+            continue
+        toks.extend(t for t in range(c, c + span_width) if t < ctx)
+    return toks
+
+
+def span_decode(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, starts: torch.Tensor, *,
+                local_window: int, span_width: int, context_lens: list[int] | None = None) -> torch.Tensor:
+    """Attention over span_tokens per sequence; keys/values contiguous [B, Hkv, L, D]."""
+    out = []
+    for i in range(query.size(0)):
+        ctx = context_lens[i] if context_lens is not None else keys.size(2)
+        toks = torch.tensor(span_tokens(ctx, local_window, starts[i].tolist(), span_width), dtype=torch.int64)
+        out.append(reference_attention(query[i : i + 1], keys[i : i + 1, :, toks], values[i : i + 1, :, toks]))
+    return torch.cat(out)
 
 
 def gather_decode(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, selected: torch.Tensor, *,

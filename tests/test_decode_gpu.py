@@ -201,3 +201,38 @@ def test_dense_decode_32k_full_size():
                                         cfg.context)
         ref = oracle.dense_decode(wl["query"][b : b + 1].cpu(), kc, vc, [cfg.context])
         assert_close(out[b : b + 1], ref, torch.bfloat16)
+
+
+# ---------------------------------------------------------------- span gather decode
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("dim,span", [(64, 3), (128, 3), (128, 70), (16, 5)])
+def test_span_gather_contiguous(dtype, dim, span):
+    """Reference layout: spans at arbitrary token starts (unaligned, overlapping the window)."""
+    gen = torch.Generator().manual_seed(dim + span)
+    b, hq, hkv, length, win = 3, 8, 4, 1500, 64
+    q = _rand((b, hq, dim), dtype, gen, 0.5)
+    k = _rand((b, hkv, length, dim), dtype, gen, 0.5)
+    v = _rand((b, hkv, length, dim), dtype, gen, 0.5)
+    starts = torch.tensor([[5, 700, 63, 1499], [0, -1, 1436, 900], [128, 129, 64, 1000]], dtype=torch.int64)
+    out = spa.span_gather_decode_attention(q.to(DEV), k.to(DEV), v.to(DEV), starts.to(DEV), local_window=win,
+                                           span_width=span)
+    assert_close(out, oracle.span_decode(q, k, v, starts, local_window=win, span_width=span), dtype)
+
+
+def test_span_gather_page_pool():
+    gen = torch.Generator().manual_seed(77)
+    b, hq, hkv, d, page = 2, 16, 4, 128, 128
+    ctx = [6 * page + 30, 4 * page]
+    k_pool = _rand((20, hkv, page, d), torch.bfloat16, gen, 0.5)
+    v_pool = _rand((20, hkv, page, d), torch.bfloat16, gen, 0.5)
+    table = torch.randperm(20, generator=gen)[:14].view(b, 7).to(torch.int32)
+    q = _rand((b, hq, d), torch.bfloat16, gen, 0.5)
+    # spans crossing page boundaries
+    starts = torch.tensor([[120, 250, 600], [0, 383, -1]], dtype=torch.int64)
+    out = spa.span_gather_decode_attention(q.to(DEV), k_pool.to(DEV), v_pool.to(DEV), starts.to(DEV),
+                                           local_window=100, span_width=40, page_table=table.to(DEV),
+                                           context_lens=torch.tensor(ctx, dtype=torch.int32).to(DEV))
+    kc = oracle.paged_to_contiguous(k_pool, table, 7 * page)
+    vc = oracle.paged_to_contiguous(v_pool, table, 7 * page)
+    ref = oracle.span_decode(q, kc, vc, starts, local_window=100, span_width=40, context_lens=ctx)
+    assert_close(out, ref, torch.bfloat16)

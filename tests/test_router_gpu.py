@@ -111,3 +111,27 @@ def test_sparse_decode_128k_full_size(m):
         ref = oracle.reference_attention(q[b : b + 1].cpu(), kc, vc)
         o = out[b : b + 1].double().cpu()
         assert ((o - ref).abs() <= 2e-2 + 1e-2 * ref.abs()).all()
+
+
+# ---------------------------------------------------------------- periodic causal router
+def test_periodic_router_golden(golden_dir):
+    import numpy as np
+
+    fx = dict(np.load(golden_dir / "periodic_router.npz"))
+    b, h, ctx, d, page, stride, m = fx["shape"].tolist()
+    torch.manual_seed(int(fx["seed"]))
+    q = torch.randn(b, h, ctx, d)
+    k = torch.randn_like(q)
+    out = spa.periodic_router(q.to(DEV), k.to(DEV), block_size=page, router_stride=stride, top_blocks=m)
+    assert torch.equal(out.cpu(), torch.from_numpy(fx["selected"]))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_periodic_router_matches_oracle(dtype):
+    gen = torch.Generator().manual_seed(11)
+    b, h, s, d, page, stride, m = 2, 3, 4096, 64, 256, 128, 4
+    q = (torch.randn(b, h, s, d, generator=gen) * 0.5).to(dtype)
+    k = (torch.randn(b, h, s, d, generator=gen) * 0.5).to(dtype)
+    out = spa.periodic_router(q.to(DEV), k.to(DEV), block_size=page, router_stride=stride, top_blocks=m)
+    ref = oracle.periodic_router(q, k, block_size=page, router_stride=stride, top_blocks=m)
+    assert torch.equal(out.cpu(), ref)
