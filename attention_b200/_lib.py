@@ -59,7 +59,7 @@ PROTOTYPES = {
     "spa_paged_decode_noalloc": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp]),
     "spa_kv_append": (_i, [_KV, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "spa_local_prefill": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),
-    "spa_promotion_update": (_i, [_vp, _vp, _i, _i, _vp, _i, _i, _i, _vp]),
+    "spa_promotion_update": (_i, [_vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _vp]),
 }
 
 

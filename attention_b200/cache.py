@@ -62,12 +62,19 @@ class PromotionCache:
         self.last_hit = torch.zeros((rows, slots), dtype=torch.int32, device=device)
         self.rows, self.slots, self.ttl = rows, slots, ttl
 
-    def update(self, selected: torch.Tensor, step: int) -> None:
-        """Applies one step's selections ``[rows, m]`` (int64 or int32 page ids)."""
+    def update(self, selected: torch.Tensor, step) -> None:
+        """Applies one step's selections ``[rows, m]`` (int64 or int32 page ids).  ``step``
+        is an int, or a device int32 tensor of one element read by the kernel (graph replay)."""
         sel = as_int64(selected).contiguous()
         if sel.dim() != 2 or sel.size(0) != self.rows or not sel.is_cuda:
             raise ValueError("selected must be a CUDA tensor [rows, m]")
+        if isinstance(step, torch.Tensor):
+            if step.dtype != torch.int32 or not step.is_cuda or step.numel() != 1:
+                raise ValueError("a device step must be a one-element int32 CUDA tensor")
+            step_val, step_ptr = 0, step.data_ptr()
+        else:
+            step_val, step_ptr = int(step), None
         rc = _lib.lib.spa_promotion_update(self.pages.data_ptr(), self.last_hit.data_ptr(), self.rows, self.slots,
-                                           sel.data_ptr(), sel.size(1), step, self.ttl,
+                                           sel.data_ptr(), sel.size(1), step_val, step_ptr, self.ttl,
                                            stream_ptr(self.pages.device))
         _lib.check(rc, "spa_promotion_update")

@@ -30,10 +30,11 @@ __global__ void kv_append_kernel(T* __restrict__ k, T* __restrict__ v, KvAddr ad
 // refresh of promoted ids, evaluate_promotion_ttl.py:134-135; promoted-id reuse,
 // triton_promotion_cache_benchmark.py:53-60.
 __global__ void promotion_update_kernel(int32_t* __restrict__ pages, int32_t* __restrict__ last_hit, int rows,
-                                        int slots, const int64_t* __restrict__ selected, int top_m, int step,
-                                        int ttl) {
+                                        int slots, const int64_t* __restrict__ selected, int top_m, int step_arg,
+                                        const int32_t* __restrict__ step_dev, int ttl) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
+  const int step = step_dev ? *step_dev : step_arg;
   int32_t* pg = pages + static_cast<int64_t>(r) * slots;
   int32_t* lh = last_hit + static_cast<int64_t>(r) * slots;
   const int64_t* sel = selected + static_cast<int64_t>(r) * top_m;
@@ -93,12 +94,12 @@ extern "C" int spa_kv_append(const spa_kv_layout* kv, int dtype, int batch, int 
 }
 
 extern "C" int spa_promotion_update(int32_t* pages, int32_t* last_hit, int rows, int slots, const int64_t* selected,
-                                    int top_m, int step, int ttl, spa_stream_t stream) {
+                                    int top_m, int step, const int32_t* step_dev, int ttl, spa_stream_t stream) {
   if (!pages || !last_hit || !selected || rows <= 0 || slots <= 0 || top_m <= 0 || top_m > slots || ttl <= 0)
     return SPA_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   spa::promotion_update_kernel<<<(rows + 127) / 128, 128, 0, st>>>(pages, last_hit, rows, slots, selected, top_m,
-                                                                   step, ttl);
+                                                                   step, step_dev, ttl);
   SPA_CHECK_CUDA(cudaGetLastError());
   return SPA_OK;
 }

@@ -150,40 +150,108 @@ class SparseDecoder:
         return F.linear(rms_norm(x[:, -1], self.w["norm_f"], cfg.eps), self.w["head"]).float()
 
     # ---------------------------------------------------------------- decode
-    @torch.no_grad()
-    def decode_step(self, token: torch.Tensor):
-        """token [B] at position ctx -> (logits [B, vocab] fp32, selected [layers, B, m])."""
+    def _state(self):
+        """Persistent device state of the decode loop (so one captured step replays)."""
+        if not hasattr(self, "_token"):
+            b = self.batch
+            self._token = torch.zeros(b, dtype=torch.int64, device=self.device)
+            self._position = torch.zeros(b, dtype=torch.int32, device=self.device)
+            self._ctx_len = torch.zeros(b, dtype=torch.int32, device=self.device)
+            self._step_dev = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self._logits = torch.zeros(b, self.cfg.vocab, dtype=torch.float32, device=self.device)
+            self._graphs: dict = {}
+
+    def _step_body(self):
+        """One decode step on the persistent state (no host synchronisation, capturable)."""
         cfg = self.cfg
         b = self.batch
         h, dh = cfg.heads, cfg.head_dim
-        pos = self.ctx
-        x = self.w["emb"][token] + self.w["pos"][pos]
-        ctx_len = torch.full((b,), pos + 1, dtype=torch.int32, device=self.device)
-        positions = torch.full((b,), pos, dtype=torch.int32, device=self.device)
-        n_routable = self._routable_pages(pos + 1)
-        if n_routable != self.n_routable:
-            self._refresh_summaries(n_routable)  # its pages were all written by earlier steps
+        x = self.w["emb"].index_select(0, self._token) + self.w["pos"].index_select(0, self._position.long())
         selected = []
         scale = 1.0 / math.sqrt(dh)
+        m = min(cfg.top_m, self.n_routable)
         for i in range(cfg.layers):
             hid = rms_norm(x, self.w[f"l{i}.norm1"], cfg.eps)
             qkv = self._linear(hid, f"l{i}.qkv").view(b, 3, h, dh)
             q, k, v = qkv[:, 0].contiguous(), qkv[:, 1].contiguous(), qkv[:, 2].contiguous()
-            kv_append(self.k_pool[i], self.v_pool[i], self.page_table, k, v, positions)
-            m = min(cfg.top_m, self.n_routable)
+            kv_append(self.k_pool[i], self.v_pool[i], self.page_table, k, v, self._position)
             if m > 0:
-                sel = select_blocks(q, self.summaries[i][:, :, : self.n_routable], m, scale=scale)
+                sel = select_blocks(q, self.summaries[i], m, scale=scale)
             else:
                 sel = torch.full((b, 1), -1, dtype=torch.int64, device=self.device)
             att = paged_gather_decode_attention(q, self.k_pool[i], self.v_pool[i], sel,
                                                 local_window=cfg.local_window, block_size=cfg.page_size,
-                                                page_table=self.page_table, context_lens=ctx_len)
+                                                page_table=self.page_table, context_lens=self._ctx_len)
             x = x + self._linear(att.reshape(b, cfg.d_model), f"l{i}.out")
             x = x + self._mlp(x, i)
             selected.append(sel)
         sel_all = torch.stack(selected)  # [layers, B, m]
-        self.promotion.update(sel_all.reshape(cfg.layers * b, -1), self.step_index)
+        self.promotion.update(sel_all.reshape(cfg.layers * b, -1), self._step_dev)
+        self._logits.copy_(F.linear(rms_norm(x, self.w["norm_f"], cfg.eps), self.w["head"]).float())
+        self._token.copy_(self._logits.argmax(-1))
+        self._position.add_(1)
+        self._ctx_len.add_(1)
+        self._step_dev.add_(1)
+        return sel_all
+
+    def _begin_step(self):
+        """Host bookkeeping before a step: refresh summaries when a page becomes routable."""
+        n_routable = self._routable_pages(self.ctx + 1)
+        if n_routable != self.n_routable:
+            self._refresh_summaries(n_routable)  # its pages were all written by earlier steps
+
+    @torch.no_grad()
+    def decode_step(self, token: torch.Tensor):
+        """token [B] at position ctx -> (logits [B, vocab] fp32, selected [layers, B, m])."""
+        self._state()
+        if self.step_index == 0 or self._position[0].item() != self.ctx:
+            self._position.fill_(self.ctx)
+            self._ctx_len.fill_(self.ctx + 1)
+            self._step_dev.fill_(self.step_index)
+        self._token.copy_(token)
+        self._begin_step()
+        sel = self._step_body()
         self.step_index += 1
-        self.ctx = pos + 1
-        logits = F.linear(rms_norm(x, self.w["norm_f"], cfg.eps), self.w["head"]).float()
-        return logits, sel_all
+        self.ctx += 1
+        return self._logits.clone(), sel
+
+    @torch.no_grad()
+    def generate(self, token: torch.Tensor, steps: int, *, graphed: bool = True) -> torch.Tensor:
+        """Greedy decode of ``steps`` tokens starting from ``token`` [B]; returns the
+        tokens [steps, B].  With ``graphed`` every step is one CUDA-graph replay (a new
+        graph is captured only when the number of routable pages changes)."""
+        self._state()
+        self._token.copy_(token)
+        self._position.fill_(self.ctx)
+        self._ctx_len.fill_(self.ctx + 1)
+        self._step_dev.fill_(self.step_index)
+        out = torch.empty(steps, self.batch, dtype=torch.int64, device=self.device)
+        for t in range(steps):
+            self._begin_step()
+            if graphed:
+                key = self.n_routable
+                g = self._graphs.get(key)
+                if g is None:
+                    # capture on a side stream; the capture itself must not advance the state
+                    saved = [x.clone() for x in (self._token, self._position, self._ctx_len, self._step_dev)]
+                    pages, last = self.promotion.pages.clone(), self.promotion.last_hit.clone()
+                    s = torch.cuda.Stream(device=self.device)
+                    s.wait_stream(torch.cuda.current_stream(self.device))
+                    with torch.cuda.stream(s):
+                        self._step_body()  # warm-up (allocates workspaces outside the graph)
+                    torch.cuda.current_stream(self.device).wait_stream(s)
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g):
+                        self._step_body()
+                    for dst, src in zip((self._token, self._position, self._ctx_len, self._step_dev), saved):
+                        dst.copy_(src)
+                    self.promotion.pages.copy_(pages)
+                    self.promotion.last_hit.copy_(last)
+                    self._graphs[key] = g
+                g.replay()
+            else:
+                self._step_body()
+            out[t].copy_(self._token)
+            self.step_index += 1
+            self.ctx += 1
+        return out

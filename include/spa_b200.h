@@ -253,12 +253,15 @@ int spa_local_prefill(const void* q, const void* k, const void* v, int dtype,
  *      the lowest index, else evicts the entry with the smallest last_hit,
  *      ties to the smallest page id.
  * Requires top_m <= slots; duplicate ids in one selection count once.
+ * step_dev != NULL: the step is read from that device int32 instead of `step`
+ * (for calls captured once in a CUDA graph and replayed every step).
  * Replaces the host-side promoted-id swap of triton_promotion_cache_benchmark.py:53-60
  *   with a fixed-TTL policy (evaluate_promotion_ttl.py:134-135).
  */
 int spa_promotion_update(int32_t* pages, int32_t* last_hit, int rows,
                          int slots, const int64_t* selected, int top_m,
-                         int step, int ttl, spa_stream_t stream);
+                         int step, const int32_t* step_dev, int ttl,
+                         spa_stream_t stream);
 
 #ifdef __cplusplus
 }

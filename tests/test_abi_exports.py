@@ -41,7 +41,7 @@ def test_invalid_arguments_rejected_without_gpu():
 
     assert _lib.lib.spa_paged_decode(None, 2, 1, 1, 1, 64, None, None, 0, None, 0, 0, 1.0, None, None, 0,
                                      None) == _lib.SPA_ERR_INVALID
-    assert _lib.lib.spa_promotion_update(None, None, 1, 64, None, 8, 0, 32, None) == _lib.SPA_ERR_INVALID
+    assert _lib.lib.spa_promotion_update(None, None, 1, 64, None, 8, 0, None, 32, None) == _lib.SPA_ERR_INVALID
     assert _lib.lib.spa_local_prefill(None, None, None, 2, 1, 1, 1, 64, 1, None, None, 0, 0, 0, None,
                                       None) == _lib.SPA_ERR_INVALID
     assert _lib.lib.spa_decode_workspace_size(0, 1, 1, 64, 10) == 0

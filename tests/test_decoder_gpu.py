@@ -52,3 +52,26 @@ def test_decoder_bf16_runs_full_size_prompt_pages():
         assert ((sel >= 0) & (sel < dec.n_routable)).all()
         tok = logits.argmax(-1)
     assert spa.device_error_flags() == 0
+
+
+def test_graphed_generation_equals_eager():
+    """generate() replays one captured graph per step; it must produce the eager tokens,
+    pages and promotion table, across pages becoming routable."""
+    cfg = DecoderConfig(vocab=512, d_model=128, heads=4, layers=2, page_size=128, local_window=128, top_m=4,
+                        promo_slots=8, promo_ttl=5, max_context=1024 + 300)
+    w = init_weights(cfg, seed=5)
+    prompt = torch.randint(0, cfg.vocab, (2, 1024), generator=torch.Generator().manual_seed(6)).cuda()
+    a = SparseDecoder(cfg, w, 2)
+    b = SparseDecoder(cfg, w, 2)
+    tok_a = a.prefill(prompt).argmax(-1)
+    tok_b = b.prefill(prompt).argmax(-1)
+    eager = []
+    for _ in range(140):
+        logits, _ = a.decode_step(tok_a)
+        tok_a = logits.argmax(-1)
+        eager.append(tok_a)
+    graphed = b.generate(tok_b, 140, graphed=True)
+    assert torch.equal(torch.stack(eager), graphed)
+    assert torch.equal(a.promotion.pages, b.promotion.pages)
+    assert torch.equal(a.promotion.last_hit, b.promotion.last_hit)
+    assert len(b._graphs) >= 2  # a page became routable during the run
