@@ -47,6 +47,8 @@ _KV = ctypes.POINTER(KvLayout)
 PROTOTYPES = {
     "spa_version": (ctypes.c_char_p, []),
     "spa_device_error": (_i, [ctypes.POINTER(ctypes.c_uint32)]),
+    "spa_last_error": (ctypes.c_char_p, []),
+    "spa_debug_exp2_poly": (_i, [_vp, _vp, ctypes.c_int64, _vp]),
     "spa_summaries_build": (_i, [_KV, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp]),
     "spa_router_topm": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _d, _i, _vp, _vp, _vp]),
     "spa_router_tree_topm": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _vp, _i, _i, _i, _d, _i, _vp, _vp]),
@@ -88,7 +90,8 @@ def check(rc: int, what: str) -> None:
     if rc != SPA_OK:
         if rc == SPA_ERR_INVALID:
             raise ValueError(f"{what}: {STATUS_NAMES[rc]}")
-        raise SpaError(f"{what}: {STATUS_NAMES.get(rc, rc)} (status {rc})")
+        detail = lib.spa_last_error().decode() if rc == SPA_ERR_CUDA else ""
+        raise SpaError(f"{what}: {STATUS_NAMES.get(rc, rc)} (status {rc})" + (f": {detail}" if detail else ""))
 
 
 def device_error_flags() -> int:

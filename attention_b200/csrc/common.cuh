@@ -11,10 +11,20 @@
 
 #include "spa_b200.h"
 
+// Last CUDA runtime error an entry point returned SPA_ERR_CUDA for, per host thread
+// (read by spa_last_error()).
+inline cudaError_t& spa_last_cuda_error() {
+  static thread_local cudaError_t e = cudaSuccess;
+  return e;
+}
+
 #define SPA_CHECK_CUDA(expr)                          \
   do {                                                \
     cudaError_t _e = (expr);                          \
-    if (_e != cudaSuccess) return SPA_ERR_CUDA;       \
+    if (_e != cudaSuccess) {                          \
+      spa_last_cuda_error() = _e;                     \
+      return SPA_ERR_CUDA;                            \
+    }                                                 \
   } while (0)
 
 // Bits of the device-side error word (read by spa_device_error()).
@@ -180,6 +190,77 @@ struct MmaOp<__half> {
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes of work).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// 2^x for a pair of lanes on the FMA/ALU pipes (no MUFU), for x <= 126: x = n + f with
+// n = round(x) and f in [-1/2, 1/2] (Cody-Waite style split: adding 1.5*2^23 leaves n in
+// the low mantissa bits), 2^f by a cubic minimax polynomial (Remez exchange on the
+// relative error, coefficients from derive_exp2_poly.py: max relative error 7.5e-5, below
+// half an ulp of a bf16 or fp16 probability), and 2^n added into the exponent field.  x
+// is clamped at -125 so the exponent field stays normal; 2^-125 stands in for 0.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  // u = -(x + 1.5*2^23) rounded = -t: the low mantissa bits hold n, the sign bit is
+  // shifted out below; u + 1.5*2^23 = -n exactly, so f = x - n exactly.
+  const float2 u = ffma2(x, make_float2(-1.0f, -1.0f), make_float2(-kShift, -kShift));
+  const float2 f = fadd2(x, fadd2(u, make_float2(kShift, kShift)));
+  float2 p = ffma2(make_float2(0.0551716685295105f, 0.0551716685295105f), f,
+                   make_float2(0.2426111251115799f, 0.2426111251115799f));
+  p = ffma2(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  p = ffma2(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(u.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(u.y) << 23)));
+}
+
+// Named barrier over `count` threads (whole warps); returns the AND of `pred` over them.
+__device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t count, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
+      "barrier.cta.red.and.pred p, %2, %3, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(out)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+      : "memory");
+  return out != 0;
+}
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t count) {
+  asm volatile("barrier.cta.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// True in exactly one lane of the (converged, full) warp: the lowest one.
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred;
+  asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}" : "=r"(pred));
+  return pred != 0;
+}
+
+// max(a, b, c) in one instruction (three-input max, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float y;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
   return y;
 }
 

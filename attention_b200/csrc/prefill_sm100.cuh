@@ -5,17 +5,25 @@
 // 128-row query tiles of one (b, h) and streams the 128-key tiles that intersect their
 // windows (W/128 + 2 tiles for W a multiple of 128):
 //
-//   warp 0      TMA producer: Q tiles once, then K/V tiles into a STAGES-deep ring
+//   warp 0      TMA producer: Q tiles once, then K and V tiles into two STAGES-deep
+//               rings with separate full/empty barriers: K(j) is released as soon as
+//               both S(j) products complete, so K(j+2) streams in while V(j) is still
+//               being multiplied (about one KV-tile period of lead instead of none)
 //   warp 1      MMA issuer (one thread): S_t = Q_t K^T (SS form, both operands in
 //               shared memory, K-major), O_t += P_t V (TS form: P read from TMEM,
 //               V from shared memory, MN-major)
-//   warps 4-7   softmax of query tile 0 (thread = row = TMEM lane)
-//   warps 8-11  softmax of query tile 1
+//   warps 4-11  softmax, both query tiles in turn: warp w reaches TMEM lanes
+//               [32*(w%4), 32*(w%4)+32) (= rows), warps 4-7 take key columns 0-63 and
+//               warps 8-11 columns 64-127; the two warps of a row range exchange their
+//               partial row maxima through shared memory (a 64-thread named barrier)
+//   warps 2-3   idle
 //
 // TMEM (512 columns): S_0 [0,128), S_1 [128,256), O_0 [256,256+D), O_1 [384,384+D).
-// P_t (bf16 pairs) overwrites the first 64 columns of S_t once S_t is in registers.
-// The MMA warp interleaves O_0(j), S_0(j+1), O_1(j), S_1(j+1) so each softmax warp
-// group overlaps the other tile's tensor-core work.  The running max is only moved
+// P_t (bf16 pairs) overwrites the first 64 columns of S_t once S_t is in registers: keys
+// 0-63 (from warps 4-7) and keys 64-127 (warps 8-11) each signal their own barrier, and
+// the PV product of one half starts as soon as that half is stored.
+// The MMA warp interleaves O_0(j), S_0(j+1), O_1(j), S_1(j+1), so the softmax of one
+// tile overlaps the other tile's tensor-core work.  The running max is only moved
 // (and O rescaled in TMEM) when a tile's max exceeds it by more than 2^8.
 //
 // Keys are indexed in the concatenation [halo ; keys] (halo_len a multiple of 128):
@@ -46,9 +54,14 @@ struct PfSmem {
   static constexpr int kQ1 = kTileBytes;
   static constexpr int kK = 2 * kTileBytes;
   static constexpr int kV = kK + kPfStages * kTileBytes;
-  static constexpr int kBar = kV + kPfStages * kTileBytes;
-  // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_final[2], mma_done; + tmem slot
-  static constexpr int kNumBars = 1 + 2 * kPfStages + 2 + 2 + 2 + 1;
+  // softmax exchange: partial row maxima [2 step parities][2 column halves][128 rows] and
+  // partial row sums [2 tiles][2 column halves][128 rows], fp32
+  static constexpr int kX = kV + kPfStages * kTileBytes;
+  static constexpr int kXBytes = (2 * 2 * kPfTile + 2 * 2 * kPfTile) * 4;
+  static constexpr int kBar = kX + kXBytes;
+  // barriers: q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_half[2], p_full[2],
+  // o_final[2], mma_done; + tmem slot
+  static constexpr int kNumBars = 1 + 4 * kPfStages + 2 + 2 + 2 + 2 + 1;
   static constexpr int kBytes = kBar + kNumBars * 8 + 16 + 1024;
 };
 
@@ -115,6 +128,13 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
                "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),          \
                "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])     \
                : "memory")
+
+#define SPA_TMEM_LD16(taddr, r)                                                                                  \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];" \
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),  \
+                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),        \
+                 "=r"(r[15])                                                                                     \
+               : "r"(taddr))
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -185,10 +205,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + kPfStages;
-  uint64_t* s_full = kv_empty + kPfStages;
-  uint64_t* p_full = s_full + 2;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + kPfStages;
+  uint64_t* v_full = k_empty + kPfStages;
+  uint64_t* v_empty = v_full + kPfStages;
+  uint64_t* s_full = v_empty + kPfStages;
+  uint64_t* p_half = s_full + 2;
+  uint64_t* p_full = p_half + 2;
   uint64_t* o_final = p_full + 2;
   uint64_t* mma_done = o_final + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
@@ -211,11 +234,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kPfStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
+      mbar_init(&p_half[t], 4);
       mbar_init(&p_full[t], 4);
       mbar_init(&o_final[t], 1);
     }
@@ -245,229 +271,268 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           tma_load_3d(smem + (t ? L::kQ1 : L::kQ0) + bx * L::kBoxBytes, &qmap, q_full, bx * 64,
                       (qt0 + t) * kPfTile, bh);
       }
+      // K(j) before V(j): stages free in the order K(j-2) (after S(j-2)), V(j-2) (after PV(j-2))
       for (int j = J0; j <= J1; ++j) {
         const int i = j - J0, s = i % kPfStages;
-        if (i >= kPfStages && !mbar_wait_bounded(&kv_empty[s], ((i / kPfStages) - 1) & 1)) break;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * L::kTileBytes);
         const bool from_halo = j < halo_tiles;
         const CUtensorMap* km = from_halo ? &khmap : &kmap;
         const CUtensorMap* vm = from_halo ? &vhmap : &vmap;
         const int y = from_halo ? j * kPfTile : (j - halo_tiles) * kPfTile;
-        for (int bx = 0; bx < L::kBoxes; ++bx) {
-          tma_load_3d(smem + L::kK + s * L::kTileBytes + bx * L::kBoxBytes, km, &kv_full[s], bx * 64, y, bh);
-          tma_load_3d(smem + L::kV + s * L::kTileBytes + bx * L::kBoxBytes, vm, &kv_full[s], bx * 64, y, bh);
-        }
+        if (i >= kPfStages && !mbar_wait_bounded(&k_empty[s], ((i / kPfStages) - 1) & 1)) break;
+        mbar_arrive_expect_tx(&k_full[s], L::kTileBytes);
+        for (int bx = 0; bx < L::kBoxes; ++bx)
+          tma_load_3d(smem + L::kK + s * L::kTileBytes + bx * L::kBoxBytes, km, &k_full[s], bx * 64, y, bh);
+        if (i >= kPfStages && !mbar_wait_bounded(&v_empty[s], ((i / kPfStages) - 1) & 1)) break;
+        mbar_arrive_expect_tx(&v_full[s], L::kTileBytes);
+        for (int bx = 0; bx < L::kBoxes; ++bx)
+          tma_load_3d(smem + L::kV + s * L::kTileBytes + bx * L::kBoxBytes, vm, &v_full[s], bx * 64, y, bh);
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0 && (act[0] || act[1])) {
+    // The whole warp runs the control flow, so descriptors stay warp-uniform; one
+    // elected lane (always the same one) issues each batch of tcgen05.mma and the
+    // commits that track them.  Issuing from a single-lane branch instead costs about
+    // twice the 64 cycles a 128x128x16 product takes on the tensor cores.
+    if (act[0] || act[1]) {
       constexpr uint32_t kIdQK = instr_desc_f16(PfFmt<T>::kFmt, kPfTile, kPfTile, 0, 0);
       constexpr uint32_t kIdPV = instr_desc_f16(PfFmt<T>::kFmt, kPfTile, D, 0, 1);
-      const uint32_t q_addr[2] = {smem_u32(smem + L::kQ0), smem_u32(smem + L::kQ1)};
-      const uint32_t k_addr = smem_u32(smem + L::kK), v_addr = smem_u32(smem + L::kV);
+      // descriptor start addresses are in 16-byte units in the low 14 bits; smem offsets
+      // below 256 KB never carry out of that field
+      const uint64_t q_desc[2] = {smem_desc(smem_u32(smem + L::kQ0), 16, 1024),
+                                  smem_desc(smem_u32(smem + L::kQ1), 16, 1024)};
+      const uint64_t k_desc = smem_desc(smem_u32(smem + L::kK), 16, 1024);
+      const uint64_t v_desc = smem_desc(smem_u32(smem + L::kV), L::kBoxBytes, 1024);
       const uint32_t s_col[2] = {0u, 128u}, o_col[2] = {256u, 384u};
       bool ok = mbar_wait_bounded(q_full, 0);
       int it[2] = {0, 0};
-      int kv_ready = J0 - 1;  // last key tile whose kv_full has been waited on
-      auto wait_kv = [&](int j) -> bool {
-        if (j <= kv_ready) return true;
+      int k_ready = J0 - 1, v_ready = J0 - 1;  // last key tile whose K / V has been waited on
+      auto wait_tile = [&](uint64_t* full, int& ready, int j) -> bool {
+        if (j <= ready) return true;
         const int i = j - J0;
-        if (!mbar_wait_bounded(&kv_full[i % kPfStages], (i / kPfStages) & 1)) return false;
-        kv_ready = j;
+        if (!mbar_wait_bounded(&full[i % kPfStages], (i / kPfStages) & 1)) return false;
+        ready = j;
         tc_fence_after();
         return true;
       };
+      auto commit = [&](uint64_t* bar) {
+        if (elect_one_sync()) tc_commit(bar);
+        __syncwarp();
+      };
       auto issue_s = [&](int t, int j) {
-        const uint32_t kb = k_addr + ((j - J0) % kPfStages) * L::kTileBytes;
+        const uint64_t kd = k_desc + ((((j - J0) % kPfStages) * L::kTileBytes) >> 4);
+        if (elect_one_sync()) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::kBoxBytes + (kk & 3) * 32;
-          mma_ss(tmem + s_col[t], smem_desc(q_addr[t] + off, 16, 1024), smem_desc(kb + off, 16, 1024), kIdQK,
-                 kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = ((kk >> 2) * L::kBoxBytes + (kk & 3) * 32) >> 4;
+            mma_ss(tmem + s_col[t], q_desc[t] + off, kd + off, kIdQK, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&s_full[t]);
         }
-        tc_commit(&s_full[t]);
+        __syncwarp();
+      };
+      // O_t += P_t V over key rows [16*k0, 16*k1) of the tile (P columns 8*k0 ..)
+      auto issue_pv = [&](int t, uint64_t vd, int k0, int k1, bool first) {
+        if (elect_one_sync()) {
+#pragma unroll
+          for (int kk = k0; kk < k1; ++kk)
+            mma_ts(tmem + o_col[t], tmem + s_col[t] + kk * 8, vd + ((kk * 16 * 128) >> 4), kIdPV,
+                   (!first || kk > 0) ? 1u : 0u);
+        }
+        __syncwarp();
       };
       // prologue: S_t(J0)
-      if (ok && wait_kv(J0)) {
+      if (ok && wait_tile(k_full, k_ready, J0)) {
         for (int t = 0; t < 2; ++t)
           if (act[t] && lo[t] <= J0 && J0 <= hi[t]) issue_s(t, J0);
+        commit(&k_empty[0]);
       } else {
         ok = false;
       }
       for (int j = J0; ok && j <= J1; ++j) {
-        const uint32_t vb = v_addr + ((j - J0) % kPfStages) * L::kTileBytes;
+        const uint64_t vd = v_desc + ((((j - J0) % kPfStages) * L::kTileBytes) >> 4);
         for (int t = 0; t < 2 && ok; ++t) {
           if (act[t] && lo[t] <= j && j <= hi[t]) {
+            if (!mbar_wait_bounded(&p_half[t], it[t] & 1) || !wait_tile(v_full, v_ready, j)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(t, vd, 0, kPfTile / 32, it[t] == 0);
             if (!mbar_wait_bounded(&p_full[t], it[t] & 1)) {
               ok = false;
               break;
             }
             tc_fence_after();
-#pragma unroll
-            for (int kk = 0; kk < kPfTile / 16; ++kk)
-              mma_ts(tmem + o_col[t], tmem + s_col[t] + kk * 8,
-                     smem_desc(vb + kk * 16 * 128, L::kBoxBytes, 1024), kIdPV, (it[t] > 0 || kk > 0) ? 1u : 0u);
+            issue_pv(t, vd, kPfTile / 32, kPfTile / 16, false);
             ++it[t];
-            if (j == hi[t]) tc_commit(&o_final[t]);
+            if (j == hi[t]) commit(&o_final[t]);
           }
           if (act[t] && lo[t] <= j + 1 && j + 1 <= hi[t]) {
-            if (!wait_kv(j + 1)) {
+            if (!wait_tile(k_full, k_ready, j + 1)) {
               ok = false;
               break;
             }
             issue_s(t, j + 1);
           }
         }
-        tc_commit(&kv_empty[(j - J0) % kPfStages]);
+        // V(j) is free after PV(j); K(j+1) after both S(j+1) (the key-tile ranges of the two
+        // query tiles overlap, so every j+1 <= J1 was used by at least one of them)
+        commit(&v_empty[(j - J0) % kPfStages]);
+        if (ok && j + 1 <= J1) commit(&k_empty[(j + 1 - J0) % kPfStages]);
       }
       // every issued MMA completes before TMEM is released
-      tc_commit(mma_done);
+      commit(mma_done);
       mbar_wait_bounded(mma_done, 0);
     }
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- softmax
-    const int t = (warp - 4) >> 2;
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // row within the tile == TMEM lane
-    if (act[t]) {
-      const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-      const uint32_t s_addr = lane_base + (t ? 128u : 0u);
-      const uint32_t o_addr = lane_base + (t ? 384u : 256u);
-      const int qc = (qt0 + t) * kPfTile + r + a.halo;  // this row's query position
-      float m_run = -INFINITY, l_run = 0.f;
-      bool ok = true;
-      const int n = hi[t] - lo[t] + 1;
-      for (int it = 0; it < n; ++it) {
-        const int j = lo[t] + it;
-        if (!mbar_wait_bounded(&s_full[t], it & 1)) {
-          ok = false;
-          break;
-        }
+    const int chalf = (warp - 4) >> 2;  // key columns [64*chalf, 64*chalf + 64)
+    const int r = quad * 32 + lane;     // row within the tile == TMEM lane
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    float* xmax = reinterpret_cast<float*>(smem + L::kX);  // [parity][half][row]
+    float* xsum = xmax + 4 * kPfTile;                       // [tile][half][row]
+    const uint32_t pair_bar = 1 + quad;                     // named barrier of warps 4+quad, 8+quad
+    constexpr int kHalfD = D / 2;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    int its[2] = {0, 0};
+    int step = 0;
+    bool ok = true;
+    for (int j = J0; ok && j <= J1; ++j) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {  // unrolled: per-tile state stays in registers
+        if (!ok || !(act[t] && lo[t] <= j && j <= hi[t])) continue;
+        const bool got = mbar_wait_bounded(&s_full[t], its[t] & 1);
         tc_fence_after();
+        const uint32_t s_addr = lane_base + (t ? 128u : 0u);
+        const uint32_t o_addr = lane_base + (t ? 384u : 256u) + kHalfD * chalf;
+        const int qc = (qt0 + t) * kPfTile + r + a.halo;  // this row's query position
         const int kc0 = j * kPfTile;
         const int tile_q0 = (qt0 + t) * kPfTile + a.halo;
         const bool full_tile =
             kc0 + kPfTile - 1 <= tile_q0 && kc0 > tile_q0 + kPfTile - 1 - a.W && kc0 + kPfTile <= a.halo + a.S;
-        const int kmax = full_tile ? 127 : min(qc, a.halo + a.S - 1) - kc0;  // last valid column
-        const int kmin = full_tile ? 0 : qc - a.W + 1 - kc0;                 // first valid column
-        // pass 1: row max of the raw scores (scale > 0 commutes with max); S stays in TMEM
-        float raw_max = -INFINITY;
-        if (full_tile) {
+        {
+          if (got && !full_tile) {
+            // partial tile: scores outside [kmin, kmax] (causal, window, sequence end) are
+            // set to -inf in TMEM first, so one code path serves every tile
+            const int kmax = min(qc, a.halo + a.S - 1) - kc0 - 64 * chalf;
+            const int kmin = qc - a.W + 1 - kc0 - 64 * chalf;
 #pragma unroll 1
-          for (int c = 0; c < 4; c += 2) {
-            uint32_t u[32], w[32];
-            SPA_TMEM_LD32(s_addr + 32 * c, u);
-            SPA_TMEM_LD32(s_addr + 32 * c + 32, w);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) raw_max = fmaxf(raw_max, fmaxf(__uint_as_float(u[e]), __uint_as_float(w[e])));
-          }
-        } else {
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t u[32];
-            SPA_TMEM_LD32(s_addr + 32 * c, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int col = 32 * c + e;
-              raw_max = (col >= kmin && col <= kmax) ? fmaxf(raw_max, __uint_as_float(u[e])) : raw_max;
-            }
-          }
-        }
-        const float mt = raw_max * a.scale_log2;
-        if (mt > m_run + kPfRescaleThreshold || (m_run == -INFINITY && mt > -INFINITY)) {
-          // move the running max; rescale O (complete: S_t(j) was issued after O_t(j-1))
-          const float alpha = fast_exp2(m_run - mt);  // 0 when m_run = -inf
-          if (it > 0 && m_run > -INFINITY) {
-#pragma unroll 1
-            for (int c = 0; c < D / 32; ++c) {
-              uint32_t o[32];
-              SPA_TMEM_LD32(o_addr + 32 * c, o);
+            for (int c = 0; c < 4; ++c) {
+              uint32_t mk[16];
+              SPA_TMEM_LD16(s_addr + 64 * chalf + 16 * c, mk);
               tmem_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-              SPA_TMEM_ST32(o_addr + 32 * c, o);
+              for (int e = 0; e < 16; ++e) mk[e] = (16 * c + e >= kmin && 16 * c + e <= kmax) ? mk[e] : 0xff800000u;
+              SPA_TMEM_ST16(s_addr + 64 * chalf + 16 * c, mk);
             }
+            tmem_wait_st();
           }
-          l_run *= alpha;
-          m_run = mt;
-        }
-        const float neg_mu = m_run == -INFINITY ? 0.f : -m_run;
-        const float sc = a.scale_log2;
-        // pass 2: P = exp2(s*scale - m) as 16-bit pairs into the first 64 columns of S_t.
-        // Chunk pair (c, c+1) reads columns [32c, 32c+64) and writes [16c, 16c+32), which
-        // were read by earlier chunks (or by this one): writes never overtake reads.
-        float lsum = 0.f;
-        if (full_tile) {
-#pragma unroll 1
-          for (int c = 0; c < 4; c += 2) {
-            uint32_t u[32], w[32];
-            SPA_TMEM_LD32(s_addr + 32 * c, u);
-            SPA_TMEM_LD32(s_addr + 32 * c + 32, w);
+          uint32_t sv[64];
+          float pm = -INFINITY;
+          if (got) {
+            SPA_TMEM_LD32(s_addr + 64 * chalf, sv);
+            SPA_TMEM_LD32(s_addr + 64 * chalf + 32, (sv + 32));
             tmem_wait_ld();
-            uint32_t pk[16], pw[16];
+            // partial row max of the raw scores (scale > 0 commutes with max), 8 chains
+            float mx[8];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float p0 = fast_exp2(fmaf(__uint_as_float(u[2 * e]), sc, neg_mu));
-              const float p1 = fast_exp2(fmaf(__uint_as_float(u[2 * e + 1]), sc, neg_mu));
-              const float q0 = fast_exp2(fmaf(__uint_as_float(w[2 * e]), sc, neg_mu));
-              const float q1 = fast_exp2(fmaf(__uint_as_float(w[2 * e + 1]), sc, neg_mu));
-              lsum += (p0 + p1) + (q0 + q1);
-              pk[e] = PfFmt<T>::pack(p0, p1);
-              pw[e] = PfFmt<T>::pack(q0, q1);
+            for (int c = 0; c < 8; ++c) mx[c] = fmaxf(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1]));
+#pragma unroll
+            for (int e = 16; e < 64; e += 16) {
+#pragma unroll
+              for (int c = 0; c < 8; ++c)
+                mx[c] = fmax3(mx[c], __uint_as_float(sv[e + 2 * c]), __uint_as_float(sv[e + 2 * c + 1]));
             }
-            SPA_TMEM_ST16(s_addr + 16 * c, pk);
-            SPA_TMEM_ST16(s_addr + 16 * c + 16, pw);
+            pm = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7]));
           }
-        } else {
+          // exchange with the other column half; both warps leave the loop together if
+          // either one's wait gave up (the barrier also reduces the ok flags)
+          xmax[(step & 1) * 2 * kPfTile + chalf * kPfTile + r] = pm;
+          ok = named_barrier_and(pair_bar, 64, got);
+          if (!ok) continue;
+          const float other = xmax[(step & 1) * 2 * kPfTile + (1 - chalf) * kPfTile + r];
+          const float mt = fmaxf(pm, other) * a.scale_log2;
+          if (mt > m_run[t] + kPfRescaleThreshold || (m_run[t] == -INFINITY && mt > -INFINITY)) {
+            // move the running max; rescale this warp's half of O (complete: S_t(j) was
+            // issued after O_t(j-1))
+            const float alpha = fast_exp2(m_run[t] - mt);  // 0 when m_run = -inf
+            if (its[t] > 0 && m_run[t] > -INFINITY) {
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t u[32];
-            SPA_TMEM_LD32(s_addr + 32 * c, u);
-            tmem_wait_ld();
-            uint32_t pk[16];
+              for (int c = 0; c < kHalfD / 16; ++c) {
+                uint32_t o[16];
+                SPA_TMEM_LD16(o_addr + 16 * c, o);
+                tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int col = 32 * c + 2 * e;
-              const float p0 =
-                  (col >= kmin && col <= kmax) ? fast_exp2(fmaf(__uint_as_float(u[2 * e]), sc, neg_mu)) : 0.f;
-              const float p1 = (col + 1 >= kmin && col + 1 <= kmax)
-                                   ? fast_exp2(fmaf(__uint_as_float(u[2 * e + 1]), sc, neg_mu))
-                                   : 0.f;
-              lsum += p0 + p1;
-              pk[e] = PfFmt<T>::pack(p0, p1);
+                for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                SPA_TMEM_ST16(o_addr + 16 * c, o);
+              }
             }
-            SPA_TMEM_ST16(s_addr + 16 * c, pk);
+            l_run[t] *= alpha;
+            m_run[t] = mt;
           }
+          const float neg_mu = m_run[t] == -INFINITY ? 0.f : -m_run[t];
+          const float sc = a.scale_log2;
+          // P = exp2(s*scale - m) as 16-bit pairs into columns [32*chalf, 32*chalf + 32) of
+          // S_t; those scores were loaded before the exchange barrier.  One pair in four
+          // takes its exponentials on the FMA pipes (exp2_poly2): the MUFU unit evaluates
+          // 16 exponentials per SM per clock, the rate at which the tensor cores consume
+          // scores at head_dim 128.  Masked columns hold -inf: ex2 gives 0, exp2_poly2
+          // gives 2^-125 (below any contribution a valid key makes).
+          const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(neg_mu, neg_mu);
+          float2 ls[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+          uint32_t pk[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float2 x =
+                ffma2(make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2, nm2);
+            const float2 pr = ((e & 3) == 3) ? exp2_poly2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
+            ls[e & 1] = fadd2(ls[e & 1], pr);
+            pk[e] = PfFmt<T>::pack(pr.x, pr.y);
+          }
+          SPA_TMEM_ST32(s_addr + 32 * chalf, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(chalf == 0 ? &p_half[t] : &p_full[t]);
+          l_run[t] += (ls[0].x + ls[0].y) + (ls[1].x + ls[1].y);
         }
-        l_run += lsum;
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[t]);
+        ++its[t];
+        ++step;
       }
-      // epilogue: O / l -> global
-      if (ok && mbar_wait_bounded(&o_final[t], 0)) {
-        tc_fence_after();
-        const int q = (qt0 + t) * kPfTile + r;
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        T* orow = static_cast<T*>(a.out) + (static_cast<int64_t>(bh) * a.S + q) * D;
+    }
+    // epilogue: O / l -> global, this warp's half of the columns; the two partial row
+    // sums meet in shared memory (every warp of a pair reaches this barrier once)
+#pragma unroll
+    for (int t = 0; t < 2; ++t) xsum[t * 2 * kPfTile + chalf * kPfTile + r] = l_run[t];
+    named_barrier_sync(pair_bar, 64);
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (!ok || !act[t]) continue;
+      if (!mbar_wait_bounded(&o_final[t], 0)) {
+        ok = false;
+        continue;
+      }
+      tc_fence_after();
+      const float l = l_run[t] + xsum[t * 2 * kPfTile + (1 - chalf) * kPfTile + r];
+      const int q = (qt0 + t) * kPfTile + r;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* orow = static_cast<T*>(a.out) + (static_cast<int64_t>(bh) * a.S + q) * D + kHalfD * chalf;
+      const uint32_t o_addr = lane_base + (t ? 384u : 256u) + kHalfD * chalf;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          SPA_TMEM_LD32(o_addr + 32 * c, o);
-          tmem_wait_ld();
-          if (q < a.row1) {
-            uint32_t pk[16];
+      for (int c = 0; c < kHalfD / 32; ++c) {
+        uint32_t o[32];
+        SPA_TMEM_LD32(o_addr + 32 * c, o);
+        tmem_wait_ld();
+        if (q < a.row1) {
+          uint32_t pk[16];
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              pk[e] = PfFmt<T>::pack(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
-            uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+          for (int e = 0; e < 16; ++e)
+            pk[e] = PfFmt<T>::pack(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+          uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
 #pragma unroll
-            for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-          }
+          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
         }
       }
     }

@@ -9,7 +9,35 @@
 #include "common.cuh"
 
 extern "C" const char* spa_version(void) {
-  return "spa_b200 0.1 (sm_100a; tcgen05 prefill, TMA+mma.sync paged decode, fp64 router)";
+  return "spa_b200 0.2 (sm_100a; tcgen05 prefill, TMA+mma.sync paged decode, fp32 cluster router)";
+}
+
+namespace spa {
+// Thread i evaluates the pair (2i, 2i+1); an odd tail element is paired with itself.
+__global__ void debug_exp2_poly_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; 2 * i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const bool pair = 2 * i + 1 < n;
+    const float2 r = exp2_poly2(make_float2(x[2 * i], pair ? x[2 * i + 1] : x[2 * i]));
+    y[2 * i] = r.x;
+    if (pair) y[2 * i + 1] = r.y;
+  }
+}
+}  // namespace spa
+
+extern "C" int spa_debug_exp2_poly(const float* x, float* y, int64_t n, spa_stream_t stream) {
+  if (!x || !y || n < 0) return SPA_ERR_INVALID;
+  if (n == 0) return SPA_OK;
+  const int64_t blocks = ((n + 1) / 2 + 255) / 256;
+  spa::debug_exp2_poly_kernel<<<static_cast<unsigned>(blocks < 4096 ? blocks : 4096), 256, 0,
+                                reinterpret_cast<cudaStream_t>(stream)>>>(x, y, n);
+  SPA_CHECK_CUDA(cudaGetLastError());
+  return SPA_OK;
+}
+
+extern "C" const char* spa_last_error(void) {
+  const cudaError_t e = spa_last_cuda_error();
+  return e == cudaSuccess ? "" : cudaGetErrorString(e);
 }
 
 extern "C" int spa_device_error(uint32_t* out_flags) {

@@ -62,6 +62,10 @@ typedef struct {
 /* Library version and build information (NUL-terminated, static storage). */
 const char* spa_version(void);
 
+/* CUDA runtime error text of the last call in this host thread that returned
+ * SPA_ERR_CUDA ("" if none); static storage. */
+const char* spa_last_error(void);
+
 /* Reads and clears the library's device-side error word on the current device
  * (nonzero after a bounded wait gave up or a kernel saw an invalid page id).
  * Synchronises the current device.  Returns SPA_OK or SPA_ERR_CUDA. */
@@ -140,9 +144,9 @@ int spa_periodic_router(const void* q, int q_dtype, int batch, int heads,
  * q: [B, Hq, D]; out: [B, Hq, D] (same dtype as q).
  * Replaces: paged_decode_attention_kernel launch (triton_paged_attention.py:56-81)
  *   and paged_gather_decode_attention_kernel launch (:139-168).
- * workspace: spa_decode_workspace_size() bytes of device memory, zero-filled
- *   before its first use (it begins with arrival counters that every call leaves
- *   at zero; re-zero it after spa_device_error reports a failed wait).
+ * workspace: spa_decode_workspace_size() bytes of device memory (per-split
+ *   partial outputs and log-sum-exps of the global split merge; no initial
+ *   contents are required).
  *   Requires batch * kv_heads <= 65536.
  */
 size_t spa_decode_workspace_size(int batch, int q_heads, int kv_heads,
@@ -262,6 +266,15 @@ int spa_promotion_update(int32_t* pages, int32_t* last_hit, int rows,
                          int slots, const int64_t* selected, int top_m,
                          int step, const int32_t* step_dev, int ttl,
                          spa_stream_t stream);
+
+/*
+ * Diagnostic: y[i] = 2^x[i] through the FMA-pipe exponential that the prefill
+ * softmax uses for part of its probabilities (n = round(x), cubic minimax
+ * polynomial for 2^(x-n), relative error <= 7.5e-5 for -125 <= x <= 126; x below
+ * -125 gives 2^-125).  No reference counterpart: it lets a test hold the
+ * approximation against exp2 computed elsewhere.
+ */
+int spa_debug_exp2_poly(const float* x, float* y, int64_t n, spa_stream_t stream);
 
 #ifdef __cplusplus
 }
