@@ -54,6 +54,7 @@ PROTOTYPES = {
     "spa_router_tree_topm": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _vp, _i, _i, _i, _d, _i, _vp, _vp]),
     "spa_periodic_router": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _i, _i, _i, _vp, _vp]),
     "spa_decode_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "spa_decode_plan": (_i, [_i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "spa_paged_decode": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp, _sz, _vp]),
     "spa_span_gather_decode": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp, _sz, _vp]),
     "spa_sparse_decode_step": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _d, _d, _vp,
@@ -99,3 +100,11 @@ def device_error_flags() -> int:
     v = ctypes.c_uint32(0)
     check(lib.spa_device_error(ctypes.byref(v)), "spa_device_error")
     return int(v.value)
+
+
+def decode_plan(batch: int, q_heads: int, kv_heads: int, max_candidates: int) -> tuple[int, bool]:
+    """(splits per (sequence, kv head), merged on chip in a cluster) for the decode kernel."""
+    ns, cl = _i(0), _i(0)
+    check(lib.spa_decode_plan(batch, q_heads, kv_heads, max_candidates, ctypes.byref(ns), ctypes.byref(cl)),
+          "spa_decode_plan")
+    return int(ns.value), bool(cl.value)

@@ -38,14 +38,14 @@ _CONST_I32: dict[tuple, torch.Tensor] = {}
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """A zero-initialised device byte buffer of at least ``nbytes`` reserved for the
-    caller's current stream (one buffer per (device, stream); calls on one stream are
-    ordered, so the buffer is never used by two kernels at once).  The decode kernels
-    keep arrival counters at its start and leave them zero after every call."""
+    """A device byte buffer of at least ``nbytes`` reserved for the caller's current
+    stream (one buffer per (device, stream); calls on one stream are ordered, so the
+    buffer is never used by two kernels at once).  The decode kernels write every
+    partial they read back, so no initial contents are needed."""
     key = (device.index, torch.cuda.current_stream(device).cuda_stream)
     buf = _WORKSPACES.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _WORKSPACES[key] = buf
     return buf
 

@@ -743,6 +743,16 @@ extern "C" size_t spa_decode_workspace_size(int batch, int q_heads, int kv_heads
   return static_cast<size_t>(batch) * q_heads * slots * (head_dim + 1) * sizeof(float);
 }
 
+extern "C" int spa_decode_plan(int batch, int q_heads, int kv_heads, int max_candidates, int* nsplit,
+                               int* cluster_merge) {
+  if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || max_candidates < 0 || !nsplit || !cluster_merge)
+    return SPA_ERR_INVALID;
+  const spa::SplitPlan plan = spa::decode_plan(batch, q_heads, kv_heads, max_candidates);
+  *nsplit = plan.nsplit;
+  *cluster_merge = plan.cluster ? 1 : 0;
+  return SPA_OK;
+}
+
 namespace spa {
 int paged_decode_impl(const void* q, int dtype, int batch, int q_heads, int kv_heads, int head_dim,
                       const spa_kv_layout* kv, const int32_t* context_lens, int local_window, const int64_t* selected,

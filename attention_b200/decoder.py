@@ -97,7 +97,9 @@ class SparseDecoder:
         self.page_table = torch.arange(n_pool, dtype=torch.int32, device=self.device).view(batch, cfg.max_pages)
         self.ctx = 0
         self.summaries: list[torch.Tensor | None] = [None] * cfg.layers
+        self._summary_store: dict[int, torch.Tensor] = {}
         self.n_routable = 0
+        self.prompt_len = 0
         self.promotion = PromotionCache(cfg.layers * batch, slots=cfg.promo_slots, ttl=cfg.promo_ttl,
                                         device=self.device)
         self.step_index = 0
@@ -114,12 +116,25 @@ class SparseDecoder:
         return max(0, (ctx - self.cfg.local_window) // self.cfg.page_size)
 
     def _refresh_summaries(self, n: int):
-        """Summaries of pages [0, n) of every layer (recomputed when n grows: a page becomes
-        routable once all its tokens are older than the local window)."""
+        """Summaries of pages [0, n) of every layer (recomputed when n changes: a page becomes
+        routable once all its tokens are older than the local window).  They live at a fixed
+        address per layer, so a step graph captured for n pages reads current summaries
+        whenever it is replayed, after a rewind included."""
         self.n_routable = n
         for i in range(self.cfg.layers):
-            self.summaries[i] = (page_summaries(self.k_pool[i], block_size=self.cfg.page_size, n_pages=n,
-                                                page_table=self.page_table) if n > 0 else None)
+            if n <= 0:
+                self.summaries[i] = None
+                continue
+            fresh = page_summaries(self.k_pool[i], block_size=self.cfg.page_size, n_pages=n,
+                                   page_table=self.page_table)
+            store = self._summary_store.get(i)
+            if store is None:
+                store = torch.empty(self.batch * self.cfg.heads * self.cfg.max_pages * self.cfg.head_dim,
+                                    dtype=fresh.dtype, device=self.device)
+                self._summary_store[i] = store
+            view = store[: fresh.numel()].view(fresh.shape)
+            view.copy_(fresh)
+            self.summaries[i] = view
 
     # ---------------------------------------------------------------- prefill
     @torch.no_grad()
@@ -146,6 +161,7 @@ class SparseDecoder:
             x = x + self._linear(att.transpose(1, 2).reshape(b, s, cfg.d_model), f"l{i}.out")
             x = x + self._mlp(x, i)
         self.ctx = s
+        self.prompt_len = s
         self._refresh_summaries(self._routable_pages(s + 1))
         return F.linear(rms_norm(x[:, -1], self.w["norm_f"], cfg.eps), self.w["head"]).float()
 
@@ -194,6 +210,20 @@ class SparseDecoder:
         self._step_dev.add_(1)
         return sel_all
 
+    def _check_room(self, steps: int) -> None:
+        if self.ctx + steps > self.cfg.max_context:
+            raise ValueError(f"decoding {steps} more tokens from position {self.ctx} exceeds max_context "
+                             f"{self.cfg.max_context}")
+
+    def rewind(self, ctx: int) -> None:
+        """Moves the decode position back to ``ctx`` (between the prompt length and the
+        current position), as after rejected speculative tokens: later steps overwrite the
+        K/V from there.  The promotion table and the step counter are kept."""
+        if not getattr(self, "prompt_len", None) or not self.prompt_len <= ctx <= self.ctx:
+            raise ValueError("rewind target must lie between the prompt length and the current position")
+        self.ctx = ctx
+        self._begin_step()
+
     def _begin_step(self):
         """Host bookkeeping before a step: refresh summaries when a page becomes routable."""
         n_routable = self._routable_pages(self.ctx + 1)
@@ -203,6 +233,7 @@ class SparseDecoder:
     @torch.no_grad()
     def decode_step(self, token: torch.Tensor):
         """token [B] at position ctx -> (logits [B, vocab] fp32, selected [layers, B, m])."""
+        self._check_room(1)
         self._state()
         if self.step_index == 0 or self._position[0].item() != self.ctx:
             self._position.fill_(self.ctx)
@@ -220,6 +251,7 @@ class SparseDecoder:
         """Greedy decode of ``steps`` tokens starting from ``token`` [B]; returns the
         tokens [steps, B].  With ``graphed`` every step is one CUDA-graph replay (a new
         graph is captured only when the number of routable pages changes)."""
+        self._check_room(steps)
         self._state()
         self._token.copy_(token)
         self._position.fill_(self.ctx)

@@ -404,8 +404,16 @@ def run_ours(args, world, rank, local):
     if not args.skip_integrated:
         integrated = run_integrated(args, dev)
 
-    launches_per_step = 2 + (1 if spa._lib.lib.spa_decode_workspace_size(
-        cfg.batch, cfg.q_heads, cfg.kv_heads, cfg.head_dim, cfg.local_window + cfg.top_m * cfg.page_size) else 0)
+    dense = None
+    if not args.skip_dense:
+        dense = run_dense(args, world, rank, dev, peaks)
+
+    # kernels per step: the router, then the decode (plus a merge kernel when its splits
+    # do not merge on chip)
+    nsplit, on_chip = spa._lib.decode_plan(cfg.batch, cfg.q_heads, cfg.kv_heads,
+                                           cfg.local_window + cfg.top_m * cfg.page_size)
+    decode_kernels = "decode_mma_kernel" if (nsplit == 1 or on_chip) else "decode_mma_kernel + decode_combine_kernel"
+    launches_per_step = 2 + (0 if (nsplit == 1 or on_chip) else 1)
     result = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -428,7 +436,9 @@ def run_ours(args, world, rank, local):
                    "l2": f"inputs larger than L2: {groups} rotating batches, {groups * bytes_step / 1e6:.0f} MB "
                          "re-read footprint vs 126 MB L2",
                    "parallelism": f"replicas x{world} (no collective)", "graph": "CUDA graph replay"},
-        "roofline": {"bound": "hbm", "kernel": "decode_mma_kernel + decode_combine_kernel",
+        "roofline": {"bound": "hbm", "kernel": decode_kernels,
+                     "split_plan": f"{nsplit} splits per (sequence, kv head)"
+                                   + (", merged on chip in a cluster" if on_chip and nsplit > 1 else ""),
                      "achieved": round(att_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(att_gbs / hbm_peak, 4), "traffic": traffic,
                      "peak_source": f"{peaks_src} (MEASURED_PEAKS.json hbm_gbs)" if peaks_src == "measured"
@@ -437,6 +447,7 @@ def run_ours(args, world, rank, local):
         "e2e": e2e,
         "cpu_baseline": cpu,
         "prefill": prefill,
+        "dense_decode": dense,
         "integrated_decode": integrated,
         "clocks": clocks.summary(),
         "gpu_launches": steps * launches_per_step,
@@ -502,6 +513,69 @@ def run_prefill(args, world, rank, dev, peaks):
             "periodic_router": "block 256, stride 256, top-4, summaries included" if router_ms is not None else None}
 
 
+def run_dense(args, world, rank, dev, peaks):
+    """Dense paged decode at 32k: B8, Hq32/Hkv8, D128, bf16, 256 pages of 128 tokens per
+    sequence in a 4096-page pool behind a random page table.  A step appends one token per
+    (sequence, kv head) in place (the last position, so the context stays 32k) and attends
+    over the whole context; the 2.1 GB pool is far larger than L2."""
+    import attention_b200 as spa
+    from attention_b200 import workloads
+
+    cfg = workloads.DenseDecodeConfig()
+    wl = workloads.dense_decode_workload(cfg, seed=11 + rank, device=dev)
+    q, kp, vp, table, lens = (wl[n] for n in ("query", "k_pool", "v_pool", "page_table", "context_lens"))
+    g = torch.Generator(device=dev).manual_seed(12 + rank)
+    k_new = (torch.randn(cfg.batch, cfg.kv_heads, cfg.head_dim, generator=g, device=dev) * 0.5).to(cfg.dtype)
+    v_new = (torch.randn(cfg.batch, cfg.kv_heads, cfg.head_dim, generator=g, device=dev) * 0.5).to(cfg.dtype)
+    pos = (lens - 1).contiguous()
+
+    def step():
+        spa.kv_append(kp, vp, table, k_new, v_new, pos)
+        return spa.paged_decode_attention(q, kp, vp, page_table=table, context_lens=lens)
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):  # warm-up on the capture stream: its workspace exists before capture
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        step()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    reps = args.dense_steps
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
+    kv_bytes = 2 * cfg.batch * cfg.kv_heads * cfg.context * cfg.head_dim * 2
+    io_bytes = 2 * cfg.batch * cfg.q_heads * cfg.head_dim * 2 + cfg.batch * cfg.pages_per_seq * 4
+    append_bytes = 2 * 2 * cfg.batch * cfg.kv_heads * cfg.head_dim * 2
+    step_bytes = kv_bytes + io_bytes + append_bytes
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    nsplit, on_chip = spa._lib.decode_plan(cfg.batch, cfg.q_heads, cfg.kv_heads, cfg.context)
+    del wl, kp, vp, graph
+    torch.cuda.empty_cache()
+    return {"workload": f"dense paged decode 32k: B{cfg.batch} Hq{cfg.q_heads}/Hkv{cfg.kv_heads} D{cfg.head_dim} "
+                        f"bf16, {cfg.pages_per_seq} pages x {cfg.page_size} in a {cfg.pool_pages}-page pool, "
+                        "one appended token per step",
+            "us_per_step": round(ms * 1e3, 2), "bytes_per_step": step_bytes,
+            "value": round(gbs * world, 1), "unit": "GB/s (all GPUs)", "frac": round(gbs / peak, 4),
+            "peak": peak, "peak_source": "MEASURED_PEAKS.json hbm_gbs",
+            "kernels": "kv_append_kernel + decode_mma_kernel" + ("" if (nsplit == 1 or on_chip) else " + decode_combine_kernel"),
+            "split_plan": f"{nsplit} splits per (sequence, kv head)" + (", merged on chip" if on_chip and nsplit > 1 else ""),
+            "steps": reps, "graph": "CUDA graph replay"}
+
+
 def run_integrated(args, dev):
     """Integrated 4-layer decoder (d_model 512, 8 heads, vocab 4096, bf16): a 16k-token
     prompt prefilled into 128-token pages, then greedy decode steps with router top-8 +
@@ -524,7 +598,10 @@ def run_integrated(args, dev):
     torch.cuda.synchronize()
     prefill_ms = e0.elapsed_time(e1)
     tok = logits.argmax(-1)
-    tok = dec.generate(tok, steps)[-1]  # captures the step graphs (one per routable-page count)
+    # untimed pass: captures the step graphs of these positions (one per routable-page
+    # count); then the same positions again, timed, as pure graph replays
+    dec.generate(tok, steps)
+    dec.rewind(dec.prompt_len)
     torch.cuda.synchronize()
     e0.record()
     dec.generate(tok, steps)
@@ -535,7 +612,8 @@ def run_integrated(args, dev):
             "prefill_ms": round(prefill_ms, 3), "decode_steps": steps,
             "decode_us_per_step": round(e0.elapsed_time(e1) * 1e3 / steps, 2),
             "mode": "one CUDA-graph replay per step (cuBLAS GEMMs + library kernels), greedy tokens on the "
-                    "device; steps 257-512 after the prompt"}
+                    f"device; the first {steps} positions after the prompt, decoded once untimed (graph "
+                    "captures) and again timed after a rewind"}
 
 
 # ------------------------------------------------------------------ reference arm
@@ -589,6 +667,8 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-integrated", action="store_true")
+    ap.add_argument("--skip-dense", action="store_true")
+    ap.add_argument("--dense-steps", type=int, default=200)
     ap.add_argument("--integrated-steps", type=int, default=256)
     args = ap.parse_args()
     world, rank, local = init_dist()

@@ -151,12 +151,24 @@ int spa_periodic_router(const void* q, int q_dtype, int batch, int heads,
  */
 size_t spa_decode_workspace_size(int batch, int q_heads, int kv_heads,
                                  int head_dim, int max_candidates);
+
 int spa_paged_decode(const void* q, int dtype, int batch, int q_heads,
                      int kv_heads, int head_dim, const spa_kv_layout* kv,
                      const int32_t* context_lens, int local_window,
                      const int64_t* selected, int top_m, int max_candidates,
                      double scale, void* out, void* workspace,
                      size_t workspace_bytes, spa_stream_t stream);
+
+/*
+ * Split plan of the tensor-core decode for this shape on the current device:
+ * *nsplit CTAs per (sequence, kv head); *cluster_merge = 1 when they form one
+ * thread-block cluster and merge on chip (one kernel launch), 0 when partials go
+ * to the workspace and a merge kernel follows (two launches; one when nsplit = 1).
+ * No reference counterpart (the reference's Triton launch has one program per
+ * (batch, head), triton_paged_attention.py:74-80).
+ */
+int spa_decode_plan(int batch, int q_heads, int kv_heads, int max_candidates,
+                    int* nsplit, int* cluster_merge);
 
 /*
  * Span gather decode: as spa_paged_decode with selected pages, but the candidates

@@ -75,3 +75,33 @@ def test_graphed_generation_equals_eager():
     assert torch.equal(a.promotion.pages, b.promotion.pages)
     assert torch.equal(a.promotion.last_hit, b.promotion.last_hit)
     assert len(b._graphs) >= 2  # a page became routable during the run
+
+
+def test_rewind_replays_cached_graphs_with_current_summaries():
+    """After rewind() to the prompt end, generate() replays the graphs captured on the first
+    pass (no new captures) and reproduces its tokens: the summaries a replayed graph reads
+    are the current ones, not those of the capture."""
+    cfg = DecoderConfig(vocab=512, d_model=128, heads=4, layers=2, page_size=128, local_window=128, top_m=4,
+                        promo_slots=8, promo_ttl=5, max_context=1024 + 300)
+    w = init_weights(cfg, seed=7)
+    prompt = torch.randint(0, cfg.vocab, (2, 1024), generator=torch.Generator().manual_seed(8)).cuda()
+    dec = SparseDecoder(cfg, w, 2)
+    tok = dec.prefill(prompt).argmax(-1)
+    first = dec.generate(tok, 280)
+    n_graphs = len(dec._graphs)
+    assert n_graphs >= 3
+    dec.rewind(dec.prompt_len)
+    second = dec.generate(tok, 280)
+    assert len(dec._graphs) == n_graphs
+    assert torch.equal(first, second)
+
+
+def test_generation_past_max_context_is_rejected():
+    cfg = DecoderConfig(vocab=256, d_model=64, heads=2, layers=1, page_size=128, local_window=128, top_m=2,
+                        promo_slots=4, promo_ttl=3, max_context=256 + 8)
+    dec = SparseDecoder(cfg, init_weights(cfg, seed=1), 1)
+    tok = dec.prefill(torch.randint(0, cfg.vocab, (1, 256), generator=torch.Generator().manual_seed(2)).cuda())
+    with pytest.raises(ValueError):
+        dec.generate(tok.argmax(-1), 9)
+    with pytest.raises(ValueError):
+        dec.rewind(dec.prompt_len + 1)
