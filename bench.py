@@ -315,7 +315,7 @@ def run_ours(args, world, rank, local):
     barrier(world)
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local) as clocks, torch.cuda.nvtx.range("sparse_step"):
         ev0.record()
         for _ in range(full):
             g_all.replay()
@@ -333,11 +333,12 @@ def run_ours(args, world, rank, local):
     att_reps = max(1, min(200, steps // groups + 1))
     ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
-    ea.record()
-    for _ in range(att_reps):
-        g_att.replay()
-    eb.record()
-    torch.cuda.synchronize()
+    with torch.cuda.nvtx.range("decode_roofline"):
+        ea.record()
+        for _ in range(att_reps):
+            g_att.replay()
+        eb.record()
+        torch.cuda.synchronize()
     att_us = ea.elapsed_time(eb) * 1e3 / (att_reps * groups)
     es = 2
     att_bytes = (2 * cfg.batch * cfg.kv_heads * (cfg.local_window + cfg.top_m * cfg.page_size) * cfg.head_dim * es
@@ -482,11 +483,12 @@ def run_prefill(args, world, rank, dev, peaks):
     reps = args.prefill_reps
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        run()
-    e1.record()
-    torch.cuda.synchronize()
+    with torch.cuda.nvtx.range("prefill"):
+        e0.record()
+        for _ in range(reps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
     # periodic causal router over the same chunk (reference: prefill + router overhead benchmark)
@@ -507,6 +509,8 @@ def run_prefill(args, world, rank, dev, peaks):
     return {"seq_len": seq, "window": window, "heads": heads, "head_dim": dim, "ms": round(ms, 4),
             "tflops": round(tf, 1), "peak_tflops": peak * world, "frac": round(tf / (peak * world), 4),
             "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst) x GPUs",
+            "traffic_16k": read_profile_traffic("local_prefill_tc_16k_ncu.md"),
+            "traffic_source": "profiles/local_prefill_tc_16k_ncu.md (dram read+write of one S=16384 launch)",
             "flops": flops, "sharding": f"{world} contiguous chunks, 2048-token K/V halo over NCCL" if world > 1
             else "single GPU", "reps": reps,
             "periodic_router_ms": round(router_ms, 4) if router_ms is not None else None,
@@ -549,11 +553,12 @@ def run_dense(args, world, rank, dev, peaks):
     reps = args.dense_steps
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize()
+    with torch.cuda.nvtx.range("dense_decode"):
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
     kv_bytes = 2 * cfg.batch * cfg.kv_heads * cfg.context * cfg.head_dim * 2
@@ -571,6 +576,8 @@ def run_dense(args, world, rank, dev, peaks):
             "us_per_step": round(ms * 1e3, 2), "bytes_per_step": step_bytes,
             "value": round(gbs * world, 1), "unit": "GB/s (all GPUs)", "frac": round(gbs / peak, 4),
             "peak": peak, "peak_source": "MEASURED_PEAKS.json hbm_gbs",
+            "traffic": read_profile_traffic("dense_decode_32k_ncu.md"),
+            "traffic_source": "profiles/dense_decode_32k_ncu.md (dram read+write per decode launch)",
             "kernels": "kv_append_kernel + decode_mma_kernel" + ("" if (nsplit == 1 or on_chip) else " + decode_combine_kernel"),
             "split_plan": f"{nsplit} splits per (sequence, kv head)" + (", merged on chip" if on_chip and nsplit > 1 else ""),
             "steps": reps, "graph": "CUDA graph replay"}
