@@ -7,6 +7,7 @@ Drop-in replacements for the reference's decode / prefill / router entry points
 
 from ._lib import LIB_PATH, SpaError, device_error_flags
 from .cache import PagedKVCache, PromotionCache, kv_append
+from .gate import RefreshGate
 from .paged_attention import paged_decode_attention, paged_gather_decode_attention, span_gather_decode_attention
 from .prefill import local_causal_prefill
 from .router import page_summaries, periodic_router, select_blocks, select_blocks_tree
@@ -18,6 +19,7 @@ __all__ = [
     "device_error_flags",
     "PagedKVCache",
     "PromotionCache",
+    "RefreshGate",
     "kv_append",
     "paged_decode_attention",
     "paged_gather_decode_attention",

@@ -44,6 +44,19 @@ _vp, _i, _i64, _d, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c
 _KV = ctypes.POINTER(KvLayout)
 
 # name -> (restype, argtypes); keep in the order of include/spa_b200.h
+class RefreshGateArgs(ctypes.Structure):
+    """spa_refresh_gate_args (include/spa_b200.h)."""
+
+    _fields_ = [("mode", ctypes.c_int), ("batch", ctypes.c_int), ("ttl", ctypes.c_int), ("step", ctypes.c_int),
+                ("step_dev", ctypes.c_void_p), ("signature", ctypes.c_void_p), ("cached_signature", ctypes.c_void_p),
+                ("sig_len", ctypes.c_int), ("state", ctypes.c_void_p), ("cached_state", ctypes.c_void_p),
+                ("width", ctypes.c_int), ("w1", ctypes.c_void_p), ("b1", ctypes.c_void_p), ("w2", ctypes.c_void_p),
+                ("b2", ctypes.c_void_p), ("hidden", ctypes.c_int), ("threshold", ctypes.c_float),
+                ("gate", ctypes.c_void_p), ("score_out", ctypes.c_void_p)]
+
+
+GATE_TTL, GATE_SIGNATURE, GATE_DRIFT, GATE_LEARNED = 0, 1, 2, 3
+
 PROTOTYPES = {
     "spa_version": (ctypes.c_char_p, []),
     "spa_device_error": (_i, [ctypes.POINTER(ctypes.c_uint32)]),
@@ -52,6 +65,10 @@ PROTOTYPES = {
     "spa_summaries_build": (_i, [_KV, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp]),
     "spa_router_topm": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _d, _i, _vp, _vp, _vp]),
     "spa_router_tree_topm": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _vp, _i, _i, _i, _d, _i, _vp, _vp]),
+    "spa_router_topm_gated": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _d, _i, _vp, _vp, _vp, _vp]),
+    "spa_router_tree_topm_gated": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _vp, _i, _i, _i, _d, _i, _vp, _vp, _vp,
+                                        _vp]),
+    "spa_refresh_gate": (_i, [ctypes.POINTER(RefreshGateArgs), _vp]),
     "spa_periodic_router": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _i, _i, _i, _vp, _vp]),
     "spa_decode_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "spa_decode_plan": (_i, [_i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
@@ -59,6 +76,8 @@ PROTOTYPES = {
     "spa_span_gather_decode": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp, _sz, _vp]),
     "spa_sparse_decode_step": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _d, _d, _vp,
                                     _vp, _vp, _sz, _vp]),
+    "spa_sparse_decode_step_gated": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _d,
+                                          _d, _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
     "spa_paged_decode_noalloc": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp]),
     "spa_kv_append": (_i, [_KV, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "spa_local_prefill": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),

@@ -158,6 +158,10 @@ struct RouterArgs {
   float scale;
   int64_t* selected;  // [B, top_m]
   float* scores_out;  // [B, n_pages] (single-level mode) or nullptr
+  // promotion refresh gate or nullptr: gate[0] = refresh decision of this step,
+  // gate[1] = a selection has been promoted; promoted [B, top_m] holds it
+  int32_t* gate = nullptr;
+  int64_t* promoted = nullptr;
 };
 
 // qg (fp32, [Hkv][D]) for batch row b, summed over each kv head's query heads in
@@ -311,6 +315,15 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
   pdl_launch_dependents();
   const int b = blockIdx.y;
   const uint32_t rank = cluster_rank();
+  if (a.gate && a.gate[0] == 0 && a.gate[1] != 0) {
+    // promotion reuse: the refresh gate is closed, so the promoted pages are this step's
+    // selection and no summary is read.  The flags are the same for every CTA, so whole
+    // clusters leave here together, before any cluster barrier.
+    if (rank == 0)
+      for (int j = threadIdx.x; j < a.top_m; j += blockDim.x)
+        a.selected[static_cast<int64_t>(b) * a.top_m + j] = a.promoted[static_cast<int64_t>(b) * a.top_m + j];
+    return;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kRouterThreads / 32;
   // first level's rows (the warp's first owned candidate, first kv-head batch) are
   // requested before the query row so both loads are in flight together
@@ -424,6 +437,13 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
     if (rank == 0)
       select_top(all_score, all_id, n_cand, a.top_m, a.selected + static_cast<int64_t>(b) * a.top_m, red_s, red_i,
                  &chosen_pos);
+  }
+  if (a.gate && rank == 0) {
+    // a routed step becomes the promoted selection
+    __syncthreads();
+    for (int j = threadIdx.x; j < a.top_m; j += blockDim.x)
+      a.promoted[static_cast<int64_t>(b) * a.top_m + j] = a.selected[static_cast<int64_t>(b) * a.top_m + j];
+    if (threadIdx.x == 0) a.gate[1] = 1;
   }
 }
 
@@ -547,9 +567,11 @@ int router_common_checks(const void* q, int q_dtype, int batch, int q_heads, int
 }
 }  // namespace
 
-extern "C" int spa_router_topm(const void* q, int q_dtype, int batch, int q_heads, int kv_heads, int head_dim,
-                               const float* summaries, int n_pages, double scale, int top_m, int64_t* selected,
-                               float* scores_out, spa_stream_t stream) {
+namespace spa {
+int router_topm_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_heads, int head_dim,
+                     const float* summaries, int n_pages, double scale, int top_m, int64_t* selected,
+                     float* scores_out, int32_t* gate, int64_t* promoted, spa_stream_t stream) {
+  if ((gate == nullptr) != (promoted == nullptr)) return SPA_ERR_INVALID;
   int rc = router_common_checks(q, q_dtype, batch, q_heads, kv_heads, head_dim);
   if (rc) return rc;
   if (!summaries || !selected || n_pages <= 0 || top_m <= 0 || top_m > n_pages) return SPA_ERR_INVALID;
@@ -570,16 +592,19 @@ extern "C" int spa_router_topm(const void* q, int q_dtype, int batch, int q_head
   a.scale = static_cast<float>(scale);
   a.selected = selected;
   a.scores_out = scores_out;
+  a.gate = gate;
+  a.promoted = promoted;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (q_dtype == SPA_F32) return spa::launch_router<float>(a, batch, st);
   if (q_dtype == SPA_F16) return spa::launch_router<__half>(a, batch, st);
   return spa::launch_router<__nv_bfloat16>(a, batch, st);
 }
 
-extern "C" int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q_heads, int kv_heads,
-                                    int head_dim, const float* super_summaries, int n_super,
-                                    const float* summaries, int n_pages, int superblock, int top_super,
-                                    double scale, int top_m, int64_t* selected, spa_stream_t stream) {
+int router_tree_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_heads, int head_dim,
+                     const float* super_summaries, int n_super, const float* summaries, int n_pages, int superblock,
+                     int top_super, double scale, int top_m, int64_t* selected, int32_t* gate, int64_t* promoted,
+                     spa_stream_t stream) {
+  if ((gate == nullptr) != (promoted == nullptr)) return SPA_ERR_INVALID;
   int rc = router_common_checks(q, q_dtype, batch, q_heads, kv_heads, head_dim);
   if (rc) return rc;
   if (!super_summaries || !summaries || !selected || n_pages <= 0 || superblock <= 0) return SPA_ERR_INVALID;
@@ -606,10 +631,46 @@ extern "C" int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q
   a.scale = static_cast<float>(scale);
   a.selected = selected;
   a.scores_out = nullptr;
+  a.gate = gate;
+  a.promoted = promoted;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (q_dtype == SPA_F32) return spa::launch_router<float>(a, batch, st);
   if (q_dtype == SPA_F16) return spa::launch_router<__half>(a, batch, st);
   return spa::launch_router<__nv_bfloat16>(a, batch, st);
+}
+}  // namespace spa
+
+extern "C" int spa_router_topm(const void* q, int q_dtype, int batch, int q_heads, int kv_heads, int head_dim,
+                               const float* summaries, int n_pages, double scale, int top_m, int64_t* selected,
+                               float* scores_out, spa_stream_t stream) {
+  return spa::router_topm_impl(q, q_dtype, batch, q_heads, kv_heads, head_dim, summaries, n_pages, scale, top_m,
+                               selected, scores_out, nullptr, nullptr, stream);
+}
+
+extern "C" int spa_router_topm_gated(const void* q, int q_dtype, int batch, int q_heads, int kv_heads, int head_dim,
+                                     const float* summaries, int n_pages, double scale, int top_m, int64_t* selected,
+                                     int32_t* gate, int64_t* promoted, spa_stream_t stream) {
+  if (!gate || !promoted) return SPA_ERR_INVALID;
+  return spa::router_topm_impl(q, q_dtype, batch, q_heads, kv_heads, head_dim, summaries, n_pages, scale, top_m,
+                               selected, nullptr, gate, promoted, stream);
+}
+
+extern "C" int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q_heads, int kv_heads,
+                                    int head_dim, const float* super_summaries, int n_super,
+                                    const float* summaries, int n_pages, int superblock, int top_super,
+                                    double scale, int top_m, int64_t* selected, spa_stream_t stream) {
+  return spa::router_tree_impl(q, q_dtype, batch, q_heads, kv_heads, head_dim, super_summaries, n_super, summaries,
+                               n_pages, superblock, top_super, scale, top_m, selected, nullptr, nullptr, stream);
+}
+
+extern "C" int spa_router_tree_topm_gated(const void* q, int q_dtype, int batch, int q_heads, int kv_heads,
+                                          int head_dim, const float* super_summaries, int n_super,
+                                          const float* summaries, int n_pages, int superblock, int top_super,
+                                          double scale, int top_m, int64_t* selected, int32_t* gate,
+                                          int64_t* promoted, spa_stream_t stream) {
+  if (!gate || !promoted) return SPA_ERR_INVALID;
+  return spa::router_tree_impl(q, q_dtype, batch, q_heads, kv_heads, head_dim, super_summaries, n_super, summaries,
+                               n_pages, superblock, top_super, scale, top_m, selected, gate, promoted, stream);
 }
 
 extern "C" int spa_periodic_router(const void* q, int q_dtype, int batch, int heads, int seq_len, int head_dim,

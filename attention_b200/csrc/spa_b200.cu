@@ -6,6 +6,7 @@
 #include "decode.cuh"
 #include "decode_noalloc.cuh"
 #include "step.cuh"
+#include "gate.cuh"
 #include "cache.cuh"
 #include "prefill_generic.cuh"
 #include "prefill_sm100.cuh"

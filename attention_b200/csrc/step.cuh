@@ -10,22 +10,23 @@
 #include "decode.cuh"
 #include "router.cuh"
 
-extern "C" int spa_sparse_decode_step(const void* q, int dtype, int batch, int q_heads, int kv_heads, int head_dim,
-                                      const spa_kv_layout* kv, const int32_t* context_lens, int local_window,
-                                      const float* super_summaries, int n_super, const float* summaries,
-                                      int n_pages, int superblock, int top_super, int top_m, double router_scale,
-                                      double attn_scale, int64_t* selected, void* out, void* workspace,
-                                      size_t workspace_bytes, spa_stream_t stream) {
+namespace spa {
+int sparse_step_impl(const void* q, int dtype, int batch, int q_heads, int kv_heads, int head_dim,
+                     const spa_kv_layout* kv, const int32_t* context_lens, int local_window,
+                     const float* super_summaries, int n_super, const float* summaries, int n_pages, int superblock,
+                     int top_super, int top_m, double router_scale, double attn_scale, int64_t* selected, void* out,
+                     void* workspace, size_t workspace_bytes, int32_t* gate, int64_t* promoted,
+                     spa_stream_t stream) {
   if (!q || !out || !kv || !kv->k || !kv->v || !context_lens || !summaries || !selected) return SPA_ERR_INVALID;
   if (dtype != SPA_F16 && dtype != SPA_BF16 && dtype != SPA_F32) return SPA_ERR_INVALID;
   if (local_window < 0 || top_m <= 0) return SPA_ERR_INVALID;
   int rc;
   if (super_summaries)
-    rc = spa_router_tree_topm(q, dtype, batch, q_heads, kv_heads, head_dim, super_summaries, n_super, summaries,
-                              n_pages, superblock, top_super, router_scale, top_m, selected, stream);
+    rc = router_tree_impl(q, dtype, batch, q_heads, kv_heads, head_dim, super_summaries, n_super, summaries, n_pages,
+                          superblock, top_super, router_scale, top_m, selected, gate, promoted, stream);
   else
-    rc = spa_router_topm(q, dtype, batch, q_heads, kv_heads, head_dim, summaries, n_pages, router_scale, top_m,
-                         selected, nullptr, stream);
+    rc = router_topm_impl(q, dtype, batch, q_heads, kv_heads, head_dim, summaries, n_pages, router_scale, top_m,
+                          selected, nullptr, gate, promoted, stream);
   if (rc) return rc;
   spa::DecodeArgs a;
   a.q = q;
@@ -70,4 +71,31 @@ extern "C" int spa_sparse_decode_step(const void* q, int dtype, int batch, int q
     default:
       return spa::launch_decode<__nv_bfloat16>(*kv, dtype, a, fast, st);
   }
+}
+}  // namespace spa
+
+extern "C" int spa_sparse_decode_step(const void* q, int dtype, int batch, int q_heads, int kv_heads, int head_dim,
+                                      const spa_kv_layout* kv, const int32_t* context_lens, int local_window,
+                                      const float* super_summaries, int n_super, const float* summaries,
+                                      int n_pages, int superblock, int top_super, int top_m, double router_scale,
+                                      double attn_scale, int64_t* selected, void* out, void* workspace,
+                                      size_t workspace_bytes, spa_stream_t stream) {
+  return spa::sparse_step_impl(q, dtype, batch, q_heads, kv_heads, head_dim, kv, context_lens, local_window,
+                               super_summaries, n_super, summaries, n_pages, superblock, top_super, top_m,
+                               router_scale, attn_scale, selected, out, workspace, workspace_bytes, nullptr, nullptr,
+                               stream);
+}
+
+extern "C" int spa_sparse_decode_step_gated(const void* q, int dtype, int batch, int q_heads, int kv_heads,
+                                            int head_dim, const spa_kv_layout* kv, const int32_t* context_lens,
+                                            int local_window, const float* super_summaries, int n_super,
+                                            const float* summaries, int n_pages, int superblock, int top_super,
+                                            int top_m, double router_scale, double attn_scale, int64_t* selected,
+                                            void* out, void* workspace, size_t workspace_bytes, int32_t* gate,
+                                            int64_t* promoted, spa_stream_t stream) {
+  if (!gate || !promoted) return SPA_ERR_INVALID;
+  return spa::sparse_step_impl(q, dtype, batch, q_heads, kv_heads, head_dim, kv, context_lens, local_window,
+                               super_summaries, n_super, summaries, n_pages, superblock, top_super, top_m,
+                               router_scale, attn_scale, selected, out, workspace, workspace_bytes, gate, promoted,
+                               stream);
 }

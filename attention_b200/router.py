@@ -83,15 +83,25 @@ def _router_args(query: torch.Tensor, summaries: torch.Tensor):
 
 
 def select_blocks(query: torch.Tensor, summaries: torch.Tensor, top_blocks: int, *, scale: float = 1.0,
-                  return_scores: bool = False):
+                  return_scores: bool = False, gate=None):
     """Top ``top_blocks`` pages per batch row, int64 ``[B, m]`` by descending score
-    (ties to the lower page index)."""
+    (ties to the lower page index).  With ``gate`` (a ``RefreshGate`` whose ``decide``
+    ran for this step) a closed gate reuses the promoted pages without routing."""
     q, s = _router_args(query, summaries)
     b, hq, d = q.shape
     hkv, n_pages = s.size(1), s.size(2)
     if not 0 < top_blocks <= n_pages:
         raise ValueError("top_blocks must be in [1, pages]")
     out = torch.empty(b, top_blocks, dtype=torch.int64, device=q.device)
+    if gate is not None:
+        if return_scores:
+            raise ValueError("return_scores is not available with a refresh gate")
+        promoted = gate.promoted_for(b, top_blocks)
+        rc = _lib.lib.spa_router_topm_gated(q.data_ptr(), dtype_code(q), b, hq, hkv, d, s.data_ptr(), n_pages,
+                                            float(scale), top_blocks, out.data_ptr(), gate.flags.data_ptr(),
+                                            promoted.data_ptr(), stream_ptr(q.device))
+        _lib.check(rc, "spa_router_topm_gated")
+        return out
     scores = torch.empty(b, n_pages, dtype=torch.float32, device=q.device) if return_scores else None
     rc = _lib.lib.spa_router_topm(q.data_ptr(), dtype_code(q), b, hq, hkv, d, s.data_ptr(), n_pages, float(scale),
                                   top_blocks, out.data_ptr(), scores.data_ptr() if scores is not None else None,
@@ -101,9 +111,11 @@ def select_blocks(query: torch.Tensor, summaries: torch.Tensor, top_blocks: int,
 
 
 def select_blocks_tree(query: torch.Tensor, super_summaries: torch.Tensor, summaries: torch.Tensor, *,
-                       superblock: int, top_super: int, top_blocks: int, scale: float = 1.0) -> torch.Tensor:
+                       superblock: int, top_super: int, top_blocks: int, scale: float = 1.0,
+                       gate=None) -> torch.Tensor:
     """Two-level router: top ``top_super`` superblocks, then the top ``top_blocks``
-    pages inside them.  int64 ``[B, m]`` by descending page score."""
+    pages inside them.  int64 ``[B, m]`` by descending page score.  ``gate`` as in
+    ``select_blocks``."""
     q, s = _router_args(query, summaries)
     _, sup = _router_args(query, super_summaries)
     b, hq, d = q.shape
@@ -111,6 +123,14 @@ def select_blocks_tree(query: torch.Tensor, super_summaries: torch.Tensor, summa
     if sup.size(1) != hkv or n_super != -(-n_pages // superblock):
         raise ValueError("super_summaries must be [B, Hkv, ceil(pages/superblock), D]")
     out = torch.empty(b, top_blocks, dtype=torch.int64, device=q.device)
+    if gate is not None:
+        promoted = gate.promoted_for(b, top_blocks)
+        rc = _lib.lib.spa_router_tree_topm_gated(q.data_ptr(), dtype_code(q), b, hq, hkv, d, sup.data_ptr(), n_super,
+                                                 s.data_ptr(), n_pages, superblock, top_super, float(scale),
+                                                 top_blocks, out.data_ptr(), gate.flags.data_ptr(),
+                                                 promoted.data_ptr(), stream_ptr(q.device))
+        _lib.check(rc, "spa_router_tree_topm_gated")
+        return out
     rc = _lib.lib.spa_router_tree_topm(q.data_ptr(), dtype_code(q), b, hq, hkv, d, sup.data_ptr(), n_super,
                                        s.data_ptr(), n_pages, superblock, top_super, float(scale), top_blocks,
                                        out.data_ptr(), stream_ptr(q.device))

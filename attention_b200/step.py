@@ -7,6 +7,9 @@ Here the router and the decode are chained kernels on the device: the decode gri
 starts while the router runs and streams the local window before it reads the
 selected page ids.  Returns ``(out, selected)``; both equal what
 ``select_blocks[_tree]`` followed by ``paged_gather_decode_attention`` return.
+With ``gate`` (a ``RefreshGate``), a step whose gate is closed reuses the promoted
+pages and the router reads no summaries (promotion reuse,
+triton_promotion_cache_benchmark.py:53-60).
 """
 
 from __future__ import annotations
@@ -25,7 +28,7 @@ def sparse_decode_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Te
                        super_summaries: torch.Tensor | None = None, superblock: int = 0, top_super: int = 0,
                        router_scale: float = 1.0, page_table: torch.Tensor | None = None,
                        context_lens: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                       selected: torch.Tensor | None = None):
+                       selected: torch.Tensor | None = None, gate=None):
     if not (query.is_cuda and keys.is_cuda and values.is_cuda and summaries.is_cuda):
         raise ValueError("CUDA tensors are required")
     if not (query.is_contiguous() and keys.is_contiguous() and values.is_contiguous()):
@@ -62,10 +65,16 @@ def sparse_decode_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Te
     max_cand = local_window + top_blocks * block_size
     ws_bytes = _lib.lib.spa_decode_workspace_size(batch, q_heads, kv_heads, head_dim, max_cand)
     ws = workspace(dev, ws_bytes) if ws_bytes else None
-    rc = _lib.lib.spa_sparse_decode_step(
-        query.data_ptr(), dtype_code(query), batch, q_heads, kv_heads, head_dim, ctypes.byref(layout), lens.data_ptr(),
-        local_window, sup.data_ptr() if sup is not None else None, sup.size(2) if sup is not None else 0,
-        summ.data_ptr(), summ.size(2), superblock, top_super, top_blocks, float(router_scale), head_dim ** -0.5,
-        selected.data_ptr(), out.data_ptr(), ws.data_ptr() if ws is not None else None, ws_bytes, stream_ptr(dev))
-    _lib.check(rc, "spa_sparse_decode_step")
+    args = (query.data_ptr(), dtype_code(query), batch, q_heads, kv_heads, head_dim, ctypes.byref(layout),
+            lens.data_ptr(), local_window, sup.data_ptr() if sup is not None else None,
+            sup.size(2) if sup is not None else 0, summ.data_ptr(), summ.size(2), superblock, top_super, top_blocks,
+            float(router_scale), head_dim ** -0.5, selected.data_ptr(), out.data_ptr(),
+            ws.data_ptr() if ws is not None else None, ws_bytes)
+    if gate is not None:
+        promoted = gate.promoted_for(batch, top_blocks)
+        rc = _lib.lib.spa_sparse_decode_step_gated(*args, gate.flags.data_ptr(), promoted.data_ptr(), stream_ptr(dev))
+        _lib.check(rc, "spa_sparse_decode_step_gated")
+    else:
+        rc = _lib.lib.spa_sparse_decode_step(*args, stream_ptr(dev))
+        _lib.check(rc, "spa_sparse_decode_step")
     return out, selected

@@ -280,6 +280,77 @@ int spa_promotion_update(int32_t* pages, int32_t* last_hit, int rows,
                          spa_stream_t stream);
 
 /*
+ * Promotion refresh gate (one decision per decode step for the whole batch, on the
+ * device).  Policies of evaluate_promotion_ttl.py:125-139 and train_refresh_head.py:
+ *   SPA_GATE_TTL        refresh when step % ttl == 0 (step from step_dev if non-NULL)
+ *   SPA_GATE_SIGNATURE  refresh when signature [batch, sig_len] (token ids) differs
+ *                       from cached_signature
+ *   SPA_GATE_DRIFT      refresh when mean_b (1 - cos(state[b], cached_state[b])) >
+ *                       threshold (cos as torch.nn.functional.cosine_similarity)
+ *   SPA_GATE_LEARNED    refresh when mean_b sigmoid(head(state[b], cached_state[b])) >=
+ *                       threshold; head = Linear(4*width, hidden) (w1 [hidden, 4*width],
+ *                       b1 [hidden]) -> exact GELU -> Linear(hidden, 1) (w2 [hidden], b2 [1])
+ *                       over [state, cached, |state - cached|, state * cached]
+ * gate[2] (device int32): gate[0] receives the decision (1 = route); gate[1] is nonzero
+ * once a gated router has promoted a selection (zero it to start over: the next step
+ * then always routes).  On refresh, cached_state / cached_signature (when given) take
+ * the current values.  score_out (optional, device float): the batch mean compared with
+ * the threshold.  States are fp32 [batch, width].
+ * Replaces the host-side should_refresh logic of the reference's promotion-reuse loops.
+ */
+enum { SPA_GATE_TTL = 0, SPA_GATE_SIGNATURE = 1, SPA_GATE_DRIFT = 2, SPA_GATE_LEARNED = 3 };
+typedef struct spa_refresh_gate_args {
+  int mode;
+  int batch;
+  int ttl;
+  int step;
+  const int32_t* step_dev;
+  const int64_t* signature;
+  int64_t* cached_signature;
+  int sig_len;
+  const float* state;
+  float* cached_state;
+  int width;
+  const float* w1;
+  const float* b1;
+  const float* w2;
+  const float* b2;
+  int hidden;
+  float threshold;
+  int32_t* gate;
+  float* score_out;
+} spa_refresh_gate_args;
+int spa_refresh_gate(const spa_refresh_gate_args* args, spa_stream_t stream);
+
+/*
+ * Gated routers and step: as spa_router_topm / spa_router_tree_topm /
+ * spa_sparse_decode_step, with promotion reuse.  When gate[0] == 0 and gate[1] != 0 the
+ * router reads no summary and copies promoted [batch, top_m] into selected; otherwise it
+ * routes, then copies selected into promoted and sets gate[1] = 1.  (The reference reuses
+ * promoted ids in place of routing: triton_promotion_cache_benchmark.py:53-60.)
+ */
+int spa_router_topm_gated(const void* q, int q_dtype, int batch, int q_heads,
+                          int kv_heads, int head_dim, const float* summaries,
+                          int n_pages, double scale, int top_m, int64_t* selected,
+                          int32_t* gate, int64_t* promoted, spa_stream_t stream);
+int spa_router_tree_topm_gated(const void* q, int q_dtype, int batch, int q_heads,
+                               int kv_heads, int head_dim,
+                               const float* super_summaries, int n_super,
+                               const float* summaries, int n_pages, int superblock,
+                               int top_super, double scale, int top_m,
+                               int64_t* selected, int32_t* gate, int64_t* promoted,
+                               spa_stream_t stream);
+int spa_sparse_decode_step_gated(const void* q, int dtype, int batch, int q_heads,
+                                 int kv_heads, int head_dim, const spa_kv_layout* kv,
+                                 const int32_t* context_lens, int local_window,
+                                 const float* super_summaries, int n_super,
+                                 const float* summaries, int n_pages, int superblock,
+                                 int top_super, int top_m, double router_scale,
+                                 double attn_scale, int64_t* selected, void* out,
+                                 void* workspace, size_t workspace_bytes,
+                                 int32_t* gate, int64_t* promoted, spa_stream_t stream);
+
+/*
  * Diagnostic: y[i] = 2^x[i] through the FMA-pipe exponential that the prefill
  * softmax uses for part of its probabilities (n = round(x), cubic minimax
  * polynomial for 2^(x-n), relative error <= 7.5e-5 for -125 <= x <= 126; x below

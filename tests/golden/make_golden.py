@@ -17,6 +17,9 @@ checksums to prove the regeneration, and the reference's outputs:
 * dense_small         -- seed 7: reference_attention over the whole buffer.
 * prefill_small       -- seed 7: local_reference (masked causal window).
 * periodic_router     -- seed 7: periodic_router indices with -1 padding.
+* refresh_gate        -- seed 7: the reference's RefreshHead (train_refresh_head.py) on
+  three (state, cached state) sets of growing drift, its sigmoid probabilities, and the
+  drift distance 1 - cosine_similarity of evaluate_promotion_ttl.py:130.
 """
 
 from __future__ import annotations
@@ -109,6 +112,27 @@ def main(ref_root: str) -> None:
     sel = tpr.periodic_router(query, keys, block_size=page, router_stride=stride, top_blocks=m)
     np.savez(HERE / "periodic_router.npz", seed=7, shape=np.array([b, h, ctx, d, page, stride, m]),
              k_sum=keys.double().sum().item(), q_sum=query.double().sum().item(), selected=sel.numpy())
+
+    # ---- promotion refresh gates
+    import train_refresh_head as trh  # noqa: E402
+
+    torch.manual_seed(7)
+    b, w = 8, 64
+    head = trh.RefreshHead(w)
+    states, cached, probs, drifts = [], [], [], []
+    with torch.no_grad():
+        for noise in (0.05, 0.3, 1.5):
+            x = torch.randn(b, w)
+            y = x + noise * torch.randn(b, w)
+            states.append(x)
+            cached.append(y)
+            probs.append(torch.sigmoid(head(x, y)))
+            drifts.append(1.0 - torch.nn.functional.cosine_similarity(x, y, dim=-1))
+    np.savez(HERE / "refresh_gate.npz", seed=7, shape=np.array([b, w]),
+             w1=head.network[0].weight.detach().numpy(), b1=head.network[0].bias.detach().numpy(),
+             w2=head.network[2].weight.detach().numpy(), b2=head.network[2].bias.detach().numpy(),
+             state=torch.stack(states).numpy(), cached=torch.stack(cached).numpy(),
+             prob=torch.stack(probs).numpy(), drift=torch.stack(drifts).numpy())
     print("wrote fixtures to", HERE)
 
 

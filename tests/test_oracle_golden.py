@@ -141,3 +141,29 @@ def test_tree_router_is_two_select_levels():
         allowed = [g for s in chosen[b].tolist() for g in range(s * 8, min(s * 8 + 8, 37))]
         best = sorted(allowed, key=lambda g: (-scores[b, g].item(), g))[:3]
         assert sel[b].tolist() == best
+
+
+def test_refresh_gate_restatement(golden_dir):
+    """Drift distance and learned refresh probability restated from the reference
+    (evaluate_promotion_ttl.py:130, train_refresh_head.py:24-31)."""
+    from oracle.refresh_gate import drift_distance, refresh_probability
+
+    fx = _load(golden_dir, "refresh_gate.npz")
+    head = (fx["w1"], fx["b1"], fx["w2"], fx["b2"])
+    for case in range(fx["state"].shape[0]):
+        s, c = torch.from_numpy(fx["state"][case]), torch.from_numpy(fx["cached"][case])
+        assert torch.allclose(drift_distance(s, c), torch.from_numpy(fx["drift"][case]), atol=1e-6, rtol=0)
+        assert torch.allclose(refresh_probability(s, c, *head), torch.from_numpy(fx["prob"][case]), atol=1e-6, rtol=0)
+
+
+def test_gate_sim_policies():
+    from oracle.refresh_gate import GateSim
+
+    fresh = [torch.tensor([[i, i + 1]]) for i in range(10)]
+    ttl = GateSim("ttl", ttl=4)
+    used = [ttl.step(fresh[t], step=t) for t in range(10)]
+    assert [r for _, r in used] == [t % 4 == 0 for t in range(10)]
+    assert torch.equal(used[5][0], fresh[4])
+    sig = GateSim("signature")
+    sigs = [torch.tensor([[1, 2, 3]])] * 3 + [torch.tensor([[1, 2, 4]])] * 2
+    assert [sig.step(fresh[t], signature=sigs[t])[1] for t in range(5)] == [True, False, False, True, False]
