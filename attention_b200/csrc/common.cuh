@@ -99,14 +99,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // raises SPA_DEVERR_WAIT_TIMEOUT) if it has not completed after SPA_WAIT_CYCLES.
 // Once any wait on the device has given up, every other bounded wait returns at
 // once (the error word is polled), so a broken pipeline ends within one bound.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  long long limit_cycles = SPA_WAIT_CYCLES) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++spins & 255u) == 0) {
       if (*reinterpret_cast<volatile uint32_t*>(&g_spa_error_flags) & SPA_DEVERR_WAIT_TIMEOUT) return false;
-      if (clock64() - t0 > SPA_WAIT_CYCLES) {
+      if (clock64() - t0 > limit_cycles) {
         spa_raise(SPA_DEVERR_WAIT_TIMEOUT);
         return false;
       }

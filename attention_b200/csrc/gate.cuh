@@ -30,7 +30,10 @@ __device__ __forceinline__ float gate_warp_sum(float v) {
 __global__ void __launch_bounds__(kGateThreads) refresh_gate_kernel(const spa_refresh_gate_args a) {
   extern __shared__ float gsm[];
   float* row_val = gsm;             // [batch]
-  float* unit_val = gsm + a.batch;  // [batch * hidden]
+  float* unit_val = gsm + a.batch;  // [batch * hidden] (learned) or [batch * warps per row * 3] (drift)
+  // a gated router launched after this kernel may start now; it waits for this grid to
+  // complete before it reads the decision
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ int mismatch;
   __shared__ int decision;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = kGateThreads / 32;
@@ -43,21 +46,56 @@ __global__ void __launch_bounds__(kGateThreads) refresh_gate_kernel(const spa_re
     for (int64_t i = threadIdx.x; i < n; i += kGateThreads) diff |= a.signature[i] != a.cached_signature[i];
     if (__syncthreads_or(diff) && threadIdx.x == 0) mismatch = 1;
   } else if (a.mode == SPA_GATE_DRIFT) {
-    // torch cosine_similarity: (x / max(|x|, eps)) . (y / max(|y|, eps)), eps = 1e-8
-    for (int b = warp; b < a.batch; b += nw) {
+    // torch cosine_similarity: (x / max(|x|, eps)) . (y / max(|y|, eps)), eps = 1e-8.
+    // Each row is cut into `wpr` contiguous segments, one warp each; the segment partials
+    // are added in segment order (deterministic).
+    const int wpr = a.batch >= nw ? 1 : nw / a.batch;
+    const int seg = (W + wpr - 1) / wpr;
+    const bool vec = (W % 4 == 0) && (seg % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.state) |
+                                                          reinterpret_cast<uintptr_t>(a.cached_state)) % 16 == 0);
+    for (int t = warp; t < a.batch * wpr; t += nw) {
+      const int b = t / wpr, sidx = t - b * wpr;
+      const int k0 = sidx * seg, k1 = min(W, k0 + seg);
       const float* x = a.state + static_cast<int64_t>(b) * W;
       const float* y = a.cached_state + static_cast<int64_t>(b) * W;
       float xy = 0.f, xx = 0.f, yy = 0.f;
-      for (int k = lane; k < W; k += 32) {
-        const float u = x[k], v = y[k];
-        xy = fmaf(u, v, xy);
-        xx = fmaf(u, u, xx);
-        yy = fmaf(v, v, yy);
+      if (vec) {
+        const float4* x4 = reinterpret_cast<const float4*>(x + k0);
+        const float4* y4 = reinterpret_cast<const float4*>(y + k0);
+        const int n4 = (k1 - k0) / 4;
+#pragma unroll 4
+        for (int i = lane; i < n4; i += 32) {
+          const float4 u = x4[i], v = y4[i];
+          xy = fmaf(u.x, v.x, fmaf(u.y, v.y, fmaf(u.z, v.z, fmaf(u.w, v.w, xy))));
+          xx = fmaf(u.x, u.x, fmaf(u.y, u.y, fmaf(u.z, u.z, fmaf(u.w, u.w, xx))));
+          yy = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, yy))));
+        }
+      } else {
+        for (int k = k0 + lane; k < k1; k += 32) {
+          const float u = x[k], v = y[k];
+          xy = fmaf(u, v, xy);
+          xx = fmaf(u, u, xx);
+          yy = fmaf(v, v, yy);
+        }
       }
       xy = gate_warp_sum(xy);
       xx = gate_warp_sum(xx);
       yy = gate_warp_sum(yy);
-      if (lane == 0) row_val[b] = 1.f - xy / (fmaxf(sqrtf(xx), 1e-8f) * fmaxf(sqrtf(yy), 1e-8f));
+      if (lane == 0) {
+        unit_val[3 * t] = xy;
+        unit_val[3 * t + 1] = xx;
+        unit_val[3 * t + 2] = yy;
+      }
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < a.batch; b += kGateThreads) {
+      float xy = 0.f, xx = 0.f, yy = 0.f;
+      for (int sidx = 0; sidx < wpr; ++sidx) {
+        xy += unit_val[3 * (b * wpr + sidx)];
+        xx += unit_val[3 * (b * wpr + sidx) + 1];
+        yy += unit_val[3 * (b * wpr + sidx) + 2];
+      }
+      row_val[b] = 1.f - xy / (fmaxf(sqrtf(xx), 1e-8f) * fmaxf(sqrtf(yy), 1e-8f));
     }
   } else if (a.mode == SPA_GATE_LEARNED) {
     // one warp per (row, hidden unit): GELU(w1[u] . features(row) + b1[u]) * w2[u]
@@ -133,9 +171,13 @@ extern "C" int spa_refresh_gate(const spa_refresh_gate_args* args, spa_stream_t 
     case SPA_GATE_SIGNATURE:
       if (!a.signature || !a.cached_signature || a.sig_len <= 0) return SPA_ERR_INVALID;
       break;
-    case SPA_GATE_DRIFT:
+    case SPA_GATE_DRIFT: {
       if (!a.state || !a.cached_state || a.width <= 0) return SPA_ERR_INVALID;
+      const int nw = spa::kGateThreads / 32;
+      const int wpr = a.batch >= nw ? 1 : nw / a.batch;
+      smem += sizeof(float) * 3 * static_cast<size_t>(a.batch) * wpr;
       break;
+    }
     case SPA_GATE_LEARNED:
       if (!a.state || !a.cached_state || a.width <= 0 || !a.w1 || !a.b1 || !a.w2 || !a.b2 || a.hidden <= 0)
         return SPA_ERR_INVALID;

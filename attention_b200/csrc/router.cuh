@@ -145,6 +145,7 @@ __device__ __forceinline__ float ld_dsmem_f32(const float* local_ptr, uint32_t r
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
   return v;
 }
+__device__ __forceinline__ void pdl_wait_prerequisite() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
@@ -315,6 +316,7 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
   pdl_launch_dependents();
   const int b = blockIdx.y;
   const uint32_t rank = cluster_rank();
+  if (a.gate) pdl_wait_prerequisite();  // the gate kernel's decision (launched as its dependent)
   if (a.gate && a.gate[0] == 0 && a.gate[1] != 0) {
     // promotion reuse: the refresh gate is closed, so the promoted pages are this step's
     // selection and no summary is read.  The flags are the same for every CTA, so whole
@@ -459,13 +461,17 @@ int launch_router(const RouterArgs& a, int batch, cudaStream_t st) {
   cfg.blockDim = dim3(kRouterThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = kRouterCluster;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // gated: launched as a programmatic dependent of the gate kernel, which it waits for
+  // (griddepcontrol.wait) before reading the decision
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = a.gate ? 2 : 1;
   SPA_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
   return SPA_OK;
 }

@@ -25,6 +25,27 @@ __global__ void debug_exp2_poly_kernel(const float* __restrict__ x, float* __res
 }
 }  // namespace spa
 
+namespace spa {
+// One thread waits on an mbarrier that nothing arrives on; the bounded wait gives up
+// after `cycles` and raises SPA_DEVERR_WAIT_TIMEOUT.
+__global__ void debug_wait_timeout_kernel(long long cycles) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_bounded(&bar, 0, cycles);
+}
+}  // namespace spa
+
+extern "C" int spa_debug_wait_timeout(long long cycles, spa_stream_t stream) {
+  if (cycles <= 0 || cycles > SPA_WAIT_CYCLES) return SPA_ERR_INVALID;
+  spa::debug_wait_timeout_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(cycles);
+  SPA_CHECK_CUDA(cudaGetLastError());
+  return SPA_OK;
+}
+
 extern "C" int spa_debug_exp2_poly(const float* x, float* y, int64_t n, spa_stream_t stream) {
   if (!x || !y || n < 0) return SPA_ERR_INVALID;
   if (n == 0) return SPA_OK;

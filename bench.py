@@ -347,6 +347,10 @@ def run_ours(args, world, rank, local):
     hbm_peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
     traffic = read_profile_traffic("sparse_decode_128k_attention_ncu.md")
 
+    gated = None
+    if not args.skip_gated:
+        gated = run_gated(cfg, wl, summ, sup, sel_buf, out_buf, scale, groups, dev, world, att_reps)
+
     # end to end through the public API: pinned host query in, output + pages out, every step
     e2e = None
     if not args.skip_e2e:
@@ -448,6 +452,7 @@ def run_ours(args, world, rank, local):
         "e2e": e2e,
         "cpu_baseline": cpu,
         "prefill": prefill,
+        "gated_step": gated,
         "dense_decode": dense,
         "integrated_decode": integrated,
         "clocks": clocks.summary(),
@@ -515,6 +520,56 @@ def run_prefill(args, world, rank, dev, peaks):
             else "single GPU", "reps": reps,
             "periodic_router_ms": round(router_ms, 4) if router_ms is not None else None,
             "periodic_router": "block 256, stride 256, top-4, summaries included" if router_ms is not None else None}
+
+
+def run_gated(cfg, wl, summ, sup, sel_buf, out_buf, scale, groups, dev, world, reps):
+    """The decode step behind an embedding-drift refresh gate evaluated on the device
+    (state = the step's query, B x Hq*D): with the gate closed the router copies the
+    promoted pages and reads no summary; with it open every step routes."""
+    import attention_b200 as spa
+
+    states = [wl["query"][g].float().reshape(cfg.batch, -1).contiguous() for g in range(groups)]
+    result = {}
+    # cosine distance lies in [0, 2]: threshold 3 never refreshes after the first step,
+    # threshold -1 refreshes every step
+    for name, thr in (("reuse", 3.0), ("route", -1.0)):
+        gate = spa.RefreshGate("drift", cfg.batch, width=cfg.q_heads * cfg.head_dim, threshold=thr, device=dev)
+
+        def gstep(g):
+            gate.decide(state=states[g])
+            spa.sparse_decode_step(wl["query"][g], wl["k_pool"], wl["v_pool"], summ[g], super_summaries=sup[g],
+                                   superblock=cfg.superblock, top_super=cfg.top_super, top_blocks=cfg.top_m,
+                                   local_window=cfg.local_window, block_size=cfg.page_size, router_scale=scale,
+                                   page_table=wl["page_table"][g], context_lens=wl["context_lens"],
+                                   out=out_buf[g], selected=sel_buf[g], gate=gate)
+
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for g in range(groups):
+                gstep(g)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for g in range(groups):
+                gstep(g)
+        graph.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.nvtx.range(f"gated_{name}"):
+            e0.record()
+            for _ in range(reps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+        barrier(world)
+        result[f"{name}_us_per_step"] = round(max_over_ranks(e0.elapsed_time(e1), world) * 1e3 / (reps * groups), 3)
+        del graph
+    result["gate"] = "embedding drift (1 - cosine) of the step's query, one device decision per step"
+    result["launches_per_step"] = 3
+    return result
 
 
 def run_dense(args, world, rank, dev, peaks):
@@ -675,6 +730,7 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-integrated", action="store_true")
     ap.add_argument("--skip-dense", action="store_true")
+    ap.add_argument("--skip-gated", action="store_true")
     ap.add_argument("--dense-steps", type=int, default=200)
     ap.add_argument("--integrated-steps", type=int, default=256)
     args = ap.parse_args()

@@ -359,6 +359,14 @@ int spa_sparse_decode_step_gated(const void* q, int dtype, int batch, int q_head
  */
 int spa_debug_exp2_poly(const float* x, float* y, int64_t n, spa_stream_t stream);
 
+/*
+ * Diagnostic for the failure path: one kernel waits on an mbarrier that nothing
+ * completes, with the library's bounded wait limited to `cycles` (1 .. 4e9 clock
+ * cycles).  The wait gives up, the kernel returns, and spa_device_error then reports
+ * the wait-timeout bit (1).  No reference counterpart.
+ */
+int spa_debug_wait_timeout(long long cycles, spa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
