@@ -50,6 +50,18 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 __device__ __forceinline__ void cluster_barrier() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Split cluster barrier: every thread arrives once at kernel start (relaxed) and waits
+// before its first store into a peer's shared memory, which guarantees every CTA of the
+// cluster is running by then.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+__device__ __forceinline__ void st_dsmem(float* local_ptr, int rank, float v) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
 __device__ __forceinline__ float ld_dsmem(const float* local_ptr, int rank) {
   uint32_t ra;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
@@ -83,8 +95,9 @@ struct ChunkInfo {
   int t0, vlo, vhi;  // tokens [t0, t0+chunk) are loaded; [vlo, vhi) are candidates
 };
 
-__device__ __forceinline__ ChunkInfo chunk_info(const DecodeArgs& a, const ChunkPlan& p, int b, int k,
-                                                int chunk) {
+// sel_row: the sequence's selected ids (a.selected + b * top_m, or a copy of them)
+__device__ __forceinline__ ChunkInfo chunk_info(const DecodeArgs& a, const ChunkPlan& p, const int64_t* sel_row,
+                                                int k, int chunk) {
   ChunkInfo c;
   if (k < p.n_seg) {
     c.t0 = p.seg_a + k * chunk;
@@ -93,7 +106,7 @@ __device__ __forceinline__ ChunkInfo chunk_info(const DecodeArgs& a, const Chunk
   } else {
     const int kk = k - p.n_seg;
     const int j = kk / p.cpp, ci = kk - j * p.cpp;
-    const int64_t lp = a.selected[static_cast<int64_t>(b) * a.top_m + j];
+    const int64_t lp = sel_row[j];
     const int P = a.addr.page_size;
     if (a.span_len > 0) {
       // span [lp, lp + span_len) in chunk-aligned pieces, clipped to the context
@@ -138,7 +151,9 @@ struct DecodeSmem {
   static constexpr int kStageBytes = 2 * kKvBytes;
   static constexpr int kRingBytes = STAGES * kStageBytes;
   static constexpr int kTabCap = 2048;  // page-table entries prefetched into shared memory
-  static constexpr int kBytes = kRingBytes + STAGES * 16 + STAGES * 16 + kTabCap * 4 + 1024;  // + bars, info, table
+  static constexpr int kSelCap = 32;    // selected ids prefetched into shared memory
+  // + barriers, chunk info, page table, selected ids (the cluster receive buffer follows)
+  static constexpr int kBytes = kRingBytes + STAGES * 16 + STAGES * 16 + kTabCap * 4 + kSelCap * 8 + 1024;
 };
 
 template <int D>
@@ -160,10 +175,15 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   uint64_t* empty = full + STAGES;
   int4* info = reinterpret_cast<int4*>(empty + STAGES);
   int32_t* tab = reinterpret_cast<int32_t*>(info + STAGES);
+  int64_t* sel_s = reinterpret_cast<int64_t*>(tab + S::kTabCap);
+  // partials pushed by the cluster's splits for the columns this CTA merges
+  float* recv = reinterpret_cast<float*>(sel_s + S::kSelCap);
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool cluster_push = a.cluster_merge && a.nsplit > 1;
   pdl_trigger();
+  if (cluster_push) cluster_arrive_relaxed();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -172,6 +192,22 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     fence_mbar_init();
   }
   if (!a.early_local) pdl_block();
+  // prologue loads issued together (one memory round trip): the producer's page-table row
+  // and selected ids, every thread's context length.  With early_local the selected ids
+  // come from the kernel this one overlaps, so they are read after it completes.
+  const int tstride = a.addr.table_stride;
+  const bool use_tab = a.addr.page_table != nullptr && tstride <= S::kTabCap;
+  const bool sel_early = a.selected && !a.early_local && a.top_m <= S::kSelCap;
+  int32_t tab_r[16];
+  int64_t sel_r = -1;
+  if (warp == kConsumerWarps) {
+    if (use_tab) {
+      const int32_t* src = a.addr.page_table + static_cast<int64_t>(b) * tstride;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) tab_r[u] = lane + 32 * u < tstride ? __ldg(src + lane + 32 * u) : -1;
+    }
+    if (sel_early && lane < a.top_m) sel_r = a.selected[static_cast<int64_t>(b) * a.top_m + lane];
+  }
   const ChunkPlan plan = make_plan(a, b, kChunk);
   const int k0 = static_cast<int>(static_cast<int64_t>(plan.n_total) * split / a.nsplit);
   const int k1 = static_cast<int>(static_cast<int64_t>(plan.n_total) * (split + 1) / a.nsplit);
@@ -186,12 +222,14 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     }
     const uint64_t policy = l2_policy_evict_first();
     bool ok = true;
-    // the sequence's page-table row, prefetched with independent loads (one round trip)
-    const int tstride = a.addr.table_stride;
-    const bool use_tab = a.addr.page_table != nullptr && tstride <= S::kTabCap;
+    // the sequence's page-table row: the first 512 entries were loaded with the plan,
+    // the rest (long rows) here with independent loads
     if (use_tab) {
       const int32_t* src = a.addr.page_table + static_cast<int64_t>(b) * tstride;
-      for (int e0 = lane; e0 < tstride; e0 += 32 * 16) {
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+        if (lane + 32 * u < tstride) tab[lane + 32 * u] = tab_r[u];
+      for (int e0 = lane + 32 * 16; e0 < tstride; e0 += 32 * 16) {
         int32_t r[16];
 #pragma unroll
         for (int u = 0; u < 16; ++u) r[u] = e0 + 32 * u < tstride ? __ldg(src + e0 + 32 * u) : -1;
@@ -199,8 +237,10 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
         for (int u = 0; u < 16; ++u)
           if (e0 + 32 * u < tstride) tab[e0 + 32 * u] = r[u];
       }
-      __syncwarp();
     }
+    if (sel_early && lane < a.top_m) sel_s[lane] = sel_r;
+    __syncwarp();
+    const int64_t* sel_row = sel_early ? sel_s : (a.selected ? a.selected + static_cast<int64_t>(b) * a.top_m : nullptr);
     auto row_of = [&](int t) -> long long {
       if (!use_tab) return a.addr.row(b, kvh, t);
       const int lp = t / a.addr.page_size;
@@ -215,12 +255,20 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     const int n_local = max(0, min(k1, plan.n_seg) - k0);
     for (int part = 0; part < 2 && ok; ++part) {
       const int lo = part ? n_local : 0, hi = part ? nk : n_local;
-      if (part == 1 && a.early_local) pdl_block();
+      if (part == 1 && a.early_local) {
+        pdl_block();
+        // the router has completed: its selected ids for this sequence, one round trip
+        if (a.selected && a.top_m <= S::kSelCap) {
+          if (lane < a.top_m) sel_s[lane] = a.selected[static_cast<int64_t>(b) * a.top_m + lane];
+          __syncwarp();
+          sel_row = sel_s;
+        }
+      }
       for (int base = lo; base < hi && ok; base += 32) {
         ChunkInfo ci{0, 0, 0};
         long long row = -1;
         if (base + lane < hi) {
-          ci = chunk_info(a, plan, b, k0 + base + lane, kChunk);
+          ci = chunk_info(a, plan, sel_row, k0 + base + lane, kChunk);
           if (ci.vlo < ci.vhi) {
             row = row_of(ci.t0);
             if (row < 0 || row >= a.addr.total_rows) {
@@ -261,9 +309,9 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
         }
       }
     }
-    // every thread of every CTA in a merging cluster reaches both cluster barriers
-    if (a.cluster_merge && a.nsplit > 1) {
-      cluster_barrier();
+    // every thread of every CTA in a merging cluster completes both cluster phases
+    if (cluster_push) {
+      cluster_wait();
       cluster_barrier();
     }
     return;
@@ -382,8 +430,8 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     if (lane == 0) mbar_arrive(&empty[stage]);
   }
   if (!ok) {  // error word already raised; outputs of this split are undefined
-    if (a.cluster_merge && a.nsplit > 1) {
-      cluster_barrier();
+    if (cluster_push) {
+      cluster_wait();
       cluster_barrier();
     }
     return;
@@ -400,8 +448,6 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   constexpr int LD = D + 8;
   float* red = reinterpret_cast<float*>(smem);                 // [warp][group][LD]
   float* ml = red + kConsumerWarps * group * LD;               // [warp][group][2]
-  float* cta_o = ml + kConsumerWarps * group * 2;              // [group][D]  this CTA's partial
-  float* cta_lse = cta_o + group * D;                          // [group]
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");  // ring reads done
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
@@ -417,63 +463,73 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     }
   }
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-  const int64_t bh0 = static_cast<int64_t>(b) * a.Hq + kvh * group;
-  for (int idx = threadIdx.x; idx < group * D; idx += kConsumerWarps * 32) {
-    const int row = idx / D, col = idx - row * D;
+  // per head, once: the warps' weights exp2(m_w - M) / L and the log2-sum-exp
+  float* fw = ml + kConsumerWarps * group * 2;   // [group][kConsumerWarps]
+  float* row_lse = fw + group * kConsumerWarps;  // [group]
+  if (threadIdx.x < group) {
+    const int row = threadIdx.x;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ml[(w * group + row) * 2]);
     const float Mu = M == -INFINITY ? 0.f : M;
-    float L = 0.f, O = 0.f;
+    float e[kConsumerWarps], L = 0.f;
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) {
-      const float f = fast_exp2(ml[(w * group + row) * 2] - Mu);
-      L += ml[(w * group + row) * 2 + 1] * f;
-      O += red[(w * group + row) * LD + col] * f;
+      e[w] = fast_exp2(ml[(w * group + row) * 2] - Mu);
+      L += ml[(w * group + row) * 2 + 1] * e[w];
     }
-    const float o = L > 0.f ? O / L : 0.f;
-    const float lse = L > 0.f ? M + __log2f(L) : -INFINITY;
-    if (a.nsplit == 1) {
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) fw[row * kConsumerWarps + w] = e[w] * inv;
+    row_lse[row] = L > 0.f ? M + __log2f(L) : -INFINITY;
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+  const int64_t bh0 = static_cast<int64_t>(b) * a.Hq + kvh * group;
+  const int ns = a.nsplit;
+  // cluster merge: rank r merges output columns [r*D/ns, (r+1)*D/ns) of every head; every
+  // split pushes its normalised partial of those columns, and its log-sum-exps, into rank
+  // r's receive buffer (recv_lse [split][group], recv_o [split][group][wmax])
+  const int wmax = (D + ns - 1) / ns;
+  float* recv_lse = recv;
+  float* recv_o = recv + ns * group;
+  if (cluster_push) cluster_wait();  // every CTA of the cluster runs: remote stores are safe
+  for (int idx = threadIdx.x; idx < group * D; idx += kConsumerWarps * 32) {
+    const int row = idx / D, col = idx - row * D;
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w)
+      o = fmaf(red[(w * group + row) * LD + col], fw[row * kConsumerWarps + w], o);
+    if (ns == 1) {
       static_cast<T*>(a.out)[(bh0 + row) * D + col] = from_f32<T>(o);
-    } else if (a.cluster_merge) {
-      cta_o[row * D + col] = o;
-      if (col == 0) cta_lse[row] = lse;
+    } else if (cluster_push) {
+      const int r = ((col + 1) * ns - 1) / D;  // the rank whose column slice holds col
+      st_dsmem(recv_o + (split * group + row) * wmax + (col - r * D / ns), r, o);
     } else {
-      a.part_o[((bh0 + row) * a.nsplit + split) * D + col] = o;
-      if (col == 0) a.part_lse[(bh0 + row) * a.nsplit + split] = lse;
+      a.part_o[((bh0 + row) * ns + split) * D + col] = o;
+      if (col == 0) a.part_lse[(bh0 + row) * ns + split] = row_lse[row];
     }
   }
-  if (a.nsplit == 1 || !a.cluster_merge) return;
-
-  // ------------------------------------------------ cluster merge of the pair's splits
-  // The nsplit CTAs of this (b, kv head) form one cluster; after a cluster barrier,
-  // rank r merges output columns [r*D/nsplit, (r+1)*D/nsplit) of every head from the
-  // peers' shared memory, and a second barrier keeps that memory alive until all read.
-  cluster_barrier();
-  const int ns = a.nsplit;
-  const int c0 = split * D / ns, c1 = (split + 1) * D / ns;
-  for (int idx = threadIdx.x; idx < group * (c1 - c0); idx += kConsumerWarps * 32) {
-    const int row = idx / (c1 - c0), col = c0 + (idx - row * (c1 - c0));
-    float lse[16], ov[16];
-#pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      lse[r] = r < ns ? ld_dsmem(cta_lse + row, r) : -INFINITY;
-      ov[r] = r < ns ? ld_dsmem(cta_o + row * D + col, r) : 0.f;
-    }
+  if (!cluster_push) return;
+  for (int i = threadIdx.x; i < group * ns; i += kConsumerWarps * 32) {
+    const int row = i / ns, r = i - row * ns;
+    st_dsmem(recv_lse + split * group + row, r, row_lse[row]);
+  }
+  cluster_barrier();  // every split's pushes are visible in the receive buffers
+  // after the barrier this CTA reads only its own shared memory: no second barrier
+  const int c0 = split * D / ns, c1 = (split + 1) * D / ns, w = c1 - c0;
+  for (int idx = threadIdx.x; idx < group * w; idx += kConsumerWarps * 32) {
+    const int row = idx / w, j = idx - row * w;
     float M = -INFINITY;
-#pragma unroll
-    for (int r = 0; r < 16; ++r) M = fmaxf(M, lse[r]);
+    for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, recv_lse[s2 * group + row]);
     const float Mu = M == -INFINITY ? 0.f : M;
     float W = 0.f, O = 0.f;
-#pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const float f = r < ns ? fast_exp2(lse[r] - Mu) : 0.f;
+    for (int s2 = 0; s2 < ns; ++s2) {
+      const float f = fast_exp2(recv_lse[s2 * group + row] - Mu);
       W += f;
-      O += ov[r] * f;
+      O = fmaf(recv_o[(s2 * group + row) * wmax + j], f, O);
     }
-    static_cast<T*>(a.out)[(bh0 + row) * D + col] = from_f32<T>(W > 0.f ? O / W : 0.f);
+    static_cast<T*>(a.out)[(bh0 + row) * D + c0 + j] = from_f32<T>(W > 0.f ? O / W : 0.f);
   }
-  cluster_barrier();
 }
 
 // ---------------------------------------------------------------------------
@@ -501,7 +557,8 @@ __global__ void __launch_bounds__(32) decode_generic_kernel(const T* __restrict_
   }
   float m = -INFINITY, l = 0.f;
   for (int kk = k0; kk < k1; ++kk) {
-    const ChunkInfo ci = chunk_info(a, plan, b, kk, kGenericChunk);
+    const ChunkInfo ci =
+        chunk_info(a, plan, a.selected ? a.selected + static_cast<int64_t>(b) * a.top_m : nullptr, kk, kGenericChunk);
     for (int t = ci.vlo; t < ci.vhi; ++t) {
       const int64_t row = a.addr.row(b, kvh, t);
       if (row < 0 || row >= a.addr.total_rows) {
@@ -692,8 +749,14 @@ int launch_decode_mma(const spa_kv_layout& kv, int dtype, const DecodeArgs& a, c
   if (!spa_make_tensor_map_2d(&kmap, kv.k, dtype, kv.total_rows, D, kChunk, 64, true)) return SPA_ERR_INVALID;
   if (!spa_make_tensor_map_2d(&vmap, kv.v, dtype, kv.total_rows, D, kChunk, 64, true)) return SPA_ERR_INVALID;
   auto kern = decode_mma_kernel<T, D, kDecodeStages>;
-  SPA_CHECK_CUDA(spa_set_smem_once(kern, S::kBytes));
-  SPA_CHECK_CUDA(launch_ex(kern, dim3(a.nsplit, a.Hkv, a.B), dim3(kDecodeThreads), S::kBytes, st, a.early_local != 0,
+  // the receive buffer of the cluster merge: [ns][group] log-sum-exps + [ns][group][ceil(D/ns)]
+  const int ns = a.nsplit;
+  const size_t recv = a.cluster_merge && ns > 1
+                          ? sizeof(float) * static_cast<size_t>(ns) * a.group * (1 + (D + ns - 1) / ns)
+                          : 0;
+  const size_t smem = S::kBytes + recv;
+  SPA_CHECK_CUDA(spa_set_smem_once(kern, static_cast<int>(smem)));
+  SPA_CHECK_CUDA(launch_ex(kern, dim3(a.nsplit, a.Hkv, a.B), dim3(kDecodeThreads), smem, st, a.early_local != 0,
                            a.cluster_merge ? a.nsplit : 1, kmap, vmap, a));
   return SPA_OK;
 }
