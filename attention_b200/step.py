@@ -78,3 +78,79 @@ def sparse_decode_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Te
         rc = _lib.lib.spa_sparse_decode_step(*args, stream_ptr(dev))
         _lib.check(rc, "spa_sparse_decode_step")
     return out, selected
+
+
+class SparseDecodeSession:
+    """One prepared sparse decode step for a fixed pool, page table and summaries.
+
+    The host->device copy of the query (from a pinned host buffer), the fused step and the
+    device->host copies of the output and page ids (into pinned host buffers) are captured
+    once as CUDA graphs; ``step(query)`` copies the host query into the pinned buffer and
+    replays, so a decode step costs one graph launch on the host.  The host buffers are
+    double-buffered: step i reuses the buffers of step i-2 after waiting for its
+    completion, so the host can prepare one step ahead of the device.  The returned
+    tensors are filled when the step's work completes (``torch.cuda.synchronize()``)."""
+
+    def __init__(self, keys: torch.Tensor, values: torch.Tensor, summaries: torch.Tensor, *, q_heads: int,
+                 top_blocks: int, local_window: int, block_size: int, batch: int | None = None,
+                 super_summaries: torch.Tensor | None = None, superblock: int = 0, top_super: int = 0,
+                 router_scale: float = 1.0, page_table: torch.Tensor | None = None,
+                 context_lens: torch.Tensor | None = None, gate=None):
+        dev = keys.device
+        batch = batch if batch is not None else summaries.size(0)
+        shape = (batch, q_heads, keys.size(3))
+        # output and page ids share one buffer (page ids at an 8-byte aligned offset), so one
+        # device->host copy returns both
+        n_out = batch * q_heads * keys.size(3) * keys.element_size()
+        off = -(-n_out // 8) * 8
+        nbytes = off + batch * top_blocks * 8
+
+        def views(buf):
+            return (buf[:n_out].view(keys.dtype).view(shape), buf[off:].view(torch.int64).view(batch, top_blocks))
+
+        self.host_query = [torch.zeros(shape, dtype=keys.dtype).pin_memory() for _ in range(2)]
+        self._host_buf = [torch.empty(nbytes, dtype=torch.uint8).pin_memory() for _ in range(2)]
+        self.host_out, self.host_selected = zip(*(views(b) for b in self._host_buf))
+        self._q = torch.zeros(shape, dtype=keys.dtype, device=dev)
+        self._buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self._out, self._sel = views(self._buf)
+        self._done = [torch.cuda.Event(), torch.cuda.Event()]
+        self._n = 0
+        kw = dict(top_blocks=top_blocks, local_window=local_window, block_size=block_size,
+                  super_summaries=super_summaries, superblock=superblock, top_super=top_super,
+                  router_scale=router_scale, page_table=page_table, context_lens=context_lens,
+                  out=self._out, selected=self._sel, gate=gate)
+
+        def body(k):
+            self._q.copy_(self.host_query[k], non_blocking=True)
+            sparse_decode_step(self._q, keys, values, summaries, **kw)
+            self._host_buf[k].copy_(self._buf, non_blocking=True)
+
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):  # warm-up on the capture stream (workspace, descriptors)
+            body(0)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self._graphs = []
+        for k in range(2):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                body(k)
+            self._graphs.append(g)
+        for e in self._done:
+            e.record()
+        self._keep = (keys, values, summaries, super_summaries, page_table, context_lens, gate)
+
+    def step(self, query: torch.Tensor | None = None):
+        """Runs one step; returns (host_out, host_selected) of this step, filled when the
+        step completes.  Without ``query``, the query already in ``host_query[i % 2]``
+        (pinned) is copied to the device."""
+        k = self._n & 1
+        self._done[k].synchronize()  # step i-2 used these host buffers
+        if query is not None:
+            self.host_query[k].copy_(query)
+        self._graphs[k].replay()
+        self._done[k].record()
+        self._n += 1
+        return self.host_out[k], self.host_selected[k]

@@ -77,3 +77,34 @@ def test_step_head_dim_64(dtype):
     ref = oracle.gather_decode(q, k, v, exp_sel, local_window=win, block_size=page)
     o = out.double().cpu()
     assert ((o - ref).abs() <= 2e-2 + 1e-2 * ref.abs()).all()
+
+
+def test_session_replays_match_direct_steps():
+    """SparseDecodeSession (captured copy-in, step, copy-out) returns the same outputs and
+    page ids as sparse_decode_step, for consecutive steps with different queries (both host
+    buffers of the double buffering are checked)."""
+    cfg = workloads.SparseDecodeConfig(top_m=4)
+    wl = workloads.sparse_decode_workload(cfg, groups=3, seed=9)
+    table = wl["page_table"][0]
+    summ, sup = spa.page_summaries(wl["k_pool"], block_size=cfg.page_size, n_pages=cfg.routable_pages,
+                                   page_table=table, superblock=cfg.superblock)
+    kw = dict(top_blocks=cfg.top_m, local_window=cfg.local_window, block_size=cfg.page_size,
+              super_summaries=sup, superblock=cfg.superblock, top_super=cfg.top_super,
+              router_scale=cfg.head_dim ** -0.5, page_table=table, context_lens=wl["context_lens"])
+    sess = spa.SparseDecodeSession(wl["k_pool"], wl["v_pool"], summ, q_heads=cfg.q_heads, **kw)
+    queries = [wl["query"][g] for g in range(3)]
+    results = []
+    for q in queries:
+        out, sel = sess.step(q.cpu())
+        results.append((out, sel))
+        torch.cuda.synchronize()
+        results[-1] = (out.clone(), sel.clone())
+    for q, (out, sel) in zip(queries, results):
+        ref_out, ref_sel = spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ, **kw)
+        assert torch.equal(out, ref_out.cpu()) and torch.equal(sel, ref_sel.cpu())
+    # two steps in flight before one synchronisation: each keeps its own host buffers
+    o1, s1 = sess.step(queries[1].cpu())
+    o2, s2 = sess.step(queries[2].cpu())
+    torch.cuda.synchronize()
+    assert torch.equal(o1, results[1][0]) and torch.equal(s1, results[1][1])
+    assert torch.equal(o2, results[2][0]) and torch.equal(s2, results[2][1])
