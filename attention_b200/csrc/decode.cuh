@@ -62,6 +62,12 @@ __device__ __forceinline__ void st_dsmem(float* local_ptr, int rank, float v) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
 }
+__device__ __forceinline__ void st_dsmem_v4(float* local_ptr, int rank, float4 v) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
 __device__ __forceinline__ float ld_dsmem(const float* local_ptr, int rank) {
   uint32_t ra;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
@@ -491,9 +497,28 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   // r's receive buffer (recv_lse [split][group], recv_o [split][group][wmax])
   const int wmax = (D + ns - 1) / ns;
   float* recv_lse = recv;
-  float* recv_o = recv + ns * group;
+  float* recv_o = recv + ((ns * group + 3) & ~3);  // 16-byte aligned
+  // equal column slices of a multiple of 4: 16-byte loads and remote stores
+  const bool vec4 = cluster_push && D % (4 * ns) == 0;
   if (cluster_push) cluster_wait();  // every CTA of the cluster runs: remote stores are safe
-  for (int idx = threadIdx.x; idx < group * D; idx += kConsumerWarps * 32) {
+  if (vec4) {
+    for (int idx = threadIdx.x; idx < group * (D / 4); idx += kConsumerWarps * 32) {
+      const int row = idx / (D / 4), col = (idx - row * (D / 4)) * 4;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float4 r4 = *reinterpret_cast<const float4*>(red + (w * group + row) * LD + col);
+        const float f = fw[row * kConsumerWarps + w];
+        o.x = fmaf(r4.x, f, o.x);
+        o.y = fmaf(r4.y, f, o.y);
+        o.z = fmaf(r4.z, f, o.z);
+        o.w = fmaf(r4.w, f, o.w);
+      }
+      const int r = col / wmax;  // slices are exactly wmax = D / ns wide
+      st_dsmem_v4(recv_o + (split * group + row) * wmax + (col - r * wmax), r, o);
+    }
+  }
+  for (int idx = threadIdx.x; !vec4 && idx < group * D; idx += kConsumerWarps * 32) {
     const int row = idx / D, col = idx - row * D;
     float o = 0.f;
 #pragma unroll
@@ -752,7 +777,8 @@ int launch_decode_mma(const spa_kv_layout& kv, int dtype, const DecodeArgs& a, c
   // the receive buffer of the cluster merge: [ns][group] log-sum-exps + [ns][group][ceil(D/ns)]
   const int ns = a.nsplit;
   const size_t recv = a.cluster_merge && ns > 1
-                          ? sizeof(float) * static_cast<size_t>(ns) * a.group * (1 + (D + ns - 1) / ns)
+                          ? sizeof(float) * (((static_cast<size_t>(ns) * a.group + 3) & ~size_t(3)) +
+                                             static_cast<size_t>(ns) * a.group * ((D + ns - 1) / ns))
                           : 0;
   const size_t smem = S::kBytes + recv;
   SPA_CHECK_CUDA(spa_set_smem_once(kern, static_cast<int>(smem)));
