@@ -1,9 +1,11 @@
 // Causal sliding-window prefill on the sm_100a tensor cores (tcgen05 + TMEM).
 //
 // Reference: local_causal_prefill_kernel (triton_local_prefill.py:17-58), one program
-// per query row scanning keys [i-W+1, i] with an online softmax.  Here one CTA owns two
-// 128-row query tiles of one (b, h) and streams the 128-key tiles that intersect their
-// windows (W/128 + 2 tiles for W a multiple of 128):
+// per query row scanning keys [i-W+1, i] with an online softmax.  Here a persistent CTA
+// per SM walks work items round-robin; an item is two 128-row query tiles of one (b, h),
+// and the CTA streams the 128-key tiles that intersect their windows (W/128 + 2 tiles for
+// W a multiple of 128).  Barrier phases, the K/V ring and TMEM carry over from item to
+// item, so one item's Q load, first products and write-out overlap its neighbours:
 //
 //   warp 0      TMA producer: Q tiles once, then K and V tiles into two STAGES-deep
 //               rings with separate full/empty barriers: K(j) is released as soon as
@@ -30,6 +32,8 @@
 // query i sits at position i + halo_len and sees positions (i+halo-W, i+halo].
 #pragma once
 
+#include <algorithm>
+
 #include "prefill_generic.cuh"
 
 namespace spa {
@@ -41,7 +45,7 @@ constexpr float kPfRescaleThreshold = 8.0f;  // log2 units
 
 struct PfTcArgs {
   void* out;
-  int S, W, halo, row0, row1, H, n_pairs;
+  int S, W, halo, row0, row1, H, n_pairs, n_items;  // item = (query-tile pair, b*H + h)
   float scale_log2;
 };
 
@@ -58,10 +62,15 @@ struct PfSmem {
   // partial row sums [2 tiles][2 column halves][128 rows], fp32
   static constexpr int kX = kV + kPfStages * kTileBytes;
   static constexpr int kXBytes = (2 * 2 * kPfTile + 2 * 2 * kPfTile) * 4;
-  static constexpr int kBar = kX + kXBytes;
-  // barriers: q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_half[2], p_full[2],
-  // o_final[2], mma_done; + tmem slot
-  static constexpr int kNumBars = 1 + 4 * kPfStages + 2 + 2 + 2 + 2 + 1;
+  // epilogue staging: per softmax warp 32 rows x 32 output columns (16-bit), rows padded
+  // to 80 bytes so the row-wise writes and the column-wise reads avoid bank conflicts
+  static constexpr int kStageRow = 80;
+  static constexpr int kStage = kX + kXBytes;
+  static constexpr int kStageBytes = 8 * 32 * kStageRow;
+  static constexpr int kBar = kStage + kStageBytes;
+  // barriers: q_full[2], k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_half[2],
+  // p_full[2], o_final[2], mma_done, q_empty[2], o_empty[2]; + tmem slot
+  static constexpr int kNumBars = 2 + 4 * kPfStages + 2 + 2 + 2 + 2 + 1 + 2 + 2;
   static constexpr int kBytes = kBar + kNumBars * 8 + 16 + 1024;
 };
 
@@ -194,6 +203,29 @@ __device__ __forceinline__ void pf_tile_range(const PfTcArgs& a, int qt, int& lo
   hi = qlast / kPfTile;
 }
 
+// One work item of the persistent kernel: a pair of query tiles of one (b, h).
+struct PfItem {
+  int qt0, bh, J0, J1;
+  int lo[2], hi[2];
+  bool act[2];
+};
+__device__ __forceinline__ PfItem pf_item(const PfTcArgs& a, int w) {
+  PfItem I;
+  const int p = w % a.n_pairs;
+  I.bh = w / a.n_pairs;
+  I.qt0 = a.row0 / kPfTile + 2 * p;
+  const int last_tile = (a.row1 - 1) / kPfTile;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    I.act[t] = I.qt0 + t <= last_tile;
+    pf_tile_range(a, I.qt0 + t, I.lo[t], I.hi[t]);
+    if (I.lo[t] > I.hi[t]) I.act[t] = false;
+  }
+  I.J0 = I.act[0] ? I.lo[0] : I.lo[1];
+  I.J1 = I.act[1] ? I.hi[1] : I.hi[0];
+  return I;
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -204,8 +236,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
+  uint64_t* q_full = bars;  // [2] Q_t of the current item loaded
+  uint64_t* k_full = bars + 2;
   uint64_t* k_empty = k_full + kPfStages;
   uint64_t* v_full = k_empty + kPfStages;
   uint64_t* v_empty = v_full + kPfStages;
@@ -214,25 +246,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* p_full = p_half + 2;
   uint64_t* o_final = p_full + 2;
   uint64_t* mma_done = o_final + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* q_empty = mma_done + 1;  // [2] Q_t free: every S_t product of an item completed
+  uint64_t* o_empty = q_empty + 2;   // [2] O_t read out by the softmax warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
-  const int qt0 = a.row0 / kPfTile + 2 * blockIdx.x;
-  const int last_tile = (a.row1 - 1) / kPfTile;
-  bool act[2];
-  int lo[2], hi[2];
-  for (int t = 0; t < 2; ++t) {
-    act[t] = qt0 + t <= last_tile;
-    pf_tile_range(a, qt0 + t, lo[t], hi[t]);
-    if (lo[t] > hi[t]) act[t] = false;
-  }
-  const int J0 = act[0] ? lo[0] : lo[1];
-  const int J1 = act[1] ? hi[1] : hi[0];
   const int halo_tiles = a.halo / kPfTile;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
     for (int s = 0; s < kPfStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -244,6 +265,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&p_half[t], 4);
       mbar_init(&p_full[t], 4);
       mbar_init(&o_final[t], 1);
+      mbar_init(&o_empty[t], 8);
+      mbar_init(&q_full[t], 1);
+      mbar_init(&q_empty[t], 1);
     }
     mbar_init(mma_done, 1);
     fence_mbar_init();
@@ -259,33 +283,52 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
-    if (lane == 0 && (act[0] || act[1])) {
+    if (lane == 0) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      const int nq = (act[0] ? 1 : 0) + (act[1] ? 1 : 0);
-      mbar_arrive_expect_tx(q_full, nq * L::kTileBytes);
-      for (int t = 0; t < 2; ++t) {
-        if (!act[t]) continue;
-        for (int bx = 0; bx < L::kBoxes; ++bx)
-          tma_load_3d(smem + (t ? L::kQ1 : L::kQ0) + bx * L::kBoxBytes, &qmap, q_full, bx * 64,
-                      (qt0 + t) * kPfTile, bh);
-      }
-      // K(j) before V(j): stages free in the order K(j-2) (after S(j-2)), V(j-2) (after PV(j-2))
-      for (int j = J0; j <= J1; ++j) {
-        const int i = j - J0, s = i % kPfStages;
-        const bool from_halo = j < halo_tiles;
-        const CUtensorMap* km = from_halo ? &khmap : &kmap;
-        const CUtensorMap* vm = from_halo ? &vhmap : &vmap;
-        const int y = from_halo ? j * kPfTile : (j - halo_tiles) * kPfTile;
-        if (i >= kPfStages && !mbar_wait_bounded(&k_empty[s], ((i / kPfStages) - 1) & 1)) break;
-        mbar_arrive_expect_tx(&k_full[s], L::kTileBytes);
-        for (int bx = 0; bx < L::kBoxes; ++bx)
-          tma_load_3d(smem + L::kK + s * L::kTileBytes + bx * L::kBoxBytes, km, &k_full[s], bx * 64, y, bh);
-        if (i >= kPfStages && !mbar_wait_bounded(&v_empty[s], ((i / kPfStages) - 1) & 1)) break;
-        mbar_arrive_expect_tx(&v_full[s], L::kTileBytes);
-        for (int bx = 0; bx < L::kBoxes; ++bx)
-          tma_load_3d(smem + L::kV + s * L::kTileBytes + bx * L::kBoxBytes, vm, &v_full[s], bx * 64, y, bh);
+      int kv_i = 0;             // running K/V tile counter
+      int q_loads[2] = {0, 0};  // running Q_t loads
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < a.n_items; w += gridDim.x) {
+        const PfItem I = pf_item(a, w);
+        if (!I.act[0] && !I.act[1]) continue;
+        // Q_t: after every S_t product of the previous item completed (Q_0 frees a step
+        // before Q_1, so it loads while the previous item finishes)
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!I.act[t]) continue;
+          if (q_loads[t] > 0 && !mbar_wait_bounded(&q_empty[t], (q_loads[t] - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&q_full[t], L::kTileBytes);
+          for (int bx = 0; bx < L::kBoxes; ++bx)
+            tma_load_3d(smem + (t ? L::kQ1 : L::kQ0) + bx * L::kBoxBytes, &qmap, &q_full[t], bx * 64,
+                        (I.qt0 + t) * kPfTile, I.bh);
+          ++q_loads[t];
+        }
+        // K(j) before V(j): stages free in the order K(j-2) (after S(j-2)), V(j-2) (after PV(j-2))
+        for (int j = I.J0; j <= I.J1; ++j) {
+          const int i = kv_i++, s = i % kPfStages;
+          const bool from_halo = j < halo_tiles;
+          const CUtensorMap* km = from_halo ? &khmap : &kmap;
+          const CUtensorMap* vm = from_halo ? &vhmap : &vmap;
+          const int y = from_halo ? j * kPfTile : (j - halo_tiles) * kPfTile;
+          if (i >= kPfStages && !mbar_wait_bounded(&k_empty[s], ((i / kPfStages) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[s], L::kTileBytes);
+          for (int bx = 0; bx < L::kBoxes; ++bx)
+            tma_load_3d(smem + L::kK + s * L::kTileBytes + bx * L::kBoxBytes, km, &k_full[s], bx * 64, y, I.bh);
+          if (i >= kPfStages && !mbar_wait_bounded(&v_empty[s], ((i / kPfStages) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&v_full[s], L::kTileBytes);
+          for (int bx = 0; bx < L::kBoxes; ++bx)
+            tma_load_3d(smem + L::kV + s * L::kTileBytes + bx * L::kBoxBytes, vm, &v_full[s], bx * 64, y, I.bh);
+        }
       }
     }
   } else if (warp == 1) {
@@ -294,33 +337,46 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // elected lane (always the same one) issues each batch of tcgen05.mma and the
     // commits that track them.  Issuing from a single-lane branch instead costs about
     // twice the 64 cycles a 128x128x16 product takes on the tensor cores.
-    if (act[0] || act[1]) {
-      constexpr uint32_t kIdQK = instr_desc_f16(PfFmt<T>::kFmt, kPfTile, kPfTile, 0, 0);
-      constexpr uint32_t kIdPV = instr_desc_f16(PfFmt<T>::kFmt, kPfTile, D, 0, 1);
-      // descriptor start addresses are in 16-byte units in the low 14 bits; smem offsets
-      // below 256 KB never carry out of that field
-      const uint64_t q_desc[2] = {smem_desc(smem_u32(smem + L::kQ0), 16, 1024),
-                                  smem_desc(smem_u32(smem + L::kQ1), 16, 1024)};
-      const uint64_t k_desc = smem_desc(smem_u32(smem + L::kK), 16, 1024);
-      const uint64_t v_desc = smem_desc(smem_u32(smem + L::kV), L::kBoxBytes, 1024);
-      const uint32_t s_col[2] = {0u, 128u}, o_col[2] = {256u, 384u};
-      bool ok = mbar_wait_bounded(q_full, 0);
-      int it[2] = {0, 0};
+    constexpr uint32_t kIdQK = instr_desc_f16(PfFmt<T>::kFmt, kPfTile, kPfTile, 0, 0);
+    constexpr uint32_t kIdPV = instr_desc_f16(PfFmt<T>::kFmt, kPfTile, D, 0, 1);
+    // descriptor start addresses are in 16-byte units in the low 14 bits; smem offsets
+    // below 256 KB never carry out of that field
+    const uint64_t q_desc[2] = {smem_desc(smem_u32(smem + L::kQ0), 16, 1024),
+                                smem_desc(smem_u32(smem + L::kQ1), 16, 1024)};
+    const uint64_t k_desc = smem_desc(smem_u32(smem + L::kK), 16, 1024);
+    const uint64_t v_desc = smem_desc(smem_u32(smem + L::kV), L::kBoxBytes, 1024);
+    const uint32_t s_col[2] = {0u, 128u}, o_col[2] = {256u, 384u};
+    auto commit = [&](uint64_t* bar) {
+      if (elect_one_sync()) tc_commit(bar);
+      __syncwarp();
+    };
+    // running counters: K/V tiles before this item, P signals per tile, items per tile
+    int kv_base = 0;
+    int it[2] = {0, 0}, o_uses[2] = {0, 0};
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < a.n_items; w += gridDim.x) {
+      const PfItem I = pf_item(a, w);
+      if (!I.act[0] && !I.act[1]) continue;
+      const int J0 = I.J0, J1 = I.J1;
+      bool q_ready[2] = {false, false};
+      auto stage_of = [&](int j) { return (kv_base + j - J0) % kPfStages; };
       int k_ready = J0 - 1, v_ready = J0 - 1;  // last key tile whose K / V has been waited on
       auto wait_tile = [&](uint64_t* full, int& ready, int j) -> bool {
         if (j <= ready) return true;
-        const int i = j - J0;
+        const int i = kv_base + j - J0;
         if (!mbar_wait_bounded(&full[i % kPfStages], (i / kPfStages) & 1)) return false;
         ready = j;
         tc_fence_after();
         return true;
       };
-      auto commit = [&](uint64_t* bar) {
-        if (elect_one_sync()) tc_commit(bar);
-        __syncwarp();
-      };
-      auto issue_s = [&](int t, int j) {
-        const uint64_t kd = k_desc + ((((j - J0) % kPfStages) * L::kTileBytes) >> 4);
+      // S_t = Q_t K(j)^T; the last one of the item frees Q_t for the next item
+      auto issue_s = [&](int t, int j) -> bool {
+        if (!q_ready[t]) {
+          if (!mbar_wait_bounded(&q_full[t], o_uses[t] & 1)) return false;
+          tc_fence_after();
+          q_ready[t] = true;
+        }
+        const uint64_t kd = k_desc + ((stage_of(j) * L::kTileBytes) >> 4);
         if (elect_one_sync()) {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
@@ -328,8 +384,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mma_ss(tmem + s_col[t], q_desc[t] + off, kd + off, kIdQK, kk > 0 ? 1u : 0u);
           }
           tc_commit(&s_full[t]);
+          if (j == I.hi[t]) tc_commit(&q_empty[t]);
         }
         __syncwarp();
+        return true;
       };
       // O_t += P_t V over key rows [16*k0, 16*k1) of the tile (P columns 8*k0 ..)
       auto issue_pv = [&](int t, uint64_t vd, int k0, int k1, bool first) {
@@ -343,22 +401,29 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       };
       // prologue: S_t(J0)
       if (ok && wait_tile(k_full, k_ready, J0)) {
-        for (int t = 0; t < 2; ++t)
-          if (act[t] && lo[t] <= J0 && J0 <= hi[t]) issue_s(t, J0);
-        commit(&k_empty[0]);
+        for (int t = 0; t < 2 && ok; ++t)
+          if (I.act[t] && I.lo[t] <= J0 && J0 <= I.hi[t]) ok = issue_s(t, J0);
+        commit(&k_empty[stage_of(J0)]);
       } else {
         ok = false;
       }
       for (int j = J0; ok && j <= J1; ++j) {
-        const uint64_t vd = v_desc + ((((j - J0) % kPfStages) * L::kTileBytes) >> 4);
+        const uint64_t vd = v_desc + ((stage_of(j) * L::kTileBytes) >> 4);
         for (int t = 0; t < 2 && ok; ++t) {
-          if (act[t] && lo[t] <= j && j <= hi[t]) {
+          if (I.act[t] && I.lo[t] <= j && j <= I.hi[t]) {
+            const bool first = j == I.lo[t];
+            // the first product of an item overwrites O_t: the previous item's O_t must
+            // have been read out
+            if (first && o_uses[t] > 0 && !mbar_wait_bounded(&o_empty[t], (o_uses[t] - 1) & 1)) {
+              ok = false;
+              break;
+            }
             if (!mbar_wait_bounded(&p_half[t], it[t] & 1) || !wait_tile(v_full, v_ready, j)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_pv(t, vd, 0, kPfTile / 32, it[t] == 0);
+            issue_pv(t, vd, 0, kPfTile / 32, first);
             if (!mbar_wait_bounded(&p_full[t], it[t] & 1)) {
               ok = false;
               break;
@@ -366,25 +431,29 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             tc_fence_after();
             issue_pv(t, vd, kPfTile / 32, kPfTile / 16, false);
             ++it[t];
-            if (j == hi[t]) commit(&o_final[t]);
+            if (j == I.hi[t]) commit(&o_final[t]);
           }
-          if (act[t] && lo[t] <= j + 1 && j + 1 <= hi[t]) {
-            if (!wait_tile(k_full, k_ready, j + 1)) {
+          if (I.act[t] && I.lo[t] <= j + 1 && j + 1 <= I.hi[t]) {
+            if (!wait_tile(k_full, k_ready, j + 1) || !issue_s(t, j + 1)) {
               ok = false;
               break;
             }
-            issue_s(t, j + 1);
           }
         }
         // V(j) is free after PV(j); K(j+1) after both S(j+1) (the key-tile ranges of the two
         // query tiles overlap, so every j+1 <= J1 was used by at least one of them)
-        commit(&v_empty[(j - J0) % kPfStages]);
-        if (ok && j + 1 <= J1) commit(&k_empty[(j + 1 - J0) % kPfStages]);
+        commit(&v_empty[stage_of(j)]);
+        if (ok && j + 1 <= J1) commit(&k_empty[stage_of(j + 1)]);
       }
-      // every issued MMA completes before TMEM is released
-      commit(mma_done);
-      mbar_wait_bounded(mma_done, 0);
+      if (!ok) break;
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+        if (I.act[t]) ++o_uses[t];
+      kv_base += J1 - J0 + 1;
     }
+    // every issued MMA completes before TMEM is released
+    commit(mma_done);
+    mbar_wait_bounded(mma_done, 0);
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- softmax
     const int quad = warp & 3;
@@ -395,14 +464,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     float* xsum = xmax + 4 * kPfTile;                       // [tile][half][row]
     const uint32_t pair_bar = 1 + quad;                     // named barrier of warps 4+quad, 8+quad
     constexpr int kHalfD = D / 2;
-    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-    int its[2] = {0, 0};
+    // running counters: S signals per tile, exchanges (parity of xmax), items per tile
+    int its[2] = {0, 0}, o_cnt[2] = {0, 0};
     int step = 0;
     bool ok = true;
-    for (int j = J0; ok && j <= J1; ++j) {
+    for (int w = blockIdx.x; ok && w < a.n_items; w += gridDim.x) {
+    const PfItem I = pf_item(a, w);
+    if (!I.act[0] && !I.act[1]) continue;
+    const int qt0 = I.qt0;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    int itl[2] = {0, 0};  // steps of this item per tile
+    for (int j = I.J0; ok && j <= I.J1; ++j) {
 #pragma unroll
       for (int t = 0; t < 2; ++t) {  // unrolled: per-tile state stays in registers
-        if (!ok || !(act[t] && lo[t] <= j && j <= hi[t])) continue;
+        if (!ok || !(I.act[t] && I.lo[t] <= j && j <= I.hi[t])) continue;
         const bool got = mbar_wait_bounded(&s_full[t], its[t] & 1);
         tc_fence_after();
         const uint32_t s_addr = lane_base + (t ? 128u : 0u);
@@ -458,7 +533,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             // move the running max; rescale this warp's half of O (complete: S_t(j) was
             // issued after O_t(j-1))
             const float alpha = fast_exp2(m_run[t] - mt);  // 0 when m_run = -inf
-            if (its[t] > 0 && m_run[t] > -INFINITY) {
+            if (itl[t] > 0 && m_run[t] > -INFINITY) {
 #pragma unroll 1
               for (int c = 0; c < kHalfD / 16; ++c) {
                 uint32_t o[16];
@@ -499,43 +574,65 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           l_run[t] += (ls[0].x + ls[0].y) + (ls[1].x + ls[1].y);
         }
         ++its[t];
+        ++itl[t];
         ++step;
       }
     }
-    // epilogue: O / l -> global, this warp's half of the columns; the two partial row
-    // sums meet in shared memory (every warp of a pair reaches this barrier once)
+    if (!ok) break;
+    // epilogue: O / l -> global, this warp's half of the columns.  The two partial row
+    // sums meet in shared memory; the pair's barrier also ANDs the outcome of the waits
+    // for the last products, so both warps leave together if one gave up.
 #pragma unroll
     for (int t = 0; t < 2; ++t) xsum[t * 2 * kPfTile + chalf * kPfTile + r] = l_run[t];
-    named_barrier_sync(pair_bar, 64);
+    bool got_o = true;
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+      if (I.act[t]) got_o = mbar_wait_bounded(&o_final[t], o_cnt[t] & 1) && got_o;
+    ok = named_barrier_and(pair_bar, 64, got_o);
+    if (!ok) break;
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      if (!ok || !act[t]) continue;
-      if (!mbar_wait_bounded(&o_final[t], 0)) {
-        ok = false;
-        continue;
-      }
+      if (!I.act[t]) continue;
       tc_fence_after();
       const float l = l_run[t] + xsum[t * 2 * kPfTile + (1 - chalf) * kPfTile + r];
       const int q = (qt0 + t) * kPfTile + r;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* orow = static_cast<T*>(a.out) + (static_cast<int64_t>(bh) * a.S + q) * D + kHalfD * chalf;
       const uint32_t o_addr = lane_base + (t ? 384u : 256u) + kHalfD * chalf;
+      // 32 output columns at a time: each thread writes its row into the warp's staging
+      // tile, then the warp stores 8 rows x 64 contiguous bytes per instruction
+      unsigned char* stg = smem + L::kStage + (warp - 4) * 32 * L::kStageRow;
+      const int q_row0 = (qt0 + t) * kPfTile + quad * 32;  // the warp's first query row
 #pragma unroll 1
       for (int c = 0; c < kHalfD / 32; ++c) {
         uint32_t o[32];
         SPA_TMEM_LD32(o_addr + 32 * c, o);
         tmem_wait_ld();
-        if (q < a.row1) {
-          uint32_t pk[16];
+        uint32_t pk[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            pk[e] = PfFmt<T>::pack(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
-          uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+        for (int e = 0; e < 16; ++e)
+          pk[e] = PfFmt<T>::pack(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+        uint4* mine = reinterpret_cast<uint4*>(stg + lane * L::kStageRow);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        for (int v = 0; v < 4; ++v) mine[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int row = k * 8 + (lane >> 2), part = lane & 3;
+          const int qr = q_row0 + row;
+          const uint4 v = *reinterpret_cast<const uint4*>(stg + row * L::kStageRow + part * 16);
+          if (qr < a.row1)
+            *reinterpret_cast<uint4*>(static_cast<T*>(a.out) + (static_cast<int64_t>(I.bh) * a.S + qr) * D +
+                                      kHalfD * chalf + 32 * c + part * 8) = v;
         }
+        __syncwarp();
       }
+      // O_t has been read: the next item's first product may overwrite it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[t]);
+      ++o_cnt[t];
     }
+    }  // items
   }
   tc_fence_before();
   __syncthreads();
@@ -550,7 +647,6 @@ inline bool prefill_sm100_supported(const PrefillArgs& a, int dtype) {
   if (dtype != SPA_BF16 && dtype != SPA_F16) return false;
   if (a.D != 128 && a.D != 64) return false;
   if (a.halo % kPfTile != 0 || a.row0 % kPfTile != 0) return false;
-  if (static_cast<int64_t>(a.B) * a.H > 65535) return false;
   const uintptr_t m = reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
                       reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.out) |
                       reinterpret_cast<uintptr_t>(a.k_halo) | reinterpret_cast<uintptr_t>(a.v_halo);
@@ -582,15 +678,20 @@ int launch_prefill_sm100(const PrefillArgs& a, int dtype, cudaStream_t st) {
   t.H = a.H;
   const int tiles = (a.row1 - 1) / kPfTile - a.row0 / kPfTile + 1;
   t.n_pairs = (tiles + 1) / 2;
+  const int64_t items = static_cast<int64_t>(t.n_pairs) * static_cast<int64_t>(bh);
+  if (items > 0x7fffffff) return SPA_ERR_UNSUPPORTED;
+  t.n_items = static_cast<int>(items);
+  // persistent: one CTA per SM (the kernel's shared memory and TMEM admit one)
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, device_sm_count()));
   t.scale_log2 = a.scale * 1.4426950408889634f;
   if (a.D == 128) {
     auto kern = prefill_tc_kernel<T, 128>;
     SPA_CHECK_CUDA(spa_set_smem_once(kern, PfSmem<128>::kBytes));
-    kern<<<dim3(t.n_pairs, static_cast<unsigned>(bh)), kPfThreads, PfSmem<128>::kBytes, st>>>(qm, km, vm, khm, vhm, t);
+    kern<<<grid, kPfThreads, PfSmem<128>::kBytes, st>>>(qm, km, vm, khm, vhm, t);
   } else {
     auto kern = prefill_tc_kernel<T, 64>;
     SPA_CHECK_CUDA(spa_set_smem_once(kern, PfSmem<64>::kBytes));
-    kern<<<dim3(t.n_pairs, static_cast<unsigned>(bh)), kPfThreads, PfSmem<64>::kBytes, st>>>(qm, km, vm, khm, vhm, t);
+    kern<<<grid, kPfThreads, PfSmem<64>::kBytes, st>>>(qm, km, vm, khm, vhm, t);
   }
   SPA_CHECK_CUDA(cudaGetLastError());
   return SPA_OK;
