@@ -236,21 +236,6 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
                      __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(u.y) << 23)));
 }
 
-// Named barrier over `count` threads (whole warps); returns the AND of `pred` over them.
-__device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t count, bool pred) {
-  uint32_t out;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
-      "barrier.cta.red.and.pred p, %2, %3, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(out)
-      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
-      : "memory");
-  return out != 0;
-}
-__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t count) {
-  asm volatile("barrier.cta.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 // True in exactly one lane of the (converged, full) warp: the lowest one.
 __device__ __forceinline__ bool elect_one_sync() {
   uint32_t pred;

@@ -11,19 +11,19 @@
 //               rings with separate full/empty barriers: K(j) is released as soon as
 //               both S(j) products complete, so K(j+2) streams in while V(j) is still
 //               being multiplied (about one KV-tile period of lead instead of none)
-//   warp 1      MMA issuer (one thread): S_t = Q_t K^T (SS form, both operands in
-//               shared memory, K-major), O_t += P_t V (TS form: P read from TMEM,
-//               V from shared memory, MN-major)
-//   warps 4-11  softmax, both query tiles in turn: warp w reaches TMEM lanes
-//               [32*(w%4), 32*(w%4)+32) (= rows), warps 4-7 take key columns 0-63 and
-//               warps 8-11 columns 64-127; the two warps of a row range exchange their
-//               partial row maxima through shared memory (a 64-thread named barrier)
+//   warp 1      MMA issuer (whole warp, one elected lane issues): S_t = Q_t K^T (SS
+//               form, both operands in shared memory, K-major), O_t += P_t V (TS form:
+//               P read from TMEM, V from shared memory, MN-major)
+//   warps 4-7   softmax of query tile 0, warps 8-11 of query tile 1: thread = row =
+//               TMEM lane (warp w reaches lanes [32*(w%4), 32*(w%4)+32)); a thread holds
+//               its 128 scores in registers (setmaxnreg gives the softmax warpgroups 184
+//               registers and the control warpgroup 128)
 //   warps 2-3   idle
 //
 // TMEM (512 columns): S_0 [0,128), S_1 [128,256), O_0 [256,256+D), O_1 [384,384+D).
-// P_t (bf16 pairs) overwrites the first 64 columns of S_t once S_t is in registers: keys
-// 0-63 (from warps 4-7) and keys 64-127 (warps 8-11) each signal their own barrier, and
-// the PV product of one half starts as soon as that half is stored.
+// P_t (bf16 pairs) overwrites the first 64 columns of S_t once S_t is in registers, in two
+// halves (keys 0-63, then 64-127) with a barrier each, so the PV product of the first half
+// runs while the softmax warps compute the second.
 // The MMA warp interleaves O_0(j), S_0(j+1), O_1(j), S_1(j+1), so the softmax of one
 // tile overlaps the other tile's tensor-core work.  The running max is only moved
 // (and O rescaled in TMEM) when a tile's max exceeds it by more than 2^8.
@@ -41,6 +41,10 @@ namespace spa {
 constexpr int kPfTile = 128;
 constexpr int kPfStages = 2;
 constexpr int kPfThreads = 384;
+constexpr int kPfRegsCtl = 128;      // warps 0-3 (TMA, MMA, idle) after setmaxnreg.dec
+constexpr int kPfRegsSoftmax = 184;  // warps 4-11 after setmaxnreg.inc
+static_assert(128 * kPfRegsCtl + 256 * kPfRegsSoftmax <= kPfThreads * 168, "register split exceeds the launch");
+static_assert(kPfRegsCtl + 2 * kPfRegsSoftmax <= 512, "register split exceeds a sub-partition");
 constexpr float kPfRescaleThreshold = 8.0f;  // log2 units
 
 struct PfTcArgs {
@@ -58,14 +62,10 @@ struct PfSmem {
   static constexpr int kQ1 = kTileBytes;
   static constexpr int kK = 2 * kTileBytes;
   static constexpr int kV = kK + kPfStages * kTileBytes;
-  // softmax exchange: partial row maxima [2 step parities][2 column halves][128 rows] and
-  // partial row sums [2 tiles][2 column halves][128 rows], fp32
-  static constexpr int kX = kV + kPfStages * kTileBytes;
-  static constexpr int kXBytes = (2 * 2 * kPfTile + 2 * 2 * kPfTile) * 4;
   // epilogue staging: per softmax warp 32 rows x 32 output columns (16-bit), rows padded
   // to 80 bytes so the row-wise writes and the column-wise reads avoid bank conflicts
   static constexpr int kStageRow = 80;
-  static constexpr int kStage = kX + kXBytes;
+  static constexpr int kStage = kV + kPfStages * kTileBytes;
   static constexpr int kStageBytes = 8 * 32 * kStageRow;
   static constexpr int kBar = kStage + kStageBytes;
   // barriers: q_full[2], k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_half[2],
@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&p_half[t], 4);
       mbar_init(&p_full[t], 4);
       mbar_init(&o_final[t], 1);
-      mbar_init(&o_empty[t], 8);
+      mbar_init(&o_empty[t], 4);
       mbar_init(&q_full[t], 1);
       mbar_init(&q_empty[t], 1);
     }
@@ -281,6 +281,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Register split (whole warpgroups, each at one instruction address heading all of its
+  // role code): launch 384 x 168 = 64512; after: 128 x 128 + 256 x 184 = 63488, and per SM
+  // sub-partition (one warp of each group) 128 + 2 x 184 = 496 <= 512 registers per lane.
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPfRegsCtl));
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
@@ -454,156 +459,125 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // every issued MMA completes before TMEM is released
     commit(mma_done);
     mbar_wait_bounded(mma_done, 0);
-  } else if (warp >= 4) {
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPfRegsSoftmax));
     // ---------------------------------------------------------------- softmax
+    // warps 4-7: query tile 0, warps 8-11: query tile 1; thread = row = TMEM lane
+    const int t = (warp - 4) >> 2;
     const int quad = warp & 3;
-    const int chalf = (warp - 4) >> 2;  // key columns [64*chalf, 64*chalf + 64)
-    const int r = quad * 32 + lane;     // row within the tile == TMEM lane
+    const int r = quad * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    float* xmax = reinterpret_cast<float*>(smem + L::kX);  // [parity][half][row]
-    float* xsum = xmax + 4 * kPfTile;                       // [tile][half][row]
-    const uint32_t pair_bar = 1 + quad;                     // named barrier of warps 4+quad, 8+quad
-    constexpr int kHalfD = D / 2;
-    // running counters: S signals per tile, exchanges (parity of xmax), items per tile
-    int its[2] = {0, 0}, o_cnt[2] = {0, 0};
-    int step = 0;
+    const uint32_t s_addr = lane_base + (t ? 128u : 0u);
+    const uint32_t o_addr = lane_base + (t ? 384u : 256u);
+    unsigned char* stg = smem + L::kStage + (warp - 4) * 32 * L::kStageRow;
+    int its = 0, o_cnt = 0;  // running: S signals of tile t, items with tile t
     bool ok = true;
     for (int w = blockIdx.x; ok && w < a.n_items; w += gridDim.x) {
-    const PfItem I = pf_item(a, w);
-    if (!I.act[0] && !I.act[1]) continue;
-    const int qt0 = I.qt0;
-    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-    int itl[2] = {0, 0};  // steps of this item per tile
-    for (int j = I.J0; ok && j <= I.J1; ++j) {
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {  // unrolled: per-tile state stays in registers
-        if (!ok || !(I.act[t] && I.lo[t] <= j && j <= I.hi[t])) continue;
-        const bool got = mbar_wait_bounded(&s_full[t], its[t] & 1);
+      const PfItem I = pf_item(a, w);
+      if (!I.act[t]) continue;
+      const int qt = I.qt0 + t;
+      const int qc = qt * kPfTile + r + a.halo;  // this row's query position
+      const int tile_q0 = qt * kPfTile + a.halo;
+      float m_run = -INFINITY, l_run = 0.f;
+      int itl = 0;
+      for (int j = I.lo[t]; j <= I.hi[t]; ++j) {
+        if (!mbar_wait_bounded(&s_full[t], its & 1)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t s_addr = lane_base + (t ? 128u : 0u);
-        const uint32_t o_addr = lane_base + (t ? 384u : 256u) + kHalfD * chalf;
-        const int qc = (qt0 + t) * kPfTile + r + a.halo;  // this row's query position
         const int kc0 = j * kPfTile;
-        const int tile_q0 = (qt0 + t) * kPfTile + a.halo;
         const bool full_tile =
             kc0 + kPfTile - 1 <= tile_q0 && kc0 > tile_q0 + kPfTile - 1 - a.W && kc0 + kPfTile <= a.halo + a.S;
-        {
-          if (got && !full_tile) {
-            // partial tile: scores outside [kmin, kmax] (causal, window, sequence end) are
-            // set to -inf in TMEM first, so one code path serves every tile
-            const int kmax = min(qc, a.halo + a.S - 1) - kc0 - 64 * chalf;
-            const int kmin = qc - a.W + 1 - kc0 - 64 * chalf;
+        if (!full_tile) {
+          // scores outside [kmin, kmax] (causal, window, sequence end) become -inf in TMEM
+          const int kmax = min(qc, a.halo + a.S - 1) - kc0;
+          const int kmin = qc - a.W + 1 - kc0;
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-              uint32_t mk[16];
-              SPA_TMEM_LD16(s_addr + 64 * chalf + 16 * c, mk);
+          for (int c = 0; c < 8; ++c) {
+            uint32_t mk[16];
+            SPA_TMEM_LD16(s_addr + 16 * c, mk);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) mk[e] = (16 * c + e >= kmin && 16 * c + e <= kmax) ? mk[e] : 0xff800000u;
+            SPA_TMEM_ST16(s_addr + 16 * c, mk);
+          }
+          tmem_wait_st();
+        }
+        // the whole row of S_t in registers: one TMEM round trip
+        uint32_t sv[kPfTile];
+        SPA_TMEM_LD32(s_addr, sv);
+        SPA_TMEM_LD32(s_addr + 32, (sv + 32));
+        SPA_TMEM_LD32(s_addr + 64, (sv + 64));
+        SPA_TMEM_LD32(s_addr + 96, (sv + 96));
+        tmem_wait_ld();
+        float mx[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) mx[c] = fmaxf(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1]));
+#pragma unroll
+        for (int e = 16; e < kPfTile; e += 16) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            mx[c] = fmax3(mx[c], __uint_as_float(sv[e + 2 * c]), __uint_as_float(sv[e + 2 * c + 1]));
+        }
+        const float mt =
+            fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7])) * a.scale_log2;
+        if (mt > m_run + kPfRescaleThreshold || (m_run == -INFINITY && mt > -INFINITY)) {
+          // move the running max; rescale O (complete: S_t(j) was issued after O_t(j-1))
+          const float alpha = fast_exp2(m_run - mt);  // 0 when m_run = -inf
+          if (itl > 0 && m_run > -INFINITY) {
+#pragma unroll 1
+            for (int c = 0; c < D / 16; ++c) {
+              uint32_t o[16];
+              SPA_TMEM_LD16(o_addr + 16 * c, o);
               tmem_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 16; ++e) mk[e] = (16 * c + e >= kmin && 16 * c + e <= kmax) ? mk[e] : 0xff800000u;
-              SPA_TMEM_ST16(s_addr + 64 * chalf + 16 * c, mk);
+              for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              SPA_TMEM_ST16(o_addr + 16 * c, o);
             }
-            tmem_wait_st();
           }
-          uint32_t sv[64];
-          float pm = -INFINITY;
-          if (got) {
-            SPA_TMEM_LD32(s_addr + 64 * chalf, sv);
-            SPA_TMEM_LD32(s_addr + 64 * chalf + 32, (sv + 32));
-            tmem_wait_ld();
-            // partial row max of the raw scores (scale > 0 commutes with max), 8 chains
-            float mx[8];
+          l_run *= alpha;
+          m_run = mt;
+        }
+        const float neg_mu = m_run == -INFINITY ? 0.f : -m_run;
+        const float sc = a.scale_log2;
+        // P = exp2(s*scale - m) as 16-bit pairs into columns [0, 64) of S_t: keys 0-63 into
+        // [0, 32), signal, then keys 64-127 into [32, 64).  One pair in four on the FMA pipes.
+        const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(neg_mu, neg_mu);
+        float2 ls[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-            for (int c = 0; c < 8; ++c) mx[c] = fmaxf(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1]));
-#pragma unroll
-            for (int e = 16; e < 64; e += 16) {
-#pragma unroll
-              for (int c = 0; c < 8; ++c)
-                mx[c] = fmax3(mx[c], __uint_as_float(sv[e + 2 * c]), __uint_as_float(sv[e + 2 * c + 1]));
-            }
-            pm = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7]));
-          }
-          // exchange with the other column half; both warps leave the loop together if
-          // either one's wait gave up (the barrier also reduces the ok flags)
-          xmax[(step & 1) * 2 * kPfTile + chalf * kPfTile + r] = pm;
-          ok = named_barrier_and(pair_bar, 64, got);
-          if (!ok) continue;
-          const float other = xmax[(step & 1) * 2 * kPfTile + (1 - chalf) * kPfTile + r];
-          const float mt = fmaxf(pm, other) * a.scale_log2;
-          if (mt > m_run[t] + kPfRescaleThreshold || (m_run[t] == -INFINITY && mt > -INFINITY)) {
-            // move the running max; rescale this warp's half of O (complete: S_t(j) was
-            // issued after O_t(j-1))
-            const float alpha = fast_exp2(m_run[t] - mt);  // 0 when m_run = -inf
-            if (itl[t] > 0 && m_run[t] > -INFINITY) {
-#pragma unroll 1
-              for (int c = 0; c < kHalfD / 16; ++c) {
-                uint32_t o[16];
-                SPA_TMEM_LD16(o_addr + 16 * c, o);
-                tmem_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                SPA_TMEM_ST16(o_addr + 16 * c, o);
-              }
-            }
-            l_run[t] *= alpha;
-            m_run[t] = mt;
-          }
-          const float neg_mu = m_run[t] == -INFINITY ? 0.f : -m_run[t];
-          const float sc = a.scale_log2;
-          // P = exp2(s*scale - m) as 16-bit pairs into columns [32*chalf, 32*chalf + 32) of
-          // S_t; those scores were loaded before the exchange barrier.  One pair in four
-          // takes its exponentials on the FMA pipes (exp2_poly2): the MUFU unit evaluates
-          // 16 exponentials per SM per clock, the rate at which the tensor cores consume
-          // scores at head_dim 128.  Masked columns hold -inf: ex2 gives 0, exp2_poly2
-          // gives 2^-125 (below any contribution a valid key makes).
-          const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(neg_mu, neg_mu);
-          float2 ls[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        for (int h = 0; h < 2; ++h) {
           uint32_t pk[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const float2 x =
-                ffma2(make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2, nm2);
+            const float2 x = ffma2(
+                make_float2(__uint_as_float(sv[64 * h + 2 * e]), __uint_as_float(sv[64 * h + 2 * e + 1])), sc2, nm2);
             const float2 pr = ((e & 3) == 3) ? exp2_poly2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
             ls[e & 1] = fadd2(ls[e & 1], pr);
             pk[e] = PfFmt<T>::pack(pr.x, pr.y);
           }
-          SPA_TMEM_ST32(s_addr + 32 * chalf, pk);
+          SPA_TMEM_ST32(s_addr + 32 * h, pk);
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(chalf == 0 ? &p_half[t] : &p_full[t]);
-          l_run[t] += (ls[0].x + ls[0].y) + (ls[1].x + ls[1].y);
+          if (lane == 0) mbar_arrive(h == 0 ? &p_half[t] : &p_full[t]);
         }
-        ++its[t];
-        ++itl[t];
-        ++step;
+        l_run += (ls[0].x + ls[0].y) + (ls[1].x + ls[1].y);
+        ++its;
+        ++itl;
       }
-    }
-    if (!ok) break;
-    // epilogue: O / l -> global, this warp's half of the columns.  The two partial row
-    // sums meet in shared memory; the pair's barrier also ANDs the outcome of the waits
-    // for the last products, so both warps leave together if one gave up.
-#pragma unroll
-    for (int t = 0; t < 2; ++t) xsum[t * 2 * kPfTile + chalf * kPfTile + r] = l_run[t];
-    bool got_o = true;
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-      if (I.act[t]) got_o = mbar_wait_bounded(&o_final[t], o_cnt[t] & 1) && got_o;
-    ok = named_barrier_and(pair_bar, 64, got_o);
-    if (!ok) break;
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      if (!I.act[t]) continue;
+      if (!ok) break;
+      // epilogue: O / l -> global through the warp's staging tile
+      if (!mbar_wait_bounded(&o_final[t], o_cnt & 1)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      const float l = l_run[t] + xsum[t * 2 * kPfTile + (1 - chalf) * kPfTile + r];
-      const int q = (qt0 + t) * kPfTile + r;
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      const uint32_t o_addr = lane_base + (t ? 384u : 256u) + kHalfD * chalf;
-      // 32 output columns at a time: each thread writes its row into the warp's staging
-      // tile, then the warp stores 8 rows x 64 contiguous bytes per instruction
-      unsigned char* stg = smem + L::kStage + (warp - 4) * 32 * L::kStageRow;
-      const int q_row0 = (qt0 + t) * kPfTile + quad * 32;  // the warp's first query row
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const int q_row0 = qt * kPfTile + quad * 32;
 #pragma unroll 1
-      for (int c = 0; c < kHalfD / 32; ++c) {
+      for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         SPA_TMEM_LD32(o_addr + 32 * c, o);
         tmem_wait_ld();
@@ -621,18 +595,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           const int qr = q_row0 + row;
           const uint4 v = *reinterpret_cast<const uint4*>(stg + row * L::kStageRow + part * 16);
           if (qr < a.row1)
-            *reinterpret_cast<uint4*>(static_cast<T*>(a.out) + (static_cast<int64_t>(I.bh) * a.S + qr) * D +
-                                      kHalfD * chalf + 32 * c + part * 8) = v;
+            *reinterpret_cast<uint4*>(static_cast<T*>(a.out) + (static_cast<int64_t>(I.bh) * a.S + qr) * D + 32 * c +
+                                      part * 8) = v;
         }
         __syncwarp();
       }
-      // O_t has been read: the next item's first product may overwrite it
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&o_empty[t]);
-      ++o_cnt[t];
+      ++o_cnt;
     }
-    }  // items
   }
   tc_fence_before();
   __syncthreads();
