@@ -61,7 +61,6 @@ PROTOTYPES = {
     "spa_version": (ctypes.c_char_p, []),
     "spa_device_error": (_i, [ctypes.POINTER(ctypes.c_uint32)]),
     "spa_last_error": (ctypes.c_char_p, []),
-    "spa_debug_exp2_poly": (_i, [_vp, _vp, ctypes.c_int64, _vp]),
     "spa_debug_wait_timeout": (_i, [ctypes.c_longlong, _vp]),
     "spa_summaries_build": (_i, [_KV, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp]),
     "spa_router_topm": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _d, _i, _vp, _vp, _vp]),

@@ -214,28 +214,6 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
   return d;
 }
 
-// 2^x for a pair of lanes on the FMA/ALU pipes (no MUFU), for x <= 126: x = n + f with
-// n = round(x) and f in [-1/2, 1/2] (Cody-Waite style split: adding 1.5*2^23 leaves n in
-// the low mantissa bits), 2^f by a cubic minimax polynomial (Remez exchange on the
-// relative error, coefficients from derive_exp2_poly.py: max relative error 7.5e-5, below
-// half an ulp of a bf16 or fp16 probability), and 2^n added into the exponent field.  x
-// is clamped at -125 so the exponent field stays normal; 2^-125 stands in for 0.
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-  x.x = fmaxf(x.x, -125.0f);
-  x.y = fmaxf(x.y, -125.0f);
-  // u = -(x + 1.5*2^23) rounded = -t: the low mantissa bits hold n, the sign bit is
-  // shifted out below; u + 1.5*2^23 = -n exactly, so f = x - n exactly.
-  const float2 u = ffma2(x, make_float2(-1.0f, -1.0f), make_float2(-kShift, -kShift));
-  const float2 f = fadd2(x, fadd2(u, make_float2(kShift, kShift)));
-  float2 p = ffma2(make_float2(0.0551716685295105f, 0.0551716685295105f), f,
-                   make_float2(0.2426111251115799f, 0.2426111251115799f));
-  p = ffma2(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
-  p = ffma2(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
-  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(u.x) << 23)),
-                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(u.y) << 23)));
-}
-
 // True in exactly one lane of the (converged, full) warp: the lowest one.
 __device__ __forceinline__ bool elect_one_sync() {
   uint32_t pred;

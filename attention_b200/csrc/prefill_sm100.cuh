@@ -490,21 +490,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int kc0 = j * kPfTile;
         const bool full_tile =
             kc0 + kPfTile - 1 <= tile_q0 && kc0 > tile_q0 + kPfTile - 1 - a.W && kc0 + kPfTile <= a.halo + a.S;
-        if (!full_tile) {
-          // scores outside [kmin, kmax] (causal, window, sequence end) become -inf in TMEM
-          const int kmax = min(qc, a.halo + a.S - 1) - kc0;
-          const int kmin = qc - a.W + 1 - kc0;
-#pragma unroll 1
-          for (int c = 0; c < 8; ++c) {
-            uint32_t mk[16];
-            SPA_TMEM_LD16(s_addr + 16 * c, mk);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) mk[e] = (16 * c + e >= kmin && 16 * c + e <= kmax) ? mk[e] : 0xff800000u;
-            SPA_TMEM_ST16(s_addr + 16 * c, mk);
-          }
-          tmem_wait_st();
-        }
         // the whole row of S_t in registers: one TMEM round trip
         uint32_t sv[kPfTile];
         SPA_TMEM_LD32(s_addr, sv);
@@ -512,6 +497,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         SPA_TMEM_LD32(s_addr + 64, (sv + 64));
         SPA_TMEM_LD32(s_addr + 96, (sv + 96));
         tmem_wait_ld();
+        if (!full_tile) {
+          // scores outside [kmin, kmax] (causal, window, sequence end) become -inf; a row
+          // with no key of this tile in range keeps none
+          const int kmin = max(qc - a.W + 1 - kc0, 0);
+          const int kmax = min(min(qc, a.halo + a.S - 1) - kc0, kPfTile - 1);
+          const uint32_t span = kmax >= kmin ? static_cast<uint32_t>(kmax - kmin) : 0u;
+          const int first = kmax >= kmin ? kmin : kPfTile;
+#pragma unroll
+          for (int e = 0; e < kPfTile; ++e)
+            sv[e] = static_cast<uint32_t>(e - first) <= span ? sv[e] : 0xff800000u;
+        }
         float mx[8];
 #pragma unroll
         for (int c = 0; c < 8; ++c) mx[c] = fmaxf(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1]));
@@ -543,7 +539,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const float neg_mu = m_run == -INFINITY ? 0.f : -m_run;
         const float sc = a.scale_log2;
         // P = exp2(s*scale - m) as 16-bit pairs into columns [0, 64) of S_t: keys 0-63 into
-        // [0, 32), signal, then keys 64-127 into [32, 64).  One pair in four on the FMA pipes.
+        // [0, 32), signal, then keys 64-127 into [32, 64)
         const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(neg_mu, neg_mu);
         float2 ls[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -553,7 +549,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           for (int e = 0; e < 32; ++e) {
             const float2 x = ffma2(
                 make_float2(__uint_as_float(sv[64 * h + 2 * e]), __uint_as_float(sv[64 * h + 2 * e + 1])), sc2, nm2);
-            const float2 pr = ((e & 3) == 3) ? exp2_poly2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
+            const float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
             ls[e & 1] = fadd2(ls[e & 1], pr);
             pk[e] = PfFmt<T>::pack(pr.x, pr.y);
           }

@@ -13,19 +13,6 @@ extern "C" const char* spa_version(void) {
 }
 
 namespace spa {
-// Thread i evaluates the pair (2i, 2i+1); an odd tail element is paired with itself.
-__global__ void debug_exp2_poly_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; 2 * i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const bool pair = 2 * i + 1 < n;
-    const float2 r = exp2_poly2(make_float2(x[2 * i], pair ? x[2 * i + 1] : x[2 * i]));
-    y[2 * i] = r.x;
-    if (pair) y[2 * i + 1] = r.y;
-  }
-}
-}  // namespace spa
-
-namespace spa {
 // One thread waits on an mbarrier that nothing arrives on; the bounded wait gives up
 // after `cycles` and raises SPA_DEVERR_WAIT_TIMEOUT.
 __global__ void debug_wait_timeout_kernel(long long cycles) {
@@ -42,16 +29,6 @@ __global__ void debug_wait_timeout_kernel(long long cycles) {
 extern "C" int spa_debug_wait_timeout(long long cycles, spa_stream_t stream) {
   if (cycles <= 0 || cycles > SPA_WAIT_CYCLES) return SPA_ERR_INVALID;
   spa::debug_wait_timeout_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(cycles);
-  SPA_CHECK_CUDA(cudaGetLastError());
-  return SPA_OK;
-}
-
-extern "C" int spa_debug_exp2_poly(const float* x, float* y, int64_t n, spa_stream_t stream) {
-  if (!x || !y || n < 0) return SPA_ERR_INVALID;
-  if (n == 0) return SPA_OK;
-  const int64_t blocks = ((n + 1) / 2 + 255) / 256;
-  spa::debug_exp2_poly_kernel<<<static_cast<unsigned>(blocks < 4096 ? blocks : 4096), 256, 0,
-                                reinterpret_cast<cudaStream_t>(stream)>>>(x, y, n);
   SPA_CHECK_CUDA(cudaGetLastError());
   return SPA_OK;
 }

@@ -69,7 +69,7 @@ def read_profile_traffic(name: str):
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """Samples SM clock and clocks-event reasons of one GPU through NVML (read-only)."""
+    """Samples SM clock, power draw and clocks-event reasons of one GPU through NVML (read-only)."""
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
@@ -78,7 +78,7 @@ class ClockSampler:
     }
 
     def __init__(self, index: int, period_s: float = 0.02):
-        self.samples: list[tuple[int, int]] = []
+        self.samples: list[tuple[int, int, int | None]] = []
         self.max_mhz = None
         self._stop = threading.Event()
         self._ok = False
@@ -102,7 +102,11 @@ class ClockSampler:
             reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
         except Exception:
             reasons = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
-        self.samples.append((mhz, reasons))
+        try:
+            mw = nv.nvmlDeviceGetPowerUsage(self._h)
+        except Exception:
+            mw = None
+        self.samples.append((mhz, reasons, mw))
 
     def _run(self):
         while not self._stop.is_set():
@@ -130,13 +134,15 @@ class ClockSampler:
     def summary(self) -> dict:
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
-        mhz = [m for m, _ in self.samples]
+        mhz = [m for m, _, _ in self.samples]
+        watts = [w / 1000.0 for _, _, w in self.samples if w is not None]
         mask = 0
-        for _, r in self.samples:
+        for _, r, _ in self.samples:
             mask |= r
         names = [n for bit, n in self.REASONS.items() if mask & bit and n != "gpu_idle"]
         return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": names,
-                "samples": len(self.samples)}
+                "samples": len(self.samples),
+                "power_w": round(statistics.median(watts), 1) if watts else None}
 
 
 # ------------------------------------------------------------------ distributed
@@ -508,7 +514,8 @@ def run_prefill(args, world, rank, dev, peaks):
     reps = args.prefill_reps
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.nvtx.range("prefill"):
+    with ClockSampler(dev.index if dev.index is not None else 0, period_s=0.005) as clocks, \
+            torch.cuda.nvtx.range("prefill"):
         e0.record()
         for _ in range(reps):
             run()
@@ -536,7 +543,7 @@ def run_prefill(args, world, rank, dev, peaks):
             "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst) x GPUs",
             "traffic_16k": read_profile_traffic("local_prefill_tc_16k_ncu.md"),
             "traffic_source": "profiles/local_prefill_tc_16k_ncu.md (dram read+write of one S=16384 launch)",
-            "flops": flops, "sharding": f"{world} contiguous chunks, 2048-token K/V halo over NCCL" if world > 1
+            "flops": flops, "clocks": clocks.summary(), "sharding": f"{world} contiguous chunks, 2048-token K/V halo over NCCL" if world > 1
             else "single GPU", "reps": reps,
             "periodic_router_ms": round(router_ms, 4) if router_ms is not None else None,
             "periodic_router": "block 256, stride 256, top-4, summaries included" if router_ms is not None else None}

@@ -351,15 +351,6 @@ int spa_sparse_decode_step_gated(const void* q, int dtype, int batch, int q_head
                                  int32_t* gate, int64_t* promoted, spa_stream_t stream);
 
 /*
- * Diagnostic: y[i] = 2^x[i] through the FMA-pipe exponential that the prefill
- * softmax uses for part of its probabilities (n = round(x), cubic minimax
- * polynomial for 2^(x-n), relative error <= 7.5e-5 for -125 <= x <= 126; x below
- * -125 gives 2^-125).  No reference counterpart: it lets a test hold the
- * approximation against exp2 computed elsewhere.
- */
-int spa_debug_exp2_poly(const float* x, float* y, int64_t n, spa_stream_t stream);
-
-/*
  * Diagnostic for the failure path: one kernel waits on an mbarrier that nothing
  * completes, with the library's bounded wait limited to `cycles` (1 .. 4e9 clock
  * cycles).  The wait gives up, the kernel returns, and spa_device_error then reports
