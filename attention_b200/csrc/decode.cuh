@@ -44,39 +44,6 @@ struct DecodeArgs {
   int early_local;
 };
 
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-// Barrier over the consumer threads of every CTA in the cluster (the producer warps have
-// exited; barrier.cluster counts the threads that are still running).
-__device__ __forceinline__ void cluster_barrier() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// Split cluster barrier: every thread arrives once at kernel start (relaxed) and waits
-// before its first store into a peer's shared memory, which guarantees every CTA of the
-// cluster is running by then.
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
-__device__ __forceinline__ void st_dsmem(float* local_ptr, int rank, float v) {
-  uint32_t ra;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
-}
-__device__ __forceinline__ void st_dsmem_v4(float* local_ptr, int rank, float4 v) {
-  uint32_t ra;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
-               : "memory");
-}
-__device__ __forceinline__ float ld_dsmem(const float* local_ptr, int rank) {
-  uint32_t ra;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-  return v;
-}
-__device__ __forceinline__ void pdl_block() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
 struct ChunkPlan {
   int lo, hi, seg_a, n_seg, cpp, n_total, ctx;
 };

@@ -72,7 +72,7 @@ __device__ __forceinline__ bool beats(float sa, int ia, float sb, int ib) {
 // Block-wide top-m over cand_score[0..n) (indices cand_idx[0..n)), written in
 // descending order to out[0..m).  Chosen entries are overwritten with -inf and
 // index INT_MAX.  Uses red_s / red_i scratch of blockDim.x/32 entries.
-__device__ void block_topm(float* cand_score, int* cand_idx, int n, int m, int64_t* out, float* red_s,
+__device__ __noinline__ void block_topm(float* cand_score, int* cand_idx, int n, int m, int64_t* out, float* red_s,
                            int* red_i, int* chosen_pos) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   for (int r = 0; r < m; ++r) {
@@ -117,37 +117,25 @@ __device__ void block_topm(float* cand_score, int* cand_idx, int n, int m, int64
 }
 
 // ---------------------------------------------------------------------------
-// Cluster router.  One cluster of kRouterCluster CTAs per batch row; candidate c is
-// owned by CTA rank c % kRouterCluster and scored by one warp: each lane loads its
-// lane-strided slice of the candidate's summary rows for every kv head (independent
-// loads, one memory round trip), forms the lane partials, and the kv heads' butterflies
-// run interleaved.  The cluster exchanges scores through distributed shared memory.
-// Tree mode: level 1 over superblocks (every CTA selects the top_super -- identical
-// inputs, identical result), level 2 over the pages of the chosen superblocks; rank 0
-// selects the final top_m.
+// Cluster router.  One cluster of kRouterCluster CTAs per batch row.  Candidate c of a
+// level is owned by CTA rank c % kRouterCluster and scored by one warp: each lane loads
+// its lane-strided slices of the candidate's summary rows for a batch of kv heads
+// (independent loads, one memory round trip), forms the lane partials, and the heads'
+// butterflies run interleaved.  Lane 0..7 push the score into the shared memory of the
+// CTAs that select from it (st.shared::cluster): after level 1 of the tree every CTA
+// selects the same top_super superblocks from the same scores; after the last level rank
+// 0 selects the top_m pages.  One cluster barrier per level orders the pushes before the
+// selection.  Tree mode: level 1 over superblocks, level 2 over the pages of the chosen
+// superblocks.  Both levels run through one copy of the scoring loop: the kernel is
+// latency-bound, and its instructions, fetched afresh every step, are part of that.
 constexpr int kRouterCluster = 8;
 constexpr int kRouterThreads = 256;
-constexpr int kRouterKvBatch = 8;   // kv heads per register batch
-constexpr int kRouterMaxSlices = 8; // head_dim / 32 (head_dim <= 256)
+constexpr int kRouterKvBatch = 8;  // kv heads per register batch
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ float ld_dsmem_f32(const float* local_ptr, uint32_t rank) {
-  uint32_t ra;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-  return v;
-}
-__device__ __forceinline__ void pdl_wait_prerequisite() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 struct RouterArgs {
@@ -155,7 +143,7 @@ struct RouterArgs {
   int q_heads, kv_heads, head_dim;
   const float* supers;     // [B, Hkv, n_super, D] (tree mode) or nullptr
   const float* summaries;  // [B, Hkv, n_pages, D]
-  int n_super, n_pages, superblock, top_super, top_m, max_cand;
+  int n_super, n_pages, superblock, top_super, top_m;
   float scale;
   int64_t* selected;  // [B, top_m]
   float* scores_out;  // [B, n_pages] (single-level mode) or nullptr
@@ -167,26 +155,28 @@ struct RouterArgs {
 
 // qg (fp32, [Hkv][D]) for batch row b, summed over each kv head's query heads in
 // order.  The raw query row [Hq, D] is first copied to shared memory with 16-byte
-// loads that are all issued before any is consumed (one memory round trip).
+// loads, four per thread in flight (one memory round trip for rows up to 16 KB).
 template <typename T>
 __device__ void load_group_query(const T* __restrict__ q, int b, int q_heads, int kv_heads, int head_dim,
                                  T* __restrict__ qraw, float* __restrict__ qg) {
   const int n = q_heads * head_dim;
   const int nvec = n * static_cast<int>(sizeof(T)) / 16;
   const uint4* src = reinterpret_cast<const uint4*>(q + static_cast<int64_t>(b) * n);
-  constexpr int U = 8;
-  for (int v0 = threadIdx.x; v0 < nvec; v0 += U * blockDim.x) {
-    uint4 r[U];
+  const int nt = static_cast<int>(blockDim.x);
+#pragma unroll 1
+  for (int v0 = threadIdx.x; v0 < nvec; v0 += 4 * nt) {
+    uint4 r[4];
 #pragma unroll
-    for (int u = 0; u < U; ++u)
-      if (v0 + u * static_cast<int>(blockDim.x) < nvec) r[u] = __ldg(src + v0 + u * blockDim.x);
+    for (int u = 0; u < 4; ++u)
+      if (v0 + u * nt < nvec) r[u] = __ldg(src + v0 + u * nt);
 #pragma unroll
-    for (int u = 0; u < U; ++u)
-      if (v0 + u * static_cast<int>(blockDim.x) < nvec) reinterpret_cast<uint4*>(qraw)[v0 + u * blockDim.x] = r[u];
+    for (int u = 0; u < 4; ++u)
+      if (v0 + u * nt < nvec) reinterpret_cast<uint4*>(qraw)[v0 + u * nt] = r[u];
   }
   __syncthreads();
   const int group = q_heads / kv_heads;
-  for (int i = threadIdx.x; i < kv_heads * head_dim; i += blockDim.x) {
+#pragma unroll 1
+  for (int i = threadIdx.x; i < kv_heads * head_dim; i += nt) {
     const int kvh = i / head_dim, d = i - kvh * head_dim;
     float acc = 0.f;
     for (int j = 0; j < group; ++j) acc = __fadd_rn(acc, to_f32(qraw[(kvh * group + j) * head_dim + d]));
@@ -194,40 +184,43 @@ __device__ void load_group_query(const T* __restrict__ q, int b, int q_heads, in
   }
 }
 
-// One warp's view of a candidate: its lane-strided summary values for up to
-// kRouterKvBatch kv heads (registers), loaded with independent loads.
+// One warp's view of a candidate: its lane-strided summary values (NS slices of 32,
+// head_dim <= 32 * NS) for up to kRouterKvBatch kv heads, in registers.
+template <int NS>
 struct CandRows {
-  float v[kRouterKvBatch][kRouterMaxSlices];
+  float v[kRouterKvBatch][NS];
 };
 
-template <typename RowPtr>
-__device__ __forceinline__ void load_cand_rows(CandRows& r, int k0, int kv_heads, int head_dim, RowPtr rowp) {
+// Rows of kv heads [k0, k0 + kRouterKvBatch) of the candidate whose head-0 row is `base`.
+template <int NS>
+__device__ __forceinline__ void load_cand_rows(CandRows<NS>& r, const float* base, int64_t kv_stride, int k0,
+                                               int kv_heads, int head_dim) {
   const int lane = threadIdx.x & 31;
-  const int nk = min(kRouterKvBatch, kv_heads - k0);
 #pragma unroll
   for (int u = 0; u < kRouterKvBatch; ++u) {
-    const float* row = rowp(k0 + (u < nk ? u : 0));
+    const bool hv = k0 + u < kv_heads;
+    const float* row = base + static_cast<int64_t>(hv ? k0 + u : k0) * kv_stride;
 #pragma unroll
-    for (int k = 0; k < kRouterMaxSlices; ++k) {
+    for (int k = 0; k < NS; ++k) {
       const int d = lane + 32 * k;
-      r.v[u][k] = (u < nk && d < head_dim) ? __ldg(row + d) : 0.f;
+      r.v[u][k] = (hv && d < head_dim) ? __ldg(row + d) : 0.f;
     }
   }
 }
 
 // Adds the kv heads [k0, k0+kRouterKvBatch) of one candidate to `total` in the canonical
 // order: lane partials over the lane's slice, xor butterflies, kv heads in order.
-__device__ __forceinline__ float accumulate_cand(const CandRows& r, const float* qg, int k0, int kv_heads,
+template <int NS>
+__device__ __forceinline__ float accumulate_cand(const CandRows<NS>& r, const float* qg, int k0, int kv_heads,
                                                  int head_dim, float total) {
   const int lane = threadIdx.x & 31;
-  const int nk = min(kRouterKvBatch, kv_heads - k0);
   float part[kRouterKvBatch];
 #pragma unroll
   for (int u = 0; u < kRouterKvBatch; ++u) {
-    const float* qq = qg + (k0 + (u < nk ? u : 0)) * head_dim;
+    const float* qq = qg + (k0 + u < kv_heads ? k0 + u : k0) * head_dim;
     float acc = 0.f;
 #pragma unroll
-    for (int k = 0; k < kRouterMaxSlices; ++k) {
+    for (int k = 0; k < NS; ++k) {
       const int d = lane + 32 * k;
       if (d < head_dim) acc = __fadd_rn(acc, __fmul_rn(qq[d], r.v[u][k]));
     }
@@ -239,21 +232,8 @@ __device__ __forceinline__ float accumulate_cand(const CandRows& r, const float*
     for (int u = 0; u < kRouterKvBatch; ++u) part[u] = __fadd_rn(part[u], __shfl_xor_sync(0xffffffffu, part[u], off));
 #pragma unroll
   for (int u = 0; u < kRouterKvBatch; ++u)
-    if (u < nk) total = __fadd_rn(total, part[u]);
+    if (k0 + u < kv_heads) total = __fadd_rn(total, part[u]);
   return total;
-}
-
-// Score of one candidate by one warp (all lanes return the same value).
-template <typename RowPtr>
-__device__ __forceinline__ float warp_candidate_score(const float* qg, int kv_heads, int head_dim, int q_heads,
-                                                      float scale, RowPtr rowp) {
-  float total = 0.f;
-  for (int k0 = 0; k0 < kv_heads; k0 += kRouterKvBatch) {
-    CandRows r;
-    load_cand_rows(r, k0, kv_heads, head_dim, rowp);
-    total = accumulate_cand(r, qg, k0, kv_heads, head_dim, total);
-  }
-  return __fmul_rn(__fdiv_rn(total, static_cast<float>(q_heads)), scale);
 }
 
 // T threads (a power of two dividing 32) share one candidate's rank count: candidate i
@@ -286,37 +266,43 @@ __device__ __forceinline__ void select_top(float* sc, int* id, int n, int m, int
     block_topm(sc, id, n, m, out, red_s, red_i, pos);
 }
 
-// Dynamic shared memory of router_cluster_kernel.
-__host__ __device__ inline size_t router_smem_bytes(int kv_heads, int head_dim, int max_cand, int top_super,
-                                                    size_t q_row_bytes) {
-  const size_t loc_cap = (max_cand + kRouterCluster - 1) / kRouterCluster;
-  const size_t base = sizeof(float) * (static_cast<size_t>(kv_heads) * head_dim + 2 * loc_cap + max_cand) +
-                      sizeof(int64_t) * (top_super > 0 ? top_super : 1) + sizeof(int) * (max_cand + 4);
+// Candidates of the last level: the pages of the chosen superblocks (tree) or every page.
+__host__ __device__ inline int router_level2_cap(const RouterArgs& a) {
+  return a.supers ? a.top_super * a.superblock : a.n_pages;
+}
+
+// Dynamic shared memory of router_cluster_kernel: chosen [top_super] i64, qg [Hkv*D],
+// level-1 scores [n_super], level-2 scores [level-2 cap], ids [max of both], query row.
+__host__ __device__ inline size_t router_smem_bytes(const RouterArgs& a, size_t q_row_bytes) {
+  const size_t n1 = a.supers ? a.n_super : 0, n2 = router_level2_cap(a);
+  const size_t base = sizeof(int64_t) * (a.top_super > 0 ? a.top_super : 1) +
+                      sizeof(float) * (static_cast<size_t>(a.kv_heads) * a.head_dim + n1 + n2) +
+                      sizeof(int) * ((n1 > n2 ? n1 : n2) + 4);
   return ((base + 15) & ~size_t(15)) + q_row_bytes + 16;
 }
 
 // grid (kRouterCluster, B), cluster (kRouterCluster, 1, 1), block kRouterThreads.
-template <typename T>
+template <typename T, int NS>
 __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const RouterArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int hkv = a.kv_heads, D = a.head_dim;
-  const int loc_cap = (a.max_cand + kRouterCluster - 1) / kRouterCluster;
-  int64_t* chosen = reinterpret_cast<int64_t*>(smem_raw);                       // [top_super]
+  const bool tree = a.supers != nullptr;
+  const int n1 = tree ? a.n_super : 0, n2 = router_level2_cap(a);
+  int64_t* chosen = reinterpret_cast<int64_t*>(smem_raw);                         // [top_super]
   float* qg = reinterpret_cast<float*>(chosen + (a.top_super > 0 ? a.top_super : 1));  // [Hkv*D]
-  float* score1 = qg + hkv * D;                                                 // [loc_cap] level 1 (own)
-  float* score2 = score1 + loc_cap;                                             // [loc_cap] level 2 (own)
-  float* all_score = score2 + loc_cap;                                          // [max_cand]
-  int* all_id = reinterpret_cast<int*>(all_score + a.max_cand);                 // [max_cand]
-  T* qraw = reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(all_id + a.max_cand + 4) + 15) & ~uintptr_t(15));
+  float* score1 = qg + hkv * D;  // [n1]: every CTA's pushes of level 1
+  float* score2 = score1 + n1;   // [n2]: pushes of the last level (read by rank 0)
+  int* ids = reinterpret_cast<int*>(score2 + n2);
+  T* qraw = reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(ids + (n1 > n2 ? n1 : n2) + 4) + 15) & ~uintptr_t(15));
   __shared__ float red_s[kRouterThreads / 32];
   __shared__ int red_i[kRouterThreads / 32];
   __shared__ int chosen_pos;
   __shared__ int cand_start[65];
 
-  pdl_launch_dependents();
+  pdl_trigger();
   const int b = blockIdx.y;
-  const uint32_t rank = cluster_rank();
-  if (a.gate) pdl_wait_prerequisite();  // the gate kernel's decision (launched as its dependent)
+  const int rank = static_cast<int>(cluster_rank());
+  if (a.gate) pdl_block();  // the gate kernel's decision (launched as its dependent)
   if (a.gate && a.gate[0] == 0 && a.gate[1] != 0) {
     // promotion reuse: the refresh gate is closed, so the promoted pages are this step's
     // selection and no summary is read.  The flags are the same for every CTA, so whole
@@ -326,119 +312,77 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
         a.selected[static_cast<int64_t>(b) * a.top_m + j] = a.promoted[static_cast<int64_t>(b) * a.top_m + j];
     return;
   }
+  // every thread arrives now and waits once the query is in: every CTA of the cluster is
+  // then running, so pushes into peers' shared memory are safe
+  cluster_arrive_relaxed();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kRouterThreads / 32;
-  // first level's rows (the warp's first owned candidate, first kv-head batch) are
-  // requested before the query row so both loads are in flight together
-  CandRows first;
-  const float* sup_tab0 = a.supers ? a.supers + static_cast<int64_t>(b) * hkv * a.n_super * D : nullptr;
-  const float* page_tab0 = a.summaries + static_cast<int64_t>(b) * hkv * a.n_pages * D;
-  const int n_first = a.supers ? a.n_super : a.n_pages;
-  const int64_t first_stride = static_cast<int64_t>(n_first) * D;
-  const float* first_tab = a.supers ? sup_tab0 : page_tab0;
-  const int c_first = static_cast<int>(rank) + warp * kRouterCluster;
-  if (c_first < n_first)
-    load_cand_rows(first, 0, hkv, D, [&](int kvh) { return first_tab + kvh * first_stride + static_cast<int64_t>(c_first) * D; });
+  const float* sup_tab = tree ? a.supers + static_cast<int64_t>(b) * hkv * a.n_super * D : nullptr;
+  const float* page_tab = a.summaries + static_cast<int64_t>(b) * hkv * a.n_pages * D;
+  const int64_t sup_stride = static_cast<int64_t>(a.n_super) * D;
+  const int64_t page_stride = static_cast<int64_t>(a.n_pages) * D;
+  const int first_level = tree ? 1 : 2;
+  // the rows of the warp's first candidate (first kv-head batch) are requested before the
+  // query row, so both loads are in flight together
+  CandRows<NS> rows;
+  int n_cand = tree ? a.n_super : a.n_pages;
+  if (rank + warp * kRouterCluster < n_cand)
+    load_cand_rows(rows, (tree ? sup_tab : page_tab) + static_cast<int64_t>(rank + warp * kRouterCluster) * D,
+                   tree ? sup_stride : page_stride, 0, hkv, D);
   load_group_query(static_cast<const T*>(a.q), b, a.q_heads, hkv, D, qraw, qg);
   __syncthreads();
-  // first-level score of the warp's first candidate from the prefetched rows
-  auto first_score = [&](int c) {
-    float total = accumulate_cand(first, qg, 0, hkv, D, 0.f);
-    for (int k0 = kRouterKvBatch; k0 < hkv; k0 += kRouterKvBatch) {
-      CandRows r;
-      load_cand_rows(r, k0, hkv, D, [&](int kvh) { return first_tab + kvh * first_stride + static_cast<int64_t>(c) * D; });
-      total = accumulate_cand(r, qg, k0, hkv, D, total);
-    }
-    return __fmul_rn(__fdiv_rn(total, static_cast<float>(a.q_heads)), a.scale);
+  cluster_wait();
+  auto page_of = [&](int c) {  // page of level-2 candidate c (tree)
+    int j = 0;
+    while (j + 1 < a.top_super && cand_start[j + 1] <= c) ++j;
+    return static_cast<int>(chosen[j]) * a.superblock + (c - cand_start[j]);
   };
-
-  const float* page_tab = a.summaries + static_cast<int64_t>(b) * hkv * a.n_pages * D;
-  const int64_t page_kv_stride = static_cast<int64_t>(a.n_pages) * D;
-  int n_cand = a.n_pages;
-  auto n_local_of = [&](int n) {
-    return n > static_cast<int>(rank) ? (n - 1 - static_cast<int>(rank)) / kRouterCluster + 1 : 0;
-  };
-  if (a.supers) {
-    // ---- level 1: superblocks
-    const float* sup_tab = a.supers + static_cast<int64_t>(b) * hkv * a.n_super * D;
-    const int64_t sup_kv_stride = static_cast<int64_t>(a.n_super) * D;
-    const int nl = n_local_of(a.n_super);
+#pragma unroll 1
+  for (int level = first_level; level <= 2; ++level) {
+    const float* tab = level == 1 ? sup_tab : page_tab;
+    const int64_t kv_stride = level == 1 ? sup_stride : page_stride;
+    float* dst = level == 1 ? score1 : score2;
+    const int nl = n_cand > rank ? (n_cand - 1 - rank) / kRouterCluster + 1 : 0;
+#pragma unroll 1
     for (int i = warp; i < nl; i += nwarps) {
-      const int c = static_cast<int>(rank) + i * kRouterCluster;
-      const float v = i == warp ? first_score(c)
-                                : warp_candidate_score(qg, hkv, D, a.q_heads, a.scale, [&](int kvh) {
-                                    return sup_tab + kvh * sup_kv_stride + static_cast<int64_t>(c) * D;
-                                  });
-      if (lane == 0) score1[i] = v;
-    }
-    cluster_sync_all();
-    for (int c = threadIdx.x; c < a.n_super; c += blockDim.x) {
-      all_score[c] = ld_dsmem_f32(score1 + c / kRouterCluster, static_cast<uint32_t>(c % kRouterCluster));
-      all_id[c] = c;
-    }
-    __syncthreads();
-    select_top(all_score, all_id, a.n_super, a.top_super, chosen, red_s, red_i, &chosen_pos);
-    if (threadIdx.x == 0) {
-      int n = 0;
-      for (int j = 0; j < a.top_super; ++j) {
-        cand_start[j] = n;
-        const int sidx = static_cast<int>(chosen[j]);
-        const int g0 = sidx * a.superblock, g1 = min(g0 + a.superblock, a.n_pages);
-        n += max(0, g1 - g0);
+      const int c = rank + i * kRouterCluster;
+      const int g = (level == 2 && tree) ? page_of(c) : c;
+      const float* base = tab + static_cast<int64_t>(g) * D;
+      float total = 0.f;
+#pragma unroll 1
+      for (int k0 = 0; k0 < hkv; k0 += kRouterKvBatch) {
+        if (level != first_level || i != warp || k0 != 0) load_cand_rows(rows, base, kv_stride, k0, hkv, D);
+        total = accumulate_cand(rows, qg, k0, hkv, D, total);
       }
-      cand_start[a.top_super] = n;
-    }
-    __syncthreads();
-    n_cand = cand_start[a.top_super];
-    auto page_of = [&](int c) {
-      int j = 0;
-      while (j + 1 < a.top_super && cand_start[j + 1] <= c) ++j;
-      return static_cast<int>(chosen[j]) * a.superblock + (c - cand_start[j]);
-    };
-    // ---- level 2: pages of the chosen superblocks, listed superblock by superblock
-    const int nl2 = n_local_of(n_cand);
-    for (int i = warp; i < nl2; i += nwarps) {
-      const int g = page_of(static_cast<int>(rank) + i * kRouterCluster);
-      const float v = warp_candidate_score(qg, hkv, D, a.q_heads, a.scale,
-                                           [&](int kvh) { return page_tab + kvh * page_kv_stride + static_cast<int64_t>(g) * D; });
-      if (lane == 0) score2[i] = v;
-    }
-    cluster_sync_all();
-    if (rank == 0) {
-      for (int c = threadIdx.x; c < n_cand; c += blockDim.x) {
-        all_score[c] = ld_dsmem_f32(score2 + c / kRouterCluster, static_cast<uint32_t>(c % kRouterCluster));
-        all_id[c] = page_of(c);
-      }
-    }
-    // peers keep their shared memory alive until rank 0 has read it
-    cluster_sync_all();
-    if (rank == 0)
-      select_top(all_score, all_id, n_cand, a.top_m, a.selected + static_cast<int64_t>(b) * a.top_m, red_s, red_i,
-                 &chosen_pos);
-  } else {
-    // ---- single level: every routable page is a candidate
-    const int nl = n_local_of(n_cand);
-    for (int i = warp; i < nl; i += nwarps) {
-      const int c = static_cast<int>(rank) + i * kRouterCluster;
-      const float v = i == warp ? first_score(c)
-                                : warp_candidate_score(qg, hkv, D, a.q_heads, a.scale, [&](int kvh) {
-                                    return page_tab + kvh * page_kv_stride + static_cast<int64_t>(c) * D;
-                                  });
-      if (lane == 0) {
-        score2[i] = v;
+      const float v = __fmul_rn(__fdiv_rn(total, static_cast<float>(a.q_heads)), a.scale);
+      if (level == 1) {
+        if (lane < kRouterCluster) st_dsmem(dst + c, lane, v);  // every CTA selects superblocks
+      } else if (lane == 0) {
+        st_dsmem(dst + c, 0, v);  // rank 0 selects pages
         if (a.scores_out) a.scores_out[static_cast<int64_t>(b) * a.n_pages + c] = v;
       }
     }
-    cluster_sync_all();
-    if (rank == 0) {
-      for (int c = threadIdx.x; c < n_cand; c += blockDim.x) {
-        all_score[c] = ld_dsmem_f32(score2 + c / kRouterCluster, static_cast<uint32_t>(c % kRouterCluster));
-        all_id[c] = c;
+    cluster_barrier();  // this level's pushes are visible to the selecting CTAs
+    if (level == 1) {
+      for (int c = threadIdx.x; c < n_cand; c += blockDim.x) ids[c] = c;
+      __syncthreads();
+      select_top(score1, ids, n_cand, a.top_super, chosen, red_s, red_i, &chosen_pos);
+      if (threadIdx.x == 0) {
+        int n = 0;
+        for (int j = 0; j < a.top_super; ++j) {
+          cand_start[j] = n;
+          const int g0 = static_cast<int>(chosen[j]) * a.superblock, g1 = min(g0 + a.superblock, a.n_pages);
+          n += max(0, g1 - g0);
+        }
+        cand_start[a.top_super] = n;
       }
-    }
-    cluster_sync_all();
-    if (rank == 0)
-      select_top(all_score, all_id, n_cand, a.top_m, a.selected + static_cast<int64_t>(b) * a.top_m, red_s, red_i,
+      __syncthreads();
+      n_cand = cand_start[a.top_super];
+    } else if (rank == 0) {
+      for (int c = threadIdx.x; c < n_cand; c += blockDim.x) ids[c] = tree ? page_of(c) : c;
+      __syncthreads();
+      select_top(score2, ids, n_cand, a.top_m, a.selected + static_cast<int64_t>(b) * a.top_m, red_s, red_i,
                  &chosen_pos);
+    }
   }
   if (a.gate && rank == 0) {
     // a routed step becomes the promoted selection
@@ -449,12 +393,11 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
   }
 }
 
-template <typename T>
-int launch_router(const RouterArgs& a, int batch, cudaStream_t st) {
-  const size_t smem = router_smem_bytes(a.kv_heads, a.head_dim, a.max_cand, a.top_super,
-                                       static_cast<size_t>(a.q_heads) * a.head_dim * sizeof(T));
+template <typename T, int NS>
+int launch_router_ns(const RouterArgs& a, int batch, cudaStream_t st) {
+  const size_t smem = router_smem_bytes(a, static_cast<size_t>(a.q_heads) * a.head_dim * sizeof(T));
   if (smem > 200 * 1024) return SPA_ERR_UNSUPPORTED;
-  auto kern = router_cluster_kernel<T>;
+  auto kern = router_cluster_kernel<T, NS>;
   SPA_CHECK_CUDA(spa_set_smem_once(kern, static_cast<int>(smem)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kRouterCluster, batch, 1);
@@ -474,6 +417,16 @@ int launch_router(const RouterArgs& a, int batch, cudaStream_t st) {
   cfg.numAttrs = a.gate ? 2 : 1;
   SPA_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
   return SPA_OK;
+}
+
+// One instantiation per head_dim class: the lane slices of a summary row are unrolled
+// exactly, so the scoring loop carries no dead slices.
+template <typename T>
+int launch_router(const RouterArgs& a, int batch, cudaStream_t st) {
+  if (a.head_dim <= 32) return launch_router_ns<T, 1>(a, batch, st);
+  if (a.head_dim <= 64) return launch_router_ns<T, 2>(a, batch, st);
+  if (a.head_dim <= 128) return launch_router_ns<T, 4>(a, batch, st);
+  return launch_router_ns<T, 8>(a, batch, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -594,7 +547,6 @@ int router_topm_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_
   a.superblock = 0;
   a.top_super = 0;
   a.top_m = top_m;
-  a.max_cand = n_pages;
   a.scale = static_cast<float>(scale);
   a.selected = selected;
   a.scores_out = scores_out;
@@ -633,7 +585,6 @@ int router_tree_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_
   a.superblock = superblock;
   a.top_super = top_super;
   a.top_m = top_m;
-  a.max_cand = n_super > top_super * superblock ? n_super : top_super * superblock;
   a.scale = static_cast<float>(scale);
   a.selected = selected;
   a.scores_out = nullptr;
