@@ -61,6 +61,8 @@ PROTOTYPES = {
     "spa_version": (ctypes.c_char_p, []),
     "spa_device_error": (_i, [ctypes.POINTER(ctypes.c_uint32)]),
     "spa_last_error": (ctypes.c_char_p, []),
+    "spa_copy": (_i, [_vp, _vp, _sz, _vp]),
+    "spa_host_device_pointer": (_i, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
     "spa_debug_wait_timeout": (_i, [ctypes.c_longlong, _vp]),
     "spa_summaries_build": (_i, [_KV, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp]),
     "spa_router_topm": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _d, _i, _vp, _vp, _vp]),
@@ -127,3 +129,11 @@ def decode_plan(batch: int, q_heads: int, kv_heads: int, max_candidates: int) ->
     check(lib.spa_decode_plan(batch, q_heads, kv_heads, max_candidates, ctypes.byref(ns), ctypes.byref(cl)),
           "spa_decode_plan")
     return int(ns.value), bool(cl.value)
+
+
+def host_device_pointer(host_ptr: int) -> int:
+    """Device address of pinned, mapped host memory at ``host_ptr`` (raises ValueError
+    for memory that is not)."""
+    d = ctypes.c_void_p()
+    check(lib.spa_host_device_pointer(ctypes.c_void_p(host_ptr), ctypes.byref(d)), "spa_host_device_pointer")
+    return int(d.value)

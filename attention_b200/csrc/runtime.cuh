@@ -48,6 +48,59 @@ extern "C" int spa_device_error(uint32_t* out_flags) {
   return SPA_OK;
 }
 
+namespace spa {
+// Byte copy for small transfers between device memory and mapped pinned host memory:
+// 16-byte accesses when both ends and the size allow, bytes otherwise.  Launched as a
+// programmatic dependent of the previous kernel on the stream, it waits for that kernel
+// (griddepcontrol.wait) before the first read, so its launch overlaps that kernel's tail.
+__global__ void __launch_bounds__(256) copy_bytes_kernel(unsigned char* __restrict__ dst,
+                                                         const unsigned char* __restrict__ src, size_t bytes,
+                                                         int vec16) {
+  pdl_block();
+  const size_t tid = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  const size_t nth = static_cast<size_t>(gridDim.x) * blockDim.x;
+  if (vec16) {
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (size_t i = tid; i < bytes / 16; i += nth) d[i] = s[i];
+  } else {
+    for (size_t i = tid; i < bytes; i += nth) dst[i] = src[i];
+  }
+}
+}  // namespace spa
+
+extern "C" int spa_copy(void* dst, const void* src, size_t bytes, spa_stream_t stream) {
+  if (!dst || !src) return SPA_ERR_INVALID;
+  if (bytes == 0) return SPA_OK;
+  const int vec16 = (reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | bytes) % 16 == 0;
+  const size_t units = vec16 ? bytes / 16 : bytes;
+  const size_t blocks = (units + 255) / 256;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks < 64 ? blocks : 64), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SPA_CHECK_CUDA(cudaLaunchKernelEx(&cfg, spa::copy_bytes_kernel, static_cast<unsigned char*>(dst),
+                                    static_cast<const unsigned char*>(src), bytes, vec16));
+  return SPA_OK;
+}
+
+extern "C" int spa_host_device_pointer(void* host, void** device) {
+  if (!host || !device) return SPA_ERR_INVALID;
+  void* d = nullptr;
+  const cudaError_t e = cudaHostGetDevicePointer(&d, host, 0);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // not pinned and mapped: clear the sticky-free error state
+    return SPA_ERR_INVALID;
+  }
+  *device = d;
+  return SPA_OK;
+}
+
 namespace {
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

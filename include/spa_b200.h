@@ -71,6 +71,21 @@ const char* spa_last_error(void);
  * Synchronises the current device.  Returns SPA_OK or SPA_ERR_CUDA. */
 int spa_device_error(uint32_t* out_flags);
 
+/* Copies `bytes` from src to dst on `stream` with a kernel (16-byte accesses when
+ * both pointers and the size are multiples of 16).  Meant for small transfers
+ * between device memory and mapped pinned host memory, where a kernel's loads and
+ * stores cost less latency than a copy-engine transfer.  The kernel is launched as a
+ * programmatic dependent of the previous kernel on the stream and waits for it
+ * before reading.  No reference counterpart (the reference moves tensors with
+ * torch copies).  Returns SPA_OK, SPA_ERR_INVALID or SPA_ERR_CUDA. */
+int spa_copy(void* dst, const void* src, size_t bytes, spa_stream_t stream);
+
+/* Device address of pinned, mapped host memory (cudaHostGetDevicePointer; equal to
+ * the host address under unified addressing), for kernels that read their inputs
+ * from, or write results to, host memory directly.  SPA_ERR_INVALID when `host` is
+ * not such memory. */
+int spa_host_device_pointer(void* host, void** device);
+
 /*
  * Page summaries: summary[b, h, g, :] = mean of K rows of logical page g of
  * sequence b, kv head h, for g < n_pages (the routable, historical pages).
