@@ -136,6 +136,15 @@ __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorM
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
+// 3D form: coordinates (x, y, z) of a tensor map whose box spans all of dimension z.
+__device__ __forceinline__ void tma_load_3d_hint(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x,
+                                                 int y, int z, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(policy)
+      : "memory");
+}
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -313,5 +322,10 @@ inline cudaError_t spa_set_smem_once(K kernel, int bytes) {
 // buffer with box [box_rows, box_cols] and 128-byte swizzle.  Returns false on failure.
 bool spa_make_tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols,
                             uint32_t box_rows, uint32_t box_cols, bool swizzle128);
+// Host: a [rows, cols] row-major buffer seen as [cols / w][rows][w], w = 128 bytes of
+// elements, with box [all slabs, box_rows, w] and 128-byte swizzle: one load brings box_rows
+// full rows, slab after slab, exactly as one 2D [box_rows, w] box per slab would.
+bool spa_make_tensor_map_row_halves(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols,
+                                    uint32_t box_rows);
 // Host: 3D view [bh, rows, d] of a contiguous [B, H, rows, D] tensor, box [1, 128, 64], 128-byte swizzle.
 bool spa_make_tensor_map_3d(CUtensorMap* out, const void* base, int dtype, uint64_t d, uint64_t rows, uint64_t bh);

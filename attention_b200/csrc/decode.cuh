@@ -69,6 +69,22 @@ struct ChunkInfo {
 };
 
 // sel_row: the sequence's selected ids (a.selected + b * top_m, or a copy of them)
+// Reads every field of the argument block once.  Kernel parameters live in the constant
+// bank; a field first read after the wait for the router would add a constant-cache miss
+// to that path, so each thread touches them all at kernel start.
+__device__ __forceinline__ void touch_args(const DecodeArgs& a) {
+  uint64_t x = reinterpret_cast<uint64_t>(a.q) ^ reinterpret_cast<uint64_t>(a.out) ^
+               reinterpret_cast<uint64_t>(a.ctx_lens) ^ reinterpret_cast<uint64_t>(a.selected) ^
+               reinterpret_cast<uint64_t>(a.part_o) ^ reinterpret_cast<uint64_t>(a.part_lse) ^
+               reinterpret_cast<uint64_t>(a.addr.page_table);
+  x ^= static_cast<uint64_t>(a.addr.batch_stride_rows ^ a.addr.page_stride_rows ^ a.addr.head_stride_rows ^
+                             a.addr.total_rows);
+  x ^= static_cast<uint64_t>(a.B ^ a.Hq ^ a.Hkv ^ a.group ^ a.D ^ a.addr.table_stride ^ a.addr.page_size ^
+                             a.local_window ^ a.top_m ^ a.span_len ^ a.nsplit ^ a.cluster_merge ^ a.early_local);
+  x ^= static_cast<uint64_t>(__float_as_uint(a.scale_log2) ^ __float_as_uint(a.scale));
+  asm volatile("" ::"l"(x));
+}
+
 __device__ __forceinline__ ChunkInfo chunk_info(const DecodeArgs& a, const ChunkPlan& p, const int64_t* sel_row,
                                                 int k, int chunk) {
   ChunkInfo c;
@@ -156,6 +172,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool cluster_push = a.cluster_merge && a.nsplit > 1;
   pdl_trigger();
+  touch_args(a);
   if (cluster_push) cluster_arrive_relaxed();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -266,12 +283,8 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
               if (r >= 0) {
                 mbar_arrive_expect_tx(bar, S::kStageBytes);
                 unsigned char* dst = smem + stage * S::kStageBytes;
-#pragma unroll
-                for (int bx = 0; bx < S::kBoxes; ++bx) {
-                  tma_load_2d_hint(dst + bx * S::kBoxBytes, &kmap, bar, bx * 64, static_cast<int>(r), policy);
-                  tma_load_2d_hint(dst + S::kKvBytes + bx * S::kBoxBytes, &vmap, bar, bx * 64, static_cast<int>(r),
-                                   policy);
-                }
+                tma_load_3d_hint(dst, &kmap, bar, 0, static_cast<int>(r), 0, policy);
+                tma_load_3d_hint(dst + S::kKvBytes, &vmap, bar, 0, static_cast<int>(r), 0, policy);
               } else {
                 mbar_arrive(bar);
               }
@@ -738,8 +751,9 @@ template <typename T, int D>
 int launch_decode_mma(const spa_kv_layout& kv, int dtype, const DecodeArgs& a, cudaStream_t st) {
   using S = DecodeSmem<D, kDecodeStages>;
   CUtensorMap kmap, vmap;
-  if (!spa_make_tensor_map_2d(&kmap, kv.k, dtype, kv.total_rows, D, kChunk, 64, true)) return SPA_ERR_INVALID;
-  if (!spa_make_tensor_map_2d(&vmap, kv.v, dtype, kv.total_rows, D, kChunk, 64, true)) return SPA_ERR_INVALID;
+  // one TMA load per chunk of K (and of V) covers both 64-column slabs of a row
+  if (!spa_make_tensor_map_row_halves(&kmap, kv.k, dtype, kv.total_rows, D, kChunk)) return SPA_ERR_INVALID;
+  if (!spa_make_tensor_map_row_halves(&vmap, kv.v, dtype, kv.total_rows, D, kChunk)) return SPA_ERR_INVALID;
   auto kern = decode_mma_kernel<T, D, kDecodeStages>;
   // the receive buffer of the cluster merge: [ns][group] log-sum-exps + [ns][group][ceil(D/ns)]
   const int ns = a.nsplit;

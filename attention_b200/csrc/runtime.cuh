@@ -204,6 +204,45 @@ bool spa_make_tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint6
   return make_tensor_map(out, base, dtype, rows, cols, 0, box_rows, box_cols, swizzle128);
 }
 
+bool spa_make_tensor_map_row_halves(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols,
+                                    uint32_t box_rows) {
+  // [rows, cols] seen as [cols / w][rows][w] with w = 128 bytes of elements: one box of
+  // box_rows rows covers every w-column slab, laid out in shared memory slab by slab
+  // (the same bytes, swizzle included, as one 2D box per slab)
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t es = dtype_size(dtype);
+  const uint64_t w = 128 / es;
+  if (cols % w != 0 || cols / w > 256 || reinterpret_cast<uintptr_t>(base) % 16 != 0) return false;
+  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, 0, box_rows, static_cast<uint32_t>(w), dtype, 2, dev};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  CUtensorMapDataType dt = dtype == SPA_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                           : dtype == SPA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t dims[3] = {w, rows, cols / w};
+  cuuint64_t strides[2] = {cols * es, 128};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(w), box_rows, static_cast<cuuint32_t>(cols / w)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(out, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, *out);
+  return true;
+}
+
 bool spa_make_tensor_map_3d(CUtensorMap* out, const void* base, int dtype, uint64_t d, uint64_t rows, uint64_t bh) {
   return make_tensor_map(out, base, dtype, rows, d, bh, 128, 64, true);
 }
