@@ -57,12 +57,36 @@ class RefreshGateArgs(ctypes.Structure):
 
 GATE_TTL, GATE_SIGNATURE, GATE_DRIFT, GATE_LEARNED = 0, 1, 2, 3
 
+
+SESSION_DIRECT_IN, SESSION_COPY_IN, SESSION_ROUTER_IN_DIRECT_OUT, SESSION_COPY_IN_DIRECT_OUT = 0, 1, 2, 3
+
+
+class SessionParams(ctypes.Structure):
+    """spa_session_params (include/spa_b200.h)."""
+
+    _fields_ = [("dtype", ctypes.c_int), ("batch", ctypes.c_int), ("q_heads", ctypes.c_int),
+                ("kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("kv", KvLayout),
+                ("context_lens", ctypes.c_void_p), ("local_window", ctypes.c_int),
+                ("super_summaries", ctypes.c_void_p), ("n_super", ctypes.c_int), ("summaries", ctypes.c_void_p),
+                ("n_pages", ctypes.c_int), ("superblock", ctypes.c_int), ("top_super", ctypes.c_int),
+                ("top_m", ctypes.c_int), ("router_scale", ctypes.c_double), ("attn_scale", ctypes.c_double),
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t), ("gate", ctypes.c_void_p),
+                ("promoted", ctypes.c_void_p), ("io_mode", ctypes.c_int), ("query", ctypes.c_void_p * 2),
+                ("query_dev", ctypes.c_void_p),
+                ("query_bytes", ctypes.c_size_t), ("result_dev", ctypes.c_void_p),
+                ("result_sel_offset", ctypes.c_size_t), ("result_bytes", ctypes.c_size_t),
+                ("result_host", ctypes.c_void_p * 2)]
+
 PROTOTYPES = {
     "spa_version": (ctypes.c_char_p, []),
     "spa_device_error": (_i, [ctypes.POINTER(ctypes.c_uint32)]),
     "spa_last_error": (ctypes.c_char_p, []),
     "spa_copy": (_i, [_vp, _vp, _sz, _vp]),
     "spa_host_device_pointer": (_i, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "spa_session_create": (_i, [ctypes.POINTER(SessionParams), ctypes.POINTER(ctypes.c_void_p)]),
+    "spa_session_wait": (_i, [_vp, _i]),
+    "spa_session_step": (_i, [_vp, _i, _vp]),
+    "spa_session_destroy": (_i, [_vp]),
     "spa_debug_wait_timeout": (_i, [ctypes.c_longlong, _vp]),
     "spa_summaries_build": (_i, [_KV, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp]),
     "spa_router_topm": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _d, _i, _vp, _vp, _vp]),
@@ -91,7 +115,7 @@ def _load() -> ctypes.CDLL:
     if not LIB_PATH.exists():
         raise RuntimeError(
             f"attention_b200: CUDA library {LIB_PATH} is not built "
-            "(run `python -m attention_b200.build`); there is no CPU fallback"
+            "(run `python attention_b200/build.py`); there is no CPU fallback"
         )
     lib = ctypes.CDLL(str(LIB_PATH))
     for name, (res, args) in PROTOTYPES.items():

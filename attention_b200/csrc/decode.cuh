@@ -42,6 +42,9 @@ struct DecodeArgs {
   // except `selected` already complete: local-window chunks may stream before the
   // router finishes.  Otherwise the kernel waits for its predecessor before any read.
   int early_local;
+  // with early_local: the query is written by the kernel this one overlaps (the router's
+  // device copy of a query held in host memory), so the consumers read it after the wait
+  int q_after_wait;
 };
 
 struct ChunkPlan {
@@ -80,7 +83,8 @@ __device__ __forceinline__ void touch_args(const DecodeArgs& a) {
   x ^= static_cast<uint64_t>(a.addr.batch_stride_rows ^ a.addr.page_stride_rows ^ a.addr.head_stride_rows ^
                              a.addr.total_rows);
   x ^= static_cast<uint64_t>(a.B ^ a.Hq ^ a.Hkv ^ a.group ^ a.D ^ a.addr.table_stride ^ a.addr.page_size ^
-                             a.local_window ^ a.top_m ^ a.span_len ^ a.nsplit ^ a.cluster_merge ^ a.early_local);
+                             a.local_window ^ a.top_m ^ a.span_len ^ a.nsplit ^ a.cluster_merge ^ a.early_local ^
+                             a.q_after_wait);
   x ^= static_cast<uint64_t>(__float_as_uint(a.scale_log2) ^ __float_as_uint(a.scale));
   asm volatile("" ::"l"(x));
 }
@@ -309,6 +313,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   const int g0 = lane >> 2, tig = lane & 3;
   uint32_t qa[D / 16][4];
   {
+    if (a.q_after_wait) pdl_block();
     const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(b) * a.Hq + kvh * group) * D;
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
@@ -878,6 +883,7 @@ int spa::paged_decode_impl(const void* q, int dtype, int batch, int q_heads, int
   a.part_o = nullptr;
   a.part_lse = nullptr;
   a.early_local = 0;
+  a.q_after_wait = 0;
   {
     const size_t need = spa_decode_workspace_size(batch, q_heads, kv_heads, head_dim, max_candidates);
     if (need && (!workspace || workspace_bytes < need)) return SPA_ERR_WORKSPACE;

@@ -151,6 +151,11 @@ struct RouterArgs {
   // gate[1] = a selection has been promoted; promoted [B, top_m] holds it
   int32_t* gate = nullptr;
   int64_t* promoted = nullptr;
+  // fused step with its query in host memory: q_copy [B, Hq, D] receives a device copy of
+  // the query for the decode (rank r of a row's cluster writes the r-th eighth of the row),
+  // selected_copy [B, top_m] a second copy of the selection (host memory)
+  void* q_copy = nullptr;
+  int64_t* selected_copy = nullptr;
 };
 
 // qg (fp32, [Hkv][D]) for batch row b, summed over each kv head's query heads in
@@ -307,9 +312,22 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
     // promotion reuse: the refresh gate is closed, so the promoted pages are this step's
     // selection and no summary is read.  The flags are the same for every CTA, so whole
     // clusters leave here together, before any cluster barrier.
-    if (rank == 0)
-      for (int j = threadIdx.x; j < a.top_m; j += blockDim.x)
-        a.selected[static_cast<int64_t>(b) * a.top_m + j] = a.promoted[static_cast<int64_t>(b) * a.top_m + j];
+    if (rank == 0) {
+      for (int j = threadIdx.x; j < a.top_m; j += blockDim.x) {
+        const int64_t v = a.promoted[static_cast<int64_t>(b) * a.top_m + j];
+        a.selected[static_cast<int64_t>(b) * a.top_m + j] = v;
+        if (a.selected_copy) a.selected_copy[static_cast<int64_t>(b) * a.top_m + j] = v;
+      }
+    }
+    if (a.q_copy) {
+      // the decode reads the query from q_copy: copy this CTA's eighth of the row
+      const int nvec = a.q_heads * a.head_dim * static_cast<int>(sizeof(T)) / 16;
+      const uint4* src =
+          reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + static_cast<int64_t>(b) * a.q_heads * a.head_dim);
+      uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(a.q_copy) + static_cast<int64_t>(b) * a.q_heads * a.head_dim);
+      const int v0 = nvec * rank / kRouterCluster, v1 = nvec * (rank + 1) / kRouterCluster;
+      for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) dst[v] = src[v];
+    }
     return;
   }
   // every thread arrives now and waits once the query is in: every CTA of the cluster is
@@ -330,6 +348,13 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
                    tree ? sup_stride : page_stride, 0, hkv, D);
   load_group_query(static_cast<const T*>(a.q), b, a.q_heads, hkv, D, qraw, qg);
   __syncthreads();
+  if (a.q_copy) {
+    // the decode reads the query from q_copy: this CTA's eighth of the staged row
+    const int nvec = a.q_heads * D * static_cast<int>(sizeof(T)) / 16;
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(a.q_copy) + static_cast<int64_t>(b) * a.q_heads * D);
+    const int v0 = nvec * rank / kRouterCluster, v1 = nvec * (rank + 1) / kRouterCluster;
+    for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) dst[v] = reinterpret_cast<const uint4*>(qraw)[v];
+  }
   cluster_wait();
   auto page_of = [&](int c) {  // page of level-2 candidate c (tree)
     int j = 0;
@@ -382,6 +407,11 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
       __syncthreads();
       select_top(score2, ids, n_cand, a.top_m, a.selected + static_cast<int64_t>(b) * a.top_m, red_s, red_i,
                  &chosen_pos);
+      if (a.selected_copy) {
+        __syncthreads();
+        for (int j = threadIdx.x; j < a.top_m; j += blockDim.x)
+          a.selected_copy[static_cast<int64_t>(b) * a.top_m + j] = a.selected[static_cast<int64_t>(b) * a.top_m + j];
+      }
     }
   }
   if (a.gate && rank == 0) {
@@ -529,7 +559,8 @@ int router_common_checks(const void* q, int q_dtype, int batch, int q_heads, int
 namespace spa {
 int router_topm_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_heads, int head_dim,
                      const float* summaries, int n_pages, double scale, int top_m, int64_t* selected,
-                     float* scores_out, int32_t* gate, int64_t* promoted, spa_stream_t stream) {
+                     float* scores_out, int32_t* gate, int64_t* promoted, spa_stream_t stream,
+                     void* q_copy, int64_t* selected_copy) {
   if ((gate == nullptr) != (promoted == nullptr)) return SPA_ERR_INVALID;
   int rc = router_common_checks(q, q_dtype, batch, q_heads, kv_heads, head_dim);
   if (rc) return rc;
@@ -552,6 +583,8 @@ int router_topm_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_
   a.scores_out = scores_out;
   a.gate = gate;
   a.promoted = promoted;
+  a.q_copy = q_copy;
+  a.selected_copy = selected_copy;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (q_dtype == SPA_F32) return spa::launch_router<float>(a, batch, st);
   if (q_dtype == SPA_F16) return spa::launch_router<__half>(a, batch, st);
@@ -561,7 +594,7 @@ int router_topm_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_
 int router_tree_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_heads, int head_dim,
                      const float* super_summaries, int n_super, const float* summaries, int n_pages, int superblock,
                      int top_super, double scale, int top_m, int64_t* selected, int32_t* gate, int64_t* promoted,
-                     spa_stream_t stream) {
+                     spa_stream_t stream, void* q_copy, int64_t* selected_copy) {
   if ((gate == nullptr) != (promoted == nullptr)) return SPA_ERR_INVALID;
   int rc = router_common_checks(q, q_dtype, batch, q_heads, kv_heads, head_dim);
   if (rc) return rc;
@@ -590,6 +623,8 @@ int router_tree_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_
   a.scores_out = nullptr;
   a.gate = gate;
   a.promoted = promoted;
+  a.q_copy = q_copy;
+  a.selected_copy = selected_copy;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (q_dtype == SPA_F32) return spa::launch_router<float>(a, batch, st);
   if (q_dtype == SPA_F16) return spa::launch_router<__half>(a, batch, st);
@@ -601,7 +636,7 @@ extern "C" int spa_router_topm(const void* q, int q_dtype, int batch, int q_head
                                const float* summaries, int n_pages, double scale, int top_m, int64_t* selected,
                                float* scores_out, spa_stream_t stream) {
   return spa::router_topm_impl(q, q_dtype, batch, q_heads, kv_heads, head_dim, summaries, n_pages, scale, top_m,
-                               selected, scores_out, nullptr, nullptr, stream);
+                               selected, scores_out, nullptr, nullptr, stream, nullptr, nullptr);
 }
 
 extern "C" int spa_router_topm_gated(const void* q, int q_dtype, int batch, int q_heads, int kv_heads, int head_dim,
@@ -609,7 +644,7 @@ extern "C" int spa_router_topm_gated(const void* q, int q_dtype, int batch, int 
                                      int32_t* gate, int64_t* promoted, spa_stream_t stream) {
   if (!gate || !promoted) return SPA_ERR_INVALID;
   return spa::router_topm_impl(q, q_dtype, batch, q_heads, kv_heads, head_dim, summaries, n_pages, scale, top_m,
-                               selected, nullptr, gate, promoted, stream);
+                               selected, nullptr, gate, promoted, stream, nullptr, nullptr);
 }
 
 extern "C" int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q_heads, int kv_heads,
@@ -617,7 +652,8 @@ extern "C" int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q
                                     const float* summaries, int n_pages, int superblock, int top_super,
                                     double scale, int top_m, int64_t* selected, spa_stream_t stream) {
   return spa::router_tree_impl(q, q_dtype, batch, q_heads, kv_heads, head_dim, super_summaries, n_super, summaries,
-                               n_pages, superblock, top_super, scale, top_m, selected, nullptr, nullptr, stream);
+                               n_pages, superblock, top_super, scale, top_m, selected, nullptr, nullptr, stream, nullptr,
+                               nullptr);
 }
 
 extern "C" int spa_router_tree_topm_gated(const void* q, int q_dtype, int batch, int q_heads, int kv_heads,
@@ -627,7 +663,8 @@ extern "C" int spa_router_tree_topm_gated(const void* q, int q_dtype, int batch,
                                           int64_t* promoted, spa_stream_t stream) {
   if (!gate || !promoted) return SPA_ERR_INVALID;
   return spa::router_tree_impl(q, q_dtype, batch, q_heads, kv_heads, head_dim, super_summaries, n_super, summaries,
-                               n_pages, superblock, top_super, scale, top_m, selected, gate, promoted, stream);
+                               n_pages, superblock, top_super, scale, top_m, selected, gate, promoted, stream, nullptr,
+                               nullptr);
 }
 
 extern "C" int spa_periodic_router(const void* q, int q_dtype, int batch, int heads, int seq_len, int head_dim,

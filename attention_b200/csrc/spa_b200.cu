@@ -7,6 +7,7 @@
 #include "decode_noalloc.cuh"
 #include "step.cuh"
 #include "gate.cuh"
+#include "session.cuh"
 #include "cache.cuh"
 #include "prefill_generic.cuh"
 #include "prefill_sm100.cuh"

@@ -23,27 +23,12 @@ from ._util import as_int32, const_i32, dtype_code, stream_ptr, workspace
 from .paged_attention import contiguous_layout, pool_layout
 
 
-def sparse_decode_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, summaries: torch.Tensor, *,
-                       top_blocks: int, local_window: int, block_size: int,
-                       super_summaries: torch.Tensor | None = None, superblock: int = 0, top_super: int = 0,
-                       router_scale: float = 1.0, page_table: torch.Tensor | None = None,
-                       context_lens: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                       selected: torch.Tensor | None = None, gate=None):
-    if not query.is_cuda:
-        raise ValueError("CUDA tensors are required")
-    return _launch_step(query.data_ptr(), query, keys, values, summaries, top_blocks=top_blocks,
-                        local_window=local_window, block_size=block_size, super_summaries=super_summaries,
-                        superblock=superblock, top_super=top_super, router_scale=router_scale,
-                        page_table=page_table, context_lens=context_lens, out=out, selected=selected, gate=gate)
-
-
-def _launch_step(query_ptr: int, query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
-                 summaries: torch.Tensor, *, top_blocks: int, local_window: int, block_size: int,
-                 super_summaries: torch.Tensor | None, superblock: int, top_super: int, router_scale: float,
-                 page_table: torch.Tensor | None, context_lens: torch.Tensor | None, out: torch.Tensor | None,
-                 selected: torch.Tensor | None, gate):
-    """Validates and launches one step; the kernels read the query at ``query_ptr`` (device
-    memory, or mapped pinned host memory), shaped and typed like ``query``."""
+def _prepare_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, summaries: torch.Tensor, *,
+                  top_blocks: int, local_window: int, block_size: int, super_summaries: torch.Tensor | None,
+                  superblock: int, top_super: int, page_table: torch.Tensor | None,
+                  context_lens: torch.Tensor | None) -> dict:
+    """Validates one step's inputs (``query`` gives the query's shape and dtype) and returns
+    the C arguments with the tensors they borrow."""
     if not (keys.is_cuda and values.is_cuda and summaries.is_cuda):
         raise ValueError("CUDA tensors are required")
     if not (query.is_contiguous() and keys.is_contiguous() and values.is_contiguous()):
@@ -73,20 +58,37 @@ def _launch_step(query_ptr: int, query: torch.Tensor, keys: torch.Tensor, values
         table = as_int32(page_table).contiguous()
         lens = as_int32(context_lens).contiguous()
         layout = pool_layout(keys, values, table)
-    if out is None:
-        out = torch.empty(query.shape, dtype=query.dtype, device=dev)
-    if selected is None:
-        selected = torch.empty(batch, top_blocks, dtype=torch.int64, device=dev)
     max_cand = local_window + top_blocks * block_size
     ws_bytes = _lib.lib.spa_decode_workspace_size(batch, q_heads, kv_heads, head_dim, max_cand)
     ws = workspace(dev, ws_bytes) if ws_bytes else None
-    args = (query_ptr, dtype_code(query), batch, q_heads, kv_heads, head_dim, ctypes.byref(layout),
-            lens.data_ptr(), local_window, sup.data_ptr() if sup is not None else None,
-            sup.size(2) if sup is not None else 0, summ.data_ptr(), summ.size(2), superblock, top_super, top_blocks,
-            float(router_scale), head_dim ** -0.5, selected.data_ptr(), out.data_ptr(),
-            ws.data_ptr() if ws is not None else None, ws_bytes)
+    return dict(dev=dev, batch=batch, q_heads=q_heads, kv_heads=kv_heads, head_dim=head_dim, layout=layout,
+                lens=lens, summ=summ, sup=sup, ws=ws, ws_bytes=ws_bytes, dtype=dtype_code(query))
+
+
+def sparse_decode_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, summaries: torch.Tensor, *,
+                       top_blocks: int, local_window: int, block_size: int,
+                       super_summaries: torch.Tensor | None = None, superblock: int = 0, top_super: int = 0,
+                       router_scale: float = 1.0, page_table: torch.Tensor | None = None,
+                       context_lens: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                       selected: torch.Tensor | None = None, gate=None):
+    if not query.is_cuda:
+        raise ValueError("CUDA tensors are required")
+    pr = _prepare_step(query, keys, values, summaries, top_blocks=top_blocks, local_window=local_window,
+                       block_size=block_size, super_summaries=super_summaries, superblock=superblock,
+                       top_super=top_super, page_table=page_table, context_lens=context_lens)
+    dev, sup, ws = pr["dev"], pr["sup"], pr["ws"]
+    if out is None:
+        out = torch.empty_like(query)
+    if selected is None:
+        selected = torch.empty(pr["batch"], top_blocks, dtype=torch.int64, device=dev)
+    args = (query.data_ptr(), pr["dtype"], pr["batch"], pr["q_heads"], pr["kv_heads"], pr["head_dim"],
+            ctypes.byref(pr["layout"]), pr["lens"].data_ptr(), local_window,
+            sup.data_ptr() if sup is not None else None, sup.size(2) if sup is not None else 0,
+            pr["summ"].data_ptr(), pr["summ"].size(2), superblock, top_super, top_blocks, float(router_scale),
+            pr["head_dim"] ** -0.5, selected.data_ptr(), out.data_ptr(), ws.data_ptr() if ws is not None else None,
+            pr["ws_bytes"])
     if gate is not None:
-        promoted = gate.promoted_for(batch, top_blocks)
+        promoted = gate.promoted_for(pr["batch"], top_blocks)
         rc = _lib.lib.spa_sparse_decode_step_gated(*args, gate.flags.data_ptr(), promoted.data_ptr(), stream_ptr(dev))
         _lib.check(rc, "spa_sparse_decode_step_gated")
     else:
@@ -98,24 +100,30 @@ def _launch_step(query_ptr: int, query: torch.Tensor, keys: torch.Tensor, values
 class SparseDecodeSession:
     """One prepared sparse decode step for a fixed pool, page table and summaries.
 
-    The query lives in a pinned host buffer that the step's kernels read directly over
-    PCIe (mapped host memory, no copy-engine transfer); right after the decode, a copy
-    kernel (``spa_copy``, launched as the decode's programmatic dependent) writes the
-    output and page ids into a pinned host buffer.  The whole step is captured once as a
-    CUDA graph; ``step(query)`` writes the host query and replays, so a decode step costs
-    one graph launch on the host.  The host buffers are double-buffered: step i reuses
-    the buffers of step i-2 after waiting for its completion, so the host can prepare one
-    step ahead of the device.  The returned tensors are filled when the step's work
-    completes (``torch.cuda.synchronize()``)."""
+    A native session object (``spa_session_*`` in the C ABI) holds every argument of the
+    step and captures, per host-buffer slot, a CUDA graph of the fused step's two kernels:
+    the router reads the query from a pinned host buffer over PCIe (mapped host memory, no
+    copy-engine transfer) and leaves a device copy for the decode; the decode writes the
+    output, and the router a copy of the page ids, into a pinned host buffer.  A step is
+    one ctypes call: one graph launch and one event record on the host.  The
+    host buffers are double-buffered: step i reuses the buffers of step i-2 after waiting
+    for its completion, so the host can prepare one step ahead of the device.  The returned
+    tensors are filled when the step's work completes (``torch.cuda.synchronize()``)."""
 
     def __init__(self, keys: torch.Tensor, values: torch.Tensor, summaries: torch.Tensor, *, q_heads: int,
                  top_blocks: int, local_window: int, block_size: int, batch: int | None = None,
                  super_summaries: torch.Tensor | None = None, superblock: int = 0, top_super: int = 0,
                  router_scale: float = 1.0, page_table: torch.Tensor | None = None,
-                 context_lens: torch.Tensor | None = None, gate=None):
+                 context_lens: torch.Tensor | None = None, gate=None, io_mode: int | None = None):
         dev = keys.device
         batch = batch if batch is not None else summaries.size(0)
         shape = (batch, q_heads, keys.size(3))
+        if io_mode is None:
+            io_mode = _lib.SESSION_COPY_IN
+        q_like = torch.empty(shape, dtype=keys.dtype, device=dev)  # shape and dtype of the query
+        pr = _prepare_step(q_like, keys, values, summaries, top_blocks=top_blocks, local_window=local_window,
+                           block_size=block_size, super_summaries=super_summaries, superblock=superblock,
+                           top_super=top_super, page_table=page_table, context_lens=context_lens)
         # output and page ids share one buffer (page ids at a 16-byte aligned offset), so one
         # copy returns both
         n_out = batch * q_heads * keys.size(3) * keys.element_size()
@@ -129,49 +137,61 @@ class SparseDecodeSession:
         self.host_query = [torch.zeros(shape, dtype=keys.dtype).pin_memory() for _ in range(2)]
         self._host_buf = [torch.zeros(nbytes, dtype=torch.uint8).pin_memory() for _ in range(2)]
         self.host_out, self.host_selected = zip(*(views(b) for b in self._host_buf))
-        # device addresses of the pinned buffers, read and written by the kernels
-        self._q_dev = [_lib.host_device_pointer(t.data_ptr()) for t in self.host_query]
-        self._out_dev = [_lib.host_device_pointer(b.data_ptr()) for b in self._host_buf]
-        self._q_like = torch.empty(shape, dtype=keys.dtype, device=dev)  # shape and dtype of the query
         self._buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-        self._out, self._sel = views(self._buf)
-        self._done = [torch.cuda.Event(), torch.cuda.Event()]
-        self._n = 0
-        kw = dict(top_blocks=top_blocks, local_window=local_window, block_size=block_size,
-                  super_summaries=super_summaries, superblock=superblock, top_super=top_super,
-                  router_scale=router_scale, page_table=page_table, context_lens=context_lens,
-                  out=self._out, selected=self._sel, gate=gate)
-
-        def body(k):
-            _launch_step(self._q_dev[k], self._q_like, keys, values, summaries, **kw)
-            _lib.check(_lib.lib.spa_copy(self._out_dev[k], self._buf.data_ptr(), nbytes, stream_ptr(dev)),
-                       "spa_copy")
-
-        side = torch.cuda.Stream(device=dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):  # warm-up on the capture stream (workspace, descriptors)
-            body(0)
-        torch.cuda.current_stream(dev).wait_stream(side)
-        torch.cuda.synchronize(dev)
-        self._graphs = []
+        sup = pr["sup"]
+        p = _lib.SessionParams()
+        p.dtype, p.batch, p.q_heads, p.kv_heads, p.head_dim = (pr["dtype"], batch, q_heads, pr["kv_heads"],
+                                                              pr["head_dim"])
+        p.kv = pr["layout"]
+        p.context_lens = pr["lens"].data_ptr()
+        p.local_window = local_window
+        p.super_summaries = sup.data_ptr() if sup is not None else None
+        p.n_super = sup.size(2) if sup is not None else 0
+        p.summaries, p.n_pages = pr["summ"].data_ptr(), pr["summ"].size(2)
+        p.superblock, p.top_super, p.top_m = superblock, top_super, top_blocks
+        p.router_scale, p.attn_scale = float(router_scale), pr["head_dim"] ** -0.5
+        p.workspace = pr["ws"].data_ptr() if pr["ws"] is not None else None
+        p.workspace_bytes = pr["ws_bytes"]
+        if gate is not None:
+            promoted = gate.promoted_for(batch, top_blocks)
+            p.gate, p.promoted = gate.flags.data_ptr(), promoted.data_ptr()
         for k in range(2):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=side):
-                body(k)
-            self._graphs.append(g)
-        for e in self._done:
-            e.record()
-        self._keep = (keys, values, summaries, super_summaries, page_table, context_lens, gate)
+            p.query[k] = _lib.host_device_pointer(self.host_query[k].data_ptr())
+            p.result_host[k] = _lib.host_device_pointer(self._host_buf[k].data_ptr())
+        self._q_dev = torch.empty(shape, dtype=keys.dtype, device=dev)
+        p.query_dev, p.query_bytes = self._q_dev.data_ptr(), n_out
+        p.io_mode = int(io_mode)
+        p.result_dev, p.result_sel_offset, p.result_bytes = self._buf.data_ptr(), off, nbytes
+        handle = ctypes.c_void_p()
+        _lib.check(_lib.lib.spa_session_create(ctypes.byref(p), ctypes.byref(handle)), "spa_session_create")
+        self._handle = handle
+        self._params = p
+        self._dev = dev
+        self._n = 0
+        self._keep = (keys, values, summaries, super_summaries, page_table, context_lens, gate, pr)
 
-    def step(self, query: torch.Tensor | None = None):
+    def step(self, query: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None):
         """Runs one step; returns (host_out, host_selected) of this step, filled when the
         step completes.  Without ``query``, the step reads the query already in
-        ``host_query[i % 2]``."""
+        ``host_query[i % 2]``.  ``stream``: the CUDA stream to enqueue on (default: the
+        current stream)."""
         k = self._n & 1
-        self._done[k].synchronize()  # step i-2 used these host buffers
+        _lib.check(_lib.lib.spa_session_wait(self._handle, k), "spa_session_wait")  # step i-2 is done
         if query is not None:
             self.host_query[k].copy_(query)
-        self._graphs[k].replay()
-        self._done[k].record()
+        st = (stream if stream is not None else torch.cuda.current_stream(self._dev)).cuda_stream
+        _lib.check(_lib.lib.spa_session_step(self._handle, k, st), "spa_session_step")
         self._n += 1
         return self.host_out[k], self.host_selected[k]
+
+    def close(self) -> None:
+        """Releases the native session (waits for its steps)."""
+        if getattr(self, "_handle", None):
+            _lib.lib.spa_session_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -408,10 +408,10 @@ def run_ours(args, world, rank, local):
                "us_per_step": round(e_ms * 1e3 / e2e_steps, 3), "steps": e2e_steps,
                "h2d_bytes_per_step": qbytes,
                "d2h_bytes_per_step": qbytes + cfg.batch * cfg.top_m * 8,
-               "path": "attention_b200.SparseDecodeSession.step: one graph replay of the fused step (C ABI "
-                       "spa_sparse_decode_step), whose kernels read the query from pinned host memory over PCIe, "
-                       "and a copy kernel (spa_copy) writing output + page ids into pinned host memory; one "
-                       "synchronisation at the end",
+               "path": "attention_b200.SparseDecodeSession.step: one call into the native session (C ABI "
+                       "spa_session_step): the fused step, whose kernels read the query from pinned host memory "
+                       "over PCIe, and a copy kernel (spa_copy) writing output + page ids into pinned host "
+                       "memory; one synchronisation at the end",
                "per_call_api": {"us_per_step": round(call_ms * 1e3 / e2e_steps, 3),
                                 "value": round(bytes_step * e2e_steps * world / (call_ms * 1e-3) / 1e9, 2),
                                 "path": "attention_b200.sparse_decode_step from Python with the same copies"}}

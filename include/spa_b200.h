@@ -366,6 +366,63 @@ int spa_sparse_decode_step_gated(const void* q, int dtype, int batch, int q_head
                                  int32_t* gate, int64_t* promoted, spa_stream_t stream);
 
 /*
+ * Prepared sparse decode step for a serving loop (no reference counterpart: the
+ * reference times select_blocks + paged_gather_decode_attention,
+ * triton_paged_gather_decode_benchmark.py:69, from Python).  The session keeps every
+ * argument of spa_sparse_decode_step[_gated]; the query of step `slot` is read from
+ * query[slot] (mapped pinned host memory, see spa_host_device_pointer) and the results
+ * go to result_host[slot] (output [B, Hq, D] at offset 0, page ids [B, top_m] int64 at
+ * result_sel_offset), as io_mode says:
+ *   SPA_SESSION_DIRECT_IN: the kernels read query[slot]; spa_copy returns result_bytes
+ *     from result_dev (same layout) after the decode;
+ *   SPA_SESSION_COPY_IN: spa_copy brings the query into query_dev first (one PCIe read),
+ *     results as above;
+ *   SPA_SESSION_ROUTER_IN_DIRECT_OUT: the router reads query[slot] and leaves a device
+ *     copy in query_dev for the decode; the decode writes the output and the router a
+ *     copy of the page ids straight to result_host[slot] (no copy kernels);
+ *   SPA_SESSION_COPY_IN_DIRECT_OUT: spa_copy into query_dev, direct results.
+ * The page ids the decode reads always sit in result_dev at result_sel_offset.
+ * spa_session_create synchronises the device, runs one step and captures each slot's
+ * launches as a CUDA graph.  Two slots double-buffer the host side:
+ * spa_session_wait(s, slot) blocks until the last step enqueued on that slot has
+ * completed; spa_session_step(s, slot, stream) enqueues a step (one graph launch and one
+ * event record, no synchronisation).  gate/promoted may be NULL (ungated).
+ */
+typedef enum spa_session_io_mode {
+  SPA_SESSION_DIRECT_IN = 0,
+  SPA_SESSION_COPY_IN = 1,
+  SPA_SESSION_ROUTER_IN_DIRECT_OUT = 2,
+  SPA_SESSION_COPY_IN_DIRECT_OUT = 3
+} spa_session_io_mode;
+typedef struct spa_session_params {
+  int dtype, batch, q_heads, kv_heads, head_dim;
+  spa_kv_layout kv;
+  const int32_t* context_lens;
+  int local_window;
+  const float* super_summaries; /* NULL: single-level router */
+  int n_super;
+  const float* summaries;
+  int n_pages, superblock, top_super, top_m;
+  double router_scale, attn_scale;
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t* gate;
+  int64_t* promoted;
+  int io_mode;           /* spa_session_io_mode */
+  const void* query[2];
+  void* query_dev;       /* [B, Hq, D] device buffer (every mode but SPA_SESSION_DIRECT_IN) */
+  size_t query_bytes;    /* B * Hq * D * element size */
+  void* result_dev;
+  size_t result_sel_offset, result_bytes;
+  void* result_host[2];
+} spa_session_params;
+typedef struct spa_session spa_session;
+int spa_session_create(const spa_session_params* params, spa_session** out);
+int spa_session_wait(spa_session* session, int slot);
+int spa_session_step(spa_session* session, int slot, spa_stream_t stream);
+int spa_session_destroy(spa_session* session);
+
+/*
  * Diagnostic for the failure path: one kernel waits on an mbarrier that nothing
  * completes, with the library's bounded wait limited to `cycles` (1 .. 4e9 clock
  * cycles).  The wait gives up, the kernel returns, and spa_device_error then reports

@@ -80,7 +80,8 @@ def test_step_head_dim_64(dtype):
 
 
 def test_session_replays_match_direct_steps():
-    """SparseDecodeSession (captured copy-in, step, copy-out) returns the same outputs and
+    """SparseDecodeSession (native session: the step's kernels read the query from pinned
+    host memory, a copy kernel returns output and page ids) returns the same outputs and
     page ids as sparse_decode_step, for consecutive steps with different queries (both host
     buffers of the double buffering are checked)."""
     cfg = workloads.SparseDecodeConfig(top_m=4)
@@ -108,3 +109,40 @@ def test_session_replays_match_direct_steps():
     torch.cuda.synchronize()
     assert torch.equal(o1, results[1][0]) and torch.equal(s1, results[1][1])
     assert torch.equal(o2, results[2][0]) and torch.equal(s2, results[2][1])
+    sess.close()
+    sess.close()  # idempotent
+
+
+@pytest.mark.parametrize("io_mode", [0, 1, 2, 3])
+def test_session_transfer_modes_agree(io_mode):
+    """Every way the session moves the query in and the results out over PCIe (kernels read
+    host memory, copy kernel in, router copy, direct host writes) returns the direct step's
+    output and page ids."""
+    cfg = workloads.SparseDecodeConfig(top_m=4)
+    wl = workloads.sparse_decode_workload(cfg, groups=2, seed=11)
+    table = wl["page_table"][1]
+    summ, sup = spa.page_summaries(wl["k_pool"], block_size=cfg.page_size, n_pages=cfg.routable_pages,
+                                   page_table=table, superblock=cfg.superblock)
+    kw = dict(top_blocks=cfg.top_m, local_window=cfg.local_window, block_size=cfg.page_size,
+              super_summaries=sup, superblock=cfg.superblock, top_super=cfg.top_super,
+              router_scale=cfg.head_dim ** -0.5, page_table=table, context_lens=wl["context_lens"])
+    sess = spa.SparseDecodeSession(wl["k_pool"], wl["v_pool"], summ, q_heads=cfg.q_heads, io_mode=io_mode, **kw)
+    for g in (1, 0):
+        q = wl["query"][g]
+        out, sel = sess.step(q.cpu())
+        torch.cuda.synchronize()
+        ref_out, ref_sel = spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ, **kw)
+        assert torch.equal(out, ref_out.cpu()) and torch.equal(sel, ref_sel.cpu())
+    sess.close()
+
+
+def test_session_rejects_unknown_transfer_mode():
+    cfg = workloads.SparseDecodeConfig(top_m=4)
+    wl = workloads.sparse_decode_workload(cfg, groups=1, seed=12)
+    table = wl["page_table"][0]
+    summ = spa.page_summaries(wl["k_pool"], block_size=cfg.page_size, n_pages=cfg.routable_pages,
+                              page_table=table)
+    with pytest.raises(ValueError):
+        spa.SparseDecodeSession(wl["k_pool"], wl["v_pool"], summ, q_heads=cfg.q_heads, top_blocks=cfg.top_m,
+                                local_window=cfg.local_window, block_size=cfg.page_size, page_table=table,
+                                context_lens=wl["context_lens"], io_mode=7)
