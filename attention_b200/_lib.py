@@ -108,6 +108,7 @@ PROTOTYPES = {
     "spa_kv_append": (_i, [_KV, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "spa_local_prefill": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "spa_promotion_update": (_i, [_vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _vp]),
+    "spa_rms_norm": (_i, [_vp, _vp, _vp, _i, _i, _d, _i, _vp]),
 }
 
 

@@ -8,6 +8,7 @@
 #include "step.cuh"
 #include "gate.cuh"
 #include "session.cuh"
+#include "model.cuh"
 #include "cache.cuh"
 #include "prefill_generic.cuh"
 #include "prefill_sm100.cuh"

@@ -24,6 +24,8 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
+from . import _lib
+from ._util import dtype_code, stream_ptr
 from .cache import PromotionCache, kv_append
 from .paged_attention import paged_gather_decode_attention
 from .prefill import local_causal_prefill
@@ -78,8 +80,17 @@ def init_weights(cfg: DecoderConfig, seed: int = 0) -> dict:
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * weight.float()).to(x.dtype)
+    """RMSNorm over the last dimension in one library launch (``spa_rms_norm``):
+    ``(x * rsqrt(mean(x^2) + eps)) * weight`` in fp32, returned in x's dtype."""
+    if not (x.is_cuda and weight.is_cuda):
+        raise ValueError("CUDA tensors are required")
+    xc = x.contiguous()
+    w = weight.to(x.dtype).contiguous()
+    out = torch.empty_like(xc)
+    dim = xc.size(-1)
+    _lib.check(_lib.lib.spa_rms_norm(xc.data_ptr(), w.data_ptr(), out.data_ptr(), xc.numel() // dim, dim,
+                                     float(eps), dtype_code(xc), stream_ptr(xc.device)), "spa_rms_norm")
+    return out
 
 
 class SparseDecoder:

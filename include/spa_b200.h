@@ -423,6 +423,16 @@ int spa_session_step(spa_session* session, int slot, spa_stream_t stream);
 int spa_session_destroy(spa_session* session);
 
 /*
+ * RMSNorm of `rows` rows of `dim` elements, for the integrated decoder's model:
+ * out[r, i] = (x[r, i] * rsqrt(mean_j x[r, j]^2 + eps)) * weight[i], fp32 arithmetic,
+ * x, weight and out of type dtype, contiguous.  One launch instead of the chain of
+ * elementwise and reduction ops of its torch form (the decoder's norm, standing in for
+ * the LayerNorm of train_tiny_transformer.py:178-190).
+ */
+int spa_rms_norm(const void* x, const void* weight, void* out, int rows, int dim, double eps, int dtype,
+                 spa_stream_t stream);
+
+/*
  * Diagnostic for the failure path: one kernel waits on an mbarrier that nothing
  * completes, with the library's bounded wait limited to `cycles` (1 .. 4e9 clock
  * cycles).  The wait gives up, the kernel returns, and spa_device_error then reports
