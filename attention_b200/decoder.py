@@ -29,7 +29,8 @@ from ._util import dtype_code, stream_ptr
 from .cache import PromotionCache, kv_append
 from .paged_attention import paged_gather_decode_attention
 from .prefill import local_causal_prefill
-from .router import page_summaries, select_blocks
+from .router import page_summaries
+from .step import sparse_decode_step
 
 
 @dataclass
@@ -203,12 +204,16 @@ class SparseDecoder:
             q, k, v = qkv[:, 0].contiguous(), qkv[:, 1].contiguous(), qkv[:, 2].contiguous()
             kv_append(self.k_pool[i], self.v_pool[i], self.page_table, k, v, self._position)
             if m > 0:
-                sel = select_blocks(q, self.summaries[i], m, scale=scale)
+                # router and gather decode chained on the device (one library call)
+                att, sel = sparse_decode_step(q, self.k_pool[i], self.v_pool[i], self.summaries[i], top_blocks=m,
+                                              local_window=cfg.local_window, block_size=cfg.page_size,
+                                              router_scale=scale, page_table=self.page_table,
+                                              context_lens=self._ctx_len)
             else:
                 sel = torch.full((b, 1), -1, dtype=torch.int64, device=self.device)
-            att = paged_gather_decode_attention(q, self.k_pool[i], self.v_pool[i], sel,
-                                                local_window=cfg.local_window, block_size=cfg.page_size,
-                                                page_table=self.page_table, context_lens=self._ctx_len)
+                att = paged_gather_decode_attention(q, self.k_pool[i], self.v_pool[i], sel,
+                                                    local_window=cfg.local_window, block_size=cfg.page_size,
+                                                    page_table=self.page_table, context_lens=self._ctx_len)
             x = x + self._linear(att.reshape(b, cfg.d_model), f"l{i}.out")
             x = x + self._mlp(x, i)
             selected.append(sel)
