@@ -24,45 +24,90 @@ __global__ void kv_append_kernel(T* __restrict__ k, T* __restrict__ v, KvAddr ad
   v[row * head_dim + d] = v_new[src];
 }
 
-// One thread per table row.  Policy: hits refresh last_hit, then entries idle for
-// >= ttl steps are freed, then new pages fill the lowest free slot or evict the
-// least recently hit entry (ties: smallest page id).  Reference policy: fixed-TTL
-// refresh of promoted ids, evaluate_promotion_ttl.py:134-135; promoted-id reuse,
+// One warp per table row, the row's slots staged in shared memory.  Policy: hits refresh
+// last_hit, then entries idle for >= ttl steps are freed, then new pages, in selection
+// order, fill the lowest free slot or evict the least recently hit entry (ties: smallest
+// page id).  The scans over slots are warp-parallel; the inserts stay sequential, as the
+// policy defines them.  Reference policy: fixed-TTL refresh of promoted ids,
+// evaluate_promotion_ttl.py:134-135; promoted-id reuse,
 // triton_promotion_cache_benchmark.py:53-60.
-__global__ void promotion_update_kernel(int32_t* __restrict__ pages, int32_t* __restrict__ last_hit, int rows,
-                                        int slots, const int64_t* __restrict__ selected, int top_m, int step_arg,
-                                        const int32_t* __restrict__ step_dev, int ttl) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(32) promotion_update_kernel(int32_t* __restrict__ pages,
+                                                              int32_t* __restrict__ last_hit, int rows, int slots,
+                                                              const int64_t* __restrict__ selected, int top_m,
+                                                              int step_arg, const int32_t* __restrict__ step_dev,
+                                                              int ttl) {
+  extern __shared__ int32_t tab[];  // pg [slots], lh [slots]
+  const int r = blockIdx.x, lane = threadIdx.x;
   if (r >= rows) return;
   const int step = step_dev ? *step_dev : step_arg;
-  int32_t* pg = pages + static_cast<int64_t>(r) * slots;
-  int32_t* lh = last_hit + static_cast<int64_t>(r) * slots;
+  int32_t* pg_g = pages + static_cast<int64_t>(r) * slots;
+  int32_t* lh_g = last_hit + static_cast<int64_t>(r) * slots;
   const int64_t* sel = selected + static_cast<int64_t>(r) * top_m;
+  int32_t* pg = tab;
+  int32_t* lh = tab + slots;
+  for (int i = lane; i < slots; i += 32) {
+    pg[i] = pg_g[i];
+    lh[i] = lh_g[i];
+  }
+  __syncwarp();
+  // hits refresh last_hit
   for (int j = 0; j < top_m; ++j) {
     const int64_t id = sel[j];
     if (id < 0) continue;
-    for (int i = 0; i < slots; ++i)
+    for (int i = lane; i < slots; i += 32)
       if (pg[i] == static_cast<int32_t>(id)) lh[i] = step;
   }
-  for (int i = 0; i < slots; ++i)
+  __syncwarp();
+  // idle entries expire
+  for (int i = lane; i < slots; i += 32)
     if (pg[i] >= 0 && step - lh[i] >= ttl) pg[i] = -1;
+  __syncwarp();
+  // inserts, one selected page after another
   for (int j = 0; j < top_m; ++j) {
     const int64_t id64 = sel[j];
     if (id64 < 0 || id64 > 0x7fffffff) continue;
     const int32_t id = static_cast<int32_t>(id64);
     bool present = false;
-    for (int i = 0; i < slots; ++i) present |= (pg[i] == id);
-    if (present) continue;
-    int slot = -1;
-    for (int i = 0; i < slots && slot < 0; ++i)
-      if (pg[i] < 0) slot = i;
-    if (slot < 0) {
-      slot = 0;
-      for (int i = 1; i < slots; ++i)
-        if (lh[i] < lh[slot] || (lh[i] == lh[slot] && pg[i] < pg[slot])) slot = i;
+    int free_slot = -1;
+    for (int base = 0; base < slots; base += 32) {
+      const int i = base + lane;
+      const bool in = i < slots;
+      present |= __any_sync(0xffffffffu, in && pg[i] == id);
+      const unsigned fr = __ballot_sync(0xffffffffu, in && pg[i] < 0);
+      if (free_slot < 0 && fr) free_slot = base + __ffs(fr) - 1;
     }
-    pg[slot] = id;
-    lh[slot] = step;
+    if (present) continue;
+    int slot = free_slot;
+    if (slot < 0) {
+      // least recently hit, ties to the smallest page id (ids in a row are distinct)
+      int bl = 0x7fffffff, bp = 0x7fffffff, bi = 0x7fffffff;
+      for (int i = lane; i < slots; i += 32)
+        if (lh[i] < bl || (lh[i] == bl && pg[i] < bp)) {
+          bl = lh[i];
+          bp = pg[i];
+          bi = i;
+        }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const int ol = __shfl_xor_sync(0xffffffffu, bl, off), op = __shfl_xor_sync(0xffffffffu, bp, off),
+                  oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ol < bl || (ol == bl && (op < bp || (op == bp && oi < bi)))) {
+          bl = ol;
+          bp = op;
+          bi = oi;
+        }
+      }
+      slot = bi;
+    }
+    if (lane == 0) {
+      pg[slot] = id;
+      lh[slot] = step;
+    }
+    __syncwarp();
+  }
+  for (int i = lane; i < slots; i += 32) {
+    pg_g[i] = pg[i];
+    lh_g[i] = lh[i];
   }
 }
 
@@ -97,9 +142,12 @@ extern "C" int spa_promotion_update(int32_t* pages, int32_t* last_hit, int rows,
                                     int top_m, int step, const int32_t* step_dev, int ttl, spa_stream_t stream) {
   if (!pages || !last_hit || !selected || rows <= 0 || slots <= 0 || top_m <= 0 || top_m > slots || ttl <= 0)
     return SPA_ERR_INVALID;
+  if (slots > 8192) return SPA_ERR_UNSUPPORTED;  // the row is staged in shared memory
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  spa::promotion_update_kernel<<<(rows + 127) / 128, 128, 0, st>>>(pages, last_hit, rows, slots, selected, top_m,
-                                                                   step, step_dev, ttl);
+  const size_t smem = sizeof(int32_t) * 2 * static_cast<size_t>(slots);
+  SPA_CHECK_CUDA(spa_set_smem_once(spa::promotion_update_kernel, static_cast<int>(smem)));
+  spa::promotion_update_kernel<<<rows, 32, smem, st>>>(pages, last_hit, rows, slots, selected, top_m, step, step_dev,
+                                                      ttl);
   SPA_CHECK_CUDA(cudaGetLastError());
   return SPA_OK;
 }

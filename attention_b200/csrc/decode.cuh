@@ -708,6 +708,9 @@ inline SplitPlan decode_plan(int batch, int q_heads, int kv_heads, int max_candi
   if (ns <= kMaxClusterSplits) return {ns, ns > 1};
   // 8-CTA clusters still give every SM at least one CTA: prefer them
   if (static_cast<int64_t>(pairs) * kMaxClusterSplits >= device_sm_count()) return {kMaxClusterSplits, true};
+  // few chunks per pair (at most 3 per split of 8): the wider split would not shorten the
+  // per-split chain, and 8 splits merged in a cluster save the separate merge launch
+  if (chunks <= 3 * kMaxClusterSplits) return {kMaxClusterSplits, true};
   (void)group;
   return {ns, false};
 }
