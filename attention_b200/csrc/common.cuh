@@ -117,26 +117,9 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ---------------------------------------------------------------- TMA
-// 2D tiled tensor load into shared memory; completion is signalled on `bar`
-// as transaction bytes.  x (innermost coordinate) must be a multiple of 16 B.
-__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x,
-                                            int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-// Same, with an L2 eviction-priority hint (createpolicy result).
-__device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x,
-                                                 int y, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
-      : "memory");
-}
-// 3D form: coordinates (x, y, z) of a tensor map whose box spans all of dimension z.
+// 3D tiled tensor load into shared memory with an L2 eviction-priority hint (createpolicy
+// result); completion is signalled on `bar` as transaction bytes.  x (innermost
+// coordinate) times the element size must be a multiple of 16 B.
 __device__ __forceinline__ void tma_load_3d_hint(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x,
                                                  int y, int z, uint64_t policy) {
   asm volatile(
@@ -248,13 +231,6 @@ __device__ __forceinline__ void st_dsmem_v4(float* local_ptr, int rank, float4 v
   asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
                : "memory");
 }
-__device__ __forceinline__ float ld_dsmem(const float* local_ptr, int rank) {
-  uint32_t ra;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-  return v;
-}
 __device__ __forceinline__ void pdl_block() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // True in exactly one lane of the (converged, full) warp: the lowest one.
@@ -318,10 +294,6 @@ inline cudaError_t spa_set_smem_once(K kernel, int bytes) {
   return spa_set_smem_limit(reinterpret_cast<const void*>(kernel), bytes);
 }
 
-// Host: builds (and caches) a 2D tiled TMA descriptor over a [rows, cols] row-major
-// buffer with box [box_rows, box_cols] and 128-byte swizzle.  Returns false on failure.
-bool spa_make_tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols,
-                            uint32_t box_rows, uint32_t box_cols, bool swizzle128);
 // Host: a [rows, cols] row-major buffer seen as [cols / w][rows][w], w = 128 bytes of
 // elements, with box [all slabs, box_rows, w] and 128-byte swizzle: one load brings box_rows
 // full rows, slab after slab, exactly as one 2D [box_rows, w] box per slab would.

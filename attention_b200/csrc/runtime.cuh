@@ -199,11 +199,6 @@ bool make_tensor_map(CUtensorMap* out, const void* base, int dtype, uint64_t row
 }
 }  // namespace
 
-bool spa_make_tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols,
-                            uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
-  return make_tensor_map(out, base, dtype, rows, cols, 0, box_rows, box_cols, swizzle128);
-}
-
 bool spa_make_tensor_map_row_halves(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols,
                                     uint32_t box_rows) {
   // [rows, cols] seen as [cols / w][rows][w] with w = 128 bytes of elements: one box of
