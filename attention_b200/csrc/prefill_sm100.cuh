@@ -7,8 +7,9 @@
 // W a multiple of 128).  Barrier phases, the K/V ring and TMEM carry over from item to
 // item, so one item's Q load, first products and write-out overlap its neighbours:
 //
-//   warp 0      TMA producer: Q tiles once, then K and V tiles into two STAGES-deep
-//               rings with separate full/empty barriers: K(j) is released as soon as
+//   warp 0      TMA producer: each item's Q tiles (Q_t reloads as soon as the last S_t
+//               product of the previous item has completed), then K and V tiles into two
+//               STAGES-deep rings with separate full/empty barriers: K(j) is released as soon as
 //               both S(j) products complete, so K(j+2) streams in while V(j) is still
 //               being multiplied (about one KV-tile period of lead instead of none)
 //   warp 1      MMA issuer (whole warp, one elected lane issues): S_t = Q_t K^T (SS
@@ -26,7 +27,9 @@
 // runs while the softmax warps compute the second.
 // The MMA warp interleaves O_0(j), S_0(j+1), O_1(j), S_1(j+1), so the softmax of one
 // tile overlaps the other tile's tensor-core work.  The running max is only moved
-// (and O rescaled in TMEM) when a tile's max exceeds it by more than 2^8.
+// (and O rescaled in TMEM) when a tile's max exceeds it by more than 2^8.  Key tiles cut
+// by the causal diagonal, the window start or the sequence end are masked in registers
+// (scores out of range become -inf before the row max); exponentials run on MUFU.
 //
 // Keys are indexed in the concatenation [halo ; keys] (halo_len a multiple of 128):
 // query i sits at position i + halo_len and sees positions (i+halo-W, i+halo].
