@@ -507,6 +507,120 @@ __global__ void __launch_bounds__(256) periodic_router_kernel(const T* __restric
   }
 }
 
+
+// Tiled form of the periodic router for top_m <= MCAP: a CTA (8 warps) routes kPrUpdates
+// consecutive updates of one head, so each block summary is read once for all of them;
+// the scores are the canonical ones above (lane partials over d = lane + 32k in order,
+// butterfly, __fadd_rn(0, .)), and each update's top-m comes from per-lane sorted lists
+// of MCAP entries merged across the warp, in the same (score desc, block asc) order.
+constexpr int kPrUpdates = 8;
+
+template <typename T, int NS, int MCAP>
+__global__ void __launch_bounds__(256) periodic_router_tiled_kernel(const T* __restrict__ q, int seq_len,
+                                                                     int head_dim,
+                                                                     const float* __restrict__ summaries,
+                                                                     int n_blocks, int block_size, int stride,
+                                                                     int top_m, int64_t* __restrict__ out) {
+  extern __shared__ __align__(16) float pr_smem[];
+  const int h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
+  const int U = seq_len / stride;
+  const int u0 = blockIdx.x * kPrUpdates;
+  const int nu = min(kPrUpdates, U - u0);
+  const int64_t bh = static_cast<int64_t>(b) * H + h;
+  float* qv = pr_smem;                                  // [kPrUpdates][32 * NS]
+  float* sc = pr_smem + kPrUpdates * 32 * NS;           // [kPrUpdates][n_blocks]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto avail_of = [&](int u) { return min(n_blocks, (u + 1) * stride / block_size); };
+  for (int i = threadIdx.x; i < kPrUpdates * 32 * NS; i += blockDim.x) {
+    const int u = i / (32 * NS), d = i - u * (32 * NS);
+    const int pos = (u0 + u + 1) * stride - 1;
+    qv[i] = (u < nu && d < head_dim) ? to_f32(q[(bh * seq_len + pos) * head_dim + d]) : 0.f;
+  }
+  __syncthreads();
+  int av[kPrUpdates];
+#pragma unroll
+  for (int u = 0; u < kPrUpdates; ++u) av[u] = u < nu ? avail_of(u0 + u) : 0;
+  const int max_av = avail_of(u0 + nu - 1);  // availability grows with u
+  for (int g = warp; g < max_av; g += 8) {
+    const float* sv = summaries + (bh * n_blocks + g) * head_dim;
+    float s[NS];
+#pragma unroll
+    for (int k = 0; k < NS; ++k) s[k] = (lane + 32 * k < head_dim) ? __ldg(sv + lane + 32 * k) : 0.f;
+    float part[kPrUpdates];
+#pragma unroll
+    for (int u = 0; u < kPrUpdates; ++u) {
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < NS; ++k)
+        if (lane + 32 * k < head_dim) acc = __fadd_rn(acc, __fmul_rn(qv[u * 32 * NS + lane + 32 * k], s[k]));
+      part[u] = acc;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int u = 0; u < kPrUpdates; ++u) part[u] = __fadd_rn(part[u], __shfl_xor_sync(0xffffffffu, part[u], off));
+    if (lane == 0) {
+#pragma unroll
+      for (int u = 0; u < kPrUpdates; ++u)
+        if (g < av[u]) sc[static_cast<int64_t>(u) * n_blocks + g] = __fadd_rn(0.f, part[u]);
+    }
+  }
+  __syncthreads();
+  if (warp >= nu) return;
+  // warp `warp` selects for update u0 + warp
+  const int avail = av[warp];
+  const float* su = sc + static_cast<int64_t>(warp) * n_blocks;
+  int64_t* o = out + (bh * U + u0 + warp) * top_m;
+  const int cnt = min(top_m, avail);
+  for (int j = cnt + lane; j < top_m; j += 32) o[j] = -1;
+  float ls[MCAP];
+  int li[MCAP];
+#pragma unroll
+  for (int k = 0; k < MCAP; ++k) {
+    ls[k] = -INFINITY;
+    li[k] = 0x7fffffff;
+  }
+  for (int g = lane; g < avail; g += 32) {
+    float cs = su[g];
+    int ci = g;
+#pragma unroll
+    for (int k = 0; k < MCAP; ++k) {
+      if (beats(cs, ci, ls[k], li[k])) {
+        const float ts = ls[k];
+        const int ti = li[k];
+        ls[k] = cs;
+        li[k] = ci;
+        cs = ts;
+        ci = ti;
+      }
+    }
+  }
+  for (int r = 0; r < cnt; ++r) {
+    float bs = ls[0];
+    int bi = li[0], bl = lane;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float os = __shfl_xor_sync(0xffffffffu, bs, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off), ol = __shfl_xor_sync(0xffffffffu, bl, off);
+      if (beats(os, oi, bs, bi)) {
+        bs = os;
+        bi = oi;
+        bl = ol;
+      }
+    }
+    if (lane == 0) o[r] = bi;
+    if (lane == bl) {
+#pragma unroll
+      for (int k = 0; k + 1 < MCAP; ++k) {
+        ls[k] = ls[k + 1];
+        li[k] = li[k + 1];
+      }
+      ls[MCAP - 1] = -INFINITY;
+      li[MCAP - 1] = 0x7fffffff;
+    }
+  }
+}
+
 }  // namespace spa
 
 // ---------------------------------------------------------------------------
@@ -676,9 +790,50 @@ extern "C" int spa_periodic_router(const void* q, int q_dtype, int batch, int he
   const int U = seq_len / router_stride;
   if (U <= 0) return SPA_ERR_INVALID;
   if (heads > 65535 || batch > 65535) return SPA_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // tiled form: top_m <= 16 and the scores of kPrUpdates updates in shared memory
+  // NS: the kernel's slices of 32 (2, 4 or 8), which also size its query rows in shared memory
+  const int ns = head_dim <= 64 ? 2 : head_dim <= 128 ? 4 : 8;
+  const size_t tsmem = sizeof(float) * spa::kPrUpdates * (32 * static_cast<size_t>(ns) + n_blocks);
+  if (top_m <= 16 && tsmem <= 200 * 1024) {
+    dim3 tgrid((U + spa::kPrUpdates - 1) / spa::kPrUpdates, heads, batch);
+#define SPA_LAUNCH_PR_TILED(T, NS, MC)                                                                      \
+  do {                                                                                                      \
+    auto kern = spa::periodic_router_tiled_kernel<T, NS, MC>;                                               \
+    SPA_CHECK_CUDA(spa_set_smem_once(kern, static_cast<int>(tsmem)));                                       \
+    kern<<<tgrid, 256, tsmem, st>>>(static_cast<const T*>(q), seq_len, head_dim, summaries, n_blocks,       \
+                                    block_size, router_stride, top_m, out);                                 \
+  } while (0)
+#define SPA_LAUNCH_PR_NS(T, MC)                \
+  do {                                         \
+    if (ns == 2)                               \
+      SPA_LAUNCH_PR_TILED(T, 2, MC);           \
+    else if (ns == 4)                          \
+      SPA_LAUNCH_PR_TILED(T, 4, MC);           \
+    else                                       \
+      SPA_LAUNCH_PR_TILED(T, 8, MC);           \
+  } while (0)
+#define SPA_LAUNCH_PR_M(T)                     \
+  do {                                         \
+    if (top_m <= 4)                            \
+      SPA_LAUNCH_PR_NS(T, 4);                  \
+    else                                       \
+      SPA_LAUNCH_PR_NS(T, 16);                 \
+  } while (0)
+    if (q_dtype == SPA_F32)
+      SPA_LAUNCH_PR_M(float);
+    else if (q_dtype == SPA_F16)
+      SPA_LAUNCH_PR_M(__half);
+    else
+      SPA_LAUNCH_PR_M(__nv_bfloat16);
+#undef SPA_LAUNCH_PR_M
+#undef SPA_LAUNCH_PR_NS
+#undef SPA_LAUNCH_PR_TILED
+    SPA_CHECK_CUDA(cudaGetLastError());
+    return SPA_OK;
+  }
   const size_t smem = sizeof(float) * n_blocks + sizeof(int) * n_blocks + sizeof(float) * head_dim + 16;
   if (smem > 200 * 1024) return SPA_ERR_UNSUPPORTED;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   dim3 grid(U, heads, batch);
 #define SPA_LAUNCH_PERIODIC(T)                                                                              \
   do {                                                                                                      \

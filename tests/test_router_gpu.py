@@ -127,9 +127,15 @@ def test_periodic_router_golden(golden_dir):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_periodic_router_matches_oracle(dtype):
+@pytest.mark.parametrize("shape", [
+    (2, 3, 4096, 64, 256, 128, 4),   # tiled kernel, top-4 lists
+    (1, 2, 832, 96, 64, 64, 8),      # 13 updates (partial tile of 8), head_dim not a multiple of 32
+    (1, 2, 2048, 128, 64, 128, 20),  # top_m > 16: the untiled kernel; early updates padded with -1
+    (1, 1, 1024, 32, 128, 32, 1),    # updates before the first complete block: all -1
+])
+def test_periodic_router_matches_oracle(dtype, shape):
     gen = torch.Generator().manual_seed(11)
-    b, h, s, d, page, stride, m = 2, 3, 4096, 64, 256, 128, 4
+    b, h, s, d, page, stride, m = shape
     q = (torch.randn(b, h, s, d, generator=gen) * 0.5).to(dtype)
     k = (torch.randn(b, h, s, d, generator=gen) * 0.5).to(dtype)
     out = spa.periodic_router(q.to(DEV), k.to(DEV), block_size=page, router_stride=stride, top_blocks=m)
