@@ -99,6 +99,7 @@ PROTOTYPES = {
     "spa_decode_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "spa_decode_plan": (_i, [_i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "spa_paged_decode": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp, _sz, _vp]),
+    "spa_paged_gather_decode": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp, _sz, _vp]),
     "spa_span_gather_decode": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp, _sz, _vp]),
     "spa_sparse_decode_step": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _d, _d, _vp,
                                     _vp, _vp, _sz, _vp]),

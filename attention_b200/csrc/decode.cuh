@@ -846,6 +846,16 @@ extern "C" int spa_paged_decode(const void* q, int dtype, int batch, int q_heads
                                 selected, top_m, 0, max_candidates, scale, out, workspace, workspace_bytes, stream);
 }
 
+extern "C" int spa_paged_gather_decode(const void* q, int dtype, int batch, int q_heads, int kv_heads,
+                                       int head_dim, const spa_kv_layout* kv, const int32_t* context_lens,
+                                       int local_window, const int64_t* selected, int top_m, int max_candidates,
+                                       double scale, void* out, void* workspace, size_t workspace_bytes,
+                                       spa_stream_t stream) {
+  if (!selected || top_m <= 0) return SPA_ERR_INVALID;
+  return spa_paged_decode(q, dtype, batch, q_heads, kv_heads, head_dim, kv, context_lens, local_window, selected,
+                          top_m, max_candidates, scale, out, workspace, workspace_bytes, stream);
+}
+
 extern "C" int spa_span_gather_decode(const void* q, int dtype, int batch, int q_heads, int kv_heads, int head_dim,
                                       const spa_kv_layout* kv, const int32_t* context_lens, int local_window,
                                       const int64_t* starts, int n_spans, int span_width, double scale, void* out,

@@ -53,12 +53,14 @@ def _decode(query, kv_layout, kv_heads, context_lens, local_window, selected, to
     dev = query.device
     ws_bytes = _lib.lib.spa_decode_workspace_size(batch, q_heads, kv_heads, head_dim, max_candidates)
     ws = workspace(dev, ws_bytes) if ws_bytes else None
-    rc = _lib.lib.spa_paged_decode(
-        query.data_ptr(), dtype_code(query), batch, q_heads, kv_heads, head_dim, ctypes.byref(kv_layout),
-        context_lens.data_ptr(), local_window, selected.data_ptr() if selected is not None else None, top_m,
-        max_candidates, head_dim ** -0.5, out.data_ptr(), ws.data_ptr() if ws is not None else None, ws_bytes,
-        stream_ptr(dev))
-    _lib.check(rc, "spa_paged_decode")
+    # the dense form is spa_paged_decode; the selected-pages form its named gather entry point
+    fn, name = ((_lib.lib.spa_paged_decode, "spa_paged_decode") if selected is None
+                else (_lib.lib.spa_paged_gather_decode, "spa_paged_gather_decode"))
+    rc = fn(query.data_ptr(), dtype_code(query), batch, q_heads, kv_heads, head_dim, ctypes.byref(kv_layout),
+            context_lens.data_ptr(), local_window, selected.data_ptr() if selected is not None else None, top_m,
+            max_candidates, head_dim ** -0.5, out.data_ptr(), ws.data_ptr() if ws is not None else None, ws_bytes,
+            stream_ptr(dev))
+    _lib.check(rc, name)
     del keepalive
     return out
 

@@ -175,6 +175,20 @@ int spa_paged_decode(const void* q, int dtype, int batch, int q_heads,
                      size_t workspace_bytes, spa_stream_t stream);
 
 /*
+ * The selected-pages form of spa_paged_decode under the name of the kernel it
+ * replaces, paged_gather_decode_attention (triton_paged_attention.py:139-168):
+ * selected must be non-NULL and top_m > 0 (SPA_ERR_INVALID otherwise); the
+ * arguments and results are those of spa_paged_decode.
+ */
+int spa_paged_gather_decode(const void* q, int dtype, int batch, int q_heads,
+                            int kv_heads, int head_dim, const spa_kv_layout* kv,
+                            const int32_t* context_lens, int local_window,
+                            const int64_t* selected, int top_m,
+                            int max_candidates, double scale, void* out,
+                            void* workspace, size_t workspace_bytes,
+                            spa_stream_t stream);
+
+/*
  * Split plan of the tensor-core decode for this shape on the current device:
  * *nsplit CTAs per (sequence, kv head); *cluster_merge = 1 when they form one
  * thread-block cluster and merge on chip (one kernel launch), 0 when partials go
