@@ -45,3 +45,9 @@ def test_invalid_arguments_rejected_without_gpu():
     assert _lib.lib.spa_local_prefill(None, None, None, 2, 1, 1, 1, 64, 1, None, None, 0, 0, 0, None,
                                       None) == _lib.SPA_ERR_INVALID
     assert _lib.lib.spa_decode_workspace_size(0, 1, 1, 64, 10) == 0
+    # the gather form requires a selection
+    assert _lib.lib.spa_paged_gather_decode(None, 2, 1, 1, 1, 64, None, None, 0, None, 4, 0, 1.0, None, None, 0,
+                                            None) == _lib.SPA_ERR_INVALID
+    assert _lib.lib.spa_rms_norm(None, None, None, 2, 0, 1e-5, 2, None) == _lib.SPA_ERR_INVALID
+    assert _lib.lib.spa_copy(None, None, 16, None) == _lib.SPA_ERR_INVALID
+    assert _lib.lib.spa_session_create(None, None) == _lib.SPA_ERR_INVALID
