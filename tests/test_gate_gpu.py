@@ -133,3 +133,32 @@ def test_gated_tree_step_reuses_promoted_pages():
             exp = spa.paged_gather_decode_attention(q, k_pool, v_pool, promoted, local_window=cfg.local_window,
                                                     block_size=cfg.page_size, page_table=table, context_lens=lens)
             assert torch.equal(out, exp)
+
+
+def test_gated_session_matches_gated_steps():
+    """SparseDecodeSession built with a gate: after each gate decision on the same stream,
+    the session's step returns what sparse_decode_step with an identical gate returns."""
+    from attention_b200 import workloads
+
+    cfg = workloads.SparseDecodeConfig(top_m=4)
+    wl = workloads.sparse_decode_workload(cfg, groups=4, seed=6)
+    k_pool, v_pool, lens = wl["k_pool"], wl["v_pool"], wl["context_lens"]
+    table = wl["page_table"][0]
+    summ, sup = spa.page_summaries(k_pool, block_size=cfg.page_size, n_pages=cfg.routable_pages, page_table=table,
+                                   superblock=cfg.superblock)
+    kw = dict(top_blocks=cfg.top_m, local_window=cfg.local_window, block_size=cfg.page_size,
+              super_summaries=sup, superblock=cfg.superblock, top_super=cfg.top_super,
+              router_scale=cfg.head_dim ** -0.5, page_table=table, context_lens=lens)
+    g_sess = spa.RefreshGate("ttl", cfg.batch, ttl=2)
+    g_ref = spa.RefreshGate("ttl", cfg.batch, ttl=2)
+    sess = spa.SparseDecodeSession(k_pool, v_pool, summ, q_heads=cfg.q_heads, gate=g_sess, **kw)
+    g_sess.reset()  # the session's set-up step routed once; start both gates from scratch
+    for t in range(4):
+        q = wl["query"][t]
+        g_sess.decide(step=t)
+        out, sel = sess.step(q.cpu())
+        torch.cuda.synchronize()
+        g_ref.decide(step=t)
+        ref_out, ref_sel = spa.sparse_decode_step(q, k_pool, v_pool, summ, gate=g_ref, **kw)
+        assert torch.equal(sel, ref_sel.cpu()) and torch.equal(out, ref_out.cpu()), t
+    sess.close()
