@@ -203,9 +203,16 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     if (sel_early && lane < a.top_m) sel_r = a.selected[static_cast<int64_t>(b) * a.top_m + lane];
   }
   const ChunkPlan plan = make_plan(a, b, kChunk);
-  const int k0 = static_cast<int>(static_cast<int64_t>(plan.n_total) * split / a.nsplit);
-  const int k1 = static_cast<int>(static_cast<int64_t>(plan.n_total) * (split + 1) / a.nsplit);
-  const int nk = k1 - k0;
+  // the local-window chunks and the selected chunks are divided among the splits
+  // separately: each split gets an equal share of the selected chunks, the ones that wait
+  // for the router in the fused step, on top of at most its share of the local ones
+  const int n_sel_chunks = plan.n_total - plan.n_seg;
+  const int c_l0 = static_cast<int>(static_cast<int64_t>(plan.n_seg) * split / a.nsplit);
+  const int c_l1 = static_cast<int>(static_cast<int64_t>(plan.n_seg) * (split + 1) / a.nsplit);
+  const int c_s0 = plan.n_seg + static_cast<int>(static_cast<int64_t>(n_sel_chunks) * split / a.nsplit);
+  const int c_s1 = plan.n_seg + static_cast<int>(static_cast<int64_t>(n_sel_chunks) * (split + 1) / a.nsplit);
+  const int n_local = c_l1 - c_l0;
+  const int nk = n_local + (c_s1 - c_s0);
   __syncthreads();
 
   if (warp == kConsumerWarps) {
@@ -246,7 +253,6 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     };
     // chunks [0, n_local) of this split are local-window chunks (no router output needed);
     // with early_local they are issued before waiting for the router.
-    const int n_local = max(0, min(k1, plan.n_seg) - k0);
     for (int part = 0; part < 2 && ok; ++part) {
       const int lo = part ? n_local : 0, hi = part ? nk : n_local;
       if (part == 1 && a.early_local) {
@@ -262,7 +268,8 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
         ChunkInfo ci{0, 0, 0};
         long long row = -1;
         if (base + lane < hi) {
-          ci = chunk_info(a, plan, sel_row, k0 + base + lane, kChunk);
+          const int idx = base + lane;  // this split's idx-th chunk
+          ci = chunk_info(a, plan, sel_row, idx < n_local ? c_l0 + idx : c_s0 + (idx - n_local), kChunk);
           if (ci.vlo < ci.vhi) {
             row = row_of(ci.t0);
             if (row < 0 || row >= a.addr.total_rows) {
