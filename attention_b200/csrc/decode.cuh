@@ -98,7 +98,8 @@ __device__ __forceinline__ ChunkInfo chunk_info(const DecodeArgs& a, const Chunk
     c.vhi = min(c.t0 + chunk, p.hi);
   } else {
     const int kk = k - p.n_seg;
-    const int j = kk / p.cpp, ci = kk - j * p.cpp;
+    // chunks per page is a power of two for power-of-two pages: a shift, not a division
+    const int j = (p.cpp & (p.cpp - 1)) == 0 ? kk >> (__ffs(p.cpp) - 1) : kk / p.cpp, ci = kk - j * p.cpp;
     const int64_t lp = sel_row[j];
     const int P = a.addr.page_size;
     if (a.span_len > 0) {
@@ -244,7 +245,8 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     const int64_t* sel_row = sel_early ? sel_s : (a.selected ? a.selected + static_cast<int64_t>(b) * a.top_m : nullptr);
     auto row_of = [&](int t) -> long long {
       if (!use_tab) return a.addr.row(b, kvh, t);
-      const int lp = t / a.addr.page_size;
+      const int ps = a.addr.page_size;
+      const int lp = (ps & (ps - 1)) == 0 ? t >> (__ffs(ps) - 1) : t / ps;
       if (lp < 0 || lp >= tstride) return -1;
       const int32_t pg = tab[lp];
       if (pg < 0) return -1;
