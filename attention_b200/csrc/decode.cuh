@@ -208,10 +208,13 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   // separately: each split gets an equal share of the selected chunks, the ones that wait
   // for the router in the fused step, on top of at most its share of the local ones
   const int n_sel_chunks = plan.n_total - plan.n_seg;
-  const int c_l0 = static_cast<int>(static_cast<int64_t>(plan.n_seg) * split / a.nsplit);
-  const int c_l1 = static_cast<int>(static_cast<int64_t>(plan.n_seg) * (split + 1) / a.nsplit);
-  const int c_s0 = plan.n_seg + static_cast<int>(static_cast<int64_t>(n_sel_chunks) * split / a.nsplit);
-  const int c_s1 = plan.n_seg + static_cast<int>(static_cast<int64_t>(n_sel_chunks) * (split + 1) / a.nsplit);
+  // bounds of an even division of n items into nsplit parts (32-bit arithmetic while the
+  // products fit, which is every realistic context)
+  auto part_of = [&](int n, int s_) -> int {
+    return n <= (1 << 22) ? n * s_ / a.nsplit : static_cast<int>(static_cast<int64_t>(n) * s_ / a.nsplit);
+  };
+  const int c_l0 = part_of(plan.n_seg, split), c_l1 = part_of(plan.n_seg, split + 1);
+  const int c_s0 = plan.n_seg + part_of(n_sel_chunks, split), c_s1 = plan.n_seg + part_of(n_sel_chunks, split + 1);
   const int n_local = c_l1 - c_l0;
   const int nk = n_local + (c_s1 - c_s0);
   __syncthreads();
@@ -508,7 +511,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
         o.z = fmaf(r4.z, f, o.z);
         o.w = fmaf(r4.w, f, o.w);
       }
-      const int r = col / wmax;  // slices are exactly wmax = D / ns wide
+      const int r = col * ns / D;  // slices are exactly wmax = D / ns wide
       st_dsmem_v4(recv_o + (split * group + row) * wmax + (col - r * wmax), r, o);
     }
   }
@@ -537,7 +540,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   // after the barrier this CTA reads only its own shared memory: no second barrier
   const int c0 = split * D / ns, c1 = (split + 1) * D / ns, w = c1 - c0;
   for (int idx = threadIdx.x; idx < group * w; idx += kConsumerWarps * 32) {
-    const int row = idx / w, j = idx - row * w;
+    const int row = D % ns == 0 ? idx * ns / D : idx / w, j = idx - row * w;
     float M = -INFINITY;
     for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, recv_lse[s2 * group + row]);
     const float Mu = M == -INFINITY ? 0.f : M;
