@@ -533,7 +533,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   }
   if (!cluster_push) return;
   for (int i = threadIdx.x; i < group * ns; i += kConsumerWarps * 32) {
-    const int row = i / ns, r = i - row * ns;
+    const int row = (ns & (ns - 1)) == 0 ? i >> (__ffs(ns) - 1) : i / ns, r = i - row * ns;
     st_dsmem(recv_lse + split * group + row, r, row_lse[row]);
   }
   cluster_barrier();  // every split's pushes are visible in the receive buffers

@@ -182,7 +182,8 @@ __device__ void load_group_query(const T* __restrict__ q, int b, int q_heads, in
   const int group = q_heads / kv_heads;
 #pragma unroll 1
   for (int i = threadIdx.x; i < kv_heads * head_dim; i += nt) {
-    const int kvh = i / head_dim, d = i - kvh * head_dim;
+    const int kvh = (head_dim & (head_dim - 1)) == 0 ? i >> (__ffs(head_dim) - 1) : i / head_dim;
+    const int d = i - kvh * head_dim;
     float acc = 0.f;
     for (int j = 0; j < group; ++j) acc = __fadd_rn(acc, to_f32(qraw[(kvh * group + j) * head_dim + d]));
     qg[i] = acc;
@@ -248,7 +249,8 @@ __device__ void block_topm_rank(const float* sc, const int* id, int n, int m, in
   while (T < 32 && T * 2 * n <= static_cast<int>(blockDim.x)) T *= 2;
   const int per_round = static_cast<int>(blockDim.x) / T;
   for (int base = 0; base < n; base += per_round) {
-    const int i = base + static_cast<int>(threadIdx.x) / T, part = static_cast<int>(threadIdx.x) % T;
+    // T is a power of two
+    const int i = base + (static_cast<int>(threadIdx.x) >> (__ffs(T) - 1)), part = static_cast<int>(threadIdx.x) & (T - 1);
     int r = 0;
     float si = 0.f;
     int ii = 0;
