@@ -492,11 +492,15 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   // cluster merge: rank r merges output columns [r*D/ns, (r+1)*D/ns) of every head; every
   // split pushes its normalised partial of those columns, and its log-sum-exps, into rank
   // r's receive buffer (recv_lse [split][group], recv_o [split][group][wmax])
-  const int wmax = (D + ns - 1) / ns;
+  // a power-of-two split count (8 in the fused step) turns the divisions by ns into shifts
+  const bool ns_pow2 = (ns & (ns - 1)) == 0;
+  const int ns_lg = __ffs(ns) - 1;
+  auto div_ns = [&](int x) { return ns_pow2 ? x >> ns_lg : x / ns; };
+  const int wmax = div_ns(D + ns - 1);
   float* recv_lse = recv;
   float* recv_o = recv + ((ns * group + 3) & ~3);  // 16-byte aligned
   // equal column slices of a multiple of 4: 16-byte loads and remote stores
-  const bool vec4 = cluster_push && D % (4 * ns) == 0;
+  const bool vec4 = cluster_push && (ns_pow2 ? (D & (4 * ns - 1)) == 0 : D % (4 * ns) == 0);
   if (cluster_push) cluster_wait();  // every CTA of the cluster runs: remote stores are safe
   if (vec4) {
     for (int idx = threadIdx.x; idx < group * (D / 4); idx += kConsumerWarps * 32) {
@@ -533,14 +537,14 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   }
   if (!cluster_push) return;
   for (int i = threadIdx.x; i < group * ns; i += kConsumerWarps * 32) {
-    const int row = (ns & (ns - 1)) == 0 ? i >> (__ffs(ns) - 1) : i / ns, r = i - row * ns;
+    const int row = div_ns(i), r = i - row * ns;
     st_dsmem(recv_lse + split * group + row, r, row_lse[row]);
   }
   cluster_barrier();  // every split's pushes are visible in the receive buffers
   // after the barrier this CTA reads only its own shared memory: no second barrier
-  const int c0 = split * D / ns, c1 = (split + 1) * D / ns, w = c1 - c0;
+  const int c0 = div_ns(split * D), c1 = div_ns((split + 1) * D), w = c1 - c0;
   for (int idx = threadIdx.x; idx < group * w; idx += kConsumerWarps * 32) {
-    const int row = D % ns == 0 ? idx * ns / D : idx / w, j = idx - row * w;
+    const int row = ns_pow2 ? idx * ns / D : idx / w, j = idx - row * w;
     float M = -INFINITY;
     for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, recv_lse[s2 * group + row]);
     const float Mu = M == -INFINITY ? 0.f : M;

@@ -179,7 +179,7 @@ __device__ void load_group_query(const T* __restrict__ q, int b, int q_heads, in
       if (v0 + u * nt < nvec) reinterpret_cast<uint4*>(qraw)[v0 + u * nt] = r[u];
   }
   __syncthreads();
-  const int group = q_heads / kv_heads;
+  const int group = (kv_heads & (kv_heads - 1)) == 0 ? q_heads >> (__ffs(kv_heads) - 1) : q_heads / kv_heads;
 #pragma unroll 1
   for (int i = threadIdx.x; i < kv_heads * head_dim; i += nt) {
     const int kvh = (head_dim & (head_dim - 1)) == 0 ? i >> (__ffs(head_dim) - 1) : i / head_dim;
@@ -247,7 +247,7 @@ __device__ __forceinline__ float accumulate_cand(const CandRows<NS>& r, const fl
 __device__ void block_topm_rank(const float* sc, const int* id, int n, int m, int64_t* out) {
   int T = 1;
   while (T < 32 && T * 2 * n <= static_cast<int>(blockDim.x)) T *= 2;
-  const int per_round = static_cast<int>(blockDim.x) / T;
+  const int per_round = static_cast<int>(blockDim.x) >> (__ffs(T) - 1);
   for (int base = 0; base < n; base += per_round) {
     // T is a power of two
     const int i = base + (static_cast<int>(threadIdx.x) >> (__ffs(T) - 1)), part = static_cast<int>(threadIdx.x) & (T - 1);
