@@ -156,6 +156,10 @@ struct RouterArgs {
   // selected_copy [B, top_m] a second copy of the selection (host memory)
   void* q_copy = nullptr;
   int64_t* selected_copy = nullptr;
+  // launched as a programmatic dependent of the kernel that produces its query (the
+  // session's copy-in): waits for it before any read.  Its own dependents (the decode)
+  // may launch before that wait ends, so they must read the query only after theirs.
+  int pdl_wait = 0;
 };
 
 // qg (fp32, [Hkv][D]) for batch row b, summed over each kv head's query heads in
@@ -309,7 +313,8 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
   pdl_trigger();
   const int b = blockIdx.y;
   const int rank = static_cast<int>(cluster_rank());
-  if (a.gate) pdl_block();  // the gate kernel's decision (launched as its dependent)
+  // the gate kernel's decision, or the copied query (launched as their dependent)
+  if (a.gate || a.pdl_wait) pdl_block();
   if (a.gate && a.gate[0] == 0 && a.gate[1] != 0) {
     // promotion reuse: the refresh gate is closed, so the promoted pages are this step's
     // selection and no summary is read.  The flags are the same for every CTA, so whole
@@ -446,7 +451,7 @@ int launch_router_ns(const RouterArgs& a, int batch, cudaStream_t st) {
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = a.gate ? 2 : 1;
+  cfg.numAttrs = (a.gate || a.pdl_wait) ? 2 : 1;
   SPA_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
   return SPA_OK;
 }
@@ -676,7 +681,7 @@ namespace spa {
 int router_topm_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_heads, int head_dim,
                      const float* summaries, int n_pages, double scale, int top_m, int64_t* selected,
                      float* scores_out, int32_t* gate, int64_t* promoted, spa_stream_t stream,
-                     void* q_copy, int64_t* selected_copy) {
+                     void* q_copy, int64_t* selected_copy, bool pdl_wait) {
   if ((gate == nullptr) != (promoted == nullptr)) return SPA_ERR_INVALID;
   int rc = router_common_checks(q, q_dtype, batch, q_heads, kv_heads, head_dim);
   if (rc) return rc;
@@ -701,6 +706,7 @@ int router_topm_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_
   a.promoted = promoted;
   a.q_copy = q_copy;
   a.selected_copy = selected_copy;
+  a.pdl_wait = pdl_wait;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (q_dtype == SPA_F32) return spa::launch_router<float>(a, batch, st);
   if (q_dtype == SPA_F16) return spa::launch_router<__half>(a, batch, st);
@@ -710,7 +716,7 @@ int router_topm_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_
 int router_tree_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_heads, int head_dim,
                      const float* super_summaries, int n_super, const float* summaries, int n_pages, int superblock,
                      int top_super, double scale, int top_m, int64_t* selected, int32_t* gate, int64_t* promoted,
-                     spa_stream_t stream, void* q_copy, int64_t* selected_copy) {
+                     spa_stream_t stream, void* q_copy, int64_t* selected_copy, bool pdl_wait) {
   if ((gate == nullptr) != (promoted == nullptr)) return SPA_ERR_INVALID;
   int rc = router_common_checks(q, q_dtype, batch, q_heads, kv_heads, head_dim);
   if (rc) return rc;
@@ -741,6 +747,7 @@ int router_tree_impl(const void* q, int q_dtype, int batch, int q_heads, int kv_
   a.promoted = promoted;
   a.q_copy = q_copy;
   a.selected_copy = selected_copy;
+  a.pdl_wait = pdl_wait;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (q_dtype == SPA_F32) return spa::launch_router<float>(a, batch, st);
   if (q_dtype == SPA_F16) return spa::launch_router<__half>(a, batch, st);
@@ -752,7 +759,7 @@ extern "C" int spa_router_topm(const void* q, int q_dtype, int batch, int q_head
                                const float* summaries, int n_pages, double scale, int top_m, int64_t* selected,
                                float* scores_out, spa_stream_t stream) {
   return spa::router_topm_impl(q, q_dtype, batch, q_heads, kv_heads, head_dim, summaries, n_pages, scale, top_m,
-                               selected, scores_out, nullptr, nullptr, stream, nullptr, nullptr);
+                               selected, scores_out, nullptr, nullptr, stream, nullptr, nullptr, false);
 }
 
 extern "C" int spa_router_topm_gated(const void* q, int q_dtype, int batch, int q_heads, int kv_heads, int head_dim,
@@ -760,7 +767,7 @@ extern "C" int spa_router_topm_gated(const void* q, int q_dtype, int batch, int 
                                      int32_t* gate, int64_t* promoted, spa_stream_t stream) {
   if (!gate || !promoted) return SPA_ERR_INVALID;
   return spa::router_topm_impl(q, q_dtype, batch, q_heads, kv_heads, head_dim, summaries, n_pages, scale, top_m,
-                               selected, nullptr, gate, promoted, stream, nullptr, nullptr);
+                               selected, nullptr, gate, promoted, stream, nullptr, nullptr, false);
 }
 
 extern "C" int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q_heads, int kv_heads,
@@ -769,7 +776,7 @@ extern "C" int spa_router_tree_topm(const void* q, int q_dtype, int batch, int q
                                     double scale, int top_m, int64_t* selected, spa_stream_t stream) {
   return spa::router_tree_impl(q, q_dtype, batch, q_heads, kv_heads, head_dim, super_summaries, n_super, summaries,
                                n_pages, superblock, top_super, scale, top_m, selected, nullptr, nullptr, stream, nullptr,
-                               nullptr);
+                               nullptr, false);
 }
 
 extern "C" int spa_router_tree_topm_gated(const void* q, int q_dtype, int batch, int q_heads, int kv_heads,
@@ -780,7 +787,7 @@ extern "C" int spa_router_tree_topm_gated(const void* q, int q_dtype, int batch,
   if (!gate || !promoted) return SPA_ERR_INVALID;
   return spa::router_tree_impl(q, q_dtype, batch, q_heads, kv_heads, head_dim, super_summaries, n_super, summaries,
                                n_pages, superblock, top_super, scale, top_m, selected, gate, promoted, stream, nullptr,
-                               nullptr);
+                               nullptr, false);
 }
 
 extern "C" int spa_periodic_router(const void* q, int q_dtype, int batch, int heads, int seq_len, int head_dim,

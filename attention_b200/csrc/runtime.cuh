@@ -53,9 +53,12 @@ namespace spa {
 // 16-byte accesses when both ends and the size allow, bytes otherwise.  Launched as a
 // programmatic dependent of the previous kernel on the stream, it waits for that kernel
 // (griddepcontrol.wait) before the first read, so its launch overlaps that kernel's tail.
+// With release_early it also lets its own programmatic dependent launch at once; that
+// dependent must wait (griddepcontrol.wait) before it reads anything this copy writes.
 __global__ void __launch_bounds__(256) copy_bytes_kernel(unsigned char* __restrict__ dst,
                                                          const unsigned char* __restrict__ src, size_t bytes,
-                                                         int vec16) {
+                                                         int vec16, int release_early) {
+  if (release_early) pdl_trigger();
   pdl_block();
   const size_t tid = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
   const size_t nth = static_cast<size_t>(gridDim.x) * blockDim.x;
@@ -67,9 +70,8 @@ __global__ void __launch_bounds__(256) copy_bytes_kernel(unsigned char* __restri
     for (size_t i = tid; i < bytes; i += nth) dst[i] = src[i];
   }
 }
-}  // namespace spa
 
-extern "C" int spa_copy(void* dst, const void* src, size_t bytes, spa_stream_t stream) {
+int copy_launch(void* dst, const void* src, size_t bytes, spa_stream_t stream, bool release_early) {
   if (!dst || !src) return SPA_ERR_INVALID;
   if (bytes == 0) return SPA_OK;
   const int vec16 = (reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | bytes) % 16 == 0;
@@ -85,8 +87,14 @@ extern "C" int spa_copy(void* dst, const void* src, size_t bytes, spa_stream_t s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   SPA_CHECK_CUDA(cudaLaunchKernelEx(&cfg, spa::copy_bytes_kernel, static_cast<unsigned char*>(dst),
-                                    static_cast<const unsigned char*>(src), bytes, vec16));
+                                    static_cast<const unsigned char*>(src), bytes, vec16,
+                                    release_early ? 1 : 0));
   return SPA_OK;
+}
+}  // namespace spa
+
+extern "C" int spa_copy(void* dst, const void* src, size_t bytes, spa_stream_t stream) {
+  return spa::copy_launch(dst, src, bytes, stream, false);
 }
 
 extern "C" int spa_host_device_pointer(void* host, void** device) {

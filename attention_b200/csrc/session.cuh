@@ -34,8 +34,9 @@ int session_enqueue(const spa_session_params& p, int slot, cudaStream_t st) {
   const void* q = p.query[slot];
   int rc;
   if (copy_in) {
-    // one PCIe read of the query per step, then every CTA reads it from device memory
-    rc = spa_copy(p.query_dev, q, p.query_bytes, ss);
+    // one PCIe read of the query per step, then every CTA reads it from device memory; the
+    // router launches during the copy and waits for it before its first read
+    rc = spa::copy_launch(p.query_dev, q, p.query_bytes, ss, /*release_early=*/!p.gate);
     if (rc) return rc;
     q = p.query_dev;
   }
@@ -46,7 +47,8 @@ int session_enqueue(const spa_session_params& p, int slot, cudaStream_t st) {
                              p.local_window, p.super_summaries, p.n_super, p.summaries, p.n_pages, p.superblock,
                              p.top_super, p.top_m, p.router_scale, p.attn_scale, sel_dev, direct_out ? host : res,
                              p.workspace, p.workspace_bytes, p.gate, p.promoted, ss, router_in ? p.query_dev : nullptr,
-                             direct_out ? reinterpret_cast<int64_t*>(host + p.result_sel_offset) : nullptr);
+                             direct_out ? reinterpret_cast<int64_t*>(host + p.result_sel_offset) : nullptr,
+                             /*router_pdl=*/copy_in && !p.gate);
   if (rc || direct_out) return rc;
   return spa_copy(p.result_host[slot], res, p.result_bytes, ss);
 }

@@ -16,7 +16,8 @@ int sparse_step_impl(const void* q, int dtype, int batch, int q_heads, int kv_he
                      const float* super_summaries, int n_super, const float* summaries, int n_pages, int superblock,
                      int top_super, int top_m, double router_scale, double attn_scale, int64_t* selected, void* out,
                      void* workspace, size_t workspace_bytes, int32_t* gate, int64_t* promoted,
-                     spa_stream_t stream, void* q_copy = nullptr, int64_t* selected_copy = nullptr) {
+                     spa_stream_t stream, void* q_copy = nullptr, int64_t* selected_copy = nullptr,
+                     bool router_pdl = false) {
   if (!q || !out || !kv || !kv->k || !kv->v || !context_lens || !summaries || !selected) return SPA_ERR_INVALID;
   if (dtype != SPA_F16 && dtype != SPA_BF16 && dtype != SPA_F32) return SPA_ERR_INVALID;
   if (local_window < 0 || top_m <= 0) return SPA_ERR_INVALID;
@@ -24,10 +25,10 @@ int sparse_step_impl(const void* q, int dtype, int batch, int q_heads, int kv_he
   if (super_summaries)
     rc = router_tree_impl(q, dtype, batch, q_heads, kv_heads, head_dim, super_summaries, n_super, summaries, n_pages,
                           superblock, top_super, router_scale, top_m, selected, gate, promoted, stream, q_copy,
-                          selected_copy);
+                          selected_copy, router_pdl);
   else
     rc = router_topm_impl(q, dtype, batch, q_heads, kv_heads, head_dim, summaries, n_pages, router_scale, top_m,
-                          selected, nullptr, gate, promoted, stream, q_copy, selected_copy);
+                          selected, nullptr, gate, promoted, stream, q_copy, selected_copy, router_pdl);
   if (rc) return rc;
   spa::DecodeArgs a;
   // with q_copy the query lives in host memory: the decode reads the router's device copy
@@ -52,7 +53,9 @@ int sparse_step_impl(const void* q, int dtype, int batch, int q_heads, int kv_he
   a.part_o = nullptr;
   a.part_lse = nullptr;
   a.early_local = 1;
-  a.q_after_wait = q_copy != nullptr;
+  // the query is written by a kernel still running when the decode launches (the router's
+  // copy, or the copy-in the router waits for): read it after the wait
+  a.q_after_wait = q_copy != nullptr || router_pdl;
   {
     const size_t need = spa_decode_workspace_size(batch, q_heads, kv_heads, head_dim, max_cand);
     if (need && (!workspace || workspace_bytes < need)) return SPA_ERR_WORKSPACE;
