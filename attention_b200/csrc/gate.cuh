@@ -18,7 +18,9 @@
 
 namespace spa {
 
-constexpr int kGateThreads = 256;
+// 32 warps: at batch 4 and width 4096 each warp reduces 512 values with all of its loads
+// in flight at once
+constexpr int kGateThreads = 1024;
 
 __device__ __forceinline__ float gate_warp_sum(float v) {
 #pragma unroll
@@ -147,10 +149,37 @@ __global__ void __launch_bounds__(kGateThreads) refresh_gate_kernel(const spa_re
   }
   __syncthreads();
   if (!decision) return;
-  // refresh: the current state and signature become the cached ones
+  // refresh: the current state and signature become the cached ones.  The router waits for
+  // this grid to complete, so the copy issues four independent loads per thread before
+  // its stores: one memory round trip per 4 x kGateThreads vectors, not one per element.
   if (a.cached_state && a.state) {
     const int64_t n = static_cast<int64_t>(a.batch) * W;
-    for (int64_t i = threadIdx.x; i < n; i += kGateThreads) a.cached_state[i] = a.state[i];
+    const bool vec4 = n % 4 == 0 && ((reinterpret_cast<uintptr_t>(a.state) |
+                                      reinterpret_cast<uintptr_t>(a.cached_state)) % 16 == 0);
+    if (vec4) {
+      const float4* src = reinterpret_cast<const float4*>(a.state);
+      float4* dst = reinterpret_cast<float4*>(a.cached_state);
+      const int64_t n4 = n / 4;
+      for (int64_t i0 = threadIdx.x; i0 < n4; i0 += 4 * kGateThreads) {
+        float4 r[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i0 + u * kGateThreads < n4) r[u] = src[i0 + u * kGateThreads];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i0 + u * kGateThreads < n4) dst[i0 + u * kGateThreads] = r[u];
+      }
+    } else {
+      for (int64_t i0 = threadIdx.x; i0 < n; i0 += 4 * kGateThreads) {
+        float r[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i0 + u * kGateThreads < n) r[u] = a.state[i0 + u * kGateThreads];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i0 + u * kGateThreads < n) a.cached_state[i0 + u * kGateThreads] = r[u];
+      }
+    }
   }
   if (a.cached_signature && a.signature) {
     const int64_t n = static_cast<int64_t>(a.batch) * a.sig_len;

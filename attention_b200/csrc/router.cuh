@@ -292,6 +292,28 @@ __host__ __device__ inline size_t router_smem_bytes(const RouterArgs& a, size_t 
   return ((base + 15) & ~size_t(15)) + q_row_bytes + 16;
 }
 
+// The gated router's reuse step, out of line (it runs only while the gate is closed, and
+// the routing path's code stays compact): rank 0 copies the promoted pages into this
+// step's selection, and each CTA its eighth of the query row into q_copy when given.
+template <typename T>
+__device__ __noinline__ void router_reuse_promoted(const int64_t* promoted, int64_t* selected, int64_t* selected_copy,
+                                                   const T* q, T* q_copy, int b, int rank, int top_m, int row_elems) {
+  if (rank == 0) {
+    for (int j = threadIdx.x; j < top_m; j += blockDim.x) {
+      const int64_t v = promoted[static_cast<int64_t>(b) * top_m + j];
+      selected[static_cast<int64_t>(b) * top_m + j] = v;
+      if (selected_copy) selected_copy[static_cast<int64_t>(b) * top_m + j] = v;
+    }
+  }
+  if (q_copy) {
+    const int nvec = row_elems * static_cast<int>(sizeof(T)) / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(q + static_cast<int64_t>(b) * row_elems);
+    uint4* dst = reinterpret_cast<uint4*>(q_copy + static_cast<int64_t>(b) * row_elems);
+    const int v0 = nvec * rank / kRouterCluster, v1 = nvec * (rank + 1) / kRouterCluster;
+    for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) dst[v] = src[v];
+  }
+}
+
 // grid (kRouterCluster, B), cluster (kRouterCluster, 1, 1), block kRouterThreads.
 template <typename T, int NS>
 __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const RouterArgs a) {
@@ -313,33 +335,11 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
   pdl_trigger();
   const int b = blockIdx.y;
   const int rank = static_cast<int>(cluster_rank());
-  // the gate kernel's decision, or the copied query (launched as their dependent)
-  if (a.gate || a.pdl_wait) pdl_block();
-  if (a.gate && a.gate[0] == 0 && a.gate[1] != 0) {
-    // promotion reuse: the refresh gate is closed, so the promoted pages are this step's
-    // selection and no summary is read.  The flags are the same for every CTA, so whole
-    // clusters leave here together, before any cluster barrier.
-    if (rank == 0) {
-      for (int j = threadIdx.x; j < a.top_m; j += blockDim.x) {
-        const int64_t v = a.promoted[static_cast<int64_t>(b) * a.top_m + j];
-        a.selected[static_cast<int64_t>(b) * a.top_m + j] = v;
-        if (a.selected_copy) a.selected_copy[static_cast<int64_t>(b) * a.top_m + j] = v;
-      }
-    }
-    if (a.q_copy) {
-      // the decode reads the query from q_copy: copy this CTA's eighth of the row
-      const int nvec = a.q_heads * a.head_dim * static_cast<int>(sizeof(T)) / 16;
-      const uint4* src =
-          reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + static_cast<int64_t>(b) * a.q_heads * a.head_dim);
-      uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(a.q_copy) + static_cast<int64_t>(b) * a.q_heads * a.head_dim);
-      const int v0 = nvec * rank / kRouterCluster, v1 = nvec * (rank + 1) / kRouterCluster;
-      for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) dst[v] = src[v];
-    }
-    return;
-  }
+  if (a.pdl_wait) pdl_block();  // the copied query (launched as the copy's dependent)
   // every thread arrives now and waits once the query is in: every CTA of the cluster is
-  // then running, so pushes into peers' shared memory are safe
-  cluster_arrive_relaxed();
+  // then running, so pushes into peers' shared memory are safe.  Gated, the arrival waits
+  // for the gate's decision (a reusing cluster leaves before any cluster barrier).
+  if (!a.gate) cluster_arrive_relaxed();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kRouterThreads / 32;
   const float* sup_tab = tree ? a.supers + static_cast<int64_t>(b) * hkv * a.n_super * D : nullptr;
   const float* page_tab = a.summaries + static_cast<int64_t>(b) * hkv * a.n_pages * D;
@@ -347,13 +347,26 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
   const int64_t page_stride = static_cast<int64_t>(a.n_pages) * D;
   const int first_level = tree ? 1 : 2;
   // the rows of the warp's first candidate (first kv-head batch) are requested before the
-  // query row, so both loads are in flight together
+  // query row, so both loads are in flight together.  Gated, both were written before the
+  // gate kernel started, so they load while the gate decides.
   CandRows<NS> rows;
   int n_cand = tree ? a.n_super : a.n_pages;
   if (rank + warp * kRouterCluster < n_cand)
     load_cand_rows(rows, (tree ? sup_tab : page_tab) + static_cast<int64_t>(rank + warp * kRouterCluster) * D,
                    tree ? sup_stride : page_stride, 0, hkv, D);
   load_group_query(static_cast<const T*>(a.q), b, a.q_heads, hkv, D, qraw, qg);
+  if (a.gate) {
+    pdl_block();  // the gate kernel's decision (launched as its dependent)
+    if (a.gate[0] == 0 && a.gate[1] != 0) {
+      // promotion reuse: the refresh gate is closed, so the promoted pages are this step's
+      // selection and no summary beyond the first rows is read.  The flags are the same for
+      // every CTA, so whole clusters leave here together, before any cluster barrier.
+      router_reuse_promoted<T>(a.promoted, a.selected, a.selected_copy, static_cast<const T*>(a.q),
+                               static_cast<T*>(a.q_copy), b, rank, a.top_m, a.q_heads * a.head_dim);
+      return;
+    }
+    cluster_arrive_relaxed();
+  }
   __syncthreads();
   if (a.q_copy) {
     // the decode reads the query from q_copy: this CTA's eighth of the staged row
