@@ -110,6 +110,8 @@ PROTOTYPES = {
     "spa_local_prefill": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "spa_promotion_update": (_i, [_vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _vp]),
     "spa_rms_norm": (_i, [_vp, _vp, _vp, _i, _i, _d, _i, _vp]),
+    "spa_add_rms_norm": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _d, _i, _vp]),
+    "spa_embed_rms_norm": (_i, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i, _i, _d, _i, _vp]),
 }
 
 

@@ -31,6 +31,7 @@ inline cudaError_t& spa_last_cuda_error() {
 enum : uint32_t {
   SPA_DEVERR_WAIT_TIMEOUT = 1u,   // a bounded mbarrier / flag wait gave up
   SPA_DEVERR_BAD_PAGE = 2u,       // a page id outside the table / pool was skipped
+  SPA_DEVERR_BAD_INDEX = 4u,      // a token or position id outside its embedding table
 };
 
 // ~2 s at 1.9 GHz: far above any legitimate wait, small enough that a lost

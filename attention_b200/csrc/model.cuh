@@ -1,23 +1,51 @@
 // Model glue of the integrated decoder that would otherwise cost a chain of small library
 // launches per use: the decoder's RMSNorm (standing in for the LayerNorm of the reference
 // model, train_tiny_transformer.py:178-190) as one kernel instead of nine elementwise and
-// reduction ops.
+// reduction ops, optionally fused with the residual add before it or with the token and
+// position embedding lookup that starts a step (train_tiny_transformer.py:259,270).
 //   out[r, i] = T((x[r, i] * rsqrt(mean_j x[r, j]^2 + eps)) * w[i]), arithmetic in fp32
 #pragma once
 
 #include "common.cuh"
 
 namespace spa {
-// one CTA of 256 threads per row
+// One CTA of 256 threads per row.  Row r's input is x[x_rows ? x_rows[r] : r], plus
+// delta[delta_rows ? delta_rows[r] : r] when delta is given; the sum is rounded to T, as a
+// separate elementwise add of two T tensors rounds it.  x_out (when given) receives the
+// input row and may be x itself (the second pass then reads the row back from x_out, the
+// same thread's own writes); it must not overlap delta.  A row index outside [0, limit)
+// raises SPA_DEVERR_BAD_INDEX and gives zero rows.
 template <typename T>
-__global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w,
+__global__ void __launch_bounds__(256) rms_norm_kernel(const T* x, const int64_t* __restrict__ x_rows, int64_t x_limit,
+                                                       const T* delta, const int32_t* __restrict__ delta_rows,
+                                                       int64_t delta_limit, const T* __restrict__ w, T* x_out,
                                                        T* __restrict__ out, int dim, float eps) {
   __shared__ float part[8];
   const int64_t row = blockIdx.x;
-  const T* xr = x + row * dim;
+  const int64_t xi = x_rows ? x_rows[row] : row;
+  const int64_t di = delta_rows ? static_cast<int64_t>(delta_rows[row]) : row;
+  T* outr = out + row * dim;
+  T* xo = x_out ? x_out + row * dim : nullptr;
+  if ((x_rows && (xi < 0 || xi >= x_limit)) || (delta && delta_rows && (di < 0 || di >= delta_limit))) {
+    if (threadIdx.x == 0) spa_raise(SPA_DEVERR_BAD_INDEX);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+      outr[i] = from_f32<T>(0.f);
+      if (xo) xo[i] = from_f32<T>(0.f);
+    }
+    return;
+  }
+  const T* xr = x + xi * dim;
+  const T* dr = delta ? delta + di * dim : nullptr;
   float ss = 0.f;
   for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-    const float v = to_f32(xr[i]);
+    float v = to_f32(xr[i]);
+    if (dr) {
+      const T sum = from_f32<T>(v + to_f32(dr[i]));
+      v = to_f32(sum);
+      if (xo) xo[i] = sum;
+    } else if (xo) {
+      xo[i] = xr[i];
+    }
     ss = fmaf(v, v, ss);
   }
 #pragma unroll
@@ -28,29 +56,58 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ x, 
 #pragma unroll
   for (int k = 0; k < 8; ++k) tot += part[k];
   const float r = rsqrtf(tot / static_cast<float>(dim) + eps);
-  T* outr = out + row * dim;
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) outr[i] = from_f32<T>(to_f32(xr[i]) * r * to_f32(w[i]));
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    const float v = xo ? to_f32(xo[i]) : (dr ? to_f32(from_f32<T>(to_f32(xr[i]) + to_f32(dr[i]))) : to_f32(xr[i]));
+    outr[i] = from_f32<T>(v * r * to_f32(w[i]));
+  }
+}
+
+template <typename T>
+void launch_rms_norm(const void* x, const int64_t* x_rows, int64_t x_limit, const void* delta,
+                     const int32_t* delta_rows, int64_t delta_limit, const void* w, void* x_out, void* out, int rows,
+                     int dim, float eps, cudaStream_t st) {
+  rms_norm_kernel<T><<<rows, 256, 0, st>>>(static_cast<const T*>(x), x_rows, x_limit, static_cast<const T*>(delta),
+                                           delta_rows, delta_limit, static_cast<const T*>(w), static_cast<T*>(x_out),
+                                           static_cast<T*>(out), dim, eps);
+}
+
+int rms_norm_impl(const void* x, const int64_t* x_rows, int64_t x_limit, const void* delta, const int32_t* delta_rows,
+                  int64_t delta_limit, const void* w, void* x_out, void* out, int rows, int dim, double eps, int dtype,
+                  spa_stream_t stream) {
+  if (rows < 0 || dim <= 0 || !dtype_ok(dtype)) return SPA_ERR_INVALID;
+  if (rows == 0) return SPA_OK;
+  if (!x || !w || !out) return SPA_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const float e = static_cast<float>(eps);
+  if (dtype == SPA_F32)
+    launch_rms_norm<float>(x, x_rows, x_limit, delta, delta_rows, delta_limit, w, x_out, out, rows, dim, e, st);
+  else if (dtype == SPA_F16)
+    launch_rms_norm<__half>(x, x_rows, x_limit, delta, delta_rows, delta_limit, w, x_out, out, rows, dim, e, st);
+  else
+    launch_rms_norm<__nv_bfloat16>(x, x_rows, x_limit, delta, delta_rows, delta_limit, w, x_out, out, rows, dim, e,
+                                   st);
+  SPA_CHECK_CUDA(cudaGetLastError());
+  return SPA_OK;
 }
 }  // namespace spa
 
 extern "C" int spa_rms_norm(const void* x, const void* weight, void* out, int rows, int dim, double eps, int dtype,
                             spa_stream_t stream) {
-  if (rows < 0 || dim <= 0 || !dtype_ok(dtype)) return SPA_ERR_INVALID;
-  if (rows == 0) return SPA_OK;
-  if (!x || !weight || !out) return SPA_ERR_INVALID;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const float e = static_cast<float>(eps);
-  if (dtype == SPA_F32)
-    spa::rms_norm_kernel<float><<<rows, 256, 0, st>>>(static_cast<const float*>(x), static_cast<const float*>(weight),
-                                                      static_cast<float*>(out), dim, e);
-  else if (dtype == SPA_F16)
-    spa::rms_norm_kernel<__half><<<rows, 256, 0, st>>>(static_cast<const __half*>(x),
-                                                       static_cast<const __half*>(weight), static_cast<__half*>(out),
-                                                       dim, e);
-  else
-    spa::rms_norm_kernel<__nv_bfloat16><<<rows, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
-                                                              static_cast<const __nv_bfloat16*>(weight),
-                                                              static_cast<__nv_bfloat16*>(out), dim, e);
-  SPA_CHECK_CUDA(cudaGetLastError());
-  return SPA_OK;
+  return spa::rms_norm_impl(x, nullptr, 0, nullptr, nullptr, 0, weight, nullptr, out, rows, dim, eps, dtype,
+                            stream);
+}
+
+extern "C" int spa_add_rms_norm(const void* x, const void* delta, const void* weight, void* x_out, void* out, int rows,
+                                int dim, double eps, int dtype, spa_stream_t stream) {
+  if (rows > 0 && (!delta || !x_out)) return SPA_ERR_INVALID;
+  return spa::rms_norm_impl(x, nullptr, 0, delta, nullptr, 0, weight, x_out, out, rows, dim, eps, dtype, stream);
+}
+
+extern "C" int spa_embed_rms_norm(const void* table, int64_t table_rows, const int64_t* ids, const void* pos_table,
+                                  int64_t pos_rows, const int32_t* positions, const void* weight, void* x_out,
+                                  void* out, int rows, int dim, double eps, int dtype, spa_stream_t stream) {
+  if (rows > 0 && (!ids || !pos_table || !positions || !x_out || table_rows <= 0 || pos_rows <= 0))
+    return SPA_ERR_INVALID;
+  return spa::rms_norm_impl(table, ids, table_rows, pos_table, positions, pos_rows, weight, x_out, out, rows, dim, eps,
+                            dtype, stream);
 }

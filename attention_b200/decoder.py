@@ -94,6 +94,53 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     return out
 
 
+def add_rms_norm(x: torch.Tensor, delta: torch.Tensor, weight: torch.Tensor, eps: float, *,
+                 x_out: torch.Tensor | None = None) -> torch.Tensor:
+    """The residual add and the RMSNorm after it in one launch (``spa_add_rms_norm``):
+    ``x_out = x + delta`` (rounded as the elementwise add rounds it), returns
+    ``rms_norm(x_out, weight, eps)``.  ``x_out`` may be ``x`` (in place); by default it is x."""
+    if not (x.is_cuda and delta.is_cuda and weight.is_cuda):
+        raise ValueError("CUDA tensors are required")
+    if delta.shape != x.shape or delta.dtype != x.dtype or not (x.is_contiguous() and delta.is_contiguous()):
+        raise ValueError("x and delta must be contiguous tensors of one shape and dtype")
+    x_out = x if x_out is None else x_out
+    if x_out.shape != x.shape or x_out.dtype != x.dtype or not x_out.is_contiguous():
+        raise ValueError("x_out must be a contiguous tensor like x")
+    w = weight.to(x.dtype).contiguous()
+    out = torch.empty_like(x)
+    dim = x.size(-1)
+    _lib.check(_lib.lib.spa_add_rms_norm(x.data_ptr(), delta.data_ptr(), w.data_ptr(), x_out.data_ptr(),
+                                         out.data_ptr(), x.numel() // dim, dim, float(eps), dtype_code(x),
+                                         stream_ptr(x.device)), "spa_add_rms_norm")
+    return out
+
+
+def embed_rms_norm(table: torch.Tensor, ids: torch.Tensor, pos_table: torch.Tensor, positions: torch.Tensor,
+                   weight: torch.Tensor, eps: float, *, x_out: torch.Tensor) -> torch.Tensor:
+    """Token + position embedding lookup and the first RMSNorm in one launch
+    (``spa_embed_rms_norm``): ``x_out = table[ids] + pos_table[positions]`` (ids int64,
+    positions int32), returns ``rms_norm(x_out, weight, eps)``."""
+    for t in (table, ids, pos_table, positions, weight, x_out):
+        if not t.is_cuda:
+            raise ValueError("CUDA tensors are required")
+    if ids.dtype != torch.int64 or positions.dtype != torch.int32 or ids.shape != positions.shape or ids.dim() != 1:
+        raise ValueError("ids (int64) and positions (int32) must be matching 1-d tensors")
+    if not (ids.is_contiguous() and positions.is_contiguous() and table.is_contiguous() and pos_table.is_contiguous()):
+        raise ValueError("inputs must be contiguous")
+    dim = table.size(-1)
+    if pos_table.dtype != table.dtype or pos_table.size(-1) != dim:
+        raise ValueError("the embedding tables must share dtype and width")
+    if x_out.shape != (ids.numel(), dim) or x_out.dtype != table.dtype or not x_out.is_contiguous():
+        raise ValueError("x_out must be a contiguous [rows, dim] tensor of the tables' dtype")
+    w = weight.to(table.dtype).contiguous()
+    out = torch.empty_like(x_out)
+    _lib.check(_lib.lib.spa_embed_rms_norm(table.data_ptr(), table.size(0), ids.data_ptr(), pos_table.data_ptr(),
+                                           pos_table.size(0), positions.data_ptr(), w.data_ptr(), x_out.data_ptr(),
+                                           out.data_ptr(), ids.numel(), dim, float(eps), dtype_code(table),
+                                           stream_ptr(table.device)), "spa_embed_rms_norm")
+    return out
+
+
 class SparseDecoder:
     """Batch of sequences decoded with paged KV caches (one pool per layer).
 
@@ -183,23 +230,37 @@ class SparseDecoder:
         if not hasattr(self, "_token"):
             b = self.batch
             self._token = torch.zeros(b, dtype=torch.int64, device=self.device)
-            self._position = torch.zeros(b, dtype=torch.int32, device=self.device)
-            self._ctx_len = torch.zeros(b, dtype=torch.int32, device=self.device)
-            self._step_dev = torch.zeros(1, dtype=torch.int32, device=self.device)
+            # position, context length and step counter in one buffer: one launch advances all
+            self._counters = torch.zeros(2 * b + 1, dtype=torch.int32, device=self.device)
+            self._position = self._counters[:b]
+            self._ctx_len = self._counters[b:2 * b]
+            self._step_dev = self._counters[2 * b:]
             self._logits = torch.zeros(b, self.cfg.vocab, dtype=torch.float32, device=self.device)
+            self._x = torch.zeros(b, self.cfg.d_model, dtype=self.dtype, device=self.device)  # residual stream
+            self._sel_bufs: dict = {}  # [layers, B, m] selections, per m
             self._graphs: dict = {}
 
     def _step_body(self):
-        """One decode step on the persistent state (no host synchronisation, capturable)."""
+        """One decode step on the persistent state (no host synchronisation, capturable).
+        Each residual add runs fused with the RMSNorm after it, and the embedding lookup
+        with the first norm; the rounding is that of the separate ops."""
         cfg = self.cfg
         b = self.batch
         h, dh = cfg.heads, cfg.head_dim
-        x = self.w["emb"].index_select(0, self._token) + self.w["pos"].index_select(0, self._position.long())
-        selected = []
+        x = self._x
+        hid = embed_rms_norm(self.w["emb"], self._token, self.w["pos"], self._position, self.w["l0.norm1"], cfg.eps,
+                             x_out=x)
         scale = 1.0 / math.sqrt(dh)
         m = min(cfg.top_m, self.n_routable)
+        if m > 0:
+            sel_all = self._sel_bufs.get(m)
+            if sel_all is None:
+                sel_all = self._sel_bufs[m] = torch.empty(cfg.layers, b, m, dtype=torch.int64, device=self.device)
+        selected = []
+        mlp_out = None
         for i in range(cfg.layers):
-            hid = rms_norm(x, self.w[f"l{i}.norm1"], cfg.eps)
+            if i > 0:
+                hid = add_rms_norm(x, mlp_out, self.w[f"l{i}.norm1"], cfg.eps, x_out=x)
             qkv = self._linear(hid, f"l{i}.qkv").view(b, 3, h, dh)
             q, k, v = qkv[:, 0].contiguous(), qkv[:, 1].contiguous(), qkv[:, 2].contiguous()
             kv_append(self.k_pool[i], self.v_pool[i], self.page_table, k, v, self._position)
@@ -208,22 +269,23 @@ class SparseDecoder:
                 att, sel = sparse_decode_step(q, self.k_pool[i], self.v_pool[i], self.summaries[i], top_blocks=m,
                                               local_window=cfg.local_window, block_size=cfg.page_size,
                                               router_scale=scale, page_table=self.page_table,
-                                              context_lens=self._ctx_len)
+                                              context_lens=self._ctx_len, selected=sel_all[i])
             else:
                 sel = torch.full((b, 1), -1, dtype=torch.int64, device=self.device)
                 att = paged_gather_decode_attention(q, self.k_pool[i], self.v_pool[i], sel,
                                                     local_window=cfg.local_window, block_size=cfg.page_size,
                                                     page_table=self.page_table, context_lens=self._ctx_len)
-            x = x + self._linear(att.reshape(b, cfg.d_model), f"l{i}.out")
-            x = x + self._mlp(x, i)
+            h2 = add_rms_norm(x, self._linear(att.reshape(b, cfg.d_model), f"l{i}.out"), self.w[f"l{i}.norm2"],
+                              cfg.eps, x_out=x)
+            mlp_out = self._linear(F.gelu(self._linear(h2, f"l{i}.fc1")), f"l{i}.fc2")
             selected.append(sel)
-        sel_all = torch.stack(selected)  # [layers, B, m]
+        if m == 0:
+            sel_all = torch.stack(selected)  # [layers, B, 1]
         self.promotion.update(sel_all.reshape(cfg.layers * b, -1), self._step_dev)
-        self._logits.copy_(F.linear(rms_norm(x, self.w["norm_f"], cfg.eps), self.w["head"]).float())
-        self._token.copy_(self._logits.argmax(-1))
-        self._position.add_(1)
-        self._ctx_len.add_(1)
-        self._step_dev.add_(1)
+        hf = add_rms_norm(x, mlp_out, self.w["norm_f"], cfg.eps, x_out=x)
+        self._logits.copy_(F.linear(hf, self.w["head"]))
+        torch.argmax(self._logits, dim=-1, out=self._token)
+        self._counters.add_(1)  # position, context length, step
         return sel_all
 
     def _check_room(self, steps: int) -> None:
@@ -260,7 +322,7 @@ class SparseDecoder:
         sel = self._step_body()
         self.step_index += 1
         self.ctx += 1
-        return self._logits.clone(), sel
+        return self._logits.clone(), sel.clone()
 
     @torch.no_grad()
     def generate(self, token: torch.Tensor, steps: int, *, graphed: bool = True) -> torch.Tensor:

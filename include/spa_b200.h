@@ -67,7 +67,9 @@ const char* spa_version(void);
 const char* spa_last_error(void);
 
 /* Reads and clears the library's device-side error word on the current device
- * (nonzero after a bounded wait gave up or a kernel saw an invalid page id).
+ * (nonzero after a bounded wait gave up or a kernel saw an invalid page id).  Bits:
+ * 1 a bounded wait gave up, 2 an invalid page id was skipped, 4 an embedding row id
+ * outside its table (spa_embed_rms_norm).
  * Synchronises the current device.  Returns SPA_OK or SPA_ERR_CUDA. */
 int spa_device_error(uint32_t* out_flags);
 
@@ -445,6 +447,28 @@ int spa_session_destroy(spa_session* session);
  */
 int spa_rms_norm(const void* x, const void* weight, void* out, int rows, int dim, double eps, int dtype,
                  spa_stream_t stream);
+
+/*
+ * The decoder's residual add fused with the RMSNorm after it (one launch instead of two):
+ * x_out[r, i] = dtype(x[r, i] + delta[r, i]) (rounded once, as a separate elementwise add
+ * rounds it), out = spa_rms_norm(x_out).  x_out may be x itself (an in-place residual
+ * stream); it must not overlap delta.  Same arguments and checks as spa_rms_norm; delta
+ * and x_out are required when rows > 0.
+ */
+int spa_add_rms_norm(const void* x, const void* delta, const void* weight, void* x_out, void* out, int rows, int dim,
+                     double eps, int dtype, spa_stream_t stream);
+
+/*
+ * The start of a decode step fused into one launch: the token and position embedding
+ * lookup and the first RMSNorm (train_tiny_transformer.py:259,270, then the first block's
+ * norm):  x_out[r] = dtype(table[ids[r]] + pos_table[positions[r]]), out = spa_rms_norm(x_out).
+ * table [table_rows, dim] and pos_table [pos_rows, dim] of type dtype; ids int64 and
+ * positions int32, [rows], in device memory.  An id outside its table raises device error
+ * bit 4 (spa_device_error) and gives a zero row.
+ */
+int spa_embed_rms_norm(const void* table, int64_t table_rows, const int64_t* ids, const void* pos_table,
+                       int64_t pos_rows, const int32_t* positions, const void* weight, void* x_out, void* out,
+                       int rows, int dim, double eps, int dtype, spa_stream_t stream);
 
 /*
  * Diagnostic for the failure path: one kernel waits on an mbarrier that nothing

@@ -49,5 +49,11 @@ def test_invalid_arguments_rejected_without_gpu():
     assert _lib.lib.spa_paged_gather_decode(None, 2, 1, 1, 1, 64, None, None, 0, None, 4, 0, 1.0, None, None, 0,
                                             None) == _lib.SPA_ERR_INVALID
     assert _lib.lib.spa_rms_norm(None, None, None, 2, 0, 1e-5, 2, None) == _lib.SPA_ERR_INVALID
+    assert _lib.lib.spa_add_rms_norm(None, None, None, None, None, 2, 64, 1e-5, 2, None) == _lib.SPA_ERR_INVALID
+    assert _lib.lib.spa_add_rms_norm(None, None, None, None, None, 0, 64, 1e-5, 2, None) == _lib.SPA_OK
+    assert _lib.lib.spa_embed_rms_norm(None, 16, None, None, 16, None, None, None, None, 2, 64, 1e-5, 2,
+                                       None) == _lib.SPA_ERR_INVALID
+    assert _lib.lib.spa_embed_rms_norm(None, 0, None, None, 0, None, None, None, None, 0, 64, 1e-5, 2,
+                                       None) == _lib.SPA_OK
     assert _lib.lib.spa_copy(None, None, 16, None) == _lib.SPA_ERR_INVALID
     assert _lib.lib.spa_session_create(None, None) == _lib.SPA_ERR_INVALID

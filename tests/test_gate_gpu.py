@@ -49,6 +49,23 @@ def test_gate_scores_match_reference_fixture(golden_dir, mode):
             assert torch.equal(gate.cached_state, state if expect else cached)
 
 
+@pytest.mark.parametrize("batch,width", [(3, 6), (40, 100), (4, 4096), (1, 4099), (5, 4096)])
+def test_drift_gate_shapes(batch, width):
+    """Drift scores and the refresh copy at widths and batches that take every path of the
+    gate kernel: 16-byte and element loads, several warps per row or several rows per
+    warp, a refresh copy with and without 16-byte accesses and with a partial last round."""
+    gen = torch.Generator().manual_seed(batch * 10007 + width)
+    state = torch.randn(batch, width, generator=gen)
+    cached = state + 0.3 * torch.randn(batch, width, generator=gen)
+    ref = float(drift_distance(state, cached).mean())
+    for thr, expect in ((ref - 0.01, True), (ref + 0.01, False)):
+        gate = _primed(spa.RefreshGate("drift", batch, width=width, threshold=thr), cached.to(DEV))
+        gate.decide(state=state.to(DEV))
+        assert abs(gate.score.item() - ref) <= 1e-5
+        assert gate.refreshed == expect
+        assert torch.equal(gate.cached_state.cpu(), state if expect else cached)
+
+
 def test_first_step_always_routes():
     gate = spa.RefreshGate("drift", 2, width=16, threshold=10.0)
     gate.decide(state=torch.zeros(2, 16, device=DEV))
@@ -77,7 +94,7 @@ def test_ttl_and_signature_decisions():
 def test_gated_router_sequence_matches_oracle():
     """Drift-gated single-level router over 12 steps whose query jumps at steps 4 and 8:
     the selection used each step equals the oracle's promotion-reuse loop, and steps with a
-    closed gate read no summary (they run on NaN summaries)."""
+    closed gate use no summary (they run on NaN summaries)."""
     gen = torch.Generator().manual_seed(11)
     b, hq, hkv, d, n_pages, m = 2, 8, 2, 64, 40, 5
     summ = torch.randn(b, hkv, n_pages, d, generator=gen)

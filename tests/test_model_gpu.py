@@ -1,11 +1,12 @@
 """spa_rms_norm (the integrated decoder's norm in one launch) against a plain PyTorch fp32
-reference of the same formula."""
+reference of the same formula; its fused forms (residual add + norm, embedding lookup +
+norm) bit-exact against the separate ops they replace."""
 
 import pytest
 import torch
 
 import attention_b200 as spa
-from attention_b200.decoder import rms_norm
+from attention_b200.decoder import add_rms_norm, embed_rms_norm, rms_norm
 
 pytestmark = pytest.mark.gpu
 
@@ -36,3 +37,54 @@ def test_rms_norm_zero_rows_and_validation():
     assert rms_norm(x, w, 1e-5).shape == (0, 64)
     with pytest.raises(ValueError):
         rms_norm(torch.ones(2, 64), torch.ones(64), 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(1, 512), (3, 1000), (4, 4096)])
+@pytest.mark.parametrize("in_place", [False, True])
+def test_add_rms_norm_equals_add_then_norm(dtype, shape, in_place):
+    g = torch.Generator(device="cuda").manual_seed(7 * sum(shape))
+    x = (torch.randn(shape, device="cuda", generator=g) * 3).to(dtype)
+    d = (torch.randn(shape, device="cuda", generator=g) * 2).to(dtype)
+    w = (torch.rand(shape[-1], device="cuda", generator=g) + 0.5).to(dtype)
+    want_x = x + d
+    want = rms_norm(want_x, w, 1e-5)
+    x_out = x.clone() if in_place else torch.empty_like(x)
+    src = x_out if in_place else x
+    y = add_rms_norm(src, d, w, 1e-5, x_out=x_out)
+    assert torch.equal(x_out, want_x)
+    assert torch.equal(y, want)
+    assert spa.device_error_flags() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_embed_rms_norm_equals_lookup_add_norm(dtype):
+    g = torch.Generator(device="cuda").manual_seed(3)
+    vocab, n_pos, dim, rows = 4096, 300, 512, 5
+    table = (torch.randn(vocab, dim, device="cuda", generator=g) * 0.02).to(dtype)
+    pos = (torch.randn(n_pos, dim, device="cuda", generator=g) * 0.02).to(dtype)
+    w = (torch.rand(dim, device="cuda", generator=g) + 0.5).to(dtype)
+    ids = torch.tensor([0, 4095, 17, 17, 2048], dtype=torch.int64, device="cuda")
+    positions = torch.tensor([0, 299, 5, 6, 150], dtype=torch.int32, device="cuda")
+    x_out = torch.empty(rows, dim, dtype=dtype, device="cuda")
+    y = embed_rms_norm(table, ids, pos, positions, w, 1e-5, x_out=x_out)
+    want_x = table.index_select(0, ids) + pos.index_select(0, positions.long())
+    assert torch.equal(x_out, want_x)
+    assert torch.equal(y, rms_norm(want_x, w, 1e-5))
+    assert spa.device_error_flags() == 0
+
+
+def test_embed_rms_norm_out_of_range_id_is_flagged():
+    """The kernel's own bounds check: an id past its table gives a zero row and device
+    error bit 4; the other rows are unaffected."""
+    dim = 64
+    table = torch.randn(10, dim, device="cuda")
+    pos = torch.randn(4, dim, device="cuda")
+    w = torch.ones(dim, device="cuda")
+    ids = torch.tensor([3, 10], dtype=torch.int64, device="cuda")
+    positions = torch.tensor([1, 2], dtype=torch.int32, device="cuda")
+    x_out = torch.full((2, dim), 7.0, device="cuda")
+    y = embed_rms_norm(table, ids, pos, positions, w, 1e-5, x_out=x_out)
+    assert spa.device_error_flags() == 4
+    assert torch.equal(x_out[1], torch.zeros(dim, device="cuda")) and torch.equal(y[1], torch.zeros(dim, device="cuda"))
+    assert torch.equal(x_out[0], table[3] + pos[1])
