@@ -89,6 +89,126 @@ int rms_norm_impl(const void* x, const int64_t* x_rows, int64_t x_limit, const v
   SPA_CHECK_CUDA(cudaGetLastError());
   return SPA_OK;
 }
+
+// Linear layer for a handful of rows (the decoder's batch at decode time), where a library
+// GEMM is launch- and latency-bound: y[m, n] = act(T(x[m, :] . w[n, :] + b[n])), w [N, K]
+// row-major as a torch Linear weight.  One warp per output column n: its lanes read the
+// weight row with 16-byte loads (all of a 2048-element slice in flight) while the CTA
+// stages x in shared memory; fp32 products and sums, one warp reduction, one rounding to
+// T (as the GEMM's output is rounded), then the activation: exact GELU,
+// 0.5 f (1 + erf(f / sqrt 2)) in fp32, rounded again.  out_f32 stores float(y).
+constexpr int kLinearMaxRows = 4;
+constexpr int kLinearWarps = 8;
+constexpr int kLinearBatch = 8;  // 16-byte weight loads per lane in flight
+
+template <typename T>
+__device__ __forceinline__ float dot16(const uint4& wv, const uint4& xv, float acc) {
+  const T* we = reinterpret_cast<const T*>(&wv);
+  const T* xe = reinterpret_cast<const T*>(&xv);
+#pragma unroll
+  for (int j = 0; j < static_cast<int>(16 / sizeof(T)); ++j) acc = fmaf(to_f32(we[j]), to_f32(xe[j]), acc);
+  return acc;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kLinearWarps * 32) linear_rows_kernel(const T* __restrict__ x,
+                                                                        const T* __restrict__ w,
+                                                                        const T* __restrict__ bias,
+                                                                        void* __restrict__ out, int rows, int K,
+                                                                        int N, int gelu, int out_f32, int vec) {
+  extern __shared__ __align__(16) unsigned char linear_smem[];
+  T* xs = reinterpret_cast<T*>(linear_smem);  // [rows][K]
+  constexpr int kVec = 16 / sizeof(T);        // elements per 16-byte load
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * kLinearWarps + warp;
+  const T* wr = w + static_cast<int64_t>(n < N ? n : 0) * K;
+  // the first weight batch is requested before x is staged
+  uint4 r[kLinearBatch];
+  if (vec && n < N) {
+#pragma unroll
+    for (int u = 0; u < kLinearBatch; ++u) {
+      const int k = (lane + 32 * u) * kVec;
+      if (k < K) r[u] = __ldg(reinterpret_cast<const uint4*>(wr + k));
+    }
+  }
+  const int total = rows * K;
+  if (vec) {
+    for (int i = threadIdx.x; i < total / kVec; i += blockDim.x)
+      reinterpret_cast<uint4*>(xs)[i] = __ldg(reinterpret_cast<const uint4*>(x) + i);
+  } else {
+    for (int i = threadIdx.x; i < total; i += blockDim.x) xs[i] = x[i];
+  }
+  __syncthreads();
+  if (n >= N) return;
+  float acc[kLinearMaxRows];
+#pragma unroll
+  for (int m = 0; m < kLinearMaxRows; ++m) acc[m] = 0.f;
+  if (vec) {
+    for (int base = 0; base < K; base += 32 * kVec * kLinearBatch) {
+      if (base > 0) {
+#pragma unroll
+        for (int u = 0; u < kLinearBatch; ++u) {
+          const int k = base + (lane + 32 * u) * kVec;
+          if (k < K) r[u] = __ldg(reinterpret_cast<const uint4*>(wr + k));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kLinearBatch; ++u) {
+        const int k = base + (lane + 32 * u) * kVec;
+        if (k < K) {
+#pragma unroll
+          for (int m = 0; m < kLinearMaxRows; ++m)
+            if (m < rows) acc[m] = dot16<T>(r[u], *reinterpret_cast<const uint4*>(xs + m * K + k), acc[m]);
+        }
+      }
+    }
+  } else {
+    for (int k = lane; k < K; k += 32) {
+      const float wv = to_f32(wr[k]);
+#pragma unroll
+      for (int m = 0; m < kLinearMaxRows; ++m)
+        if (m < rows) acc[m] = fmaf(wv, to_f32(xs[m * K + k]), acc[m]);
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < kLinearMaxRows; ++m)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], off);
+  if (lane < rows) {
+    float v = acc[0];
+#pragma unroll
+    for (int m = 1; m < kLinearMaxRows; ++m)
+      if (lane == m) v = acc[m];
+    if (bias) v += to_f32(bias[n]);
+    T y = from_f32<T>(v);
+    if (gelu) {
+      const float f = to_f32(y);
+      y = from_f32<T>(f * 0.5f * (1.f + erff(f * 0.70710678118654752f)));
+    }
+    const int64_t o = static_cast<int64_t>(lane) * N + n;
+    if (out_f32)
+      static_cast<float*>(out)[o] = to_f32(y);
+    else
+      static_cast<T*>(out)[o] = y;
+  }
+}
+
+template <typename T>
+int launch_linear(const void* x, const void* w, const void* bias, void* out, int rows, int K, int N, int gelu,
+                  int out_f32, cudaStream_t st) {
+  constexpr int kVec = 16 / sizeof(T);
+  const size_t smem = static_cast<size_t>(rows) * K * sizeof(T);
+  if (smem > 200 * 1024) return SPA_ERR_UNSUPPORTED;
+  const int vec = K % kVec == 0 &&
+                  ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) % 16 == 0);
+  auto kern = linear_rows_kernel<T>;
+  SPA_CHECK_CUDA(spa_set_smem_once(kern, static_cast<int>(smem)));
+  kern<<<(N + kLinearWarps - 1) / kLinearWarps, kLinearWarps * 32, smem, st>>>(
+      static_cast<const T*>(x), static_cast<const T*>(w), static_cast<const T*>(bias), out, rows, K, N, gelu, out_f32,
+      vec);
+  SPA_CHECK_CUDA(cudaGetLastError());
+  return SPA_OK;
+}
 }  // namespace spa
 
 extern "C" int spa_rms_norm(const void* x, const void* weight, void* out, int rows, int dim, double eps, int dtype,
@@ -110,4 +230,20 @@ extern "C" int spa_embed_rms_norm(const void* table, int64_t table_rows, const i
     return SPA_ERR_INVALID;
   return spa::rms_norm_impl(table, ids, table_rows, pos_table, positions, pos_rows, weight, x_out, out, rows, dim, eps,
                             dtype, stream);
+}
+
+extern "C" int spa_linear(const void* x, const void* weight, const void* bias, void* out, int rows, int in_features,
+                          int out_features, int activation, int out_f32, int dtype, spa_stream_t stream) {
+  if (rows < 0 || rows > spa::kLinearMaxRows || in_features <= 0 || out_features <= 0 || !dtype_ok(dtype) ||
+      (activation != 0 && activation != 1) || (out_f32 != 0 && out_f32 != 1))
+    return SPA_ERR_INVALID;
+  if (rows == 0) return SPA_OK;
+  if (!x || !weight || !out) return SPA_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == SPA_F32)
+    return spa::launch_linear<float>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, st);
+  if (dtype == SPA_F16)
+    return spa::launch_linear<__half>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, st);
+  return spa::launch_linear<__nv_bfloat16>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32,
+                                           st);
 }

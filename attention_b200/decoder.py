@@ -115,6 +115,34 @@ def add_rms_norm(x: torch.Tensor, delta: torch.Tensor, weight: torch.Tensor, eps
     return out
 
 
+LINEAR_MAX_ROWS = 4
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *, gelu: bool = False,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """``F.linear`` (then exact GELU when ``gelu``) for 1..4 rows in one launch
+    (``spa_linear``): fp32 products and sums, rounded to x's dtype.  ``out`` may be an fp32
+    tensor, which then holds the rounded values."""
+    if not (x.is_cuda and weight.is_cuda and (bias is None or bias.is_cuda)):
+        raise ValueError("CUDA tensors are required")
+    if x.dim() != 2 or not 0 < x.size(0) <= LINEAR_MAX_ROWS:
+        raise ValueError(f"x must be [rows, in_features] with 1..{LINEAR_MAX_ROWS} rows")
+    n, k = weight.shape
+    if x.size(1) != k or weight.dtype != x.dtype or (bias is not None and (bias.shape != (n,) or bias.dtype != x.dtype)):
+        raise ValueError("x, weight and bias shapes or dtypes do not match")
+    if not (x.is_contiguous() and weight.is_contiguous() and (bias is None or bias.is_contiguous())):
+        raise ValueError("inputs must be contiguous")
+    if out is None:
+        out = torch.empty(x.size(0), n, dtype=x.dtype, device=x.device)
+    elif out.shape != (x.size(0), n) or out.dtype not in (x.dtype, torch.float32) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous [rows, out_features] tensor of x's dtype or fp32")
+    _lib.check(_lib.lib.spa_linear(x.data_ptr(), weight.data_ptr(), bias.data_ptr() if bias is not None else None,
+                                   out.data_ptr(), x.size(0), k, n, 1 if gelu else 0,
+                                   1 if out.dtype != x.dtype else 0, dtype_code(x), stream_ptr(x.device)),
+               "spa_linear")
+    return out
+
+
 def embed_rms_norm(table: torch.Tensor, ids: torch.Tensor, pos_table: torch.Tensor, positions: torch.Tensor,
                    weight: torch.Tensor, eps: float, *, x_out: torch.Tensor) -> torch.Tensor:
     """Token + position embedding lookup and the first RMSNorm in one launch
@@ -164,12 +192,16 @@ class SparseDecoder:
         self.step_index = 0
 
     # ---------------------------------------------------------------- helpers
-    def _linear(self, x, name):
-        return F.linear(x, self.w[f"{name}.w"], self.w[f"{name}.b"])
+    def _linear(self, x, name, *, gelu=False):
+        w, b = self.w[f"{name}.w"], self.w[f"{name}.b"]
+        if x.dim() == 2 and x.size(0) <= LINEAR_MAX_ROWS:
+            return linear(x, w, b, gelu=gelu)  # decode: a few rows, one launch
+        y = F.linear(x, w, b)
+        return F.gelu(y) if gelu else y
 
     def _mlp(self, x, i):
         h = rms_norm(x, self.w[f"l{i}.norm2"], self.cfg.eps)
-        return self._linear(F.gelu(self._linear(h, f"l{i}.fc1")), f"l{i}.fc2")
+        return self._linear(self._linear(h, f"l{i}.fc1", gelu=True), f"l{i}.fc2")
 
     def _routable_pages(self, ctx: int) -> int:
         return max(0, (ctx - self.cfg.local_window) // self.cfg.page_size)
@@ -277,13 +309,16 @@ class SparseDecoder:
                                                     page_table=self.page_table, context_lens=self._ctx_len)
             h2 = add_rms_norm(x, self._linear(att.reshape(b, cfg.d_model), f"l{i}.out"), self.w[f"l{i}.norm2"],
                               cfg.eps, x_out=x)
-            mlp_out = self._linear(F.gelu(self._linear(h2, f"l{i}.fc1")), f"l{i}.fc2")
+            mlp_out = self._linear(self._linear(h2, f"l{i}.fc1", gelu=True), f"l{i}.fc2")
             selected.append(sel)
         if m == 0:
             sel_all = torch.stack(selected)  # [layers, B, 1]
         self.promotion.update(sel_all.reshape(cfg.layers * b, -1), self._step_dev)
         hf = add_rms_norm(x, mlp_out, self.w["norm_f"], cfg.eps, x_out=x)
-        self._logits.copy_(F.linear(hf, self.w["head"]))
+        if b <= LINEAR_MAX_ROWS:
+            linear(hf, self.w["head"], out=self._logits)  # fp32 logits of the rounded products
+        else:
+            self._logits.copy_(F.linear(hf, self.w["head"]))
         torch.argmax(self._logits, dim=-1, out=self._token)
         self._counters.add_(1)  # position, context length, step
         return sel_all

@@ -471,6 +471,18 @@ int spa_embed_rms_norm(const void* table, int64_t table_rows, const int64_t* ids
                        int rows, int dim, double eps, int dtype, spa_stream_t stream);
 
 /*
+ * Linear layer for 1..4 rows (the decoder's batch at decode time, where a library GEMM is
+ * launch-bound): out[m, n] = act(dtype(x[m, :] . weight[n, :] + bias[n])), weight
+ * [out_features, in_features] row-major (a torch Linear weight), bias optional (NULL).
+ * fp32 products and sums, one rounding to dtype; activation 0 none, 1 exact GELU
+ * (0.5 f (1 + erf(f / sqrt 2)) on the rounded value, rounded again).  out is of type dtype,
+ * or fp32 holding the dtype-rounded values when out_f32 = 1.  x, weight, bias, out
+ * contiguous.  rows > 4 returns SPA_ERR_INVALID.
+ */
+int spa_linear(const void* x, const void* weight, const void* bias, void* out, int rows, int in_features,
+               int out_features, int activation, int out_f32, int dtype, spa_stream_t stream);
+
+/*
  * Diagnostic for the failure path: one kernel waits on an mbarrier that nothing
  * completes, with the library's bounded wait limited to `cycles` (1 .. 4e9 clock
  * cycles).  The wait gives up, the kernel returns, and spa_device_error then reports

@@ -1,12 +1,13 @@
 """spa_rms_norm (the integrated decoder's norm in one launch) against a plain PyTorch fp32
 reference of the same formula; its fused forms (residual add + norm, embedding lookup +
-norm) bit-exact against the separate ops they replace."""
+norm) bit-exact against the separate ops they replace; the few-row linear layer against
+a plain PyTorch fp32 reference."""
 
 import pytest
 import torch
 
 import attention_b200 as spa
-from attention_b200.decoder import add_rms_norm, embed_rms_norm, rms_norm
+from attention_b200.decoder import add_rms_norm, embed_rms_norm, linear, rms_norm
 
 pytestmark = pytest.mark.gpu
 
@@ -88,3 +89,36 @@ def test_embed_rms_norm_out_of_range_id_is_flagged():
     assert spa.device_error_flags() == 4
     assert torch.equal(x_out[1], torch.zeros(dim, device="cuda")) and torch.equal(y[1], torch.zeros(dim, device="cuda"))
     assert torch.equal(x_out[0], table[3] + pos[1])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rows,k,n", [(1, 512, 1536), (2, 2048, 512), (4, 512, 4096), (3, 100, 37), (1, 4104, 24)])
+@pytest.mark.parametrize("gelu", [False, True])
+def test_linear_rows_matches_fp32_reference(dtype, rows, k, n, gelu):
+    g = torch.Generator(device="cuda").manual_seed(rows * 131 + k + n)
+    x = torch.randn(rows, k, device="cuda", generator=g).to(dtype)
+    w = (torch.randn(n, k, device="cuda", generator=g) * k ** -0.5).to(dtype)
+    b = torch.randn(n, device="cuda", generator=g).to(dtype)
+    y = linear(x, w, b, gelu=gelu)
+    ref = x.float() @ w.float().T + b.float()
+    # the kernel rounds the sum to dtype before the activation, as the GEMM's output is
+    ref_r = ref.to(dtype).float()
+    if gelu:
+        ref_r = torch.nn.functional.gelu(ref_r)
+    # fp32: summation order only; 16-bit: one or two roundings (2^-8 relative) plus the
+    # flip of a rounding when the fp32 sums differ in their last bits
+    atol, rtol = (1e-4, 1e-4) if dtype == torch.float32 else (2e-2, 1.6e-2)
+    assert y.dtype == dtype and y.shape == (rows, n)
+    assert ((y.float() - ref_r).abs() <= atol + rtol * ref_r.abs()).all()
+    assert spa.device_error_flags() == 0
+
+
+def test_linear_fp32_out_holds_rounded_values():
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(2, 512, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(4096, 512, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    out = torch.empty(2, 4096, device="cuda")
+    linear(x, w, out=out)
+    assert torch.equal(out, linear(x, w).float())
+    with pytest.raises(ValueError):
+        linear(torch.ones(5, 512, device="cuda", dtype=torch.bfloat16), w)
