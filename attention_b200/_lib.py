@@ -61,6 +61,14 @@ GATE_TTL, GATE_SIGNATURE, GATE_DRIFT, GATE_LEARNED = 0, 1, 2, 3
 SESSION_DIRECT_IN, SESSION_COPY_IN, SESSION_ROUTER_IN_DIRECT_OUT, SESSION_COPY_IN_DIRECT_OUT = 0, 1, 2, 3
 
 
+class NormPrologue(ctypes.Structure):
+    """spa_norm_prologue (include/spa_b200.h)."""
+
+    _fields_ = [("delta", ctypes.c_void_p), ("ids", ctypes.c_void_p), ("id_limit", ctypes.c_int64),
+                ("delta_ids", ctypes.c_void_p), ("delta_limit", ctypes.c_int64), ("norm_weight", ctypes.c_void_p),
+                ("eps", ctypes.c_double), ("x_out", ctypes.c_void_p)]
+
+
 class SessionParams(ctypes.Structure):
     """spa_session_params (include/spa_b200.h)."""
 
@@ -113,6 +121,7 @@ PROTOTYPES = {
     "spa_add_rms_norm": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _d, _i, _vp]),
     "spa_embed_rms_norm": (_i, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i, _i, _d, _i, _vp]),
     "spa_linear": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "spa_norm_linear": (_i, [_vp, ctypes.POINTER(NormPrologue), _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
 }
 
 

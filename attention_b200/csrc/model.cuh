@@ -110,12 +110,29 @@ __device__ __forceinline__ float dot16(const uint4& wv, const uint4& xv, float a
   return acc;
 }
 
+// Optional prologue: the rows fed to the product are RMSNorm(x (+ delta)) computed by every
+// CTA for itself with the arithmetic of rms_norm_kernel (same thread-to-element mapping and
+// reduction order, so the normalised rows are bit-identical to a separate norm launch),
+// and CTA 0 stores the summed rows to x_out.  ids / delta_ids select table rows as in
+// rms_norm_kernel (embedding lookup).
+struct LinearPro {
+  const void* delta;
+  const int64_t* ids;
+  int64_t id_limit;
+  const int32_t* delta_ids;
+  int64_t delta_limit;
+  const void* norm_w;
+  void* x_out;
+  float eps;
+};
+
 template <typename T>
 __global__ void __launch_bounds__(kLinearWarps * 32) linear_rows_kernel(const T* __restrict__ x,
                                                                         const T* __restrict__ w,
                                                                         const T* __restrict__ bias,
                                                                         void* __restrict__ out, int rows, int K,
-                                                                        int N, int gelu, int out_f32, int vec) {
+                                                                        int N, int gelu, int out_f32, int vec,
+                                                                        const LinearPro pro) {
   extern __shared__ __align__(16) unsigned char linear_smem[];
   T* xs = reinterpret_cast<T*>(linear_smem);  // [rows][K]
   constexpr int kVec = 16 / sizeof(T);        // elements per 16-byte load
@@ -132,7 +149,54 @@ __global__ void __launch_bounds__(kLinearWarps * 32) linear_rows_kernel(const T*
     }
   }
   const int total = rows * K;
-  if (vec) {
+  if (pro.norm_w) {
+    __shared__ float part[kLinearMaxRows][kLinearWarps];
+    const T* dl = static_cast<const T*>(pro.delta);
+    const T* nw = static_cast<const T*>(pro.norm_w);
+    T* xo = blockIdx.x == 0 ? static_cast<T*>(pro.x_out) : nullptr;
+    const T* xr[kLinearMaxRows];
+    const T* dr[kLinearMaxRows];
+    bool bad[kLinearMaxRows];
+#pragma unroll
+    for (int m = 0; m < kLinearMaxRows; ++m) {
+      const int mm = m < rows ? m : 0;
+      const int64_t xi = pro.ids ? pro.ids[mm] : mm;
+      const int64_t di = pro.delta_ids ? static_cast<int64_t>(pro.delta_ids[mm]) : mm;
+      bad[m] = (pro.ids && (xi < 0 || xi >= pro.id_limit)) || (dl && pro.delta_ids && (di < 0 || di >= pro.delta_limit));
+      xr[m] = x + (bad[m] ? 0 : xi) * K;
+      dr[m] = dl ? dl + (bad[m] ? 0 : di) * K : nullptr;
+    }
+    auto value = [&](int m, int i) -> float {
+      if (bad[m]) return 0.f;
+      const float v = to_f32(xr[m][i]);
+      return dr[m] ? to_f32(from_f32<T>(v + to_f32(dr[m][i]))) : v;
+    };
+#pragma unroll
+    for (int m = 0; m < kLinearMaxRows; ++m) {
+      if (m >= rows) break;
+      if (bad[m] && blockIdx.x == 0 && threadIdx.x == 0) spa_raise(SPA_DEVERR_BAD_INDEX);
+      float ss = 0.f;
+      for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        const float v = value(m, i);
+        if (xo) xo[m * K + i] = from_f32<T>(v);
+        ss = fmaf(v, v, ss);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (lane == 0) part[m][warp] = ss;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < kLinearMaxRows; ++m) {
+      if (m >= rows) break;
+      float tot = 0.f;
+#pragma unroll
+      for (int k = 0; k < kLinearWarps; ++k) tot += part[m][k];
+      const float r = rsqrtf(tot / static_cast<float>(K) + pro.eps);
+      for (int i = threadIdx.x; i < K; i += blockDim.x)
+        xs[m * K + i] = bad[m] ? from_f32<T>(0.f) : from_f32<T>(value(m, i) * r * to_f32(nw[i]));
+    }
+  } else if (vec) {
     for (int i = threadIdx.x; i < total / kVec; i += blockDim.x)
       reinterpret_cast<uint4*>(xs)[i] = __ldg(reinterpret_cast<const uint4*>(x) + i);
   } else {
@@ -195,17 +259,18 @@ __global__ void __launch_bounds__(kLinearWarps * 32) linear_rows_kernel(const T*
 
 template <typename T>
 int launch_linear(const void* x, const void* w, const void* bias, void* out, int rows, int K, int N, int gelu,
-                  int out_f32, cudaStream_t st) {
+                  int out_f32, const LinearPro& pro, cudaStream_t st) {
   constexpr int kVec = 16 / sizeof(T);
   const size_t smem = static_cast<size_t>(rows) * K * sizeof(T);
   if (smem > 200 * 1024) return SPA_ERR_UNSUPPORTED;
-  const int vec = K % kVec == 0 &&
-                  ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) % 16 == 0);
+  // the 16-byte path needs aligned weight rows, and aligned x when x is staged as is
+  const int vec = K % kVec == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
+                  (pro.norm_w || reinterpret_cast<uintptr_t>(x) % 16 == 0);
   auto kern = linear_rows_kernel<T>;
   SPA_CHECK_CUDA(spa_set_smem_once(kern, static_cast<int>(smem)));
   kern<<<(N + kLinearWarps - 1) / kLinearWarps, kLinearWarps * 32, smem, st>>>(
       static_cast<const T*>(x), static_cast<const T*>(w), static_cast<const T*>(bias), out, rows, K, N, gelu, out_f32,
-      vec);
+      vec, pro);
   SPA_CHECK_CUDA(cudaGetLastError());
   return SPA_OK;
 }
@@ -232,18 +297,46 @@ extern "C" int spa_embed_rms_norm(const void* table, int64_t table_rows, const i
                             dtype, stream);
 }
 
-extern "C" int spa_linear(const void* x, const void* weight, const void* bias, void* out, int rows, int in_features,
-                          int out_features, int activation, int out_f32, int dtype, spa_stream_t stream) {
-  if (rows < 0 || rows > spa::kLinearMaxRows || in_features <= 0 || out_features <= 0 || !dtype_ok(dtype) ||
+namespace spa {
+int linear_impl(const void* x, const void* weight, const void* bias, void* out, int rows, int in_features,
+                int out_features, int activation, int out_f32, int dtype, const LinearPro& pro, spa_stream_t stream) {
+  if (rows < 0 || rows > kLinearMaxRows || in_features <= 0 || out_features <= 0 || !dtype_ok(dtype) ||
       (activation != 0 && activation != 1) || (out_f32 != 0 && out_f32 != 1))
     return SPA_ERR_INVALID;
   if (rows == 0) return SPA_OK;
   if (!x || !weight || !out) return SPA_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == SPA_F32)
-    return spa::launch_linear<float>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, st);
+    return launch_linear<float>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, pro, st);
   if (dtype == SPA_F16)
-    return spa::launch_linear<__half>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, st);
-  return spa::launch_linear<__nv_bfloat16>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32,
-                                           st);
+    return launch_linear<__half>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, pro, st);
+  return launch_linear<__nv_bfloat16>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, pro,
+                                      st);
+}
+}  // namespace spa
+
+extern "C" int spa_linear(const void* x, const void* weight, const void* bias, void* out, int rows, int in_features,
+                          int out_features, int activation, int out_f32, int dtype, spa_stream_t stream) {
+  const spa::LinearPro pro{};
+  return spa::linear_impl(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, dtype, pro,
+                          stream);
+}
+
+extern "C" int spa_norm_linear(const void* x, const spa_norm_prologue* norm, const void* weight, const void* bias,
+                               void* out, int rows, int in_features, int out_features, int activation, int out_f32,
+                               int dtype, spa_stream_t stream) {
+  if (!norm || !norm->norm_weight) return SPA_ERR_INVALID;
+  if (norm->ids && (norm->id_limit <= 0 || !norm->delta || !norm->delta_ids || norm->delta_limit <= 0))
+    return SPA_ERR_INVALID;
+  spa::LinearPro pro{};
+  pro.delta = norm->delta;
+  pro.ids = norm->ids;
+  pro.id_limit = norm->id_limit;
+  pro.delta_ids = norm->delta_ids;
+  pro.delta_limit = norm->delta_limit;
+  pro.norm_w = norm->norm_weight;
+  pro.x_out = norm->x_out;
+  pro.eps = static_cast<float>(norm->eps);
+  return spa::linear_impl(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, dtype, pro,
+                          stream);
 }

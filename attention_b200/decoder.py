@@ -18,6 +18,7 @@ attention, routing, KV append and the promotion table are this library's kernels
 
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 
@@ -140,6 +141,65 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
                                    out.data_ptr(), x.size(0), k, n, 1 if gelu else 0,
                                    1 if out.dtype != x.dtype else 0, dtype_code(x), stream_ptr(x.device)),
                "spa_linear")
+    return out
+
+
+def norm_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *,
+                norm_weight: torch.Tensor, eps: float, delta: torch.Tensor | None = None,
+                x_out: torch.Tensor | None = None, ids: torch.Tensor | None = None,
+                positions: torch.Tensor | None = None, gelu: bool = False,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """``linear(rms_norm(x (+ delta)), weight, bias)`` for 1..4 rows in one launch
+    (``spa_norm_linear``); the normalised rows are bit-identical to ``add_rms_norm`` /
+    ``rms_norm``.  With ``ids`` (int64) and ``positions`` (int32), ``x`` and ``delta`` are
+    the token and position embedding tables and the rows are looked up as in
+    ``embed_rms_norm``.  ``x_out`` (optional) receives the summed rows and must be a
+    separate buffer from ``x`` and ``delta``."""
+    tensors = [x, weight, norm_weight] + [t for t in (bias, delta, x_out, ids, positions, out) if t is not None]
+    if not all(t.is_cuda for t in tensors):
+        raise ValueError("CUDA tensors are required")
+    n, k = weight.shape
+    embed = ids is not None
+    if embed:
+        if (positions is None or delta is None or ids.dtype != torch.int64 or positions.dtype != torch.int32
+                or ids.dim() != 1 or ids.shape != positions.shape):
+            raise ValueError("embedding mode needs delta and matching 1-d int64 ids / int32 positions")
+        rows = ids.numel()
+        if x.dim() != 2 or delta.dim() != 2 or delta.size(1) != k:
+            raise ValueError("embedding tables must be [rows, in_features]")
+    else:
+        rows = x.size(0) if x.dim() == 2 else -1
+        if delta is not None and delta.shape != x.shape:
+            raise ValueError("delta must match x")
+    if not 0 < rows <= LINEAR_MAX_ROWS or x.size(-1) != k or norm_weight.numel() != k:
+        raise ValueError(f"x must be [rows, in_features] with 1..{LINEAR_MAX_ROWS} rows")
+    if weight.dtype != x.dtype or (delta is not None and delta.dtype != x.dtype) or (
+            bias is not None and (bias.shape != (n,) or bias.dtype != x.dtype)):
+        raise ValueError("x, delta, weight and bias shapes or dtypes do not match")
+    if not all(t.is_contiguous() for t in tensors):
+        raise ValueError("inputs must be contiguous")
+    if x_out is not None:
+        if x_out.shape != (rows, k) or x_out.dtype != x.dtype:
+            raise ValueError("x_out must be [rows, in_features] of x's dtype")
+        if x_out.data_ptr() in (x.data_ptr(), delta.data_ptr() if delta is not None else -1):
+            raise ValueError("x_out must not overlap x or delta")
+    if out is None:
+        out = torch.empty(rows, n, dtype=x.dtype, device=x.device)
+    elif out.shape != (rows, n) or out.dtype not in (x.dtype, torch.float32):
+        raise ValueError("out must be a contiguous [rows, out_features] tensor of x's dtype or fp32")
+    nw = norm_weight.to(x.dtype).contiguous()
+    pro = _lib.NormPrologue()
+    pro.delta = delta.data_ptr() if delta is not None else None
+    if embed:
+        pro.ids, pro.id_limit = ids.data_ptr(), x.size(0)
+        pro.delta_ids, pro.delta_limit = positions.data_ptr(), delta.size(0)
+    pro.norm_weight = nw.data_ptr()
+    pro.eps = float(eps)
+    pro.x_out = x_out.data_ptr() if x_out is not None else None
+    _lib.check(_lib.lib.spa_norm_linear(x.data_ptr(), ctypes.byref(pro), weight.data_ptr(),
+                                        bias.data_ptr() if bias is not None else None, out.data_ptr(), rows, k, n,
+                                        1 if gelu else 0, 1 if out.dtype != x.dtype else 0, dtype_code(x),
+                                        stream_ptr(x.device)), "spa_norm_linear")
     return out
 
 
@@ -268,20 +328,38 @@ class SparseDecoder:
             self._ctx_len = self._counters[b:2 * b]
             self._step_dev = self._counters[2 * b:]
             self._logits = torch.zeros(b, self.cfg.vocab, dtype=torch.float32, device=self.device)
-            self._x = torch.zeros(b, self.cfg.d_model, dtype=self.dtype, device=self.device)  # residual stream
+            # the residual stream, alternating between two buffers (a fused norm + linear
+            # reads one while its first CTA writes the updated rows to the other)
+            self._xa = torch.zeros(b, self.cfg.d_model, dtype=self.dtype, device=self.device)
+            self._xb = torch.zeros_like(self._xa)
             self._sel_bufs: dict = {}  # [layers, B, m] selections, per m
             self._graphs: dict = {}
 
+    def _norm_linear(self, x, delta, norm, name, x_out, *, gelu=False):
+        """x_out = x + delta; returns the linear layer ``name`` of rms_norm(x_out): one
+        launch for a batch of up to four rows, else the norm and a library GEMM."""
+        w, b = self.w[f"{name}.w"], self.w[f"{name}.b"]
+        if self.batch <= LINEAR_MAX_ROWS:
+            return norm_linear(x, w, b, norm_weight=self.w[norm], eps=self.cfg.eps, delta=delta, x_out=x_out,
+                               gelu=gelu)
+        return self._linear(add_rms_norm(x, delta, self.w[norm], self.cfg.eps, x_out=x_out), name, gelu=gelu)
+
     def _step_body(self):
         """One decode step on the persistent state (no host synchronisation, capturable).
-        Each residual add runs fused with the RMSNorm after it, and the embedding lookup
-        with the first norm; the rounding is that of the separate ops."""
+        Each RMSNorm runs fused into the linear layer after it, together with the residual
+        add before it (the embedding lookup for the first); the rounding is that of the
+        separate ops."""
         cfg = self.cfg
         b = self.batch
         h, dh = cfg.heads, cfg.head_dim
-        x = self._x
-        hid = embed_rms_norm(self.w["emb"], self._token, self.w["pos"], self._position, self.w["l0.norm1"], cfg.eps,
-                             x_out=x)
+        x, spare = self._xa, self._xb
+        if b <= LINEAR_MAX_ROWS:
+            qkv = norm_linear(self.w["emb"], self.w["l0.qkv.w"], self.w["l0.qkv.b"], norm_weight=self.w["l0.norm1"],
+                              eps=cfg.eps, delta=self.w["pos"], ids=self._token, positions=self._position, x_out=x)
+        else:
+            hid = embed_rms_norm(self.w["emb"], self._token, self.w["pos"], self._position, self.w["l0.norm1"],
+                                 cfg.eps, x_out=x)
+            qkv = self._linear(hid, "l0.qkv")
         scale = 1.0 / math.sqrt(dh)
         m = min(cfg.top_m, self.n_routable)
         if m > 0:
@@ -292,8 +370,9 @@ class SparseDecoder:
         mlp_out = None
         for i in range(cfg.layers):
             if i > 0:
-                hid = add_rms_norm(x, mlp_out, self.w[f"l{i}.norm1"], cfg.eps, x_out=x)
-            qkv = self._linear(hid, f"l{i}.qkv").view(b, 3, h, dh)
+                qkv = self._norm_linear(x, mlp_out, f"l{i}.norm1", f"l{i}.qkv", spare)
+                x, spare = spare, x
+            qkv = qkv.view(b, 3, h, dh)
             q, k, v = qkv[:, 0].contiguous(), qkv[:, 1].contiguous(), qkv[:, 2].contiguous()
             kv_append(self.k_pool[i], self.v_pool[i], self.page_table, k, v, self._position)
             if m > 0:
@@ -307,17 +386,19 @@ class SparseDecoder:
                 att = paged_gather_decode_attention(q, self.k_pool[i], self.v_pool[i], sel,
                                                     local_window=cfg.local_window, block_size=cfg.page_size,
                                                     page_table=self.page_table, context_lens=self._ctx_len)
-            h2 = add_rms_norm(x, self._linear(att.reshape(b, cfg.d_model), f"l{i}.out"), self.w[f"l{i}.norm2"],
-                              cfg.eps, x_out=x)
-            mlp_out = self._linear(self._linear(h2, f"l{i}.fc1", gelu=True), f"l{i}.fc2")
+            o = self._linear(att.reshape(b, cfg.d_model), f"l{i}.out")
+            hid = self._norm_linear(x, o, f"l{i}.norm2", f"l{i}.fc1", spare, gelu=True)
+            x, spare = spare, x
+            mlp_out = self._linear(hid, f"l{i}.fc2")
             selected.append(sel)
         if m == 0:
             sel_all = torch.stack(selected)  # [layers, B, 1]
         self.promotion.update(sel_all.reshape(cfg.layers * b, -1), self._step_dev)
-        hf = add_rms_norm(x, mlp_out, self.w["norm_f"], cfg.eps, x_out=x)
         if b <= LINEAR_MAX_ROWS:
-            linear(hf, self.w["head"], out=self._logits)  # fp32 logits of the rounded products
+            # fp32 logits of the rounded products
+            norm_linear(x, self.w["head"], norm_weight=self.w["norm_f"], eps=cfg.eps, delta=mlp_out, out=self._logits)
         else:
+            hf = add_rms_norm(x, mlp_out, self.w["norm_f"], cfg.eps, x_out=spare)
             self._logits.copy_(F.linear(hf, self.w["head"]))
         torch.argmax(self._logits, dim=-1, out=self._token)
         self._counters.add_(1)  # position, context length, step

@@ -482,6 +482,32 @@ int spa_embed_rms_norm(const void* table, int64_t table_rows, const int64_t* ids
 int spa_linear(const void* x, const void* weight, const void* bias, void* out, int rows, int in_features,
                int out_features, int activation, int out_f32, int dtype, spa_stream_t stream);
 
+/* The RMSNorm in front of a spa_linear, fused into it (spa_norm_linear). */
+typedef struct spa_norm_prologue {
+  const void* delta;        /* added to x before the norm, rounded to dtype (NULL: none) */
+  const int64_t* ids;       /* embedding mode: x row m is x[ids[m]] (NULL: row m) */
+  int64_t id_limit;         /* rows of the x table (embedding mode) */
+  const int32_t* delta_ids; /* embedding mode: delta row m is delta[delta_ids[m]] */
+  int64_t delta_limit;      /* rows of the delta table (embedding mode) */
+  const void* norm_weight;  /* RMSNorm weight [in_features], required */
+  double eps;
+  void* x_out;              /* receives the summed rows [rows, in_features] (NULL: not kept);
+                               must not overlap x or delta */
+} spa_norm_prologue;
+
+/*
+ * spa_linear applied to RMSNorm(x (+ delta)) in one launch: every CTA normalises the rows
+ * itself, bit-identical to spa_add_rms_norm / spa_embed_rms_norm / spa_rms_norm (same
+ * arithmetic and reduction order; in_features is the norm width), and one CTA stores the
+ * summed rows to x_out.  With ids, the rows come from embedding tables as in
+ * spa_embed_rms_norm (delta and delta_ids then required).  Errors as spa_linear, plus
+ * SPA_ERR_INVALID without norm or norm_weight; an id outside its table raises device
+ * error bit 4 and gives a zero row.
+ */
+int spa_norm_linear(const void* x, const spa_norm_prologue* norm, const void* weight, const void* bias, void* out,
+                    int rows, int in_features, int out_features, int activation, int out_f32, int dtype,
+                    spa_stream_t stream);
+
 /*
  * Diagnostic for the failure path: one kernel waits on an mbarrier that nothing
  * completes, with the library's bounded wait limited to `cycles` (1 .. 4e9 clock

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 import attention_b200 as spa
-from attention_b200.decoder import add_rms_norm, embed_rms_norm, linear, rms_norm
+from attention_b200.decoder import add_rms_norm, embed_rms_norm, linear, norm_linear, rms_norm
 
 pytestmark = pytest.mark.gpu
 
@@ -122,3 +122,58 @@ def test_linear_fp32_out_holds_rounded_values():
     assert torch.equal(out, linear(x, w).float())
     with pytest.raises(ValueError):
         linear(torch.ones(5, 512, device="cuda", dtype=torch.bfloat16), w)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("rows", [1, 2, 4])
+@pytest.mark.parametrize("with_delta", [False, True])
+def test_norm_linear_equals_norm_then_linear(dtype, rows, with_delta):
+    """The fused prologue normalises bit-identically to the separate norm kernels, so the
+    product equals spa_linear of their output; x_out receives the summed rows."""
+    g = torch.Generator(device="cuda").manual_seed(rows + 10 * with_delta)
+    k, n = 512, 1536
+    x = torch.randn(rows, k, device="cuda", generator=g).to(dtype)
+    d = torch.randn(rows, k, device="cuda", generator=g).to(dtype) if with_delta else None
+    nw = (torch.rand(k, device="cuda", generator=g) + 0.5).to(dtype)
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.05).to(dtype)
+    b = torch.randn(n, device="cuda", generator=g).to(dtype)
+    x_out = torch.empty_like(x)
+    y = norm_linear(x, w, b, norm_weight=nw, eps=1e-5, delta=d, x_out=x_out, gelu=True)
+    if with_delta:
+        ref_x = torch.empty_like(x)
+        h = add_rms_norm(x, d, nw, 1e-5, x_out=ref_x)
+        assert torch.equal(x_out, ref_x)
+    else:
+        h = rms_norm(x, nw, 1e-5)
+        assert torch.equal(x_out, x)
+    assert torch.equal(y, linear(h, w, b, gelu=True))
+    logits = torch.empty(rows, n, device="cuda")
+    norm_linear(x, w, norm_weight=nw, eps=1e-5, delta=d, out=logits)
+    assert torch.equal(logits, linear(h, w).float())
+    with pytest.raises(ValueError):
+        norm_linear(x, w, b, norm_weight=nw, eps=1e-5, delta=d, x_out=x)
+    assert spa.device_error_flags() == 0
+
+
+def test_norm_linear_embedding_mode():
+    g = torch.Generator(device="cuda").manual_seed(5)
+    vocab, n_pos, k, n = 4096, 200, 512, 1536
+    table = (torch.randn(vocab, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    pos = (torch.randn(n_pos, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    nw = (torch.rand(k, device="cuda", generator=g) + 0.5).to(torch.bfloat16)
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    b = torch.randn(n, device="cuda", generator=g).to(torch.bfloat16)
+    ids = torch.tensor([7, 4095], dtype=torch.int64, device="cuda")
+    positions = torch.tensor([0, 199], dtype=torch.int32, device="cuda")
+    x_out = torch.empty(2, k, dtype=torch.bfloat16, device="cuda")
+    y = norm_linear(table, w, b, norm_weight=nw, eps=1e-5, delta=pos, ids=ids, positions=positions, x_out=x_out)
+    ref_x = torch.empty_like(x_out)
+    h = embed_rms_norm(table, ids, pos, positions, nw, 1e-5, x_out=ref_x)
+    assert torch.equal(x_out, ref_x)
+    assert torch.equal(y, linear(h, w, b))
+    assert spa.device_error_flags() == 0
+    bad = torch.tensor([7, 4096], dtype=torch.int64, device="cuda")
+    y = norm_linear(table, w, b, norm_weight=nw, eps=1e-5, delta=pos, ids=bad, positions=positions, x_out=x_out)
+    assert spa.device_error_flags() == 4
+    assert torch.equal(x_out[1], torch.zeros(k, dtype=torch.bfloat16, device="cuda"))
+    assert torch.equal(y[1], b)  # a zero row times the weight, plus the bias
