@@ -58,7 +58,8 @@ def test_exact_ties_resolve_to_lower_page():
     assert tied == [1, 4, 6]
 
 
-@pytest.mark.parametrize("n_pages,superblock,top_super", [(100, 16, 4), (511, 16, 4), (37, 8, 2), (64, 16, 4)])
+@pytest.mark.parametrize("n_pages,superblock,top_super",
+                         [(100, 16, 4), (511, 16, 4), (37, 8, 2), (64, 16, 4), (600, 2, 32), (800, 4, 40)])
 def test_tree_router_matches_oracle(n_pages, superblock, top_super):
     gen = torch.Generator().manual_seed(n_pages)
     b, hq, hkv, d, page = 2, 32, 8, 128, 16
