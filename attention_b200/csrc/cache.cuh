@@ -36,15 +36,18 @@ __global__ void __launch_bounds__(32) promotion_update_kernel(int32_t* __restric
                                                               const int64_t* __restrict__ selected, int top_m,
                                                               int step_arg, const int32_t* __restrict__ step_dev,
                                                               int ttl) {
-  extern __shared__ int32_t tab[];  // pg [slots], lh [slots]
+  extern __shared__ int64_t promo_smem[];  // sel [top_m], then pg [slots], lh [slots]
   const int r = blockIdx.x, lane = threadIdx.x;
   if (r >= rows) return;
   const int step = step_dev ? *step_dev : step_arg;
   int32_t* pg_g = pages + static_cast<int64_t>(r) * slots;
   int32_t* lh_g = last_hit + static_cast<int64_t>(r) * slots;
-  const int64_t* sel = selected + static_cast<int64_t>(r) * top_m;
-  int32_t* pg = tab;
-  int32_t* lh = tab + slots;
+  // the row's selection is staged with the table (loads in flight together), so the
+  // per-page loops below read shared memory, not one global load per page
+  int64_t* sel = promo_smem;
+  int32_t* pg = reinterpret_cast<int32_t*>(sel + top_m);
+  int32_t* lh = pg + slots;
+  for (int j = lane; j < top_m; j += 32) sel[j] = selected[static_cast<int64_t>(r) * top_m + j];
   for (int i = lane; i < slots; i += 32) {
     pg[i] = pg_g[i];
     lh[i] = lh_g[i];
@@ -144,7 +147,7 @@ extern "C" int spa_promotion_update(int32_t* pages, int32_t* last_hit, int rows,
     return SPA_ERR_INVALID;
   if (slots > 8192) return SPA_ERR_UNSUPPORTED;  // the row is staged in shared memory
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const size_t smem = sizeof(int32_t) * 2 * static_cast<size_t>(slots);
+  const size_t smem = sizeof(int64_t) * static_cast<size_t>(top_m) + sizeof(int32_t) * 2 * static_cast<size_t>(slots);
   SPA_CHECK_CUDA(spa_set_smem_once(spa::promotion_update_kernel, static_cast<int>(smem)));
   spa::promotion_update_kernel<<<rows, 32, smem, st>>>(pages, last_hit, rows, slots, selected, top_m, step, step_dev,
                                                       ttl);

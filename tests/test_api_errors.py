@@ -40,3 +40,22 @@ def test_router_requires_cuda():
     s = torch.randn(1, 2, 5, 16)
     with pytest.raises(ValueError, match="CUDA tensors are required"):
         spa.select_blocks(q, s, 2)
+
+
+def test_decoder_glue_requires_cuda():
+    from attention_b200.decoder import add_rms_norm, embed_rms_norm, linear, norm_linear, rms_norm
+
+    x = torch.randn(2, 64)
+    w = torch.randn(32, 64)
+    nw = torch.ones(64)
+    with pytest.raises(ValueError, match="CUDA tensors are required"):
+        rms_norm(x, nw, 1e-5)
+    with pytest.raises(ValueError, match="CUDA tensors are required"):
+        add_rms_norm(x, x, nw, 1e-5)
+    with pytest.raises(ValueError, match="CUDA tensors are required"):
+        embed_rms_norm(x, torch.zeros(2, dtype=torch.int64), x, torch.zeros(2, dtype=torch.int32), nw, 1e-5,
+                       x_out=torch.empty(2, 64))
+    with pytest.raises(ValueError, match="CUDA tensors are required"):
+        linear(x, w)
+    with pytest.raises(ValueError, match="CUDA tensors are required"):
+        norm_linear(x, w, norm_weight=nw, eps=1e-5)
