@@ -69,6 +69,13 @@ class NormPrologue(ctypes.Structure):
                 ("eps", ctypes.c_double), ("x_out", ctypes.c_void_p)]
 
 
+class KvAppendEpilogue(ctypes.Structure):
+    """spa_kv_append_epilogue (include/spa_b200.h)."""
+
+    _fields_ = [("kv", KvLayout), ("positions", ctypes.c_void_p), ("k_col", ctypes.c_int), ("v_col", ctypes.c_int),
+                ("kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int)]
+
+
 class SessionParams(ctypes.Structure):
     """spa_session_params (include/spa_b200.h)."""
 
@@ -121,7 +128,8 @@ PROTOTYPES = {
     "spa_add_rms_norm": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _d, _i, _vp]),
     "spa_embed_rms_norm": (_i, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i, _i, _d, _i, _vp]),
     "spa_linear": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
-    "spa_norm_linear": (_i, [_vp, ctypes.POINTER(NormPrologue), _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "spa_norm_linear": (_i, [_vp, ctypes.POINTER(NormPrologue), _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
+                             ctypes.POINTER(KvAppendEpilogue), _vp]),
 }
 
 

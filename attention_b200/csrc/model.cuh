@@ -126,13 +126,25 @@ struct LinearPro {
   float eps;
 };
 
+// Optional epilogue: output columns [k_col, k_col + Hkv*D) and [v_col, v_col + Hkv*D) are
+// also the new token's K and V of batch row m, stored into the paged pools at
+// positions[m] as spa_kv_append stores them (negative position: not stored; a row outside
+// the pools raises SPA_DEVERR_BAD_PAGE).
+struct LinearAppend {
+  KvAddr addr;
+  void* k;
+  void* v;
+  const int32_t* positions;
+  int k_col, v_col, kv_heads, head_dim;
+};
+
 template <typename T>
 __global__ void __launch_bounds__(kLinearWarps * 32) linear_rows_kernel(const T* __restrict__ x,
                                                                         const T* __restrict__ w,
                                                                         const T* __restrict__ bias,
                                                                         void* __restrict__ out, int rows, int K,
                                                                         int N, int gelu, int out_f32, int vec,
-                                                                        const LinearPro pro) {
+                                                                        const LinearPro pro, const LinearAppend app) {
   extern __shared__ __align__(16) unsigned char linear_smem[];
   T* xs = reinterpret_cast<T*>(linear_smem);  // [rows][K]
   constexpr int kVec = 16 / sizeof(T);        // elements per 16-byte load
@@ -254,12 +266,33 @@ __global__ void __launch_bounds__(kLinearWarps * 32) linear_rows_kernel(const T*
       static_cast<float*>(out)[o] = to_f32(y);
     else
       static_cast<T*>(out)[o] = y;
+    if (app.k) {
+      const int width = app.kv_heads * app.head_dim;
+      T* pool = nullptr;
+      int rel = 0;
+      if (n >= app.k_col && n < app.k_col + width) {
+        pool = static_cast<T*>(app.k);
+        rel = n - app.k_col;
+      } else if (n >= app.v_col && n < app.v_col + width) {
+        pool = static_cast<T*>(app.v);
+        rel = n - app.v_col;
+      }
+      const int pos = pool ? app.positions[lane] : -1;
+      if (pos >= 0) {
+        const int h = rel / app.head_dim, j = rel - h * app.head_dim;
+        const int64_t row = app.addr.row(lane, h, pos);
+        if (row < 0 || row >= app.addr.total_rows)
+          spa_raise(SPA_DEVERR_BAD_PAGE);
+        else
+          pool[row * app.head_dim + j] = y;
+      }
+    }
   }
 }
 
 template <typename T>
 int launch_linear(const void* x, const void* w, const void* bias, void* out, int rows, int K, int N, int gelu,
-                  int out_f32, const LinearPro& pro, cudaStream_t st) {
+                  int out_f32, const LinearPro& pro, const LinearAppend& app, cudaStream_t st) {
   constexpr int kVec = 16 / sizeof(T);
   const size_t smem = static_cast<size_t>(rows) * K * sizeof(T);
   if (smem > 200 * 1024) return SPA_ERR_UNSUPPORTED;
@@ -270,7 +303,7 @@ int launch_linear(const void* x, const void* w, const void* bias, void* out, int
   SPA_CHECK_CUDA(spa_set_smem_once(kern, static_cast<int>(smem)));
   kern<<<(N + kLinearWarps - 1) / kLinearWarps, kLinearWarps * 32, smem, st>>>(
       static_cast<const T*>(x), static_cast<const T*>(w), static_cast<const T*>(bias), out, rows, K, N, gelu, out_f32,
-      vec, pro);
+      vec, pro, app);
   SPA_CHECK_CUDA(cudaGetLastError());
   return SPA_OK;
 }
@@ -299,7 +332,8 @@ extern "C" int spa_embed_rms_norm(const void* table, int64_t table_rows, const i
 
 namespace spa {
 int linear_impl(const void* x, const void* weight, const void* bias, void* out, int rows, int in_features,
-                int out_features, int activation, int out_f32, int dtype, const LinearPro& pro, spa_stream_t stream) {
+                int out_features, int activation, int out_f32, int dtype, const LinearPro& pro,
+                const LinearAppend& app, spa_stream_t stream) {
   if (rows < 0 || rows > kLinearMaxRows || in_features <= 0 || out_features <= 0 || !dtype_ok(dtype) ||
       (activation != 0 && activation != 1) || (out_f32 != 0 && out_f32 != 1))
     return SPA_ERR_INVALID;
@@ -307,25 +341,45 @@ int linear_impl(const void* x, const void* weight, const void* bias, void* out, 
   if (!x || !weight || !out) return SPA_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == SPA_F32)
-    return launch_linear<float>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, pro, st);
+    return launch_linear<float>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, pro, app,
+                                st);
   if (dtype == SPA_F16)
-    return launch_linear<__half>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, pro, st);
+    return launch_linear<__half>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, pro, app,
+                                 st);
   return launch_linear<__nv_bfloat16>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, pro,
-                                      st);
+                                      app, st);
 }
 }  // namespace spa
 
 extern "C" int spa_linear(const void* x, const void* weight, const void* bias, void* out, int rows, int in_features,
                           int out_features, int activation, int out_f32, int dtype, spa_stream_t stream) {
   const spa::LinearPro pro{};
-  return spa::linear_impl(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, dtype, pro,
+  const spa::LinearAppend app{};
+  return spa::linear_impl(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, dtype, pro, app,
                           stream);
 }
 
 extern "C" int spa_norm_linear(const void* x, const spa_norm_prologue* norm, const void* weight, const void* bias,
                                void* out, int rows, int in_features, int out_features, int activation, int out_f32,
-                               int dtype, spa_stream_t stream) {
+                               int dtype, const spa_kv_append_epilogue* append, spa_stream_t stream) {
   if (!norm || !norm->norm_weight) return SPA_ERR_INVALID;
+  spa::LinearAppend app{};
+  if (append) {
+    const spa_kv_layout& kv = append->kv;
+    const int64_t width = static_cast<int64_t>(append->kv_heads) * append->head_dim;
+    if (!kv.k || !kv.v || !append->positions || kv.page_size <= 0 || append->kv_heads <= 0 ||
+        append->head_dim <= 0 || (kv.page_table && kv.table_stride <= 0) || append->k_col < 0 || append->v_col < 0 ||
+        append->k_col + width > out_features || append->v_col + width > out_features)
+      return SPA_ERR_INVALID;
+    app.addr = make_kv_addr(kv);
+    app.k = const_cast<void*>(kv.k);
+    app.v = const_cast<void*>(kv.v);
+    app.positions = append->positions;
+    app.k_col = append->k_col;
+    app.v_col = append->v_col;
+    app.kv_heads = append->kv_heads;
+    app.head_dim = append->head_dim;
+  }
   if (norm->ids && (norm->id_limit <= 0 || !norm->delta || !norm->delta_ids || norm->delta_limit <= 0))
     return SPA_ERR_INVALID;
   spa::LinearPro pro{};
@@ -337,6 +391,6 @@ extern "C" int spa_norm_linear(const void* x, const spa_norm_prologue* norm, con
   pro.norm_w = norm->norm_weight;
   pro.x_out = norm->x_out;
   pro.eps = static_cast<float>(norm->eps);
-  return spa::linear_impl(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, dtype, pro,
+  return spa::linear_impl(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, dtype, pro, app,
                           stream);
 }

@@ -28,7 +28,7 @@ import torch.nn.functional as F
 from . import _lib
 from ._util import dtype_code, stream_ptr
 from .cache import PromotionCache, kv_append
-from .paged_attention import paged_gather_decode_attention
+from .paged_attention import paged_gather_decode_attention, pool_layout
 from .prefill import local_causal_prefill
 from .router import page_summaries
 from .step import sparse_decode_step
@@ -148,13 +148,15 @@ def norm_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
                 norm_weight: torch.Tensor, eps: float, delta: torch.Tensor | None = None,
                 x_out: torch.Tensor | None = None, ids: torch.Tensor | None = None,
                 positions: torch.Tensor | None = None, gelu: bool = False,
-                out: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, append: tuple | None = None) -> torch.Tensor:
     """``linear(rms_norm(x (+ delta)), weight, bias)`` for 1..4 rows in one launch
     (``spa_norm_linear``); the normalised rows are bit-identical to ``add_rms_norm`` /
     ``rms_norm``.  With ``ids`` (int64) and ``positions`` (int32), ``x`` and ``delta`` are
     the token and position embedding tables and the rows are looked up as in
     ``embed_rms_norm``.  ``x_out`` (optional) receives the summed rows and must be a
-    separate buffer from ``x`` and ``delta``."""
+    separate buffer from ``x`` and ``delta``.  ``append = (k_pool, v_pool, page_table,
+    positions, k_col, v_col)`` also stores output columns ``[k_col, k_col + Hkv*D)`` and
+    ``[v_col, ...)`` of row m as batch row m's new K and V, as ``kv_append`` would."""
     tensors = [x, weight, norm_weight] + [t for t in (bias, delta, x_out, ids, positions, out) if t is not None]
     if not all(t.is_cuda for t in tensors):
         raise ValueError("CUDA tensors are required")
@@ -187,6 +189,16 @@ def norm_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
         out = torch.empty(rows, n, dtype=x.dtype, device=x.device)
     elif out.shape != (rows, n) or out.dtype not in (x.dtype, torch.float32):
         raise ValueError("out must be a contiguous [rows, out_features] tensor of x's dtype or fp32")
+    epi = None
+    if append is not None:
+        k_pool, v_pool, table, pos, k_col, v_col = append
+        width = k_pool.size(1) * k_pool.size(3)
+        if (k_pool.dtype != x.dtype or v_pool.shape != k_pool.shape or pos.dtype != torch.int32
+                or pos.numel() != rows or table.dtype != torch.int32 or not (table.is_contiguous() and pos.is_contiguous())
+                or not 0 <= k_col <= n - width or not 0 <= v_col <= n - width):
+            raise ValueError("append needs pools of x's dtype, an int32 page table and [rows] int32 positions")
+        epi = _lib.KvAppendEpilogue(pool_layout(k_pool, v_pool, table), pos.data_ptr(), k_col, v_col,
+                                    k_pool.size(1), k_pool.size(3))
     nw = norm_weight.to(x.dtype).contiguous()
     pro = _lib.NormPrologue()
     pro.delta = delta.data_ptr() if delta is not None else None
@@ -199,7 +211,8 @@ def norm_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
     _lib.check(_lib.lib.spa_norm_linear(x.data_ptr(), ctypes.byref(pro), weight.data_ptr(),
                                         bias.data_ptr() if bias is not None else None, out.data_ptr(), rows, k, n,
                                         1 if gelu else 0, 1 if out.dtype != x.dtype else 0, dtype_code(x),
-                                        stream_ptr(x.device)), "spa_norm_linear")
+                                        ctypes.byref(epi) if epi is not None else None, stream_ptr(x.device)),
+               "spa_norm_linear")
     return out
 
 
@@ -335,13 +348,14 @@ class SparseDecoder:
             self._sel_bufs: dict = {}  # [layers, B, m] selections, per m
             self._graphs: dict = {}
 
-    def _norm_linear(self, x, delta, norm, name, x_out, *, gelu=False):
+    def _norm_linear(self, x, delta, norm, name, x_out, *, gelu=False, append=None):
         """x_out = x + delta; returns the linear layer ``name`` of rms_norm(x_out): one
-        launch for a batch of up to four rows, else the norm and a library GEMM."""
+        launch for a batch of up to four rows (with the K/V append when given), else the
+        norm and a library GEMM (the caller then appends)."""
         w, b = self.w[f"{name}.w"], self.w[f"{name}.b"]
         if self.batch <= LINEAR_MAX_ROWS:
             return norm_linear(x, w, b, norm_weight=self.w[norm], eps=self.cfg.eps, delta=delta, x_out=x_out,
-                               gelu=gelu)
+                               gelu=gelu, append=append)
         return self._linear(add_rms_norm(x, delta, self.w[norm], self.cfg.eps, x_out=x_out), name, gelu=gelu)
 
     def _step_body(self):
@@ -353,9 +367,16 @@ class SparseDecoder:
         b = self.batch
         h, dh = cfg.heads, cfg.head_dim
         x, spare = self._xa, self._xb
-        if b <= LINEAR_MAX_ROWS:
+        fused = b <= LINEAR_MAX_ROWS  # norms, products and the K/V append in few-row kernels
+        d = cfg.d_model
+
+        def append(i):  # the QKV product's K and V columns go straight into layer i's pools
+            return (self.k_pool[i], self.v_pool[i], self.page_table, self._position, d, 2 * d) if fused else None
+
+        if fused:
             qkv = norm_linear(self.w["emb"], self.w["l0.qkv.w"], self.w["l0.qkv.b"], norm_weight=self.w["l0.norm1"],
-                              eps=cfg.eps, delta=self.w["pos"], ids=self._token, positions=self._position, x_out=x)
+                              eps=cfg.eps, delta=self.w["pos"], ids=self._token, positions=self._position, x_out=x,
+                              append=append(0))
         else:
             hid = embed_rms_norm(self.w["emb"], self._token, self.w["pos"], self._position, self.w["l0.norm1"],
                                  cfg.eps, x_out=x)
@@ -370,11 +391,13 @@ class SparseDecoder:
         mlp_out = None
         for i in range(cfg.layers):
             if i > 0:
-                qkv = self._norm_linear(x, mlp_out, f"l{i}.norm1", f"l{i}.qkv", spare)
+                qkv = self._norm_linear(x, mlp_out, f"l{i}.norm1", f"l{i}.qkv", spare, append=append(i))
                 x, spare = spare, x
             qkv = qkv.view(b, 3, h, dh)
-            q, k, v = qkv[:, 0].contiguous(), qkv[:, 1].contiguous(), qkv[:, 2].contiguous()
-            kv_append(self.k_pool[i], self.v_pool[i], self.page_table, k, v, self._position)
+            q = qkv[:, 0].contiguous()
+            if not fused:
+                kv_append(self.k_pool[i], self.v_pool[i], self.page_table, qkv[:, 1].contiguous(),
+                          qkv[:, 2].contiguous(), self._position)
             if m > 0:
                 # router and gather decode chained on the device (one library call)
                 att, sel = sparse_decode_step(q, self.k_pool[i], self.v_pool[i], self.summaries[i], top_blocks=m,

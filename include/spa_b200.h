@@ -500,13 +500,27 @@ typedef struct spa_norm_prologue {
  * itself, bit-identical to spa_add_rms_norm / spa_embed_rms_norm / spa_rms_norm (same
  * arithmetic and reduction order; in_features is the norm width), and one CTA stores the
  * summed rows to x_out.  With ids, the rows come from embedding tables as in
- * spa_embed_rms_norm (delta and delta_ids then required).  Errors as spa_linear, plus
- * SPA_ERR_INVALID without norm or norm_weight; an id outside its table raises device
- * error bit 4 and gives a zero row.
+ * spa_embed_rms_norm (delta and delta_ids then required).  With append (NULL: none), the
+ * output columns [k_col, k_col + kv_heads*head_dim) and [v_col, ...) of row m are also
+ * the new K and V of batch row m, stored into the pools exactly as spa_kv_append stores
+ * them (reference: the K/V cache write of triton_kvcache_transformer_decode.py:51-55).
+ * Errors as spa_linear, plus SPA_ERR_INVALID without norm or norm_weight or with an
+ * inconsistent append; an id outside its table raises device error bit 4 and gives a zero
+ * row, a page outside the pools bit 2.
  */
+/* The new token's K/V append fused into a spa_norm_linear epilogue (the QKV projection). */
+typedef struct spa_kv_append_epilogue {
+  spa_kv_layout kv;         /* K/V pools and page table, as for spa_kv_append */
+  const int32_t* positions; /* [rows] token position of batch row m (negative: not stored) */
+  int k_col;                /* first output column of K (kv_heads * head_dim columns, head-major) */
+  int v_col;                /* first output column of V */
+  int kv_heads;
+  int head_dim;
+} spa_kv_append_epilogue;
+
 int spa_norm_linear(const void* x, const spa_norm_prologue* norm, const void* weight, const void* bias, void* out,
                     int rows, int in_features, int out_features, int activation, int out_f32, int dtype,
-                    spa_stream_t stream);
+                    const spa_kv_append_epilogue* append, spa_stream_t stream);
 
 /*
  * Diagnostic for the failure path: one kernel waits on an mbarrier that nothing

@@ -59,9 +59,10 @@ def test_invalid_arguments_rejected_without_gpu():
     assert _lib.lib.spa_linear(None, None, None, None, 1, 64, 64, 2, 0, 2, None) == _lib.SPA_ERR_INVALID
     assert _lib.lib.spa_linear(None, None, None, None, 1, 64, 64, 0, 0, 2, None) == _lib.SPA_ERR_INVALID
     assert _lib.lib.spa_linear(None, None, None, None, 0, 64, 64, 0, 0, 2, None) == _lib.SPA_OK
-    assert _lib.lib.spa_norm_linear(None, None, None, None, None, 1, 64, 64, 0, 0, 2, None) == _lib.SPA_ERR_INVALID
+    assert _lib.lib.spa_norm_linear(None, None, None, None, None, 1, 64, 64, 0, 0, 2, None,
+                                    None) == _lib.SPA_ERR_INVALID
     pro = _lib.NormPrologue()  # no norm weight
-    assert _lib.lib.spa_norm_linear(None, ctypes.byref(pro), None, None, None, 1, 64, 64, 0, 0, 2,
+    assert _lib.lib.spa_norm_linear(None, ctypes.byref(pro), None, None, None, 1, 64, 64, 0, 0, 2, None,
                                     None) == _lib.SPA_ERR_INVALID
     assert _lib.lib.spa_copy(None, None, 16, None) == _lib.SPA_ERR_INVALID
     assert _lib.lib.spa_session_create(None, None) == _lib.SPA_ERR_INVALID

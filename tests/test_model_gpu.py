@@ -177,3 +177,33 @@ def test_norm_linear_embedding_mode():
     assert spa.device_error_flags() == 4
     assert torch.equal(x_out[1], torch.zeros(k, dtype=torch.bfloat16, device="cuda"))
     assert torch.equal(y[1], b)  # a zero row times the weight, plus the bias
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_norm_linear_appends_kv_like_kv_append(dtype):
+    """The QKV product's K and V columns stored into the paged pools by the epilogue equal
+    spa_kv_append of the same columns; a negative position stores nothing."""
+    from attention_b200.cache import kv_append
+
+    g = torch.Generator(device="cuda").manual_seed(21)
+    rows, heads, dh, page, max_pages = 3, 4, 32, 16, 6
+    d = heads * dh
+    x = torch.randn(rows, d, device="cuda", generator=g).to(dtype)
+    delta = torch.randn(rows, d, device="cuda", generator=g).to(dtype)
+    nw = (torch.rand(d, device="cuda", generator=g) + 0.5).to(dtype)
+    w = (torch.randn(3 * d, d, device="cuda", generator=g) * 0.05).to(dtype)
+    b = torch.randn(3 * d, device="cuda", generator=g).to(dtype)
+    table = torch.randperm(rows * max_pages, generator=torch.Generator().manual_seed(2)).to(torch.int32).view(
+        rows, max_pages).cuda()
+    pos = torch.tensor([5, 37, -1], dtype=torch.int32, device="cuda")
+    k1 = torch.zeros(rows * max_pages, heads, page, dh, dtype=dtype, device="cuda")
+    v1, k2, v2 = torch.zeros_like(k1), torch.zeros_like(k1), torch.zeros_like(k1)
+    x_out = torch.empty_like(x)
+    y = norm_linear(x, w, b, norm_weight=nw, eps=1e-5, delta=delta, x_out=x_out,
+                    append=(k1, v1, table, pos, d, 2 * d))
+    qkv = y.view(rows, 3, heads, dh)
+    kv_append(k2, v2, table, qkv[:, 1].contiguous(), qkv[:, 2].contiguous(), pos)
+    assert torch.equal(k1, k2) and torch.equal(v1, v2)
+    assert k1.abs().sum() > 0
+    assert torch.equal(y, norm_linear(x, w, b, norm_weight=nw, eps=1e-5, delta=delta))
+    assert spa.device_error_flags() == 0
