@@ -128,6 +128,7 @@ PROTOTYPES = {
     "spa_add_rms_norm": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _d, _i, _vp]),
     "spa_embed_rms_norm": (_i, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i, _i, _d, _i, _vp]),
     "spa_linear": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "spa_argmax_advance": (_i, [_vp, _i, _i, _vp, _vp, _i, _vp]),
     "spa_norm_linear": (_i, [_vp, ctypes.POINTER(NormPrologue), _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
                              ctypes.POINTER(KvAppendEpilogue), _vp]),
 }

@@ -331,6 +331,72 @@ extern "C" int spa_embed_rms_norm(const void* table, int64_t table_rows, const i
 }
 
 namespace spa {
+// Greedy token choice at the end of a decode step, one CTA per row: the index of the
+// largest logit with torch.argmax's rules (NaN counts as the largest value; among equal
+// values the first index).  CTA 0 also adds 1 to each of the step's counters (position,
+// context length, step), which every earlier kernel of the step has already read.
+__device__ __forceinline__ bool argmax_beats(float a, int ia, float b, int ib) {
+  const bool na = a != a, nb = b != b;
+  if (na != nb) return na;
+  if (!na && a != b) return a > b;
+  return ia < ib;
+}
+
+__global__ void __launch_bounds__(256) argmax_advance_kernel(const float* __restrict__ logits, int cols,
+                                                             int64_t* __restrict__ token, int32_t* __restrict__ counters,
+                                                             int n_counters) {
+  __shared__ float bv[8];
+  __shared__ int bi[8];
+  const int row = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float* lr = logits + static_cast<int64_t>(row) * cols;
+  float v = -INFINITY;
+  int i = 0x7fffffff;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    const float x = lr[c];
+    if (argmax_beats(x, c, v, i)) {
+      v = x;
+      i = c;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, off);
+    if (argmax_beats(ov, oi, v, i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+  if (lane == 0) {
+    bv[warp] = v;
+    bi[warp] = i;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; ++w)
+      if (argmax_beats(bv[w], bi[w], v, i)) {
+        v = bv[w];
+        i = bi[w];
+      }
+    token[row] = i;
+  }
+  if (row == 0)
+    for (int c = threadIdx.x; c < n_counters; c += blockDim.x) counters[c] += 1;
+}
+}  // namespace spa
+
+extern "C" int spa_argmax_advance(const float* logits, int rows, int cols, int64_t* token, int32_t* counters,
+                                  int n_counters, spa_stream_t stream) {
+  if (rows < 0 || cols <= 0 || n_counters < 0 || (n_counters > 0 && !counters)) return SPA_ERR_INVALID;
+  if (rows == 0) return SPA_OK;
+  if (!logits || !token) return SPA_ERR_INVALID;
+  spa::argmax_advance_kernel<<<rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(logits, cols, token, counters,
+                                                                                       n_counters);
+  SPA_CHECK_CUDA(cudaGetLastError());
+  return SPA_OK;
+}
+
+namespace spa {
 int linear_impl(const void* x, const void* weight, const void* bias, void* out, int rows, int in_features,
                 int out_features, int activation, int out_f32, int dtype, const LinearPro& pro,
                 const LinearAppend& app, spa_stream_t stream) {

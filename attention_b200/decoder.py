@@ -216,6 +216,22 @@ def norm_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
     return out
 
 
+def argmax_advance(logits: torch.Tensor, token: torch.Tensor, counters: torch.Tensor | None = None) -> None:
+    """``token[r] = logits[r].argmax()`` (torch.argmax's rules) and ``counters += 1`` in one
+    launch (``spa_argmax_advance``); logits fp32 [rows, cols], token int64 [rows], counters int32."""
+    if not (logits.is_cuda and token.is_cuda and (counters is None or counters.is_cuda)):
+        raise ValueError("CUDA tensors are required")
+    if (logits.dtype != torch.float32 or logits.dim() != 2 or not logits.is_contiguous() or token.dtype != torch.int64
+            or token.shape != (logits.size(0),) or not token.is_contiguous()):
+        raise ValueError("logits must be contiguous fp32 [rows, cols] and token int64 [rows]")
+    if counters is not None and (counters.dtype != torch.int32 or not counters.is_contiguous()):
+        raise ValueError("counters must be a contiguous int32 tensor")
+    _lib.check(_lib.lib.spa_argmax_advance(logits.data_ptr(), logits.size(0), logits.size(1), token.data_ptr(),
+                                           counters.data_ptr() if counters is not None else None,
+                                           counters.numel() if counters is not None else 0,
+                                           stream_ptr(logits.device)), "spa_argmax_advance")
+
+
 def embed_rms_norm(table: torch.Tensor, ids: torch.Tensor, pos_table: torch.Tensor, positions: torch.Tensor,
                    weight: torch.Tensor, eps: float, *, x_out: torch.Tensor) -> torch.Tensor:
     """Token + position embedding lookup and the first RMSNorm in one launch
@@ -423,8 +439,8 @@ class SparseDecoder:
         else:
             hf = add_rms_norm(x, mlp_out, self.w["norm_f"], cfg.eps, x_out=spare)
             self._logits.copy_(F.linear(hf, self.w["head"]))
-        torch.argmax(self._logits, dim=-1, out=self._token)
-        self._counters.add_(1)  # position, context length, step
+        # greedy token, then position, context length and step advance (one launch)
+        argmax_advance(self._logits, self._token, self._counters)
         return sel_all
 
     def _check_room(self, steps: int) -> None:

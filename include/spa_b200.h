@@ -508,6 +508,15 @@ typedef struct spa_norm_prologue {
  * inconsistent append; an id outside its table raises device error bit 4 and gives a zero
  * row, a page outside the pools bit 2.
  */
+/*
+ * End of a greedy decode step in one launch: token[r] = argmax of logits[r, 0..cols) (fp32,
+ * torch.argmax's rules: NaN counts as the largest value, the first index among equal
+ * values), and counters[0..n_counters) each incremented by one (the decoder's position,
+ * context length and step counter; NULL when n_counters is 0).
+ */
+int spa_argmax_advance(const float* logits, int rows, int cols, int64_t* token, int32_t* counters, int n_counters,
+                       spa_stream_t stream);
+
 /* The new token's K/V append fused into a spa_norm_linear epilogue (the QKV projection). */
 typedef struct spa_kv_append_epilogue {
   spa_kv_layout kv;         /* K/V pools and page table, as for spa_kv_append */

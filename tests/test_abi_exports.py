@@ -59,6 +59,8 @@ def test_invalid_arguments_rejected_without_gpu():
     assert _lib.lib.spa_linear(None, None, None, None, 1, 64, 64, 2, 0, 2, None) == _lib.SPA_ERR_INVALID
     assert _lib.lib.spa_linear(None, None, None, None, 1, 64, 64, 0, 0, 2, None) == _lib.SPA_ERR_INVALID
     assert _lib.lib.spa_linear(None, None, None, None, 0, 64, 64, 0, 0, 2, None) == _lib.SPA_OK
+    assert _lib.lib.spa_argmax_advance(None, 2, 16, None, None, 0, None) == _lib.SPA_ERR_INVALID
+    assert _lib.lib.spa_argmax_advance(None, 2, 16, None, None, 3, None) == _lib.SPA_ERR_INVALID
     assert _lib.lib.spa_norm_linear(None, None, None, None, None, 1, 64, 64, 0, 0, 2, None,
                                     None) == _lib.SPA_ERR_INVALID
     pro = _lib.NormPrologue()  # no norm weight

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 import attention_b200 as spa
-from attention_b200.decoder import add_rms_norm, embed_rms_norm, linear, norm_linear, rms_norm
+from attention_b200.decoder import add_rms_norm, argmax_advance, embed_rms_norm, linear, norm_linear, rms_norm
 
 pytestmark = pytest.mark.gpu
 
@@ -206,4 +206,20 @@ def test_norm_linear_appends_kv_like_kv_append(dtype):
     assert torch.equal(k1, k2) and torch.equal(v1, v2)
     assert k1.abs().sum() > 0
     assert torch.equal(y, norm_linear(x, w, b, norm_weight=nw, eps=1e-5, delta=delta))
+    assert spa.device_error_flags() == 0
+
+
+def test_argmax_advance_matches_torch_argmax():
+    g = torch.Generator(device="cuda").manual_seed(8)
+    logits = torch.randn(4, 4096, device="cuda", generator=g)
+    logits[1, 100] = logits[1, 3000] = 50.0  # a tie: the first index wins
+    logits[2, 7] = float("nan")              # NaN counts as the largest value
+    logits[2, 9] = float("nan")
+    logits[3] = 0.0                          # all equal
+    token = torch.full((4,), -5, dtype=torch.int64, device="cuda")
+    counters = torch.tensor([3, 4, 5, 6, 7], dtype=torch.int32, device="cuda")
+    argmax_advance(logits, token, counters)
+    assert torch.equal(token, torch.argmax(logits, dim=-1))
+    assert token.tolist() == [int(logits[0].argmax()), 100, 7, 0]
+    assert counters.tolist() == [4, 5, 6, 7, 8]
     assert spa.device_error_flags() == 0
