@@ -24,7 +24,7 @@ typedef struct CUstream_st* spa_stream_t; /* same type as cudaStream_t */
 typedef enum {
   SPA_OK = 0,
   SPA_ERR_INVALID = 1,     /* bad shape, pointer, alignment or argument */
-  SPA_ERR_UNSUPPORTED = 2, /* valid request this build does not implement */
+  SPA_ERR_UNSUPPORTED = 2, /* valid request the library does not implement */
   SPA_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed */
   SPA_ERR_WORKSPACE = 4,   /* workspace pointer missing or too small */
   SPA_ERR_TIMEOUT = 5      /* a bounded device-side wait gave up */

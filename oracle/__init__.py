@@ -1,7 +1,7 @@
 """CPU oracle for the sparse paged-attention hot path -- TEST INFRASTRUCTURE ONLY.
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference arm
-may import this package, and only as the checker or the timed CPU baseline.  The
+may import this package, and only to check results or as the timed CPU baseline.  The
 product (attention_b200) never imports it.
 
 Parity pin: tests/golden/ holds fixtures produced by running the reference's
