@@ -315,7 +315,10 @@ __device__ __noinline__ void router_reuse_promoted(const int64_t* promoted, int6
 }
 
 // grid (kRouterCluster, B), cluster (kRouterCluster, 1, 1), block kRouterThreads.
-template <typename T, int NS>
+// PIPE (single-level routing, kv heads <= kRouterKvBatch, several candidates per warp):
+// each warp requests its next candidate's rows before it scores the current one, so a
+// warp's candidates cost one memory round trip instead of one each.
+template <typename T, int NS, bool PIPE>
 __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const RouterArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int hkv = a.kv_heads, D = a.head_dim;
@@ -393,10 +396,19 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
       const int g = (level == 2 && tree) ? page_of(c) : c;
       const float* base = tab + static_cast<int64_t>(g) * D;
       float total = 0.f;
+      if constexpr (PIPE) {
+        // rows holds this candidate (requested with the query, or in the previous pass)
+        CandRows<NS> next;
+        if (i + nwarps < nl)
+          load_cand_rows(next, tab + static_cast<int64_t>(c + nwarps * kRouterCluster) * D, kv_stride, 0, hkv, D);
+        total = accumulate_cand(rows, qg, 0, hkv, D, total);
+        rows = next;
+      } else {
 #pragma unroll 1
-      for (int k0 = 0; k0 < hkv; k0 += kRouterKvBatch) {
-        if (level != first_level || i != warp || k0 != 0) load_cand_rows(rows, base, kv_stride, k0, hkv, D);
-        total = accumulate_cand(rows, qg, k0, hkv, D, total);
+        for (int k0 = 0; k0 < hkv; k0 += kRouterKvBatch) {
+          if (level != first_level || i != warp || k0 != 0) load_cand_rows(rows, base, kv_stride, k0, hkv, D);
+          total = accumulate_cand(rows, qg, k0, hkv, D, total);
+        }
       }
       const float v = __fmul_rn(__fdiv_rn(total, static_cast<float>(a.q_heads)), a.scale);
       if (level == 1) {
@@ -443,11 +455,11 @@ __global__ void __launch_bounds__(kRouterThreads) router_cluster_kernel(const Ro
   }
 }
 
-template <typename T, int NS>
+template <typename T, int NS, bool PIPE>
 int launch_router_ns(const RouterArgs& a, int batch, cudaStream_t st) {
   const size_t smem = router_smem_bytes(a, static_cast<size_t>(a.q_heads) * a.head_dim * sizeof(T));
   if (smem > 200 * 1024) return SPA_ERR_UNSUPPORTED;
-  auto kern = router_cluster_kernel<T, NS>;
+  auto kern = router_cluster_kernel<T, NS, PIPE>;
   SPA_CHECK_CUDA(spa_set_smem_once(kern, static_cast<int>(smem)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kRouterCluster, batch, 1);
@@ -473,10 +485,18 @@ int launch_router_ns(const RouterArgs& a, int batch, cudaStream_t st) {
 // exactly, so the scoring loop carries no dead slices.
 template <typename T>
 int launch_router(const RouterArgs& a, int batch, cudaStream_t st) {
-  if (a.head_dim <= 32) return launch_router_ns<T, 1>(a, batch, st);
-  if (a.head_dim <= 64) return launch_router_ns<T, 2>(a, batch, st);
-  if (a.head_dim <= 128) return launch_router_ns<T, 4>(a, batch, st);
-  return launch_router_ns<T, 8>(a, batch, st);
+  // single level with more candidates than one per warp: prefetching scoring loop
+  const bool pipe = !a.supers && a.kv_heads <= kRouterKvBatch && a.n_pages > kRouterCluster * (kRouterThreads / 32);
+  if (pipe) {
+    if (a.head_dim <= 32) return launch_router_ns<T, 1, true>(a, batch, st);
+    if (a.head_dim <= 64) return launch_router_ns<T, 2, true>(a, batch, st);
+    if (a.head_dim <= 128) return launch_router_ns<T, 4, true>(a, batch, st);
+    return launch_router_ns<T, 8, true>(a, batch, st);
+  }
+  if (a.head_dim <= 32) return launch_router_ns<T, 1, false>(a, batch, st);
+  if (a.head_dim <= 64) return launch_router_ns<T, 2, false>(a, batch, st);
+  if (a.head_dim <= 128) return launch_router_ns<T, 4, false>(a, batch, st);
+  return launch_router_ns<T, 8, false>(a, batch, st);
 }
 
 // ---------------------------------------------------------------------------

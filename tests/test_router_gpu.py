@@ -37,6 +37,26 @@ def test_summaries_and_scores_bit_exact(dtype, heads, dim):
         assert torch.equal(sel.cpu(), oracle.topm(ref_scores, m))
 
 
+@pytest.mark.parametrize("heads,dim,n_pages", [((8, 8), 64, 130), ((32, 8), 128, 200), ((16, 16), 64, 150),
+                                               ((8, 8), 64, 65)])
+def test_single_level_router_many_pages(heads, dim, n_pages):
+    """Single-level routing with more candidates than warps in the cluster (several per
+    warp: the prefetching scoring loop when kv heads <= 8), scores bit-exact."""
+    hq, hkv = heads
+    gen = torch.Generator().manual_seed(n_pages + hq)
+    b, page = 2, 16
+    k = (torch.randn(b, hkv, n_pages * page, dim, generator=gen) * 0.5).to(torch.bfloat16)
+    q = (torch.randn(b, hq, dim, generator=gen) * 0.5).to(torch.bfloat16)
+    summ, _ = spa.page_summaries(k.to(DEV), block_size=page, superblock=4)
+    ref, _ = oracle.summaries_fp64(k, page, n_pages)
+    assert torch.equal(summ.cpu(), ref)
+    for m in (1, 8, 33):
+        sel, scores = spa.select_blocks(q.to(DEV), summ, m, scale=dim ** -0.5, return_scores=True)
+        ref_scores = oracle.router_scores(q, ref, dim ** -0.5)
+        assert torch.equal(scores.cpu(), ref_scores)
+        assert torch.equal(sel.cpu(), oracle.topm(ref_scores, m))
+
+
 def test_exact_ties_resolve_to_lower_page():
     gen = torch.Generator().manual_seed(4)
     b, h, d, page = 2, 4, 64, 32
