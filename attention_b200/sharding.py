@@ -1,8 +1,15 @@
 """Multi-GPU plumbing for the path (one process per GPU, torch.distributed).
 
-* Decode needs no exchange: ranks own disjoint batch rows (``shard_rows``) or run
-  independent replicas; the router of a row sees all of that row's heads on one
-  rank, so selections never need a collective.
+* Decode shards over (sequence, kv head) pairs (``DecodeShard``): the B x Hkv pairs,
+  sequence-major, are cut into equal contiguous ranges, one per rank, each a block of
+  whole sequences or a group of kv heads inside one sequence.  A rank holds the K/V
+  pages of its pairs only.  The router's score of a page averages over all query
+  heads of the sequence, so every rank keeps the query rows and the (small) page
+  summaries of its sequences for all heads and computes the selection itself:
+  ranks that share a sequence run the same deterministic kernel on the same inputs
+  and pick the same pages, with no collective.  The decode then reads only the
+  rank's kv heads and their query heads.  Gathering the outputs (``gather``) is
+  optional; the step itself exchanges nothing.
 * Long-context prefill splits the sequence into contiguous chunks.  Query i of a
   chunk needs the window-1 keys before it, so rank r receives the last
   ``window`` K/V tokens of rank r-1 (the halo, 2 x H x window x D elements per
@@ -24,6 +31,60 @@ def shard_rows(n: int, world: int, rank: int) -> slice:
     base, extra = divmod(n, world)
     start = rank * base + min(rank, extra)
     return slice(start, start + base + (1 if rank < extra else 0))
+
+
+def decode_shard(batch: int, kv_heads: int, world: int, rank: int) -> tuple[slice, slice]:
+    """The (sequence, kv head) pairs of ``rank``: (sequences, kv heads) slices.
+
+    Pairs are numbered sequence-major and split into ``world`` equal contiguous
+    ranges; each must be whole sequences or one sequence's kv-head group."""
+    pairs = batch * kv_heads
+    if world < 1 or pairs % world:
+        raise ValueError(f"{batch} x {kv_heads} (sequence, kv head) pairs do not split evenly over {world} ranks")
+    per = pairs // world
+    p0 = rank * per
+    if per >= kv_heads:
+        if per % kv_heads:
+            raise ValueError(f"{per} pairs per rank is not a whole number of sequences of {kv_heads} kv heads")
+        return slice(p0 // kv_heads, (p0 + per) // kv_heads), slice(0, kv_heads)
+    if kv_heads % per:
+        raise ValueError(f"{per} pairs per rank does not divide {kv_heads} kv heads")
+    h0 = p0 % kv_heads
+    return slice(p0 // kv_heads, p0 // kv_heads + 1), slice(h0, h0 + per)
+
+
+class DecodeShard:
+    """One rank's (sequence, kv head) block of a decode batch (see the module notes).
+
+    ``rows`` and ``kv`` select the sequences and kv heads; ``q_heads`` the query heads
+    of those kv heads (GQA groups are contiguous: q head h reads kv head h // group)."""
+
+    def __init__(self, batch: int, q_heads: int, kv_heads: int, world: int, rank: int, *, group=None):
+        if q_heads % kv_heads:
+            raise ValueError("query heads must be a multiple of kv heads")
+        self.batch, self.n_q_heads, self.n_kv_heads = batch, q_heads, kv_heads
+        self.world, self.rank, self.group = world, rank, group
+        self.rows, self.kv = decode_shard(batch, kv_heads, world, rank)
+        self.q_heads = self._q_slice(self.kv)
+        self.full_heads = self.kv.start == 0 and self.kv.stop == kv_heads
+
+    def _q_slice(self, kv: slice) -> slice:
+        g = self.n_q_heads // self.n_kv_heads
+        return slice(kv.start * g, kv.stop * g)
+
+    def local(self, t: torch.Tensor, heads: str = "q") -> torch.Tensor:
+        """The shard's block of a [B, heads, ...] tensor: query heads (``"q"``) or kv heads."""
+        return t[self.rows, self.q_heads if heads == "q" else self.kv].contiguous()
+
+    def gather(self, out_local: torch.Tensor) -> torch.Tensor:
+        """All ranks' output blocks assembled into [B, Hq, D] (one all_gather)."""
+        parts = [torch.empty_like(out_local) for _ in range(self.world)]
+        dist.all_gather(parts, out_local.contiguous(), group=self.group)
+        full = out_local.new_empty(self.batch, self.n_q_heads, out_local.size(-1))
+        for r, part in enumerate(parts):
+            rows, kv = decode_shard(self.batch, self.n_kv_heads, self.world, r)
+            full[rows, self._q_slice(kv)] = part
+        return full
 
 
 def _device_compute(q, k, v, out, window, rows, k_halo, v_halo):

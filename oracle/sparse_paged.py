@@ -25,7 +25,8 @@ __all__ = [
     "summaries_fp64", "super_summaries", "router_scores", "topm", "select_blocks", "select_blocks_tree",
     "expand_kv", "reference_attention", "make_candidates", "candidate_tokens", "gather_decode",
     "dense_decode", "paged_to_contiguous", "local_reference", "local_reference_chunked", "promotion_update",
-    "masked_dense_attention", "periodic_router", "span_tokens", "span_decode",
+    "masked_dense_attention", "periodic_router", "span_tokens", "span_decode", "select_blocks_einsum",
+    "select_blocks_tree_einsum", "span_candidate_indices", "span_candidate_attention", "reference_decode_step",
 ]
 
 
@@ -131,17 +132,52 @@ def select_blocks_tree(query: torch.Tensor, supers: torch.Tensor, summaries: tor
     return torch.stack(out)
 
 
+def select_blocks_einsum(query: torch.Tensor, summaries: torch.Tensor, top_blocks: int,
+                         dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """The reference's own router expression in the reference's arithmetic order:
+    einsum("bhd,bhgd->bhg").mean(dim=1).topk(m).indices
+    (triton_paged_gather_decode_benchmark.py:16-17), evaluated in ``dtype``, with the
+    kv-head summaries repeated over their query heads for GQA.  Unlike select_blocks
+    above it does not follow the CUDA kernels' canonical order: it is the yardstick the
+    canonical order is compared with (ties follow torch.topk)."""
+    q = query.to(dtype)
+    s = expand_kv(summaries.to(dtype), query.size(1))
+    return torch.einsum("bhd,bhgd->bhg", q, s).mean(dim=1).topk(top_blocks, dim=-1).indices.contiguous()
+
+
+def select_blocks_tree_einsum(query: torch.Tensor, supers: torch.Tensor, summaries: torch.Tensor, *, superblock: int,
+                              top_super: int, top_blocks: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Two levels of select_blocks_einsum, the way hierarchical_retrieval composes its
+    stages (benchmark_decode_attention.py:58-67): level 1 picks top_super superblocks
+    from the superblock summaries; level 2 runs the same expression over the gathered
+    summaries of those superblocks' pages (superblock order, pages ascending) and maps
+    the winners back to page ids."""
+    n_pages = summaries.size(2)
+    chosen = select_blocks_einsum(query, supers, top_super, dtype)
+    out = []
+    for b in range(query.size(0)):
+        ids = []
+        for s in chosen[b].tolist():
+            ids.extend(range(s * superblock, min((s + 1) * superblock, n_pages)))
+        ids_t = torch.tensor(ids, dtype=torch.int64)
+        pick = select_blocks_einsum(query[b : b + 1], summaries[b : b + 1, :, ids_t], top_blocks, dtype)[0]
+        out.append(ids_t[pick])
+    return torch.stack(out)
+
+
 # ------------------------------------------------------------------ attention
 def expand_kv(t: torch.Tensor, q_heads: int) -> torch.Tensor:
     """[B, Hkv, L, D] -> [B, Hq, L, D]: q head h reads kv head h // (Hq / Hkv)."""
     return t.repeat_interleave(q_heads // t.size(1), dim=1)
 
 
-def reference_attention(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor) -> torch.Tensor:
-    """softmax(q . K^T * D^-1/2) V in fp64 (triton_paged_attention.py:227-231), GQA-expanded."""
-    q = query.to(torch.float64)
-    k = expand_kv(keys.to(torch.float64), q.size(1))
-    v = expand_kv(values.to(torch.float64), q.size(1))
+def reference_attention(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
+                        dtype: torch.dtype = torch.float64) -> torch.Tensor:
+    """softmax(q . K^T * D^-1/2) V in ``dtype`` (fp64 unless asked; triton_paged_attention.py:227-231),
+    GQA-expanded."""
+    q = query.to(dtype)
+    k = expand_kv(keys.to(dtype), q.size(1))
+    v = expand_kv(values.to(dtype), q.size(1))
     scores = torch.einsum("bhd,bhld->bhl", q, k) * q.size(-1) ** -0.5
     return torch.einsum("bhl,bhld->bhd", scores.softmax(dim=-1), v)
 
@@ -160,6 +196,23 @@ def make_candidates(keys: torch.Tensor, values: torch.Tensor, selected: torch.Te
     sk = pk[bi, selected].permute(0, 2, 1, 3, 4).flatten(2, 3)
     sv = pv[bi, selected].permute(0, 2, 1, 3, 4).flatten(2, 3)
     return torch.cat((keys[:, :, hist:], sk), dim=2), torch.cat((values[:, :, hist:], sv), dim=2)
+
+
+def reference_decode_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, supers: torch.Tensor,
+                          summaries: torch.Tensor, *, superblock: int, top_super: int, top_blocks: int,
+                          local_window: int, block_size: int,
+                          dtype: torch.dtype = torch.float32) -> tuple[torch.Tensor, torch.Tensor]:
+    """One tree-routed sparse decode step the way the reference's PyTorch path computes
+    it, in ``dtype`` on contiguous K/V [B, Hkv, L, D]: the router expression of
+    select_blocks at two levels (select_blocks_tree_einsum), candidate assembly
+    (make_candidates, triton_paged_gather_decode_benchmark.py:20-28) and softmax attention
+    (reference_attention, triton_paged_attention.py:227-231; the timed unit of
+    triton_paged_gather_decode_benchmark.py:71).  Returns (selected [B, m], out [B, Hq, D]).
+    This is the reference arm's timed CPU path."""
+    sel = select_blocks_tree_einsum(query, supers, summaries, superblock=superblock, top_super=top_super,
+                                    top_blocks=top_blocks, dtype=dtype)
+    ck, cv = make_candidates(keys, values, sel, local_window, block_size)
+    return sel, reference_attention(query, ck, cv, dtype=dtype)
 
 
 def candidate_tokens(ctx: int, local_window: int, selected_row: list[int], block_size: int) -> list[int]:
@@ -196,6 +249,26 @@ def span_decode(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, s
         toks = torch.tensor(span_tokens(ctx, local_window, starts[i].tolist(), span_width), dtype=torch.int64)
         out.append(reference_attention(query[i : i + 1], keys[i : i + 1, :, toks], values[i : i + 1, :, toks]))
     return torch.cat(out)
+
+
+def span_candidate_indices(centers: torch.Tensor, context: int, local_window: int, span_width: int) -> torch.Tensor:
+    """Token indices [B, W + k*span]: the last local_window tokens, then span_width
+    tokens from each center, clamped to the last historical token.  Restates
+    build_candidate_indices (benchmark_decode_attention.py:86-90), whose record width
+    is fixed at 3, for any span width; the span kernel's index map
+    (triton_paged_attention.py:187-193) is the same for centers <= hist - span_width."""
+    hist = context - local_window
+    promoted = (centers.to(torch.int64).unsqueeze(-1) + torch.arange(span_width)).clamp_max(hist - 1).flatten(1)
+    local = torch.arange(hist, context).expand(centers.size(0), -1)
+    return torch.cat((local, promoted), dim=1)
+
+
+def span_candidate_attention(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
+                             indices: torch.Tensor) -> torch.Tensor:
+    """exact_attention over the gathered candidate tokens, fp64 (candidate_attention and
+    exact_attention, benchmark_decode_attention.py:39-49), GQA-expanded."""
+    idx = indices.to(torch.int64)[:, None, :, None].expand(-1, keys.size(1), -1, keys.size(-1))
+    return reference_attention(query, keys.gather(2, idx), values.gather(2, idx))
 
 
 def gather_decode(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, selected: torch.Tensor, *,

@@ -20,6 +20,16 @@ checksums to prove the regeneration, and the reference's outputs:
 * refresh_gate        -- seed 7: the reference's RefreshHead (train_refresh_head.py) on
   three (state, cached state) sets of growing drift, its sigmoid probabilities, and the
   drift distance 1 - cosine_similarity of evaluate_promotion_ttl.py:130.
+* router_cfg3         -- the tree-routed 128k router shape (router_inputs.py): the
+  reference's select_blocks run twice, the way hierarchical_retrieval composes its
+  stages (benchmark_decode_attention.py:58-67): top-4 superblocks from the superblock
+  summaries, then top-m (m = 2, 4, 8) among those superblocks' page summaries.  With
+  needles (batch 4, seed 11) and without (batch 16, seed 12), each in fp32 and fp64.
+* router_cfg5         -- the integrated decoder's router shape (8 heads, head_dim 64,
+  129 pages): select_blocks top-8, batch 32, seed 13, fp32 and fp64.
+* span_gather         -- seed 14: build_candidate_indices (benchmark_decode_attention.py:86-90,
+  span width 3) + candidate_attention, the reference's PyTorch form of the
+  span_gather_decode_attention index map (triton_paged_attention.py:187-193).
 """
 
 from __future__ import annotations
@@ -133,8 +143,62 @@ def main(ref_root: str) -> None:
              w2=head.network[2].weight.detach().numpy(), b2=head.network[2].bias.detach().numpy(),
              state=torch.stack(states).numpy(), cached=torch.stack(cached).numpy(),
              prob=torch.stack(probs).numpy(), drift=torch.stack(drifts).numpy())
+    # ---- router at the tree-routed 128k shape and the decoder shape
+    import benchmark_decode_attention as bda  # noqa: E402
+
+    sys.path.insert(0, str(HERE))
+    import router_inputs as ri  # noqa: E402
+
+    def ref_tree(inp, top_super, m, dt):
+        q, sup, summ = inp["query"], inp["supers"], inp["summaries"]
+        grp = q.size(1) // sup.size(1)
+        chosen = tpg.select_blocks(q.to(dt), sup.to(dt).repeat_interleave(grp, 1), top_super)
+        sb, n_pages, rows = ri.CFG3["superblock"], summ.size(2), []
+        for bb in range(q.size(0)):
+            ids = []
+            for sblk in chosen[bb].tolist():
+                ids.extend(range(sblk * sb, min((sblk + 1) * sb, n_pages)))
+            ids = torch.tensor(ids)
+            pick = tpg.select_blocks(q[bb : bb + 1].to(dt), summ[bb : bb + 1, :, ids].to(dt).repeat_interleave(grp, 1),
+                                     m)[0]
+            rows.append(ids[pick])
+        return chosen, torch.stack(rows)
+
+    fx = {}
+    for tag, seed, batch, needles in (("needles", 11, 4, 8), ("plain", 12, 16, 0)):
+        inp = ri.router_cfg3_inputs(seed, batch, needles)
+        fx[f"{tag}_seed"] = seed
+        fx[f"{tag}_shape"] = np.array([batch, needles])
+        for key, val in ri.checksums(inp).items():
+            fx[f"{tag}_{key}"] = val
+        for m in (2, 4, 8):
+            for dt, name in ((torch.float32, "f32"), (torch.float64, "f64")):
+                chosen, sel = ref_tree(inp, ri.CFG3["top_super"], m, dt)
+                fx[f"{tag}_m{m}_{name}"] = sel.numpy()
+                fx[f"{tag}_super_{name}"] = chosen.numpy()
+    np.savez(HERE / "router_cfg3.npz", **fx)
+
+    inp = ri.router_cfg5_inputs(13, 32)
+    grp = inp["query"].size(1) // inp["summaries"].size(1)
+    fx = {"seed": 13, "batch": 32, **ri.checksums(inp)}
+    for dt, name in ((torch.float32, "f32"), (torch.float64, "f64")):
+        fx[f"m8_{name}"] = tpg.select_blocks(inp["query"].to(dt),
+                                             inp["summaries"].to(dt).repeat_interleave(grp, 1), 8).numpy()
+    np.savez(HERE / "router_cfg5.npz", **fx)
+
+    # ---- span gather: the reference's PyTorch candidate path with span width 3
+    inp = ri.span_inputs(14)
+    c = ri.SPAN
+    cfg = bda.Config(context=c["context"], local_window=c["local_window"], block_size=64, top_blocks=1,
+                     top_tokens=c["centers"], batch_size=c["batch"], heads=c["heads"], head_dim=c["head_dim"],
+                     iterations=1, warmup=0, seed=14, device="cpu")
+    idx = bda.build_candidate_indices(inp["centers"], cfg, torch.device("cpu"))
+    out = bda.candidate_attention(inp["query"], inp["keys"], inp["values"], idx)
+    np.savez(HERE / "span_gather.npz", seed=14, indices=idx.numpy(), out=out.numpy(), **ri.checksums(inp))
     print("wrote fixtures to", HERE)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of a divagr18/attention checkout>")
+    main(sys.argv[1])

@@ -236,3 +236,23 @@ def test_span_gather_page_pool():
     vc = oracle.paged_to_contiguous(v_pool, table, 7 * page)
     ref = oracle.span_decode(q, kc, vc, starts, local_window=100, span_width=40, context_lens=ctx)
     assert_close(out, ref, torch.bfloat16)
+
+
+def test_span_gather_pinned_to_reference(golden_dir):
+    """fp32 span decode against the reference's build_candidate_indices +
+    candidate_attention (span width 3), within the fp32 tolerance."""
+    import importlib
+    import sys
+
+    import numpy as np
+
+    sys.path.insert(0, str(golden_dir))
+    ri = importlib.import_module("router_inputs")
+    fx = dict(np.load(golden_dir / "span_gather.npz"))
+    inp = ri.span_inputs(int(fx["seed"]))
+    c = ri.SPAN
+    out = spa.span_gather_decode_attention(inp["query"].to(DEV), inp["keys"].to(DEV), inp["values"].to(DEV),
+                                           inp["centers"].to(DEV), local_window=c["local_window"],
+                                           span_width=c["span_width"])
+    ref = torch.from_numpy(fx["out"]).double()
+    assert (out.double().cpu() - ref).abs().max().item() <= 1e-5

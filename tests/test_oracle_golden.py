@@ -167,3 +167,96 @@ def test_gate_sim_policies():
     sig = GateSim("signature")
     sigs = [torch.tensor([[1, 2, 3]])] * 3 + [torch.tensor([[1, 2, 4]])] * 2
     assert [sig.step(fresh[t], signature=sigs[t])[1] for t in range(5)] == [True, False, False, True, False]
+
+
+# ---------------------------------------------------------------- router pins at the benchmark shapes
+def _router_inputs():
+    import importlib
+    import sys
+
+    sys.path.insert(0, str(__import__("pathlib").Path(__file__).resolve().parent / "golden"))
+    return importlib.import_module("router_inputs")
+
+
+def _check_inputs(fx, prefix, inputs):
+    for key, val in _router_inputs().checksums(inputs).items():
+        exp = float(fx[prefix + key])
+        assert abs(val - exp) <= 1e-9 * max(1.0, abs(exp)), key
+
+
+def test_router_cfg3_tree_pinned(golden_dir):
+    """The canonical router (oracle.select_blocks_tree, the CUDA kernels' arithmetic) and
+    the reference-order restatement give exactly the reference's own select_blocks,
+    composed over superblocks then pages, at the 128k shape (511 pages, 32/8 heads,
+    D128), with and without needle pages, for m = 2, 4, 8."""
+    ri = _router_inputs()
+    fx = _load(golden_dir, "router_cfg3.npz")
+    c = ri.CFG3
+    for tag in ("needles", "plain"):
+        batch, needles = fx[f"{tag}_shape"].tolist()
+        inp = ri.router_cfg3_inputs(int(fx[f"{tag}_seed"]), batch, needles)
+        _check_inputs(fx, f"{tag}_", inp)
+        for m in (2, 4, 8):
+            ref = torch.from_numpy(fx[f"{tag}_m{m}_f32"])
+            assert torch.equal(ref, torch.from_numpy(fx[f"{tag}_m{m}_f64"]))
+            for scale in (1.0, c["head_dim"] ** -0.5):
+                got = oracle.select_blocks_tree(inp["query"], inp["supers"], inp["summaries"],
+                                                superblock=c["superblock"], top_super=c["top_super"], top_blocks=m,
+                                                scale=scale)
+                assert torch.equal(got, ref), (tag, m, scale)
+            einsum = oracle.select_blocks_tree_einsum(inp["query"], inp["supers"], inp["summaries"],
+                                                      superblock=c["superblock"], top_super=c["top_super"],
+                                                      top_blocks=m)
+            assert torch.equal(einsum, ref)
+
+
+def test_router_cfg5_pinned(golden_dir):
+    ri = _router_inputs()
+    fx = _load(golden_dir, "router_cfg5.npz")
+    inp = ri.router_cfg5_inputs(int(fx["seed"]), int(fx["batch"]))
+    _check_inputs(fx, "", inp)
+    ref = torch.from_numpy(fx["m8_f32"])
+    assert torch.equal(ref, torch.from_numpy(fx["m8_f64"]))
+    for scale in (1.0, ri.CFG5["head_dim"] ** -0.5):
+        assert torch.equal(oracle.select_blocks(inp["query"], inp["summaries"], 8, scale=scale), ref)
+    assert torch.equal(oracle.select_blocks_einsum(inp["query"], inp["summaries"], 8), ref)
+
+
+def test_span_gather_pinned(golden_dir):
+    """The span index map and attention restated in the oracle equal the reference's
+    build_candidate_indices + candidate_attention (span width 3)."""
+    ri = _router_inputs()
+    fx = _load(golden_dir, "span_gather.npz")
+    inp = ri.span_inputs(int(fx["seed"]))
+    _check_inputs(fx, "", inp)
+    c = ri.SPAN
+    idx = oracle.span_candidate_indices(inp["centers"], c["context"], c["local_window"], c["span_width"])
+    assert torch.equal(idx, torch.from_numpy(fx["indices"]))
+    ref = torch.from_numpy(fx["out"]).double()
+    out = oracle.span_candidate_attention(inp["query"], inp["keys"], inp["values"], idx)
+    assert (out - ref).abs().max().item() <= 1e-5
+    # the per-sequence token-list form (span_tokens) used by the GPU tests gives the same
+    out2 = oracle.span_decode(inp["query"], inp["keys"], inp["values"], inp["centers"],
+                              local_window=c["local_window"], span_width=c["span_width"])
+    assert (out2 - ref).abs().max().item() <= 1e-5
+
+
+def test_reference_decode_step_composition():
+    """The reference arm's timed CPU step (reference-order router, make_candidates, fp32
+    attention) on a reduced tree-routed shape agrees with the canonical oracle: the same
+    pages, the fp64 gather decode within the fp32 tolerance."""
+    gen = torch.Generator().manual_seed(5)
+    b, hq, hkv, d, page, n_pages, win, sb = 2, 8, 2, 32, 16, 37, 16, 8
+    ctx = n_pages * page + win
+    keys = torch.randn(b, hkv, ctx, d, generator=gen)
+    values = torch.randn(b, hkv, ctx, d, generator=gen)
+    q = torch.randn(b, hq, d, generator=gen)
+    summ, sums = oracle.summaries_fp64(keys, page, n_pages)
+    sup = oracle.super_summaries(sums, sb, page)
+    for m in (2, 4, 8):
+        sel, out = oracle.reference_decode_step(q, keys, values, sup, summ, superblock=sb, top_super=2,
+                                                top_blocks=m, local_window=win, block_size=page)
+        assert torch.equal(sel, oracle.select_blocks_tree(q, sup, summ, superblock=sb, top_super=2, top_blocks=m))
+        ref = oracle.gather_decode(q, keys, values, sel, local_window=win, block_size=page)
+        assert out.dtype == torch.float32
+        assert (out.double() - ref).abs().max().item() <= 1e-5

@@ -116,6 +116,10 @@ def test_sparse_decode_128k_full_size(m):
     exp = oracle.select_blocks_tree(q.cpu(), sup.cpu(), summ.cpu(), superblock=cfg.superblock,
                                     top_super=cfg.top_super, top_blocks=m, scale=cfg.head_dim ** -0.5)
     assert torch.equal(sel.cpu(), exp)
+    # the reference's own arithmetic order (einsum, mean over heads, topk) picks the same pages
+    ein = oracle.select_blocks_tree_einsum(q.cpu(), sup.cpu(), summ.cpu(), superblock=cfg.superblock,
+                                           top_super=cfg.top_super, top_blocks=m)
+    assert torch.equal(sel.cpu(), ein)
     out = spa.paged_gather_decode_attention(q, k_pool, v_pool, sel, local_window=cfg.local_window,
                                             block_size=cfg.page_size, page_table=table,
                                             context_lens=wl["context_lens"])
@@ -132,6 +136,68 @@ def test_sparse_decode_128k_full_size(m):
         ref = oracle.reference_attention(q[b : b + 1].cpu(), kc, vc)
         o = out[b : b + 1].double().cpu()
         assert ((o - ref).abs() <= 2e-2 + 1e-2 * ref.abs()).all()
+
+
+def _router_inputs():
+    import importlib
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+    return importlib.import_module("router_inputs")
+
+
+@pytest.mark.parametrize("tag", ["needles", "plain"])
+def test_tree_router_pinned_to_reference_cfg3(golden_dir, tag):
+    """spa_router_tree_topm returns exactly the reference's select_blocks composed over
+    superblocks then pages (fixture made by the reference's functions) at the 128k
+    shape: 511 pages, 32/8 heads, D128, m = 2, 4, 8, with the step's scale and without."""
+    import numpy as np
+
+    ri = _router_inputs()
+    fx = dict(np.load(golden_dir / "router_cfg3.npz"))
+    batch, needles = fx[f"{tag}_shape"].tolist()
+    inp = ri.router_cfg3_inputs(int(fx[f"{tag}_seed"]), batch, needles)
+    c = ri.CFG3
+    q, sup, summ = (inp[k].to(DEV) for k in ("query", "supers", "summaries"))
+    for m in (2, 4, 8):
+        ref = torch.from_numpy(fx[f"{tag}_m{m}_f32"])
+        for scale in (1.0, c["head_dim"] ** -0.5):
+            got = spa.select_blocks_tree(q, sup, summ, superblock=c["superblock"], top_super=c["top_super"],
+                                         top_blocks=m, scale=scale)
+            assert torch.equal(got.cpu(), ref), (m, scale)
+
+
+def test_router_pinned_to_reference_cfg5(golden_dir):
+    import numpy as np
+
+    ri = _router_inputs()
+    fx = dict(np.load(golden_dir / "router_cfg5.npz"))
+    inp = ri.router_cfg5_inputs(int(fx["seed"]), int(fx["batch"]))
+    ref = torch.from_numpy(fx["m8_f32"])
+    for scale in (1.0, ri.CFG5["head_dim"] ** -0.5):
+        got = spa.select_blocks(inp["query"].to(DEV), inp["summaries"].to(DEV), 8, scale=scale)
+        assert torch.equal(got.cpu(), ref)
+
+
+def test_tree_router_reference_order_bench_workload():
+    """Every batch row of the bench's 128k workload (16 independent batches of 4 rows
+    in one pool): the kernel's selection equals the reference's einsum/mean/topk order."""
+    cfg = workloads.SparseDecodeConfig(top_m=8)
+    groups = 16
+    wl = workloads.sparse_decode_workload(cfg, groups=groups, seed=0)
+    scale = cfg.head_dim ** -0.5
+    for gi in range(groups):
+        table = wl["page_table"][gi]
+        summ, sup = spa.page_summaries(wl["k_pool"], block_size=cfg.page_size, n_pages=cfg.routable_pages,
+                                       page_table=table, superblock=cfg.superblock)
+        q = wl["query"][gi]
+        for m in (2, 4, 8):
+            got = spa.select_blocks_tree(q, sup, summ, superblock=cfg.superblock, top_super=cfg.top_super,
+                                         top_blocks=m, scale=scale)
+            ref = oracle.select_blocks_tree_einsum(q.cpu(), sup.cpu(), summ.cpu(), superblock=cfg.superblock,
+                                                   top_super=cfg.top_super, top_blocks=m)
+            assert torch.equal(got.cpu(), ref), (gi, m)
 
 
 # ---------------------------------------------------------------- periodic causal router

@@ -99,3 +99,82 @@ def test_missing_peer_surfaces_as_error_not_hang(tmp_path):
     mp.start_processes(_late_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn",
                        join=True)
     assert (tmp_path / "status.txt").read_text().startswith("error")
+
+
+# ---------------------------------------------------------------- (sequence, kv head) decode shards
+def test_decode_shard_layout():
+    from attention_b200.sharding import decode_shard
+
+    # 4 sequences x 8 kv heads: whole sequences up to 4 ranks, kv-head halves at 8
+    assert decode_shard(4, 8, 1, 0) == (slice(0, 4), slice(0, 8))
+    assert decode_shard(4, 8, 2, 1) == (slice(2, 4), slice(0, 8))
+    assert decode_shard(4, 8, 4, 3) == (slice(3, 4), slice(0, 8))
+    assert decode_shard(4, 8, 8, 5) == (slice(2, 3), slice(4, 8))
+    assert decode_shard(8, 8, 8, 7) == (slice(7, 8), slice(0, 8))
+    covered = set()
+    for r in range(8):
+        rows, kv = decode_shard(4, 8, 8, r)
+        covered |= {(b, h) for b in range(rows.start, rows.stop) for h in range(kv.start, kv.stop)}
+    assert covered == {(b, h) for b in range(4) for h in range(8)}
+    with pytest.raises(ValueError):
+        decode_shard(4, 8, 3, 0)
+    with pytest.raises(ValueError):
+        decode_shard(2, 6, 3, 0)  # 4 pairs per rank: not a divisor of 6 kv heads
+
+
+def _sparse_inputs(seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    b, hq, hkv, d, page, n_pages, win, sb = 4, 16, 8, 32, 16, 37, 16, 8
+    ctx = n_pages * page + win
+    keys = torch.randn(b, hkv, ctx, d, generator=gen, dtype=torch.float64)
+    values = torch.randn(b, hkv, ctx, d, generator=gen, dtype=torch.float64)
+    q = torch.randn(b, hq, d, generator=gen, dtype=torch.float64)
+    return dict(q=q, keys=keys, values=values, page=page, n_pages=n_pages, win=win, sb=sb)
+
+
+def _decode_worker(rank, world, port, result_dir):
+    """Each rank: the router over its sequences' full query rows and summaries (the
+    oracle's canonical router), then the gather decode over its own kv heads only."""
+    from attention_b200.sharding import DecodeShard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        x = _sparse_inputs()
+        q, keys, values = x["q"], x["keys"], x["values"]
+        shard = DecodeShard(q.size(0), q.size(1), keys.size(1), world, rank)
+        # replicated router inputs of the shard's sequences (all heads)
+        summ, sums = oracle.summaries_fp64(keys[shard.rows], x["page"], x["n_pages"])
+        sup = oracle.super_summaries(sums, x["sb"], x["page"])
+        sel = oracle.select_blocks_tree(q[shard.rows], sup, summ, superblock=x["sb"], top_super=2, top_blocks=3)
+        # the rank holds only its kv heads' pages
+        k_local, v_local = shard.local(keys, "kv"), shard.local(values, "kv")
+        out_local = oracle.gather_decode(shard.local(q), k_local, v_local, sel, local_window=x["win"],
+                                         block_size=x["page"])
+        full = shard.gather(out_local)
+        sels = [torch.empty_like(sel) for _ in range(world)]
+        dist.all_gather(sels, sel)
+        if rank == 0:
+            torch.save({"out": full, "sel": sels}, os.path.join(result_dir, "decode.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_decode_shards_match_single_process(tmp_path, world):
+    mp.start_processes(_decode_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    got = torch.load(tmp_path / "decode.pt")
+    x = _sparse_inputs()
+    summ, sums = oracle.summaries_fp64(x["keys"], x["page"], x["n_pages"])
+    sup = oracle.super_summaries(sums, x["sb"], x["page"])
+    sel = oracle.select_blocks_tree(x["q"], sup, summ, superblock=x["sb"], top_super=2, top_blocks=3)
+    ref = oracle.gather_decode(x["q"], x["keys"], x["values"], sel, local_window=x["win"], block_size=x["page"])
+    assert (got["out"] - ref).abs().max().item() < 1e-12
+    # ranks that share a sequence selected the same pages, equal to the single-process ones
+    from attention_b200.sharding import decode_shard
+
+    for r in range(world):
+        rows, _ = decode_shard(4, 8, world, r)
+        assert torch.equal(got["sel"][r], sel[rows])
