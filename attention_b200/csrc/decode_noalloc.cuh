@@ -8,8 +8,6 @@
 // every GPU that loads the library, for the life of the process.
 #pragma once
 
-#include <mutex>
-
 #include "decode.cuh"
 
 namespace spa {
@@ -18,21 +16,16 @@ namespace spa {
 // it is only a stand-in, and the device address comes from cudaGetSymbolAddress.
 static __device__ __align__(256) unsigned char g_decode_scratch[SPA_DECODE_STATIC_SCRATCH_BYTES];
 
-// Device address of g_decode_scratch on the current device, looked up once per
-// device (with that device current) and cached.  Returns nullptr on failure.
+// Device address of g_decode_scratch in the context current on the calling thread, or
+// nullptr on failure.  Looked up on every call rather than cached: a cached address
+// belongs to the context it was looked up in, and a caller may decode from another
+// context on the same device (a plugin host's own driver context) or after a device
+// reset, where a cached address would point at memory the current context does not
+// own.  The first lookup in a context loads the library's device code into it.
 inline void* decode_scratch_ptr() {
-  constexpr int kMaxDevices = 64;
-  static std::mutex mu;
-  static void* ptrs[kMaxDevices] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  std::lock_guard<std::mutex> lock(mu);
-  if (!ptrs[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess) return nullptr;
-    ptrs[dev] = p;
-  }
-  return ptrs[dev];
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess) return nullptr;
+  return p;
 }
 
 }  // namespace spa
@@ -44,11 +37,10 @@ extern "C" int spa_paged_decode_noalloc(const void* q, int dtype, int batch, int
   if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || max_candidates < 0) return SPA_ERR_INVALID;
   const size_t need = spa_decode_workspace_size(batch, q_heads, kv_heads, head_dim, max_candidates);
   if (need > SPA_DECODE_STATIC_SCRATCH_BYTES) return SPA_ERR_WORKSPACE;
-  void* scratch = nullptr;
-  if (need > 0) {
-    scratch = spa::decode_scratch_ptr();
-    if (!scratch) return SPA_ERR_CUDA;
-  }
+  // resolved on every call, also when this request needs no scratch, so the first call
+  // in a context always does the lookup (callers are told to make it before any capture)
+  void* scratch = spa::decode_scratch_ptr();
+  if (!scratch) return SPA_ERR_CUDA;
   return spa_paged_decode(q, dtype, batch, q_heads, kv_heads, head_dim, kv, context_lens, local_window, selected,
-                          top_m, max_candidates, scale, out, scratch, need, stream);
+                          top_m, max_candidates, scale, out, need > 0 ? scratch : nullptr, need, stream);
 }

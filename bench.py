@@ -1,34 +1,37 @@
-"""Benchmark: 128k tree-routed sparse paged decode (+ local prefill) on B200.
+"""Benchmark: 128k tree-routed sparse paged decode (+ dense decode, local prefill,
+integrated decoder) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Workload (one "step"): the tree-routed sparse decode configuration -- batch 4,
 32 query / 8 kv heads, head_dim 128, bf16, 131072-token contexts in pages of 256,
 256-token local window, superblocks of 16 pages, top-4 superblocks, top-m pages
-(m=4 by default) -- one two-level router launch plus one fused page-gather
-split-K decode over the selected pages, for one batch.  Consecutive steps cycle
-through `--groups` independent batches (different sequences and queries) stored
-in one page pool, so the pages a step reads were last touched ~groups steps ago
-and the re-read footprint (groups x ~22.6 MB) exceeds the 126 MB L2.
+(m=4 by default) -- the two-level router plus the fused page-gather split-K decode
+over the selected pages, for one batch.  Consecutive steps cycle through
+`--groups` independent batches (different sequences and queries) stored in one
+page pool, so the pages a step reads were last touched ~groups steps ago and the
+re-read footprint (groups x ~22.6 MB) exceeds the 126 MB L2.
 
-`value` is aggregate algorithmic HBM GB/s (bytes of one step x steps x ranks /
-max-over-ranks device time); `us_per_step` is the per-step latency.  Multi-GPU
-runs are weak-scaled replicas (each rank decodes its own batches; decode needs
-no collective).  A `prefill` object reports the 128k causal sliding-window
-prefill (window 2048, 32 heads, head_dim 128, bf16) in TFLOP/s; with N > 1 the
-sequence is split in contiguous chunks and each rank receives a 2048-token K/V
-halo from the previous rank over NCCL.
+`value` is aggregate algorithmic HBM GB/s (bytes of one step x steps / max-over-
+ranks device time); `us_per_step` is the step latency.  With N > 1 GPUs the same
+batch is split over the ranks by (sequence, kv head) pairs (strong scaling: the
+total work per step is fixed): each rank holds the K/V pages of its pairs, keeps
+its sequences' query rows and page summaries for all heads, routes them itself
+and decodes its own kv heads; no collective runs inside a step.  The dense 32k
+decode is split the same way, and the 128k prefill in contiguous sequence
+chunks with a 2048-token K/V halo from the previous rank over NCCL.
 
-`--impl reference` times the reference's PyTorch path restated for the CPU
-(router einsum/mean/top-k, candidate assembly, dense attention) on the host
-cores, rank 0 only.
+`--impl reference` times the reference's PyTorch path on the host cores (rank 0
+only): the oracle's restatement of select_blocks at two levels, make_candidates
+and reference_attention, in fp32, on the same configuration.  It never loads the
+CUDA library.
 """
 
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
-import math
 import os
 import statistics
 import sys
@@ -39,8 +42,21 @@ from pathlib import Path
 import torch
 
 ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 METRIC = "128k sparse decode µs/step & HBM GB/s; local prefill TFLOP/s @1/2/4/8 GPU"
+PREFILL_SEQS = (4096, 16384, 32768, 131072, 262144)
+
+
+def load_workloads():
+    """attention_b200/workloads.py loaded on its own (it needs only torch): importing it
+    through the package would load the CUDA library, which the reference arm must not."""
+    spec = importlib.util.spec_from_file_location("spa_workloads", ROOT / "attention_b200" / "workloads.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["spa_workloads"] = mod
+    spec.loader.exec_module(mod)
+    return mod
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -180,144 +196,140 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
-# ------------------------------------------------------------------ CPU path of the reference
-def cpu_reference_step(q, k_c, v_c, supers, summaries, cfg):
-    """The reference's decode step restated for the CPU in its own ops: router
-    einsum -> mean over heads -> top-k at two levels (select_blocks,
-    triton_paged_gather_decode_benchmark.py:16-17), candidate assembly
-    (make_candidates, :20-28) and dense softmax attention
-    (reference_attention, triton_paged_attention.py:227-231), GQA-expanded."""
-    b, hq, d = q.shape
-    hkv = k_c.size(1)
-    group = hq // hkv
-    qf = q.float()
-    qg = qf.view(b, hkv, group, d).sum(2)
-    s1 = torch.einsum("bkd,bksd->bs", qg, supers) / hq
-    top_s = torch.sort(s1, dim=1, descending=True, stable=True).indices[:, : cfg.top_super]
-    pages = (top_s.unsqueeze(-1) * cfg.superblock + torch.arange(cfg.superblock)).flatten(1)
-    pages = pages.clamp_max(cfg.routable_pages - 1)
-    cand = summaries[torch.arange(b)[:, None, None], torch.arange(hkv)[None, :, None], pages[:, None, :]]
-    s2 = torch.einsum("bkd,bkpd->bp", qg, cand) / hq
-    order = torch.sort(s2, dim=1, descending=True, stable=True).indices[:, : cfg.top_m]
-    sel = torch.gather(pages, 1, order)
-    hist = cfg.context - cfg.local_window
-    pk = k_c[:, :, :hist].view(b, hkv, hist // cfg.page_size, cfg.page_size, d).permute(0, 2, 1, 3, 4)
-    pv = v_c[:, :, :hist].view(b, hkv, hist // cfg.page_size, cfg.page_size, d).permute(0, 2, 1, 3, 4)
-    bi = torch.arange(b).unsqueeze(1)
-    ck = torch.cat((k_c[:, :, hist:], pk[bi, sel].permute(0, 2, 1, 3, 4).flatten(2, 3)), dim=2).float()
-    cv = torch.cat((v_c[:, :, hist:], pv[bi, sel].permute(0, 2, 1, 3, 4).flatten(2, 3)), dim=2).float()
-    ck = ck.repeat_interleave(group, dim=1)
-    cv = cv.repeat_interleave(group, dim=1)
-    scores = torch.einsum("bhd,bhld->bhl", qf, ck) * d ** -0.5
-    out = torch.einsum("bhl,bhld->bhd", scores.softmax(-1), cv)
-    return sel, out.to(q.dtype)
+def sparse_config(cfg, groups: int, world: int) -> dict:
+    """The `config` object of both arms (identical by construction)."""
+    wk = load_workloads()
+    bytes_step = wk.sparse_decode_bytes(cfg)
+    return {"workload": f"tree-routed sparse decode 128k: B{cfg.batch} Hq{cfg.q_heads}/Hkv{cfg.kv_heads} "
+                        f"D{cfg.head_dim} bf16, P{cfg.page_size} x {cfg.pages_per_seq} pages, W{cfg.local_window}, "
+                        f"superblock {cfg.superblock} top-{cfg.top_super}, top-m {cfg.top_m}",
+            "batch": cfg.batch, "context": cfg.context, "top_m": cfg.top_m, "superblock": cfg.superblock,
+            "top_super": cfg.top_super, "groups": groups, "bytes_per_step": bytes_step,
+            "l2": f"inputs larger than L2: {groups} rotating batches, {groups * bytes_step / 1e6:.0f} MB "
+                  "re-read footprint vs 126 MB L2",
+            "parallelism": "single GPU" if world == 1 else
+            f"(sequence, kv head) shards x{world}, strong scaling, no collective in the step"}
 
 
-def cpu_inputs_from_pool(wl, group: int, cfg):
-    """Contiguous CPU copies [B, Hkv, L, D] of one group's sequences (plus its fp32 summaries)."""
-    table = wl["page_table"][group].long()
-    b, npg = table.shape
-    k = wl["k_pool"][table.reshape(-1)].view(b, npg, cfg.kv_heads, cfg.page_size, cfg.head_dim)
-    v = wl["v_pool"][table.reshape(-1)].view(b, npg, cfg.kv_heads, cfg.page_size, cfg.head_dim)
-    k = k.permute(0, 2, 1, 3, 4).reshape(b, cfg.kv_heads, npg * cfg.page_size, cfg.head_dim).cpu()
-    v = v.permute(0, 2, 1, 3, 4).reshape(b, cfg.kv_heads, npg * cfg.page_size, cfg.head_dim).cpu()
-    return wl["query"][group].cpu(), k, v
+def time_graph(graph, reps: int, world: int) -> float:
+    """ms per replay of ``graph`` (CUDA events, barrier + synchronise around, max over ranks)."""
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1) / reps, world)
 
 
-def cpu_summaries(k_c, cfg):
-    b, hkv, _, d = k_c.shape
-    n = cfg.routable_pages
-    summ = k_c[:, :, : n * cfg.page_size].float().view(b, hkv, n, cfg.page_size, d).mean(3)
-    nsup = cfg.n_super
-    pad = nsup * cfg.superblock - n
-    sums = summ * cfg.page_size
-    sums = torch.cat((sums, torch.zeros(b, hkv, pad, d)), dim=2).view(b, hkv, nsup, cfg.superblock, d).sum(3)
-    counts = torch.full((nsup,), float(cfg.superblock * cfg.page_size))
-    counts[-1] = (n - (nsup - 1) * cfg.superblock) * cfg.page_size
-    return sums / counts.view(1, 1, nsup, 1), summ
+def capture(fn):
+    """Warm ``fn`` on a side stream, then capture it once into a CUDA graph."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    return graph
 
 
-def time_cpu_steps(q, k_c, v_c, sup, summ, cfg, *, steps: int, budget_s: float):
-    cpu_reference_step(q, k_c, v_c, sup, summ, cfg)  # warm-up
-    times = []
-    t_end = time.perf_counter() + budget_s
-    for _ in range(steps):
-        t0 = time.perf_counter()
-        cpu_reference_step(q, k_c, v_c, sup, summ, cfg)
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_end:
-            break
-    return statistics.mean(times), len(times)
+# ------------------------------------------------------------------ sparse decode: inputs of this rank
+class SparseShardInputs:
+    """The rank's share of the rotating 128k batches: its sequences' query rows and
+    page summaries for all heads (router inputs), its kv heads' query heads, and a
+    compact pool holding only its (sequence, kv head) pages."""
+
+    def __init__(self, spa, wk, cfg, groups, world, rank, dev):
+        from attention_b200.sharding import DecodeShard
+
+        self.shard = DecodeShard(cfg.batch, cfg.q_heads, cfg.kv_heads, world, rank)
+        rows = self.shard.rows
+        wl = wk.sparse_decode_workload(cfg, groups=groups, seed=1000, device=dev)
+        self.summ, self.sup = [], []
+        for g in range(groups):
+            s, u = spa.page_summaries(wl["k_pool"], block_size=cfg.page_size, n_pages=cfg.routable_pages,
+                                      page_table=wl["page_table"][g], superblock=cfg.superblock)
+            self.summ.append(s[rows].contiguous())
+            self.sup.append(u[rows].contiguous())
+        self.q_rows = [wl["query"][g][rows].contiguous() for g in range(groups)]
+        self.q_local = [q[:, self.shard.q_heads].contiguous() for q in self.q_rows]
+        if world == 1:
+            self.k_pool, self.v_pool, self.table = wl["k_pool"], wl["v_pool"], wl["page_table"]
+        else:
+            tab = wl["page_table"][:, rows]
+            phys = tab.reshape(-1).long()
+            self.k_pool = wl["k_pool"][phys][:, self.shard.kv].contiguous()
+            self.v_pool = wl["v_pool"][phys][:, self.shard.kv].contiguous()
+            self.table = torch.arange(phys.numel(), dtype=torch.int32, device=dev).view(tab.shape).contiguous()
+        self.ctx = wl["context_lens"][rows].contiguous()
+        self.n_rows = rows.stop - rows.start
+        del wl
+        torch.cuda.empty_cache()
+
+
+def make_step(spa, cfg, x: SparseShardInputs, g: int, m: int, out, sel):
+    """One sparse step of batch group g for this rank (m selected pages)."""
+    scale = cfg.head_dim ** -0.5
+    kw = dict(local_window=cfg.local_window, block_size=cfg.page_size, page_table=x.table[g], context_lens=x.ctx)
+    if x.shard.full_heads:
+        def step():
+            spa.sparse_decode_step(x.q_rows[g], x.k_pool, x.v_pool, x.summ[g], super_summaries=x.sup[g],
+                                   superblock=cfg.superblock, top_super=cfg.top_super, top_blocks=m,
+                                   router_scale=scale, out=out, selected=sel, **kw)
+    else:
+        # a kv-head group of one sequence: route over all of the sequence's heads, then
+        # decode this rank's kv heads
+        def step():
+            s = spa.select_blocks_tree(x.q_rows[g], x.sup[g], x.summ[g], superblock=cfg.superblock,
+                                       top_super=cfg.top_super, top_blocks=m, scale=scale)
+            sel.copy_(s)
+            out.copy_(spa.paged_gather_decode_attention(x.q_local[g], x.k_pool, x.v_pool, sel, **kw))
+    return step
 
 
 # ------------------------------------------------------------------ our arm
 def run_ours(args, world, rank, local):
     import attention_b200 as spa
-    from attention_b200 import workloads
 
+    wk = load_workloads()
     dev = torch.device("cuda", local)
     peaks, peaks_src = load_peaks()
-    cfg = workloads.SparseDecodeConfig(top_m=args.top_m)
+    hbm_peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    cfg = wk.SparseDecodeConfig(top_m=args.top_m)
     groups = args.groups
-    wl = workloads.sparse_decode_workload(cfg, groups=groups, seed=1000 + rank, device=dev)
-    k_pool, v_pool, ctx = wl["k_pool"], wl["v_pool"], wl["context_lens"]
-    sup, summ = [], []
-    for g in range(groups):
-        s, u = spa.page_summaries(k_pool, block_size=cfg.page_size, n_pages=cfg.routable_pages,
-                                  page_table=wl["page_table"][g], superblock=cfg.superblock)
-        summ.append(s)
-        sup.append(u)
-    scale = cfg.head_dim ** -0.5
-    out_buf = [torch.empty_like(wl["query"][g]) for g in range(groups)]
-    sel_buf = [torch.empty(cfg.batch, cfg.top_m, dtype=torch.int64, device=dev) for _ in range(groups)]
+    x = SparseShardInputs(spa, wk, cfg, groups, world, rank, dev)
+    out_buf = [torch.empty_like(x.q_local[g]) for g in range(groups)]
+    sel_buf = {m: [torch.empty(x.n_rows, m, dtype=torch.int64, device=dev) for _ in range(groups)]
+               for m in (2, 4, 8)}
 
-    def step(g):
-        spa.sparse_decode_step(wl["query"][g], k_pool, v_pool, summ[g], super_summaries=sup[g],
-                               superblock=cfg.superblock, top_super=cfg.top_super, top_blocks=cfg.top_m,
-                               local_window=cfg.local_window, block_size=cfg.page_size, router_scale=scale,
-                               page_table=wl["page_table"][g], context_lens=ctx, out=out_buf[g],
-                               selected=sel_buf[g])
+    def all_groups(m):
+        fns = [make_step(spa, cfg, x, g, m, out_buf[g], sel_buf[m][g]) for g in range(groups)]
+        return lambda: [f() for f in fns]
 
-    def attention_only(g, sel):
-        spa.paged_gather_decode_attention(wl["query"][g], k_pool, v_pool, sel, local_window=cfg.local_window,
-                                          block_size=cfg.page_size, page_table=wl["page_table"][g],
-                                          context_lens=ctx)
+    def one_group(m, g):
+        return make_step(spa, cfg, x, g, m, out_buf[g], sel_buf[m][g])
 
     warm = max(args.warmup, 3)
-    for i in range(max(warm, groups)):
-        step(i % groups)
+    m0 = cfg.top_m
+    run_all = all_groups(m0)
+    for _ in range(warm):
+        run_all()
     torch.cuda.synchronize()
-    fixed_sel = [s.clone() for s in sel_buf]
-    # capture: one graph per group (one step each) and one graph of all groups
-    stream = torch.cuda.Stream(device=dev)
-    stream.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(stream):
-        for g in range(groups):
-            step(g)
-    torch.cuda.current_stream(dev).wait_stream(stream)
-    torch.cuda.synchronize()
-    g_all = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_all):
-        for g in range(groups):
-            step(g)
-    g_one = []
-    for g in range(groups):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr):
-            step(g)
-        g_one.append(gr)
-    g_att = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_att):
-        for g in range(groups):
-            attention_only(g, fixed_sel[g])
+    g_all = capture(run_all)
+    g_one = [capture(one_group(m0, g)) for g in range(groups)]
     for _ in range(2):
         g_all.replay()
-        g_att.replay()
     torch.cuda.synchronize()
 
     steps = args.steps
     full, rem = divmod(steps, groups)
-    bytes_step = workloads.sparse_decode_bytes(cfg)
+    bytes_step = wk.sparse_decode_bytes(cfg)
     barrier(world)
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -330,122 +342,79 @@ def run_ours(args, world, rank, local):
         ev1.record()
         torch.cuda.synchronize()
     barrier(world)
-    ms = ev0.elapsed_time(ev1)
-    ms_max = max_over_ranks(ms, world)
+    ms_max = max_over_ranks(ev0.elapsed_time(ev1), world)
     us_step = ms_max * 1e3 / steps
-    value = bytes_step * steps * world / (ms_max * 1e-3) / 1e9
+    value = bytes_step * steps / (ms_max * 1e-3) / 1e9
+    del g_one
 
-    # dominant kernel: the fused gather decode (split kernel + split merge), timed alone
-    att_reps = max(1, min(200, steps // groups + 1))
-    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    with torch.cuda.nvtx.range("decode_roofline"):
-        ea.record()
-        for _ in range(att_reps):
-            g_att.replay()
-        eb.record()
-        torch.cuda.synchronize()
-    att_us = ea.elapsed_time(eb) * 1e3 / (att_reps * groups)
+    # dominant kernel: the fused gather decode (split kernel + split merge), timed alone, and
+    # the step at m = 2, 4, 8
+    reps = max(3, min(200, steps // groups + 1))
     es = 2
-    att_bytes = (2 * cfg.batch * cfg.kv_heads * (cfg.local_window + cfg.top_m * cfg.page_size) * cfg.head_dim * es
-                 + 2 * cfg.batch * cfg.q_heads * cfg.head_dim * es)
-    att_gbs = att_bytes / (att_us * 1e-6) / 1e9
-    hbm_peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    local_pairs = x.n_rows * (x.shard.kv.stop - x.shard.kv.start)
+    local_q_heads = x.q_local[0].size(1)
+
+    def att_bytes(m):
+        return (2 * local_pairs * (cfg.local_window + m * cfg.page_size) * cfg.head_dim * es
+                + 2 * x.n_rows * local_q_heads * cfg.head_dim * es)
+
+    per_m = {}
+    att_us = {}
+    for m in (2, 4, 8):
+        if m == m0:
+            step_us = us_step
+        else:
+            gm = capture(all_groups(m))
+            step_us = time_graph(gm, reps, world) * 1e3 / groups
+            del gm
+        fixed = [s.clone() for s in sel_buf[m]]  # this m's selections, for the decode alone
+        ga = capture(lambda: [spa.paged_gather_decode_attention(
+            x.q_local[g], x.k_pool, x.v_pool, fixed[g], local_window=cfg.local_window, block_size=cfg.page_size,
+            page_table=x.table[g], context_lens=x.ctx) for g in range(groups)])
+        with torch.cuda.nvtx.range(f"decode_roofline_m{m}"):
+            a_us = time_graph(ga, reps, world) * 1e3 / groups
+        del ga
+        att_us[m] = a_us
+        mcfg = wk.SparseDecodeConfig(top_m=m)
+        sb = wk.sparse_decode_bytes(mcfg)
+        per_m[str(m)] = {"us_per_step": round(step_us, 3), "bytes_per_step": sb,
+                         "value": round(sb / (step_us * 1e-6) / 1e9, 1), "unit": "GB/s",
+                         "frac": round(sb / (step_us * 1e-6) / 1e9 / hbm_peak, 4),
+                         "decode_kernel_us": round(a_us, 3),
+                         "decode_kernel_gbs": round(att_bytes(m) / (a_us * 1e-6) / 1e9, 1),
+                         "decode_kernel_frac": round(att_bytes(m) / (a_us * 1e-6) / 1e9 / hbm_peak, 4)}
+    att_gbs = att_bytes(m0) / (att_us[m0] * 1e-6) / 1e9
     traffic = read_profile_traffic("sparse_decode_128k_attention_ncu.md")
 
     gated = None
-    if not args.skip_gated:
-        gated = run_gated(cfg, wl, summ, sup, sel_buf, out_buf, scale, groups, dev, world, att_reps)
+    if world == 1 and not args.skip_gated:
+        gated = run_gated(spa, cfg, x, groups, dev, reps)
 
-    # end to end through the public API: pinned host query in, output + pages out, every step
     e2e = None
     if not args.skip_e2e:
-        host_q = [wl["query"][g].cpu().pin_memory() for g in range(groups)]
-        host_out = [torch.empty_like(host_q[g]).pin_memory() for g in range(groups)]
-        host_sel = [torch.empty(cfg.batch, cfg.top_m, dtype=torch.int64).pin_memory() for g in range(groups)]
-        dq = [torch.empty_like(wl["query"][g]) for g in range(groups)]
-        e2e_steps = max(1, min(steps, args.e2e_steps))
+        e2e = run_e2e(spa, cfg, x, groups, world, bytes_step, steps, args)
 
-        def e2e_step(g):
-            dq[g].copy_(host_q[g], non_blocking=True)
-            out, sel = spa.sparse_decode_step(dq[g], k_pool, v_pool, summ[g], super_summaries=sup[g],
-                                              superblock=cfg.superblock, top_super=cfg.top_super,
-                                              top_blocks=cfg.top_m, local_window=cfg.local_window,
-                                              block_size=cfg.page_size, router_scale=scale,
-                                              page_table=wl["page_table"][g], context_lens=ctx)
-            host_out[g].copy_(out, non_blocking=True)
-            host_sel[g].copy_(sel, non_blocking=True)
-
-        def timed(fn):
-            for i in range(3):
-                fn(i % groups)
-            torch.cuda.synchronize()
-            barrier(world)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for i in range(e2e_steps):
-                fn(i % groups)
-            e1.record()
-            torch.cuda.synchronize()
-            barrier(world)
-            return max_over_ranks(e0.elapsed_time(e1), world)
-
-        # the per-call API: three copies and one library call per step from Python
-        call_ms = timed(e2e_step)
-        # the prepared session: the same copies and step captured once, one replay per step
-        sessions = [spa.SparseDecodeSession(k_pool, v_pool, summ[g], q_heads=cfg.q_heads, super_summaries=sup[g],
-                                            superblock=cfg.superblock, top_super=cfg.top_super,
-                                            top_blocks=cfg.top_m, local_window=cfg.local_window,
-                                            block_size=cfg.page_size, router_scale=scale,
-                                            page_table=wl["page_table"][g], context_lens=ctx)
-                    for g in range(groups)]
-        for g in range(groups):  # each group's query staged once in its session's pinned buffers
-            for hq in sessions[g].host_query:
-                hq.copy_(host_q[g])
-        e_ms = timed(lambda g: sessions[g].step())
-        qbytes = host_q[0].numel() * host_q[0].element_size()
-        e2e = {"value": round(bytes_step * e2e_steps * world / (e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-               "us_per_step": round(e_ms * 1e3 / e2e_steps, 3), "steps": e2e_steps,
-               "h2d_bytes_per_step": qbytes,
-               "d2h_bytes_per_step": qbytes + cfg.batch * cfg.top_m * 8,
-               "path": "attention_b200.SparseDecodeSession.step: one call into the native session (C ABI "
-                       "spa_session_step): the fused step, whose kernels read the query from pinned host memory "
-                       "over PCIe, and a copy kernel (spa_copy) writing output + page ids into pinned host "
-                       "memory; one synchronisation at the end",
-               "per_call_api": {"us_per_step": round(call_ms * 1e3 / e2e_steps, 3),
-                                "value": round(bytes_step * e2e_steps * world / (call_ms * 1e-3) / 1e9, 2),
-                                "path": "attention_b200.sparse_decode_step from Python with the same copies"}}
-        del sessions
-
-    # CPU baseline: the reference's path on the host cores, rank 0 at N=1
     cpu = None
     if world == 1 and not args.skip_cpu:
-        q_c, k_c, v_c = cpu_inputs_from_pool(wl, 0, cfg)
-        sup_c, summ_c = cpu_summaries(k_c, cfg)
-        t, n = time_cpu_steps(q_c, k_c, v_c, sup_c, summ_c, cfg, steps=1000, budget_s=args.cpu_budget)
-        cpu = {"value": round(bytes_step / t / 1e9, 3), "unit": "GB/s", "us_per_step": round(t * 1e6, 1),
-               "cores": torch.get_num_threads(), "kind": "port",
-               "sample": f"{n} full steps of the same workload (batch group 0): router + candidate assembly + "
-                         "attention in torch CPU ops, wall clock mean"}
-        del k_c, v_c
+        cpu = run_cpu_baseline(wk, cfg, args.cpu_budget, seed=1000, device=dev)
 
     prefill = None
     if not args.skip_prefill:
         prefill = run_prefill(args, world, rank, dev, peaks)
     integrated = None
-    if not args.skip_integrated:
-        integrated = run_integrated(args, dev)
-
+    if world == 1 and not args.skip_integrated:
+        integrated = run_integrated(args, dev, hbm_peak)
     dense = None
     if not args.skip_dense:
         dense = run_dense(args, world, rank, dev, peaks)
 
     # kernels per step: the router, then the decode (plus a merge kernel when its splits
     # do not merge on chip)
-    nsplit, on_chip = spa._lib.decode_plan(cfg.batch, cfg.q_heads, cfg.kv_heads,
-                                           cfg.local_window + cfg.top_m * cfg.page_size)
-    decode_kernels = "decode_mma_kernel" if (nsplit == 1 or on_chip) else "decode_mma_kernel + decode_combine_kernel"
-    launches_per_step = 2 + (0 if (nsplit == 1 or on_chip) else 1)
+    nsplit, on_chip = spa._lib.decode_plan(x.n_rows, local_q_heads, x.shard.kv.stop - x.shard.kv.start,
+                                           cfg.local_window + m0 * cfg.page_size)
+    merged = nsplit == 1 or on_chip
+    decode_kernels = "decode_mma_kernel" if merged else "decode_mma_kernel + decode_combine_kernel"
+    launches_per_step = 2 + (0 if merged else 1)
     result = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -456,26 +425,21 @@ def run_ours(args, world, rank, local):
         "ms_per_step": round(us_step / 1e3, 6),
         "us_per_step": round(us_step, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,0.5) K/V/q with planted needle pages)",
-        "config": {"workload": f"tree-routed sparse decode 128k: B{cfg.batch} Hq{cfg.q_heads}/Hkv{cfg.kv_heads} "
-                               f"D{cfg.head_dim} bf16, P{cfg.page_size} x {cfg.pages_per_seq} pages, W{cfg.local_window}, "
-                               f"superblock {cfg.superblock} top-{cfg.top_super}, top-m {cfg.top_m}",
-                   "batch": cfg.batch, "context": cfg.context, "top_m": cfg.top_m, "groups": groups,
-                   "bytes_per_step": bytes_step,
-                   "l2": f"inputs larger than L2: {groups} rotating batches, {groups * bytes_step / 1e6:.0f} MB "
-                         "re-read footprint vs 126 MB L2",
-                   "parallelism": f"replicas x{world} (no collective)", "graph": "CUDA graph replay"},
+        "config": sparse_config(cfg, groups, world),
         "roofline": {"bound": "hbm", "kernel": decode_kernels,
                      "split_plan": f"{nsplit} splits per (sequence, kv head)"
                                    + (", merged on chip in a cluster" if on_chip and nsplit > 1 else ""),
                      "achieved": round(att_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(att_gbs / hbm_peak, 4), "traffic": traffic,
+                     "frac": round(att_gbs / hbm_peak, 4), "traffic": traffic if world == 1 else None,
                      "peak_source": f"{peaks_src} (MEASURED_PEAKS.json hbm_gbs)" if peaks_src == "measured"
                      else "fallback 6650 GB/s",
-                     "algorithmic_bytes_per_launch": att_bytes, "us_per_launch": round(att_us, 3)},
+                     "algorithmic_bytes_per_launch": att_bytes(m0), "us_per_launch": round(att_us[m0], 3),
+                     "per_rank": world > 1},
+        "per_m": per_m,
         "e2e": e2e,
         "cpu_baseline": cpu,
         "prefill": prefill,
@@ -489,41 +453,188 @@ def run_ours(args, world, rank, local):
         print(json.dumps(result))
 
 
-def run_prefill(args, world, rank, dev, peaks):
-    import attention_b200 as spa
-    from attention_b200 import sharding, workloads
+def run_e2e(spa, cfg, x, groups, world, bytes_step, steps, args):
+    """End to end through the public API: each step's query from pinned host memory in,
+    output + page ids to pinned host memory out, inside the timed region."""
+    e2e_steps = max(1, min(steps, args.e2e_steps))
+    host_q = [x.q_rows[g].cpu().pin_memory() for g in range(groups)]
+    scale = cfg.head_dim ** -0.5
 
-    seq, window, heads, dim = args.prefill_seq, 2048, 32, 128
-    flops = workloads.prefill_flops(seq, window, heads, dim)
-    chunk = seq // world
-    wl = workloads.local_prefill_workload(seq, heads=heads, head_dim=dim, seed=7, device=dev)
-    sl = slice(rank * chunk, (rank + 1) * chunk)
-    q, k, v = (wl[n][:, :, sl].contiguous() for n in ("q", "k", "v"))
-    del wl
-    out = torch.empty_like(q)
-    runner = sharding.PrefillShard(rank, world, window) if world > 1 else None
-
-    def run():
-        if runner is None:
-            spa.local_causal_prefill(q, k, v, window, out=out)
-        else:
-            runner.forward(q, k, v, out=out)
-
-    for _ in range(3):
-        run()
-    torch.cuda.synchronize()
-    reps = args.prefill_reps
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev.index if dev.index is not None else 0, period_s=0.005) as clocks, \
-            torch.cuda.nvtx.range("prefill"):
+    def timed(fn, sync_each=False):
+        for i in range(3):
+            fn(i % groups)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(reps):
-            run()
+        for i in range(e2e_steps):
+            fn(i % groups)
+            if sync_each:
+                torch.cuda.current_stream().synchronize()
         e1.record()
         torch.cuda.synchronize()
-    barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
+        barrier(world)
+        return max_over_ranks(e0.elapsed_time(e1), world)
+
+    qbytes = host_q[0].numel() * host_q[0].element_size()
+    out_bytes = x.q_local[0].numel() * x.q_local[0].element_size()
+    res = {"unit": "GB/s", "steps": e2e_steps, "h2d_bytes_per_step": qbytes,
+           "d2h_bytes_per_step": out_bytes + x.n_rows * cfg.top_m * 8}
+    if x.shard.full_heads:
+        sessions = [spa.SparseDecodeSession(x.k_pool, x.v_pool, x.summ[g], q_heads=cfg.q_heads,
+                                            super_summaries=x.sup[g], superblock=cfg.superblock,
+                                            top_super=cfg.top_super, top_blocks=cfg.top_m,
+                                            local_window=cfg.local_window, block_size=cfg.page_size,
+                                            router_scale=scale, page_table=x.table[g], context_lens=x.ctx)
+                    for g in range(groups)]
+        for g in range(groups):  # each group's query staged once in its session's pinned buffers
+            for hq in sessions[g].host_query:
+                hq.copy_(host_q[g])
+        e_ms = timed(lambda g: sessions[g].step())
+        s_ms = timed(lambda g: sessions[g].step(), sync_each=True)
+        res.update(value=round(bytes_step * e2e_steps / (e_ms * 1e-3) / 1e9, 2),
+                   us_per_step=round(e_ms * 1e3 / e2e_steps, 3),
+                   path="attention_b200.SparseDecodeSession.step: one call into the native session (C ABI "
+                        "spa_session_step) that launches the CUDA graph of its host-buffer slot: a copy kernel "
+                        "brings the step's query from pinned mapped host memory into device memory, the router "
+                        "and the gather decode run, and a copy kernel (spa_copy) writes output + page ids into "
+                        "pinned host memory; the host may enqueue one step ahead (two buffer slots)",
+                   per_step_sync={"us_per_step": round(s_ms * 1e3 / e2e_steps, 3),
+                                  "value": round(bytes_step * e2e_steps / (s_ms * 1e-3) / 1e9, 2),
+                                  "path": "the same session step, followed every step by a host "
+                                          "synchronisation before the next step is enqueued (results read "
+                                          "on the host each step)"})
+        for s in sessions:
+            s.close()
+        del sessions
+    else:
+        dq = [torch.empty_like(x.q_rows[g]) for g in range(groups)]
+        host_out = [torch.empty(x.q_local[g].shape, dtype=x.q_local[g].dtype).pin_memory() for g in range(groups)]
+        host_sel = [torch.empty(x.n_rows, cfg.top_m, dtype=torch.int64).pin_memory() for g in range(groups)]
+
+        def call(g):
+            dq[g].copy_(host_q[g], non_blocking=True)
+            sel = spa.select_blocks_tree(dq[g], x.sup[g], x.summ[g], superblock=cfg.superblock,
+                                         top_super=cfg.top_super, top_blocks=cfg.top_m, scale=scale)
+            ql = dq[g][:, x.shard.q_heads]
+            out = spa.paged_gather_decode_attention(ql.contiguous(), x.k_pool, x.v_pool, sel,
+                                                    local_window=cfg.local_window, block_size=cfg.page_size,
+                                                    page_table=x.table[g], context_lens=x.ctx)
+            host_out[g].copy_(out, non_blocking=True)
+            host_sel[g].copy_(sel, non_blocking=True)
+
+        e_ms = timed(call)
+        res.update(value=round(bytes_step * e2e_steps / (e_ms * 1e-3) / 1e9, 2),
+                   us_per_step=round(e_ms * 1e3 / e2e_steps, 3),
+                   path="per call from Python: host->device copy of the sequences' query rows, "
+                        "select_blocks_tree over all heads, paged_gather_decode_attention over this rank's "
+                        "kv heads, device->host copies of output and page ids")
+    return res
+
+
+def run_cpu_baseline(wk, cfg, budget_s, *, seed, device):
+    """The reference's path on the host cores (bounded sample of the same workload)."""
+    import oracle
+
+    q_c, k_c, v_c, sup_c, summ_c = reference_inputs(wk, cfg, seed, device)
+    t, n = time_reference_steps(oracle, q_c, k_c, v_c, sup_c, summ_c, cfg, steps=1000, budget_s=budget_s)
+    bytes_step = wk.sparse_decode_bytes(cfg)
+    return {"value": round(bytes_step / t / 1e9, 3), "unit": "GB/s", "us_per_step": round(t * 1e6, 1),
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} full steps of batch group 0 of the same workload: oracle.reference_decode_step "
+                      "(select_blocks at two levels, make_candidates, reference_attention; fp32 torch CPU "
+                      "ops), wall clock mean"}
+
+
+def reference_inputs(wk, cfg, seed, device):
+    """Contiguous CPU copies [B, Hkv, L, D] of batch group 0 and its oracle summaries."""
+    import oracle
+
+    wl = wk.sparse_decode_workload(cfg, groups=1, seed=seed, device=device)
+    table = wl["page_table"][0].long()
+    b, npg = table.shape
+    k = wl["k_pool"][table.reshape(-1)].view(b, npg, cfg.kv_heads, cfg.page_size, cfg.head_dim)
+    v = wl["v_pool"][table.reshape(-1)].view(b, npg, cfg.kv_heads, cfg.page_size, cfg.head_dim)
+    k = k.permute(0, 2, 1, 3, 4).reshape(b, cfg.kv_heads, npg * cfg.page_size, cfg.head_dim).cpu()
+    v = v.permute(0, 2, 1, 3, 4).reshape(b, cfg.kv_heads, npg * cfg.page_size, cfg.head_dim).cpu()
+    q = wl["query"][0].cpu()
+    del wl
+    if torch.cuda.is_available():
+        torch.cuda.empty_cache()
+    summ, sums = oracle.summaries_fp64(k, cfg.page_size, cfg.routable_pages)
+    sup = oracle.super_summaries(sums, cfg.superblock, cfg.page_size)
+    return q, k, v, sup, summ
+
+
+def time_reference_steps(oracle, q, k_c, v_c, sup, summ, cfg, *, steps: int, budget_s: float):
+    def one():
+        oracle.reference_decode_step(q, k_c, v_c, sup, summ, superblock=cfg.superblock, top_super=cfg.top_super,
+                                     top_blocks=cfg.top_m, local_window=cfg.local_window,
+                                     block_size=cfg.page_size)
+
+    one()  # warm-up
+    times = []
+    t_end = time.perf_counter() + budget_s
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end:
+            break
+    return statistics.mean(times), len(times)
+
+
+def run_prefill(args, world, rank, dev, peaks):
+    import attention_b200 as spa
+    from attention_b200 import sharding
+
+    wk = load_workloads()
+    window, heads, dim = 2048, 32, 128
+    peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    peak_s = float(peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"]))
+    seqs = [args.prefill_seq] if (world > 1 or args.prefill_seq != 131072) else list(PREFILL_SEQS)
+    runs = {}
+    head = None
+    for seq in seqs:
+        flops = wk.prefill_flops(seq, window, heads, dim)
+        chunk = seq // world
+        wl = wk.local_prefill_workload(seq, heads=heads, head_dim=dim, seed=7, device=dev)
+        sl = slice(rank * chunk, (rank + 1) * chunk)
+        q, k, v = (wl[n][:, :, sl].contiguous() for n in ("q", "k", "v"))
+        del wl
+        out = torch.empty_like(q)
+        runner = sharding.PrefillShard(rank, world, window) if world > 1 else None
+
+        def run():
+            if runner is None:
+                spa.local_causal_prefill(q, k, v, window, out=out)
+            else:
+                runner.forward(q, k, v, out=out)
+
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        reps = max(3, min(args.prefill_reps, int(20 * 131072 / seq)))
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index if dev.index is not None else 0, period_s=0.005) as clocks, \
+                torch.cuda.nvtx.range(f"prefill_{seq}"):
+            e0.record()
+            for _ in range(reps):
+                run()
+            e1.record()
+            torch.cuda.synchronize()
+        barrier(world)
+        ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
+        tf = flops / (ms * 1e-3) / 1e12
+        runs[str(seq)] = {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / (peak * world), 4),
+                          "frac_sustained": round(tf / (peak_s * world), 4), "flops": flops, "reps": reps,
+                          "clocks": clocks.summary()}
+        if seq == args.prefill_seq:
+            head = (seq, ms, tf, flops, clocks.summary(), reps, q, k)
+        del q, k, v, out
+        torch.cuda.empty_cache()
+    seq, ms, tf, flops, clk, reps, q, k = head
     # periodic causal router over the same chunk (reference: prefill + router overhead benchmark)
     router_ms = None
     if world == 1:
@@ -537,26 +648,26 @@ def run_prefill(args, world, rank, dev, peaks):
         r1.record()
         torch.cuda.synchronize()
         router_ms = r0.elapsed_time(r1) / 5
-    peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
-    tf = flops / (ms * 1e-3) / 1e12
     return {"seq_len": seq, "window": window, "heads": heads, "head_dim": dim, "ms": round(ms, 4),
             "tflops": round(tf, 1), "peak_tflops": peak * world, "frac": round(tf / (peak * world), 4),
-            "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst) x GPUs",
+            "frac_sustained": round(tf / (peak_s * world), 4),
+            "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst) and bf16_tflops_sustained, x GPUs",
             "traffic_16k": read_profile_traffic("local_prefill_tc_16k_ncu.md"),
             "traffic_source": "profiles/local_prefill_tc_16k_ncu.md (dram read+write of one S=16384 launch)",
-            "flops": flops, "clocks": clocks.summary(), "sharding": f"{world} contiguous chunks, 2048-token K/V halo over NCCL" if world > 1
-            else "single GPU", "reps": reps,
+            "flops": flops, "clocks": clk, "reps": reps,
+            "sharding": f"{world} contiguous chunks, 2048-token K/V halo over NCCL" if world > 1 else "single GPU",
+            "by_seq_len": runs,
             "periodic_router_ms": round(router_ms, 4) if router_ms is not None else None,
             "periodic_router": "block 256, stride 256, top-4, summaries included" if router_ms is not None else None}
 
 
-def run_gated(cfg, wl, summ, sup, sel_buf, out_buf, scale, groups, dev, world, reps):
+def run_gated(spa, cfg, x, groups, dev, reps):
     """The decode step behind an embedding-drift refresh gate evaluated on the device
     (state = the step's query, B x Hq*D): with the gate closed the router copies the
     promoted pages and reads no summary; with it open every step routes."""
-    import attention_b200 as spa
-
-    states = [wl["query"][g].float().reshape(cfg.batch, -1).contiguous() for g in range(groups)]
+    states = [x.q_rows[g].float().reshape(cfg.batch, -1).contiguous() for g in range(groups)]
+    out = [torch.empty_like(x.q_rows[g]) for g in range(groups)]
+    sel = [torch.empty(cfg.batch, cfg.top_m, dtype=torch.int64, device=dev) for _ in range(groups)]
     result = {}
     # cosine distance lies in [0, 2]: threshold 3 never refreshes after the first step,
     # threshold -1 refreshes every step
@@ -565,35 +676,16 @@ def run_gated(cfg, wl, summ, sup, sel_buf, out_buf, scale, groups, dev, world, r
 
         def gstep(g):
             gate.decide(state=states[g])
-            spa.sparse_decode_step(wl["query"][g], wl["k_pool"], wl["v_pool"], summ[g], super_summaries=sup[g],
+            spa.sparse_decode_step(x.q_rows[g], x.k_pool, x.v_pool, x.summ[g], super_summaries=x.sup[g],
                                    superblock=cfg.superblock, top_super=cfg.top_super, top_blocks=cfg.top_m,
-                                   local_window=cfg.local_window, block_size=cfg.page_size, router_scale=scale,
-                                   page_table=wl["page_table"][g], context_lens=wl["context_lens"],
-                                   out=out_buf[g], selected=sel_buf[g], gate=gate)
+                                   local_window=cfg.local_window, block_size=cfg.page_size,
+                                   router_scale=cfg.head_dim ** -0.5, page_table=x.table[g], context_lens=x.ctx,
+                                   out=out[g], selected=sel[g], gate=gate)
 
-        side = torch.cuda.Stream(device=dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            for g in range(groups):
-                gstep(g)
-        torch.cuda.current_stream(dev).wait_stream(side)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=side):
-            for g in range(groups):
-                gstep(g)
+        graph = capture(lambda: [gstep(g) for g in range(groups)])
         graph.replay()
-        torch.cuda.synchronize()
-        barrier(world)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.nvtx.range(f"gated_{name}"):
-            e0.record()
-            for _ in range(reps):
-                graph.replay()
-            e1.record()
-            torch.cuda.synchronize()
-        barrier(world)
-        result[f"{name}_us_per_step"] = round(max_over_ranks(e0.elapsed_time(e1), world) * 1e3 / (reps * groups), 3)
+            result[f"{name}_us_per_step"] = round(time_graph(graph, reps, 1) * 1e3 / groups, 3)
         del graph
     result["gate"] = "embedding drift (1 - cosine) of the step's query, one device decision per step"
     result["launches_per_step"] = 3
@@ -604,69 +696,83 @@ def run_dense(args, world, rank, dev, peaks):
     """Dense paged decode at 32k: B8, Hq32/Hkv8, D128, bf16, 256 pages of 128 tokens per
     sequence in a 4096-page pool behind a random page table.  A step appends one token per
     (sequence, kv head) in place (the last position, so the context stays 32k) and attends
-    over the whole context; the 2.1 GB pool is far larger than L2."""
+    over the whole context; the 2.1 GB pool is far larger than L2.  With N > 1 GPUs each
+    rank holds the pages of its (sequence, kv head) pairs and decodes them (strong
+    scaling: the batch is fixed)."""
     import attention_b200 as spa
-    from attention_b200 import workloads
+    from attention_b200.sharding import DecodeShard
 
-    cfg = workloads.DenseDecodeConfig()
-    wl = workloads.dense_decode_workload(cfg, seed=11 + rank, device=dev)
-    q, kp, vp, table, lens = (wl[n] for n in ("query", "k_pool", "v_pool", "page_table", "context_lens"))
-    g = torch.Generator(device=dev).manual_seed(12 + rank)
+    wk = load_workloads()
+    cfg = wk.DenseDecodeConfig()
+    shard = DecodeShard(cfg.batch, cfg.q_heads, cfg.kv_heads, world, rank)
+    wl = wk.dense_decode_workload(cfg, seed=11, device=dev)
+    g = torch.Generator(device=dev).manual_seed(12)
     k_new = (torch.randn(cfg.batch, cfg.kv_heads, cfg.head_dim, generator=g, device=dev) * 0.5).to(cfg.dtype)
     v_new = (torch.randn(cfg.batch, cfg.kv_heads, cfg.head_dim, generator=g, device=dev) * 0.5).to(cfg.dtype)
+    q, kp, vp, table, lens = (wl[n] for n in ("query", "k_pool", "v_pool", "page_table", "context_lens"))
+    if world > 1:
+        tab = table[shard.rows]
+        phys = tab.reshape(-1).long()
+        kp = kp[phys][:, shard.kv].contiguous()
+        vp = vp[phys][:, shard.kv].contiguous()
+        table = torch.arange(phys.numel(), dtype=torch.int32, device=dev).view(tab.shape).contiguous()
+        q, lens = shard.local(q), lens[shard.rows].contiguous()
+        k_new, v_new = shard.local(k_new, "kv"), shard.local(v_new, "kv")
+    del wl
+    torch.cuda.empty_cache()
     pos = (lens - 1).contiguous()
 
     def step():
         spa.kv_append(kp, vp, table, k_new, v_new, pos)
         return spa.paged_decode_attention(q, kp, vp, page_table=table, context_lens=lens)
 
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(side):  # warm-up on the capture stream: its workspace exists before capture
-        for _ in range(3):
-            step()
-    torch.cuda.current_stream(dev).wait_stream(side)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=side):
+    for _ in range(3):
         step()
+    graph = capture(step)
     for _ in range(3):
         graph.replay()
-    torch.cuda.synchronize()
-    reps = args.dense_steps
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.nvtx.range("dense_decode"):
-        e0.record()
-        for _ in range(reps):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-    barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
+        ms = time_graph(graph, args.dense_steps, world)
     kv_bytes = 2 * cfg.batch * cfg.kv_heads * cfg.context * cfg.head_dim * 2
     io_bytes = 2 * cfg.batch * cfg.q_heads * cfg.head_dim * 2 + cfg.batch * cfg.pages_per_seq * 4
     append_bytes = 2 * 2 * cfg.batch * cfg.kv_heads * cfg.head_dim * 2
     step_bytes = kv_bytes + io_bytes + append_bytes
     gbs = step_bytes / (ms * 1e-3) / 1e9
     peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
-    nsplit, on_chip = spa._lib.decode_plan(cfg.batch, cfg.q_heads, cfg.kv_heads, cfg.context)
-    del wl, kp, vp, graph
+    n_rows, n_kv = shard.rows.stop - shard.rows.start, shard.kv.stop - shard.kv.start
+    nsplit, on_chip = spa._lib.decode_plan(n_rows, q.size(1), n_kv, cfg.context)
+    del kp, vp, graph
     torch.cuda.empty_cache()
     return {"workload": f"dense paged decode 32k: B{cfg.batch} Hq{cfg.q_heads}/Hkv{cfg.kv_heads} D{cfg.head_dim} "
                         f"bf16, {cfg.pages_per_seq} pages x {cfg.page_size} in a {cfg.pool_pages}-page pool, "
                         "one appended token per step",
             "us_per_step": round(ms * 1e3, 2), "bytes_per_step": step_bytes,
-            "value": round(gbs * world, 1), "unit": "GB/s (all GPUs)", "frac": round(gbs / peak, 4),
-            "peak": peak, "peak_source": "MEASURED_PEAKS.json hbm_gbs",
-            "traffic": read_profile_traffic("dense_decode_32k_ncu.md"),
+            "value": round(gbs, 1), "unit": "GB/s (all GPUs)", "frac": round(gbs / (peak * world), 4),
+            "peak": peak * world, "peak_source": "MEASURED_PEAKS.json hbm_gbs x GPUs",
+            "traffic": read_profile_traffic("dense_decode_32k_ncu.md") if world == 1 else None,
             "traffic_source": "profiles/dense_decode_32k_ncu.md (dram read+write per decode launch)",
             "kernels": "kv_append_kernel + decode_mma_kernel" + ("" if (nsplit == 1 or on_chip) else " + decode_combine_kernel"),
             "split_plan": f"{nsplit} splits per (sequence, kv head)" + (", merged on chip" if on_chip and nsplit > 1 else ""),
-            "steps": reps, "graph": "CUDA graph replay"}
+            "sharding": "single GPU" if world == 1 else f"(sequence, kv head) shards x{world}: {n_rows} sequences x "
+                                                         f"{n_kv} kv heads per rank, strong scaling",
+            "steps": args.dense_steps, "graph": "CUDA graph replay"}
 
 
-def run_integrated(args, dev):
+def decoder_step_bytes(cfg, routable_pages: int) -> int:
+    """Algorithmic HBM bytes of one decode step of the integrated model (bf16): every
+    weight matrix, bias and norm read once (embedding and position tables: one row),
+    per layer the K/V of the window + top-m pages and the fp32 summaries the router
+    scores, the appended K/V, the fp32 logits."""
+    d, f, v, hd = cfg.d_model, cfg.mlp_mult * cfg.d_model, cfg.vocab, cfg.head_dim
+    per_layer_w = (3 * d * d + 3 * d) + (d * d + d) + (f * d + f) + (d * f + d) + 2 * d
+    weights = (cfg.layers * per_layer_w + v * d + d + 2 * d) * 2
+    kv = cfg.layers * 2 * cfg.heads * (cfg.local_window + cfg.top_m * cfg.page_size) * hd * 2
+    summaries = cfg.layers * cfg.heads * routable_pages * hd * 4
+    append = cfg.layers * 2 * cfg.heads * hd * 2
+    return weights + kv + summaries + append + v * 4
+
+
+def run_integrated(args, dev, hbm_peak):
     """Integrated 4-layer decoder (d_model 512, 8 heads, vocab 4096, bf16): a 16k-token
     prompt prefilled into 128-token pages, then greedy decode steps with router top-8 +
     128-token local window per layer and the 64-slot TTL-32 promotion table."""
@@ -676,7 +782,7 @@ def run_integrated(args, dev):
     cfg = DecoderConfig(max_context=16384 + 2 * steps + 8)
     weights = init_weights(cfg, seed=0)
     prompt = torch.randint(0, cfg.vocab, (1, 16384), generator=torch.Generator().manual_seed(0)).to(dev)
-    warm = SparseDecoder(cfg, weights, 1, device=dev)  # first-call costs (cuBLAS handles, modules)
+    warm = SparseDecoder(cfg, weights, 1, device=dev)  # first-call costs (library handles, modules)
     warm.generate(warm.prefill(prompt).argmax(-1), 4)
     del warm
     dec = SparseDecoder(cfg, weights, 1, device=dev)
@@ -697,46 +803,51 @@ def run_integrated(args, dev):
     dec.generate(tok, steps)
     e1.record()
     torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    # routable pages: the historical pages before the local window, 16384 / 128 - 1 at the
+    # first step (one more page becomes routable every 128 steps)
+    nbytes = decoder_step_bytes(cfg, (16384 + steps // 2) // cfg.page_size - 1)
+    gbs = nbytes / (us * 1e-6) / 1e9
     return {"config": "4 layers, d_model 512, 8 heads x 64, vocab 4096, bf16, prompt 16384 in 128-token pages, "
                       "router top-8 + 128-token window, promotion 64 slots TTL 32",
             "prefill_ms": round(prefill_ms, 3), "decode_steps": steps,
-            "decode_us_per_step": round(e0.elapsed_time(e1) * 1e3 / steps, 2),
-            "mode": "one CUDA-graph replay per step (cuBLAS GEMMs + library kernels), greedy tokens on the "
-                    f"device; the first {steps} positions after the prompt, decoded once untimed (graph "
-                    "captures) and again timed after a rewind"}
+            "decode_us_per_step": round(us, 2), "bytes_per_step": nbytes, "gbs": round(gbs, 1),
+            "frac": round(gbs / hbm_peak, 4),
+            "mode": "one CUDA-graph replay per step: the library's few-row linear kernels (spa_norm_linear / "
+                    "spa_linear, norms and residual adds fused in front), QKV epilogue append, router + gather "
+                    f"decode, promotion update, vocabulary head and argmax on the device; the first {steps} "
+                    "positions after the prompt, decoded once untimed (graph captures) and again timed after "
+                    "a rewind"}
 
 
 # ------------------------------------------------------------------ reference arm
 def run_reference(args, world, rank, local):
+    """The reference's PyTorch CPU path on the host cores, rank 0 only, on the same
+    configuration and `config` as our arm; nothing here loads the CUDA library."""
     if rank != 0:
         return
-    from attention_b200 import workloads
+    import oracle
 
-    cfg = workloads.SparseDecodeConfig(top_m=args.top_m)
-    if torch.cuda.is_available():
-        wl = workloads.sparse_decode_workload(cfg, groups=1, seed=1000, device=torch.device("cuda", local))
-        q_c, k_c, v_c = cpu_inputs_from_pool(wl, 0, cfg)
-        del wl
-        torch.cuda.empty_cache()
-    else:
-        wl = workloads.sparse_decode_workload(cfg, groups=1, seed=1000, device="cpu")
-        q_c, k_c, v_c = cpu_inputs_from_pool(wl, 0, cfg)
-    sup_c, summ_c = cpu_summaries(k_c, cfg)
+    wk = load_workloads()
+    cfg = wk.SparseDecodeConfig(top_m=args.top_m)
+    device = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    q, k_c, v_c, sup, summ = reference_inputs(wk, cfg, 1000, device)
     for _ in range(max(args.warmup, 1)):
-        cpu_reference_step(q_c, k_c, v_c, sup_c, summ_c, cfg)
-    t, n = time_cpu_steps(q_c, k_c, v_c, sup_c, summ_c, cfg, steps=args.steps, budget_s=args.cpu_budget * 4)
-    bytes_step = workloads.sparse_decode_bytes(cfg)
+        oracle.reference_decode_step(q, k_c, v_c, sup, summ, superblock=cfg.superblock, top_super=cfg.top_super,
+                                     top_blocks=cfg.top_m, local_window=cfg.local_window, block_size=cfg.page_size)
+    t, n = time_reference_steps(oracle, q, k_c, v_c, sup, summ, cfg, steps=args.steps, budget_s=args.cpu_budget * 4)
+    bytes_step = wk.sparse_decode_bytes(cfg)
     value = bytes_step / t / 1e9
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
         "steps": n, "warmup": max(args.warmup, 1), "ms_per_step": round(t * 1e3, 4),
-        "us_per_step": round(t * 1e6, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "us_per_step": round(t * 1e6, 1), "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (seeded N(0,0.5) K/V/q with planted needle pages)",
-        "config": {"workload": f"tree-routed sparse decode 128k: B{cfg.batch} Hq{cfg.q_heads}/Hkv{cfg.kv_heads} "
-                               f"D{cfg.head_dim} bf16, P{cfg.page_size}, W{cfg.local_window}, top-m {cfg.top_m}",
-                   "batch": cfg.batch, "context": cfg.context, "top_m": cfg.top_m, "bytes_per_step": bytes_step},
+        "config": sparse_config(cfg, args.groups, world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": f"{n} full steps (router + candidate assembly + attention), torch CPU ops"},
+                         "sample": f"{n} full steps of batch group 0: oracle.reference_decode_step (select_blocks "
+                                   "at two levels, make_candidates, reference_attention; fp32 torch CPU ops)"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
 

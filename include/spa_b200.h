@@ -249,9 +249,12 @@ int spa_sparse_decode_step(const void* q, int dtype, int batch, int q_heads,
  * compiled into the library (held in device memory of every GPU that loads it
  * until the process exits).  Returns SPA_ERR_WORKSPACE when
  * spa_decode_workspace_size() of the request exceeds that size.
- * Allocates nothing.  The first call on a device looks up the scratch's device
- * address (cudaGetSymbolAddress, with that device current); make that first call
- * before any stream capture.  All calls on a device share the one array: calls
+ * Allocates nothing.  Every call looks up the scratch's device address in the
+ * CUDA context current on the calling thread (cudaGetSymbolAddress), so it works
+ * from the runtime's primary context, from a host's own driver context and after
+ * a device reset alike; the first lookup in a context loads the library's device
+ * code into it, so make the first call in each context before any stream capture.
+ * All calls on a device share the one array: calls
  * whose kernels can overlap on the GPU (different streams, no ordering) race and
  * must be serialised by the caller.  Nothing in the array needs clearing: every
  * split writes its slot before the merge reads it.
