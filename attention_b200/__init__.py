@@ -11,7 +11,7 @@ from .gate import RefreshGate
 from .paged_attention import paged_decode_attention, paged_gather_decode_attention, span_gather_decode_attention
 from .prefill import local_causal_prefill
 from .router import page_summaries, periodic_router, select_blocks, select_blocks_tree
-from .step import SparseDecodeSession, sparse_decode_step
+from .step import SparseDecodeSession, set_step_fusion, sparse_decode_step
 
 __all__ = [
     "LIB_PATH",
@@ -30,5 +30,6 @@ __all__ = [
     "select_blocks",
     "select_blocks_tree",
     "sparse_decode_step",
+    "set_step_fusion",
     "SparseDecodeSession",
 ]

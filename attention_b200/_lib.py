@@ -120,6 +120,9 @@ PROTOTYPES = {
                                     _vp, _vp, _sz, _vp]),
     "spa_sparse_decode_step_gated": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _d,
                                           _d, _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
+    "spa_sparse_decode_step_heads": (_i, [_vp, _i, _i, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i,
+                                          _i, _d, _d, _vp, _vp, _vp, _sz, _vp]),
+    "spa_set_step_fusion": (_i, [_i]),
     "spa_paged_decode_noalloc": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp]),
     "spa_kv_append": (_i, [_KV, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "spa_local_prefill": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),

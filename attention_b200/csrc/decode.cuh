@@ -17,13 +17,33 @@
 #include <utility>
 
 #include "common.cuh"
+#include "router.cuh"
 
 namespace spa {
+
+// In-kernel routing (the route instantiation of decode_mma_kernel): the router inputs of
+// the sequences the decode serves.  The query rows a.q hold q_heads heads of head_dim D
+// for every sequence; the summaries cover kv_heads kv heads (all heads of the sequence,
+// also when the decode covers only a slice of them).
+struct FusedRoute {
+  int q_heads, kv_heads;
+  const float* supers;  // [B, kv_heads, n_super, D] (two levels) or nullptr (one level)
+  int n_super, superblock, top_super;
+  const float* summaries;  // [B, kv_heads, n_pages, D]
+  int n_pages;
+  float scale;
+  int64_t* selected;       // [B, top_m]: the selection, written once per sequence
+  int64_t* selected_copy;  // [B, top_m] second copy (host memory of a session) or nullptr
+};
 
 struct DecodeArgs {
   const void* q;
   void* out;
   int B, Hq, Hkv, group, D;
+  // query head h (of Hq) of sequence b is row b * q_batch_heads + q_head_offset + h of a.q:
+  // q_batch_heads = Hq and q_head_offset = 0 unless the decode covers a kv-head slice of
+  // a wider query row
+  int q_batch_heads, q_head_offset;
   KvAddr addr;
   const int32_t* ctx_lens;
   int local_window;
@@ -45,15 +65,15 @@ struct DecodeArgs {
   // with early_local: the query is written by the kernel this one overlaps (the router's
   // device copy of a query held in host memory), so the consumers read it after the wait
   int q_after_wait;
+  FusedRoute route;  // read by the route instantiation only
 };
 
 struct ChunkPlan {
   int lo, hi, seg_a, n_seg, cpp, n_total, ctx;
 };
 
-__device__ __forceinline__ ChunkPlan make_plan(const DecodeArgs& a, int b, int chunk) {
+__device__ __forceinline__ ChunkPlan make_plan_ctx(const DecodeArgs& a, int ctx, int chunk) {
   ChunkPlan p;
-  const int ctx = a.ctx_lens[b];
   p.ctx = ctx;
   int lo = 0;
   if (a.selected || a.local_window > 0) lo = max(0, ctx - max(a.local_window, 0));
@@ -65,6 +85,9 @@ __device__ __forceinline__ ChunkPlan make_plan(const DecodeArgs& a, int b, int c
   p.cpp = !a.selected ? 0 : a.span_len > 0 ? (a.span_len + chunk - 1) / chunk + 1 : (a.addr.page_size + chunk - 1) / chunk;
   p.n_total = p.n_seg + (a.selected ? a.top_m * p.cpp : 0);
   return p;
+}
+__device__ __forceinline__ ChunkPlan make_plan(const DecodeArgs& a, int b, int chunk) {
+  return make_plan_ctx(a, a.ctx_lens[b], chunk);
 }
 
 struct ChunkInfo {
@@ -147,7 +170,8 @@ struct DecodeSmem {
   static constexpr int kTabCap = 2048;  // page-table entries prefetched into shared memory
   static constexpr int kSelCap = 32;    // selected ids prefetched into shared memory
   // + barriers, chunk info, page table, selected ids (the cluster receive buffer follows)
-  static constexpr int kBytes = kRingBytes + STAGES * 16 + STAGES * 16 + kTabCap * 4 + kSelCap * 8 + 1024;
+  // (+32: the routing and merge exchange barriers)
+  static constexpr int kBytes = kRingBytes + STAGES * 16 + STAGES * 16 + 32 + kTabCap * 4 + kSelCap * 8 + 1024;
 };
 
 template <int D>
@@ -157,17 +181,316 @@ __device__ __forceinline__ uint32_t swz_addr(uint32_t base, int row, int c16) {
   return base + (c16 >> 3) * kBoxBytes + row * 128 + (((c16 & 7) ^ (row & 7)) << 4);
 }
 
-template <typename T, int D, int STAGES>
+// ---------------------------------------------------------------------------
+// In-kernel routing.  The splits of one (sequence, kv head) pair form a cluster of ns CTAs;
+// the cluster selects its sequence's pages itself, with the arithmetic of
+// router_cluster_kernel (query heads summed per kv head, lane-strided partial dots and
+// xor butterflies, kv heads in order, / q_heads, * scale; ties to the lower page), so
+// the pages are the ones spa_router_tree_topm / spa_router_topm return, bit for bit.
+// Every cluster serving the same sequence computes the same selection from the same
+// inputs: no exchange between clusters, no grid-wide wait.  Candidate c of a level is
+// scored by CTA c % ns (one warp per candidate, up to CB candidates' rows in flight per
+// warp) and its score pushed into every CTA of the cluster; after one cluster barrier per
+// level every CTA ranks the same scores.  Scratch: the last ring stage, free until the
+// producer issues its first chunk after the selection.
+template <int NS>
+struct RouteCfg {
+  static constexpr int kCB = NS >= 8 ? 1 : 8 / NS;  // candidates per warp in flight
+};
+
+__host__ __device__ inline size_t route_align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+// The query row is staged through the consumer warps' registers: at most this many 16-byte
+// pieces per consumer thread (q_heads * head_dim * elem <= kRouteQVec * 16 * 128).
+constexpr int kRouteQVec = 4;
+constexpr int kRouteStagers = 128;  // the consumer warps
+
+// The router's first loads, issued at kernel entry together with the split plan's: this
+// warp's first batch of first-level candidate rows and this thread's pieces of the query
+// row (consumed by fused_route).
+template <int NS>
+struct RoutePrefetch {
+  CandRows<NS> rows[RouteCfg<NS>::kCB];
+  uint4 q[kRouteQVec];
+};
+
+template <typename T, int NS>
+__device__ __forceinline__ void route_prefetch(const DecodeArgs& a, int b, int rank, int ns, RoutePrefetch<NS>& pf) {
+  constexpr int CB = RouteCfg<NS>::kCB;
+  const FusedRoute& r = a.route;
+  constexpr int D = NS * 32;  // the kernel's head_dim
+  const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5;
+  // every route field is read here once: parameters sit in the constant bank, and a field
+  // first read after a cluster barrier would put a constant-cache miss on the chain
+  uint64_t x = reinterpret_cast<uint64_t>(r.supers) ^ reinterpret_cast<uint64_t>(r.summaries) ^
+               reinterpret_cast<uint64_t>(r.selected) ^ reinterpret_cast<uint64_t>(r.selected_copy);
+  x ^= static_cast<uint64_t>(r.q_heads ^ r.kv_heads ^ r.n_super ^ r.superblock ^ r.top_super ^ r.n_pages ^
+                             __float_as_int(r.scale));
+  asm volatile("" ::"l"(x));
+  const bool tree = r.supers != nullptr;
+  const int n_cand = tree ? r.n_super : r.n_pages;
+  const float* tab = tree ? r.supers + static_cast<int64_t>(b) * r.kv_heads * r.n_super * D
+                          : r.summaries + static_cast<int64_t>(b) * r.kv_heads * r.n_pages * D;
+  const int64_t stride = static_cast<int64_t>(tree ? r.n_super : r.n_pages) * D;
+  const int nl = n_cand > rank ? (n_cand - 1 - rank) / ns + 1 : 0;
+  // two levels: the consumer warps score level 1 (the producer joins at level 2)
+  const int nws = tree ? kConsumerWarps : nw;
+  if (warp < nws) {
+#pragma unroll
+    for (int u = 0; u < CB; ++u) {
+      const int i = warp + u * nws;
+      if (i < nl) load_cand_rows(pf.rows[u], tab + static_cast<int64_t>(rank + i * ns) * D, stride, 0, r.kv_heads, D);
+    }
+  }
+  const int nvec = r.q_heads * D * static_cast<int>(sizeof(T)) / 16;
+  const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + static_cast<int64_t>(b) * r.q_heads * D);
+  if (threadIdx.x < kRouteStagers) {
+#pragma unroll
+    for (int u = 0; u < kRouteQVec; ++u) {
+      const int v = threadIdx.x + u * kRouteStagers;
+      if (v < nvec) pf.q[u] = __ldg(src + v);
+    }
+  }
+}
+
+// Scratch bytes of fused_route (layout below); must fit in one ring stage.
+__host__ __device__ inline size_t route_scratch_bytes(const FusedRoute& r, int head_dim, size_t elem) {
+  const size_t n1 = r.supers ? r.n_super : 0, n2 = r.supers ? static_cast<size_t>(r.top_super) * r.superblock
+                                                            : static_cast<size_t>(r.n_pages);
+  return route_align16(static_cast<size_t>(r.q_heads) * head_dim * elem) +
+         route_align16(sizeof(float) * static_cast<size_t>(r.kv_heads) * head_dim) +
+         route_align16(sizeof(uint64_t) * n1) + route_align16(sizeof(uint64_t) * n2) +
+         route_align16(sizeof(int64_t) * (r.top_super > 0 ? r.top_super : 1));
+}
+
+// A candidate's rank key: the score mapped to an order-preserving unsigned integer in the
+// high half (-0 folded into +0, so equal scores stay equal), the id inverted in the low half
+// -- key_a > key_b exactly when a beats b (higher score, or equal score and lower id), so
+// ranking is one unsigned 64-bit compare per pair.  0 <= id <= 0x7FFFFFFF.
+__device__ __forceinline__ uint64_t rank_key(float score, int id) {
+  uint32_t u = __float_as_uint(score);
+  if (u == 0x80000000u) u = 0u;
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<uint64_t>(u) << 32) | static_cast<uint32_t>(0x7FFFFFFF - id);
+}
+__device__ __forceinline__ int key_id(uint64_t key) { return 0x7FFFFFFF - static_cast<int>(static_cast<uint32_t>(key)); }
+
+__device__ __forceinline__ void st_dsmem_u64(uint64_t* local_ptr, int rank, uint64_t v) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
+  asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(ra), "l"(v) : "memory");
+}
+
+// Asynchronous stores into a peer CTA's shared memory that complete transaction bytes on an
+// mbarrier in that CTA (st.async): the receiver waits for the byte count it expects, so no
+// cluster-wide barrier orders the exchange.
+__device__ __forceinline__ uint32_t peer_addr(const void* local_ptr, int rank) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local_ptr)), "r"(rank));
+  return ra;
+}
+__device__ __forceinline__ void st_async_b64(uint32_t raddr, uint64_t v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b64 [%0], %1, [%2];" ::"r"(raddr), "l"(v),
+               "r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
+               "r"(__float_as_uint(v)), "r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_v4(uint32_t raddr, float4 v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   raddr),
+               "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
+               "r"(__float_as_uint(v.w)), "r"(rbar)
+               : "memory");
+}
+
+// Top-m of the n rank keys (16-byte aligned): the thread of candidate t counts the keys
+// above its own with broadcast 16-byte shared reads (two keys per read); out[rank] = id
+// for rank < m.  Ranks are distinct (ids are), so out[0..min(n, m)) is filled once each.
+__device__ __forceinline__ void key_select(const uint64_t* keys, int n, int m, int64_t* out) {
+  const ulonglong2* k2 = reinterpret_cast<const ulonglong2*>(keys);
+  const int n2 = n & ~1;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const uint64_t kt = keys[t];
+    int r = 0;
+#pragma unroll 8
+    for (int j = 0; j < n2; j += 2) {
+      const ulonglong2 v = k2[j >> 1];
+      r += (v.x > kt ? 1 : 0) + (v.y > kt ? 1 : 0);
+    }
+    if (n & 1) r += keys[n - 1] > kt ? 1 : 0;
+    if (r < m && kt != 0) out[r] = key_id(kt);  // key 0: an empty candidate slot
+  }
+  __syncthreads();
+}
+
+// Called by every thread of the CTA.  Ends with the top_m logical pages of sequence b in
+// sel_s (descending score, -1 for slots without a candidate), visible to the whole CTA.
+template <typename T, int NS>
+__device__ __forceinline__ void fused_route(const DecodeArgs& a, int b, int rank, int ns, unsigned char* scratch,
+                                         int64_t* sel_s, bool write_out, RoutePrefetch<NS>& pf, uint64_t* xbar) {
+  constexpr int CB = RouteCfg<NS>::kCB;
+  const FusedRoute& r = a.route;
+  constexpr int D = NS * 32;  // the kernel's head_dim
+  const int hkv = r.kv_heads, top_m = a.top_m;
+  const bool tree = r.supers != nullptr;
+  const int n1 = tree ? r.n_super : 0, n2 = tree ? r.top_super * r.superblock : r.n_pages;
+  // scratch: query row, per-kv-head query sums, rank keys of both levels, chosen
+  // superblocks, candidate offsets (route_scratch_bytes)
+  unsigned char* sp = scratch;
+  T* qraw = reinterpret_cast<T*>(sp);
+  sp += route_align16(static_cast<size_t>(r.q_heads) * D * sizeof(T));
+  float* qg = reinterpret_cast<float*>(sp);
+  sp += route_align16(sizeof(float) * static_cast<size_t>(hkv) * D);
+  uint64_t* k1 = reinterpret_cast<uint64_t*>(sp);
+  sp += route_align16(sizeof(uint64_t) * n1);
+  uint64_t* k2 = reinterpret_cast<uint64_t*>(sp);
+  sp += route_align16(sizeof(uint64_t) * n2);
+  int64_t* chosen = reinterpret_cast<int64_t*>(sp);
+  // score = total / q_heads * scale; for a power-of-two head count the division is a
+  // multiplication by the exact reciprocal (the same correctly rounded quotient)
+  const bool hq_pow2 = (r.q_heads & (r.q_heads - 1)) == 0;
+  const float inv_hq = 1.0f / static_cast<float>(r.q_heads);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const float* sup_tab = tree ? r.supers + static_cast<int64_t>(b) * hkv * r.n_super * D : nullptr;
+  const float* page_tab = r.summaries + static_cast<int64_t>(b) * hkv * r.n_pages * D;
+  const int64_t sup_stride = static_cast<int64_t>(r.n_super) * D, page_stride = static_cast<int64_t>(r.n_pages) * D;
+  for (int j = threadIdx.x; j < top_m; j += blockDim.x) sel_s[j] = -1;
+
+  // the first batch of this warp's first-level candidate rows and the query row were
+  // requested at kernel entry (route_prefetch): stage the query, sum it per kv head
+  int n_cand = tree ? n1 : n2;
+  int nl;
+  CandRows<NS>* rows = pf.rows;
+  if (threadIdx.x < kRouteStagers) {  // the consumer warps; the producer joins after them
+    const int nvec = r.q_heads * D * static_cast<int>(sizeof(T)) / 16;
+#pragma unroll
+    for (int u = 0; u < kRouteQVec; ++u) {
+      const int v = threadIdx.x + u * kRouteStagers;
+      if (v < nvec) reinterpret_cast<uint4*>(qraw)[v] = pf.q[u];
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kRouteStagers) : "memory");
+    // qg[kvh][8c .. 8c+8): the kv head's query heads added in order, one 16-byte piece
+    // of each head row per load (all of a thread's loads issue before the adds)
+    const int group = r.q_heads / hkv;
+    constexpr int kPieces = D / 8;  // 16-byte pieces of a 16-bit head row
+    const uint4* qv = reinterpret_cast<const uint4*>(qraw);
+    for (int w = threadIdx.x; w < hkv * kPieces; w += kRouteStagers) {
+      const int kvh = w / kPieces, c = w - kvh * kPieces;
+      float acc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll 4
+      for (int j = 0; j < group; ++j) {
+        const uint4 v = qv[(kvh * group + j) * kPieces + c];
+        const T* h = reinterpret_cast<const T*>(&v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], to_f32(h[e]));
+      }
+      float4* dst4 = reinterpret_cast<float4*>(qg + kvh * D + 8 * c);
+      dst4[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      dst4[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+  }
+  // the per-kv-head sums are complete for the threads that score next: two levels, the
+  // consumer warps (the producer, still issuing the local window, scores only at level 2,
+  // after the level-1 selection's block barrier); one level, everyone
+  if (tree) {
+    if (threadIdx.x < kRouteStagers) asm volatile("bar.sync 1, %0;" ::"n"(kRouteStagers) : "memory");
+  } else {
+    __syncthreads();
+  }
+  cluster_wait();  // every CTA of the cluster runs (its exchange barriers initialised)
+  // this CTA receives every candidate's key of a level: 8 bytes per candidate slot (two
+  // levels: n_super superblocks, then top_super * superblock page slots)
+  if (threadIdx.x == 0) {
+    if (tree) mbar_arrive_expect_tx(&xbar[0], static_cast<uint32_t>(n1) * 8u);
+    mbar_arrive_expect_tx(&xbar[1], static_cast<uint32_t>(n2) * 8u);
+  }
+  // level-2 slot c of two levels: page c % superblock of the (c / superblock)-th chosen
+  // superblock; slots past the last page (a partial last superblock) carry key 0
+  const bool sb_pow2 = (r.superblock & (r.superblock - 1)) == 0;
+  const int sb_lg = __ffs(r.superblock) - 1;
+  auto page_of = [&](int c) {
+    const int j = sb_pow2 ? c >> sb_lg : c / r.superblock;
+    return static_cast<int>(chosen[j]) * r.superblock + (c - j * r.superblock);
+  };
+  const int first_level = tree ? 1 : 2;
+#pragma unroll 1
+  for (int level = first_level; level <= 2; ++level) {
+    const float* tab = level == 1 ? sup_tab : page_tab;
+    const int64_t kv_stride = level == 1 ? sup_stride : page_stride;
+    uint64_t* dst = level == 1 ? k1 : k2;
+    nl = n_cand > rank ? (n_cand - 1 - rank) / ns + 1 : 0;
+    const int nws = level == 1 ? kConsumerWarps : nw;  // scoring warps of this level
+#pragma unroll 1
+    for (int i0 = warp; warp < nws && i0 < nl; i0 += nws * CB) {
+      if (level != first_level || i0 != warp) {
+#pragma unroll
+        for (int u = 0; u < CB; ++u) {
+          const int i = i0 + u * nws;
+          if (i < nl) {
+            const int c = rank + i * ns;
+            int g = (level == 2 && tree) ? page_of(c) : c;
+            if (g >= r.n_pages) g = r.n_pages - 1;  // empty slot: any valid row, key 0 below
+            load_cand_rows(rows[u], tab + static_cast<int64_t>(g) * D, kv_stride, 0, hkv, D);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < CB; ++u) {
+        const int i = i0 + u * nws;
+        if (i < nl) {
+          const int c = rank + i * ns;
+          const int g = (level == 2 && tree) ? page_of(c) : c;
+          const float total = accumulate_cand(rows[u], qg, 0, hkv, D, 0.f);
+          const float q = hq_pow2 ? __fmul_rn(total, inv_hq) : __fdiv_rn(total, static_cast<float>(r.q_heads));
+          const uint64_t key = g < r.n_pages || level == 1 ? rank_key(__fmul_rn(q, r.scale), g) : 0ull;
+          if (lane < ns) st_async_b64(peer_addr(dst + c, lane), key, peer_addr(&xbar[level - 1], lane));
+        }
+      }
+    }
+    // every candidate's key of this level is in this CTA (a lost store ends the wait with
+    // the error word set)
+    mbar_wait_bounded(&xbar[level - 1], 0);
+    if (level == 1) {
+      key_select(k1, n_cand, r.top_super, chosen);
+      n_cand = n2;
+    } else {
+      key_select(k2, n_cand, top_m, sel_s);
+    }
+  }
+  if (write_out) {
+    for (int j = threadIdx.x; j < top_m; j += blockDim.x) {
+      const int64_t v = sel_s[j];
+      r.selected[static_cast<int64_t>(b) * top_m + j] = v;
+      if (r.selected_copy) r.selected_copy[static_cast<int64_t>(b) * top_m + j] = v;
+    }
+  }
+  // the scratch (written by this CTA and pushed into by its peers) becomes a TMA
+  // destination next: order the generic-proxy accesses before the async-proxy writes
+  fence_proxy_async_smem();
+  __syncthreads();
+}
+
+template <typename T, int D, int STAGES, bool ROUTE = false>
 __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                      const __grid_constant__ CUtensorMap vmap,
                                                                      const DecodeArgs a) {
   using S = DecodeSmem<D, STAGES>;
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base (128-byte swizzle atoms), taken by indexing the shared array so
+  // the compiler keeps every access through it in the shared address space
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kRingBytes);
   uint64_t* empty = full + STAGES;
-  int4* info = reinterpret_cast<int4*>(empty + STAGES);
+  // exchange barriers of the routing instantiation: level-1 keys, level-2 keys, merge
+  // partials (each counts the bytes its CTA's peers store into it)
+  uint64_t* xbar = empty + STAGES;
+  int4* info = reinterpret_cast<int4*>(xbar + 4);
   int32_t* tab = reinterpret_cast<int32_t*>(info + STAGES);
   int64_t* sel_s = reinterpret_cast<int64_t*>(tab + S::kTabCap);
   // partials pushed by the cluster's splits for the columns this CTA merges
@@ -178,21 +501,29 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   const bool cluster_push = a.cluster_merge && a.nsplit > 1;
   pdl_trigger();
   touch_args(a);
-  if (cluster_push) cluster_arrive_relaxed();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
+    if (ROUTE)
+      for (int k = 0; k < 3; ++k) mbar_init(&xbar[k], 1);
     fence_mbar_init();
   }
+  // routing CTAs (and merging splits) store into their peers' shared memory: every CTA
+  // arrives now, after its barriers are initialised, and waits before its first remote store
+  if (ROUTE || cluster_push) cluster_arrive_relaxed();
   if (!a.early_local) pdl_block();
+  // routing: the router's first loads go out now, with the prologue's
+  RoutePrefetch<(ROUTE ? D / 32 : 1)> pf;
+  if constexpr (ROUTE) route_prefetch<T, D / 32>(a, b, split, a.nsplit, pf);
   // prologue loads issued together (one memory round trip): the producer's page-table row
   // and selected ids, every thread's context length.  With early_local the selected ids
-  // come from the kernel this one overlaps, so they are read after it completes.
+  // come from the kernel this one overlaps, so they are read after it completes; routing
+  // CTAs select the pages themselves.
   const int tstride = a.addr.table_stride;
   const bool use_tab = a.addr.page_table != nullptr && tstride <= S::kTabCap;
-  const bool sel_early = a.selected && !a.early_local && a.top_m <= S::kSelCap;
+  const bool sel_early = !ROUTE && a.selected && !a.early_local && a.top_m <= S::kSelCap;
   int32_t tab_r[16];
   int64_t sel_r = -1;
   if (warp == kConsumerWarps) {
@@ -203,30 +534,108 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     }
     if (sel_early && lane < a.top_m) sel_r = a.selected[static_cast<int64_t>(b) * a.top_m + lane];
   }
-  const ChunkPlan plan = make_plan(a, b, kChunk);
-  // the local-window chunks and the selected chunks are divided among the splits
-  // separately: each split gets an equal share of the selected chunks, the ones that wait
-  // for the router in the fused step, on top of at most its share of the local ones
-  const int n_sel_chunks = plan.n_total - plan.n_seg;
-  // bounds of an even division of n items into nsplit parts (32-bit arithmetic while the
-  // products fit, which is every realistic context)
-  auto part_of = [&](int n, int s_) -> int {
-    return n <= (1 << 22) ? n * s_ / a.nsplit : static_cast<int>(static_cast<int64_t>(n) * s_ / a.nsplit);
+  // this split's chunks: the local-window chunks and the selected chunks are divided among
+  // the splits separately: each split gets an equal share of the selected chunks, the ones
+  // that wait for the router in the fused step, on top of at most its share of the local ones
+  struct SplitWork {
+    ChunkPlan plan;
+    int c_l0, c_s0, n_local, nk;
   };
-  const int c_l0 = part_of(plan.n_seg, split), c_l1 = part_of(plan.n_seg, split + 1);
-  const int c_s0 = plan.n_seg + part_of(n_sel_chunks, split), c_s1 = plan.n_seg + part_of(n_sel_chunks, split + 1);
-  const int n_local = c_l1 - c_l0;
-  const int nk = n_local + (c_s1 - c_s0);
-  __syncthreads();
+  auto split_work = [&](int ctx) -> SplitWork {
+    SplitWork w;
+    w.plan = make_plan_ctx(a, ctx, kChunk);
+    const int n_sel_chunks = w.plan.n_total - w.plan.n_seg;
+    // bounds of an even division of n items into nsplit parts (32-bit arithmetic while the
+    // products fit, which is every realistic context)
+    auto part_of = [&](int n, int s_) -> int {
+      return n <= (1 << 22) ? n * s_ / a.nsplit : static_cast<int>(static_cast<int64_t>(n) * s_ / a.nsplit);
+    };
+    w.c_l0 = part_of(w.plan.n_seg, split);
+    const int c_l1 = part_of(w.plan.n_seg, split + 1);
+    w.c_s0 = w.plan.n_seg + part_of(n_sel_chunks, split);
+    const int c_s1 = w.plan.n_seg + part_of(n_sel_chunks, split + 1);
+    w.n_local = c_l1 - w.c_l0;
+    w.nk = w.n_local + (c_s1 - w.c_s0);
+    return w;
+  };
+  // routing: the context length is requested now and used by the producer before routing
+  // and by the consumers only after it, so its round trip is not on their path
+  const int ctx_b = a.ctx_lens[b];
+  SplitWork sw{};
+  if constexpr (ROUTE) {
+    __syncthreads();  // the barrier initialisation is visible to every thread
+    if (warp == kConsumerWarps) sw = split_work(ctx_b);
+  } else {
+    sw = split_work(ctx_b);
+    __syncthreads();
+  }
 
+  // ------------------------------------------------------------ producer
+  bool ok = true;
+  auto row_of = [&](int t) -> long long {
+    if (!use_tab) return a.addr.row(b, kvh, t);
+    const int ps = a.addr.page_size;
+    const int lp = (ps & (ps - 1)) == 0 ? t >> (__ffs(ps) - 1) : t / ps;
+    if (lp < 0 || lp >= tstride) return -1;
+    const int32_t pg = tab[lp];
+    if (pg < 0) return -1;
+    return b * a.addr.batch_stride_rows + static_cast<long long>(pg) * a.addr.page_stride_rows +
+           kvh * a.addr.head_stride_rows + (t - lp * a.addr.page_size);
+  };
+  // issues this split's chunks [lo, hi) into the ring (producer warp; lane 0 issues)
+  auto produce = [&](int lo, int hi, const int64_t* sel_row) {
+    const uint64_t policy = l2_policy_evict_first();
+    for (int base = lo; base < hi && ok; base += 32) {
+      ChunkInfo ci{0, 0, 0};
+      long long row = -1;
+      if (base + lane < hi) {
+        const int idx = base + lane;  // this split's idx-th chunk
+        ci = chunk_info(a, sw.plan, sel_row, idx < sw.n_local ? sw.c_l0 + idx : sw.c_s0 + (idx - sw.n_local),
+                        kChunk);
+        if (ci.vlo < ci.vhi) {
+          row = row_of(ci.t0);
+          if (row < 0 || row >= a.addr.total_rows) {
+            spa_raise(SPA_DEVERR_BAD_PAGE);
+            row = -1;
+          }
+        }
+      }
+      const int cnt = min(32, hi - base);
+      for (int j = 0; j < cnt; ++j) {
+        const int i = base + j;
+        const int t0 = __shfl_sync(0xffffffffu, ci.t0, j);
+        const int vlo = __shfl_sync(0xffffffffu, ci.vlo, j);
+        const int vhi = __shfl_sync(0xffffffffu, ci.vhi, j);
+        const long long r = __shfl_sync(0xffffffffu, row, j);
+        if (lane == 0) {
+          const int stage = i % STAGES;
+          if (i >= STAGES && !mbar_wait_bounded(&empty[stage], ((i / STAGES) - 1) & 1)) ok = false;
+          if (ok) {
+            info[stage] = make_int4(t0, r >= 0 ? vlo : 0, r >= 0 ? vhi : 0, 0);
+            uint64_t* bar = &full[stage];
+            if (r >= 0) {
+              mbar_arrive_expect_tx(bar, S::kStageBytes);
+              unsigned char* dst = smem + stage * S::kStageBytes;
+              tma_load_3d_hint(dst, &kmap, bar, 0, static_cast<int>(r), 0, policy);
+              tma_load_3d_hint(dst + S::kKvBytes, &vmap, bar, 0, static_cast<int>(r), 0, policy);
+            } else {
+              mbar_arrive(bar);
+            }
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+      }
+    }
+  };
+  // routing: the local-window chunks that fit in the ring before its last stage (the
+  // router's scratch) load while the cluster selects; the rest follow the selection
+  const int n_early = ROUTE ? min(sw.n_local, STAGES - 1) : sw.n_local;
   if (warp == kConsumerWarps) {
-    // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
     }
-    const uint64_t policy = l2_policy_evict_first();
-    bool ok = true;
     // the sequence's page-table row: the first 512 entries were loaded with the plan,
     // the rest (long rows) here with independent loads
     if (use_tab) {
@@ -245,78 +654,43 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     }
     if (sel_early && lane < a.top_m) sel_s[lane] = sel_r;
     __syncwarp();
-    const int64_t* sel_row = sel_early ? sel_s : (a.selected ? a.selected + static_cast<int64_t>(b) * a.top_m : nullptr);
-    auto row_of = [&](int t) -> long long {
-      if (!use_tab) return a.addr.row(b, kvh, t);
-      const int ps = a.addr.page_size;
-      const int lp = (ps & (ps - 1)) == 0 ? t >> (__ffs(ps) - 1) : t / ps;
-      if (lp < 0 || lp >= tstride) return -1;
-      const int32_t pg = tab[lp];
-      if (pg < 0) return -1;
-      return b * a.addr.batch_stride_rows + static_cast<long long>(pg) * a.addr.page_stride_rows +
-             kvh * a.addr.head_stride_rows + (t - lp * a.addr.page_size);
-    };
-    // chunks [0, n_local) of this split are local-window chunks (no router output needed);
-    // with early_local they are issued before waiting for the router.
-    for (int part = 0; part < 2 && ok; ++part) {
-      const int lo = part ? n_local : 0, hi = part ? nk : n_local;
-      if (part == 1 && a.early_local) {
-        pdl_block();
-        // the router has completed: its selected ids for this sequence, one round trip
-        if (a.selected && a.top_m <= S::kSelCap) {
-          if (lane < a.top_m) sel_s[lane] = a.selected[static_cast<int64_t>(b) * a.top_m + lane];
-          __syncwarp();
-          sel_row = sel_s;
-        }
-      }
-      for (int base = lo; base < hi && ok; base += 32) {
-        ChunkInfo ci{0, 0, 0};
-        long long row = -1;
-        if (base + lane < hi) {
-          const int idx = base + lane;  // this split's idx-th chunk
-          ci = chunk_info(a, plan, sel_row, idx < n_local ? c_l0 + idx : c_s0 + (idx - n_local), kChunk);
-          if (ci.vlo < ci.vhi) {
-            row = row_of(ci.t0);
-            if (row < 0 || row >= a.addr.total_rows) {
-              spa_raise(SPA_DEVERR_BAD_PAGE);
-              row = -1;
-            }
+    if constexpr (ROUTE) {
+      produce(0, n_early, nullptr);
+    } else {
+      const int64_t* sel_row =
+          sel_early ? sel_s : (a.selected ? a.selected + static_cast<int64_t>(b) * a.top_m : nullptr);
+      // chunks [0, n_local) of this split are local-window chunks (no router output needed);
+      // with early_local they are issued before waiting for the router.
+      for (int part = 0; part < 2 && ok; ++part) {
+        const int lo = part ? sw.n_local : 0, hi = part ? sw.nk : sw.n_local;
+        if (part == 1 && a.early_local) {
+          pdl_block();
+          // the router has completed: its selected ids for this sequence, one round trip
+          if (a.selected && a.top_m <= S::kSelCap) {
+            if (lane < a.top_m) sel_s[lane] = a.selected[static_cast<int64_t>(b) * a.top_m + lane];
+            __syncwarp();
+            sel_row = sel_s;
           }
         }
-        const int cnt = min(32, hi - base);
-        for (int j = 0; j < cnt; ++j) {
-          const int i = base + j;
-          const int t0 = __shfl_sync(0xffffffffu, ci.t0, j);
-          const int vlo = __shfl_sync(0xffffffffu, ci.vlo, j);
-          const int vhi = __shfl_sync(0xffffffffu, ci.vhi, j);
-          const long long r = __shfl_sync(0xffffffffu, row, j);
-          if (lane == 0) {
-            const int stage = i % STAGES;
-            if (i >= STAGES && !mbar_wait_bounded(&empty[stage], ((i / STAGES) - 1) & 1)) ok = false;
-            if (ok) {
-              info[stage] = make_int4(t0, r >= 0 ? vlo : 0, r >= 0 ? vhi : 0, 0);
-              uint64_t* bar = &full[stage];
-              if (r >= 0) {
-                mbar_arrive_expect_tx(bar, S::kStageBytes);
-                unsigned char* dst = smem + stage * S::kStageBytes;
-                tma_load_3d_hint(dst, &kmap, bar, 0, static_cast<int>(r), 0, policy);
-                tma_load_3d_hint(dst + S::kKvBytes, &vmap, bar, 0, static_cast<int>(r), 0, policy);
-              } else {
-                mbar_arrive(bar);
-              }
-            }
-          }
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (!ok) break;
-        }
+        produce(lo, hi, sel_row);
       }
+      // every thread of every CTA in a merging cluster completes both cluster phases
+      if (cluster_push) {
+        cluster_wait();
+        cluster_barrier();
+      }
+      return;
     }
-    // every thread of every CTA in a merging cluster completes both cluster phases
-    if (cluster_push) {
-      cluster_wait();
-      cluster_barrier();
+  }
+  if constexpr (ROUTE) {
+    // every thread routes (the producer warp too, after its early chunks)
+    fused_route<T, D / 32>(a, b, split, a.nsplit, smem + (STAGES - 1) * S::kStageBytes, sel_s,
+                           split == 0 && kvh == 0, pf, xbar);
+    if (warp == kConsumerWarps) {
+      produce(n_early, sw.nk, sel_s);
+      return;
     }
-    return;
+    sw = split_work(ctx_b);  // the consumers' chunk count
   }
 
   // -------------------------------------------------------------- consumers
@@ -326,7 +700,8 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   uint32_t qa[D / 16][4];
   {
     if (a.q_after_wait) pdl_block();
-    const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(b) * a.Hq + kvh * group) * D;
+    const T* qb =
+        static_cast<const T*>(a.q) + (static_cast<int64_t>(b) * a.q_batch_heads + a.q_head_offset + kvh * group) * D;
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
       const int col = ks * 16 + tig * 2;
@@ -343,7 +718,8 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
 
   const int rbase = warp * 16;
   const int mi = lane >> 3, mr = lane & 7;
-  bool ok = true;
+  ok = true;
+  const int nk = sw.nk;
   for (int i = 0; i < nk; ++i) {
     const int stage = i % STAGES;
     // warp-uniform outcome: lanes must agree before any aligned barrier below
@@ -433,7 +809,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
     if (lane == 0) mbar_arrive(&empty[stage]);
   }
   if (!ok) {  // error word already raised; outputs of this split are undefined
-    if (cluster_push) {
+    if (cluster_push && !ROUTE) {
       cluster_wait();
       cluster_barrier();
     }
@@ -501,7 +877,14 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   float* recv_o = recv + ((ns * group + 3) & ~3);  // 16-byte aligned
   // equal column slices of a multiple of 4: 16-byte loads and remote stores
   const bool vec4 = cluster_push && (ns_pow2 ? (D & (4 * ns - 1)) == 0 : D % (4 * ns) == 0);
-  if (cluster_push) cluster_wait();  // every CTA of the cluster runs: remote stores are safe
+  // every CTA of the cluster runs: remote stores are safe (routing CTAs waited before routing)
+  if (cluster_push && !ROUTE) cluster_wait();
+  if (ROUTE && cluster_push && threadIdx.x == 0) {
+    // this CTA receives, from each of the ns splits, one log-sum-exp and its column slice
+    // per head
+    const int w_self = div_ns((split + 1) * D) - div_ns(split * D);
+    mbar_arrive_expect_tx(&xbar[2], static_cast<uint32_t>(ns * group * (1 + w_self)) * 4u);
+  }
   if (vec4) {
     for (int idx = threadIdx.x; idx < group * (D / 4); idx += kConsumerWarps * 32) {
       const int row = idx / (D / 4), col = (idx - row * (D / 4)) * 4;
@@ -516,7 +899,11 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
         o.w = fmaf(r4.w, f, o.w);
       }
       const int r = col * ns / D;  // slices are exactly wmax = D / ns wide
-      st_dsmem_v4(recv_o + (split * group + row) * wmax + (col - r * wmax), r, o);
+      float* dst = recv_o + (split * group + row) * wmax + (col - r * wmax);
+      if constexpr (ROUTE)
+        st_async_v4(peer_addr(dst, r), o, peer_addr(&xbar[2], r));
+      else
+        st_dsmem_v4(dst, r, o);
     }
   }
   for (int idx = threadIdx.x; !vec4 && idx < group * D; idx += kConsumerWarps * 32) {
@@ -529,7 +916,11 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
       static_cast<T*>(a.out)[(bh0 + row) * D + col] = from_f32<T>(o);
     } else if (cluster_push) {
       const int r = ((col + 1) * ns - 1) / D;  // the rank whose column slice holds col
-      st_dsmem(recv_o + (split * group + row) * wmax + (col - r * D / ns), r, o);
+      float* dst = recv_o + (split * group + row) * wmax + (col - r * D / ns);
+      if constexpr (ROUTE)
+        st_async_f32(peer_addr(dst, r), o, peer_addr(&xbar[2], r));
+      else
+        st_dsmem(dst, r, o);
     } else {
       a.part_o[((bh0 + row) * ns + split) * D + col] = o;
       if (col == 0) a.part_lse[(bh0 + row) * ns + split] = row_lse[row];
@@ -538,9 +929,17 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid
   if (!cluster_push) return;
   for (int i = threadIdx.x; i < group * ns; i += kConsumerWarps * 32) {
     const int row = div_ns(i), r = i - row * ns;
-    st_dsmem(recv_lse + split * group + row, r, row_lse[row]);
+    if constexpr (ROUTE)
+      st_async_f32(peer_addr(recv_lse + split * group + row, r), row_lse[row], peer_addr(&xbar[2], r));
+    else
+      st_dsmem(recv_lse + split * group + row, r, row_lse[row]);
   }
-  cluster_barrier();  // every split's pushes are visible in the receive buffers
+  // every split's pushes are visible in the receive buffers (routing instantiation: this
+  // CTA's byte count; a lost store ends the wait with the error word set)
+  if constexpr (ROUTE)
+    mbar_wait_bounded(&xbar[2], 0);
+  else
+    cluster_barrier();
   // after the barrier this CTA reads only its own shared memory: no second barrier
   const int c0 = div_ns(split * D), c1 = div_ns((split + 1) * D), w = c1 - c0;
   for (int idx = threadIdx.x; idx < group * w; idx += kConsumerWarps * 32) {
@@ -574,7 +973,7 @@ __global__ void __launch_bounds__(32) decode_generic_kernel(const T* __restrict_
   const int k0 = static_cast<int>(static_cast<int64_t>(plan.n_total) * split / a.nsplit);
   const int k1 = static_cast<int>(static_cast<int64_t>(plan.n_total) * (split + 1) / a.nsplit);
   float qv[8], acc[8];
-  const T* qp = static_cast<const T*>(a.q) + (static_cast<int64_t>(b) * a.Hq + h) * D;
+  const T* qp = static_cast<const T*>(a.q) + (static_cast<int64_t>(b) * a.q_batch_heads + a.q_head_offset + h) * D;
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const int d = lane + 32 * e;
@@ -771,14 +1170,21 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   return launch_ex(kern, grid, block, smem, st, pdl, 1, std::forward<Args>(args)...);
 }
 
-template <typename T, int D>
-int launch_decode_mma(const spa_kv_layout& kv, int dtype, const DecodeArgs& a, cudaStream_t st) {
+// ROUTE: the instantiation that selects the pages itself (fused_route); it needs the
+// splits of a pair in one cluster and the router's scratch within one ring stage.
+// pdl: launch as a programmatic dependent of the previous kernel in the stream (the
+// kernel waits for it before its first read unless early_local says otherwise).
+template <typename T, int D, bool ROUTE = false>
+int launch_decode_mma(const spa_kv_layout& kv, int dtype, const DecodeArgs& a, cudaStream_t st, bool pdl = false) {
   using S = DecodeSmem<D, kDecodeStages>;
+  if (ROUTE && (!a.cluster_merge || route_scratch_bytes(a.route, D, sizeof(T)) > static_cast<size_t>(S::kStageBytes) ||
+                static_cast<size_t>(a.route.q_heads) * D * sizeof(T) > kRouteQVec * 16 * kRouteStagers))
+    return SPA_ERR_UNSUPPORTED;
   CUtensorMap kmap, vmap;
   // one TMA load per chunk of K (and of V) covers both 64-column slabs of a row
   if (!spa_make_tensor_map_row_halves(&kmap, kv.k, dtype, kv.total_rows, D, kChunk)) return SPA_ERR_INVALID;
   if (!spa_make_tensor_map_row_halves(&vmap, kv.v, dtype, kv.total_rows, D, kChunk)) return SPA_ERR_INVALID;
-  auto kern = decode_mma_kernel<T, D, kDecodeStages>;
+  auto kern = decode_mma_kernel<T, D, kDecodeStages, ROUTE>;
   // the receive buffer of the cluster merge: [ns][group] log-sum-exps + [ns][group][ceil(D/ns)]
   const int ns = a.nsplit;
   const size_t recv = a.cluster_merge && ns > 1
@@ -787,8 +1193,8 @@ int launch_decode_mma(const spa_kv_layout& kv, int dtype, const DecodeArgs& a, c
                           : 0;
   const size_t smem = S::kBytes + recv;
   SPA_CHECK_CUDA(spa_set_smem_once(kern, static_cast<int>(smem)));
-  SPA_CHECK_CUDA(launch_ex(kern, dim3(a.nsplit, a.Hkv, a.B), dim3(kDecodeThreads), smem, st, a.early_local != 0,
-                           a.cluster_merge ? a.nsplit : 1, kmap, vmap, a));
+  SPA_CHECK_CUDA(launch_ex(kern, dim3(a.nsplit, a.Hkv, a.B), dim3(kDecodeThreads), smem, st,
+                           a.early_local != 0 || pdl, a.cluster_merge ? a.nsplit : 1, kmap, vmap, a));
   return SPA_OK;
 }
 
@@ -891,7 +1297,7 @@ int spa::paged_decode_impl(const void* q, int dtype, int batch, int q_heads, int
   if (head_dim <= 0 || head_dim > 256 || kv->page_size <= 0 || kv->total_rows <= 0) return SPA_ERR_INVALID;
   if (local_window < 0 || max_candidates < 0 || (selected && top_m <= 0)) return SPA_ERR_INVALID;
   if (kv->page_table && kv->table_stride <= 0) return SPA_ERR_INVALID;
-  spa::DecodeArgs a;
+  spa::DecodeArgs a{};
   a.q = q;
   a.out = out;
   a.B = batch;
@@ -899,6 +1305,8 @@ int spa::paged_decode_impl(const void* q, int dtype, int batch, int q_heads, int
   a.Hkv = kv_heads;
   a.group = q_heads / kv_heads;
   a.D = head_dim;
+  a.q_batch_heads = q_heads;
+  a.q_head_offset = 0;
   a.addr = make_kv_addr(*kv);
   a.ctx_lens = context_lens;
   a.local_window = local_window;

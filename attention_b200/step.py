@@ -3,9 +3,13 @@
 Reference: the timed unit of experiments/triton_paged_gather_decode_benchmark.py:69
 (and triton_promotion_cache_benchmark.py:59),
 ``paged_gather_decode_attention(q, K, V, select_blocks(q, summaries, m), local_window=W, block_size=P)``.
-Here the router and the decode are chained kernels on the device: the decode grid
-starts while the router runs and streams the local window before it reads the
-selected page ids.  Returns ``(out, selected)``; both equal what
+Here, for the shapes the fused kernel serves (bf16/fp16, head_dim 64 or 128, at
+most 8 kv heads, top_m <= 32, each (sequence, kv head) pair's splits merged in one
+cluster), the step is ONE kernel launch: every decode cluster scores its sequence's
+page summaries, selects the pages and streams them, while its local-window chunks
+load.  Otherwise the router and the decode are chained kernels on the device: the
+decode grid starts while the router runs and streams the local window before it
+reads the selected page ids.  Returns ``(out, selected)``; both equal what
 ``select_blocks[_tree]`` followed by ``paged_gather_decode_attention`` return.
 With ``gate`` (a ``RefreshGate``), a step whose gate is closed reuses the promoted
 pages and the router reads no summaries (promotion reuse,
@@ -65,14 +69,82 @@ def _prepare_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
                 lens=lens, summ=summ, sup=sup, ws=ws, ws_bytes=ws_bytes, dtype=dtype_code(query))
 
 
+def set_step_fusion(enabled: bool) -> bool:
+    """Process-wide: run qualifying steps as one launch (True, the default) or always as a
+    router launch followed by a decode launch (False).  Returns the previous setting."""
+    return bool(_lib.lib.spa_set_step_fusion(1 if enabled else 0))
+
+
+def _sparse_decode_step_heads(query, keys, values, summaries, *, top_blocks, local_window, block_size,
+                              super_summaries, superblock, top_super, router_scale, page_table, context_lens, out,
+                              selected, kv_head_range):
+    """The step over kv heads [begin, begin + count) of every sequence (one rank's shard):
+    query and summaries hold every head, keys/values (and the output) those kv heads."""
+    begin, count = (int(x) for x in kv_head_range)
+    batch, q_heads, head_dim = query.shape
+    kv_total = summaries.size(1)
+    if not (query.is_cuda and keys.is_cuda and values.is_cuda and summaries.is_cuda):
+        raise ValueError("CUDA tensors are required")
+    if not (query.is_contiguous() and keys.is_contiguous() and values.is_contiguous()):
+        raise ValueError("contiguous CUDA tensors are required")
+    if q_heads % kv_total or begin < 0 or count <= 0 or begin + count > kv_total or keys.size(1) != count:
+        raise ValueError("incompatible Q/K/V shapes")
+    if keys.dim() != 4 or values.shape != keys.shape or keys.size(3) != head_dim:
+        raise ValueError("incompatible Q/K/V shapes")
+    group = q_heads // kv_total
+    summ = summaries.float().contiguous()
+    if summ.dim() != 4 or summ.size(0) != batch or summ.size(3) != head_dim:
+        raise ValueError("summaries must be [B, Hkv, pages, D]")
+    sup = None
+    if super_summaries is not None:
+        sup = super_summaries.float().contiguous()
+        if sup.shape[:2] != (batch, kv_total) or sup.size(2) != -(-summ.size(2) // superblock):
+            raise ValueError("super_summaries must be [B, Hkv, ceil(pages/superblock), D]")
+    if page_table is None or context_lens is None or keys.size(2) != block_size:
+        raise ValueError("page pool needs context_lens and block_size == page size")
+    dev = keys.device
+    table = as_int32(page_table).contiguous()
+    lens = as_int32(context_lens).contiguous()
+    layout = pool_layout(keys, values, table)
+    max_cand = local_window + top_blocks * block_size
+    ws_bytes = _lib.lib.spa_decode_workspace_size(batch, count * group, count, head_dim, max_cand)
+    ws = workspace(dev, ws_bytes) if ws_bytes else None
+    if out is None:
+        out = torch.empty(batch, count * group, head_dim, dtype=query.dtype, device=dev)
+    if selected is None:
+        selected = torch.empty(batch, top_blocks, dtype=torch.int64, device=dev)
+    rc = _lib.lib.spa_sparse_decode_step_heads(
+        query.data_ptr(), dtype_code(query), batch, q_heads, kv_total, head_dim, begin, count, ctypes.byref(layout),
+        lens.data_ptr(), local_window, sup.data_ptr() if sup is not None else None,
+        sup.size(2) if sup is not None else 0, summ.data_ptr(), summ.size(2), superblock, top_super, top_blocks,
+        float(router_scale), head_dim ** -0.5, selected.data_ptr(), out.data_ptr(),
+        ws.data_ptr() if ws is not None else None, ws_bytes, stream_ptr(dev))
+    _lib.check(rc, "spa_sparse_decode_step_heads")
+    return out, selected
+
+
 def sparse_decode_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, summaries: torch.Tensor, *,
                        top_blocks: int, local_window: int, block_size: int,
                        super_summaries: torch.Tensor | None = None, superblock: int = 0, top_super: int = 0,
                        router_scale: float = 1.0, page_table: torch.Tensor | None = None,
                        context_lens: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                       selected: torch.Tensor | None = None, gate=None):
+                       selected: torch.Tensor | None = None, gate=None,
+                       kv_head_range: tuple[int, int] | None = None):
+    """``kv_head_range=(begin, count)``: one rank's (sequence, kv head) shard -- query and
+    summaries hold every head of the sequences, keys/values only kv heads
+    [begin, begin + count) of a page pool, and the output those kv heads' query heads.
+    Every shard of a sequence selects the same pages."""
     if not query.is_cuda:
         raise ValueError("CUDA tensors are required")
+    if kv_head_range is not None:
+        if gate is not None:
+            raise ValueError("a refresh gate is not supported with kv_head_range")
+        return _sparse_decode_step_heads(query, keys, values, summaries, top_blocks=top_blocks,
+                                         local_window=local_window, block_size=block_size,
+                                         super_summaries=super_summaries, superblock=superblock,
+                                         top_super=top_super, router_scale=router_scale, page_table=page_table,
+                                         context_lens=context_lens, out=out, selected=selected,
+                                         kv_head_range=kv_head_range)
     pr = _prepare_step(query, keys, values, summaries, top_blocks=top_blocks, local_window=local_window,
                        block_size=block_size, super_summaries=super_summaries, superblock=superblock,
                        top_super=top_super, page_table=page_table, context_lens=context_lens)

@@ -217,9 +217,15 @@ int spa_span_gather_decode(const void* q, int dtype, int batch, int q_heads,
                            size_t workspace_bytes, spa_stream_t stream);
 
 /*
- * One routed sparse decode step: router then gather decode, enqueued as chained
- * kernels (the decode starts while the router runs and streams the local window
- * before it reads the page ids).  super_summaries != NULL: two-level router
+ * One routed sparse decode step: router then gather decode.  For bf16/fp16,
+ * head_dim 64 or 128, at most 8 kv heads, top_m <= 32 and a split plan that merges
+ * each (sequence, kv head) pair's splits in one cluster, it is ONE kernel launch in
+ * which every decode cluster scores its sequence's summaries, selects the pages
+ * (the same pages, bit for bit, as spa_router_tree_topm / spa_router_topm) and
+ * streams them, the local window loading meanwhile; otherwise the router and the
+ * decode are enqueued as chained kernels (the decode starts while the router runs
+ * and streams the local window before it reads the page ids)
+ * (spa_set_step_fusion chooses).  super_summaries != NULL: two-level router
  * (spa_router_tree_topm); NULL: single level over n_pages (spa_router_topm).
  * router_scale multiplies the router score, attn_scale the attention logits.
  * selected: int64 [B, top_m] (written); out: [B, Hq, D]; workspace as for
@@ -238,6 +244,39 @@ int spa_sparse_decode_step(const void* q, int dtype, int batch, int q_heads,
                            double attn_scale, int64_t* selected, void* out,
                            void* workspace, size_t workspace_bytes,
                            spa_stream_t stream);
+
+/*
+ * spa_sparse_decode_step over a kv-head slice: one rank's (sequence, kv head)
+ * shard of a decode batch.  q [B, q_heads, D] holds every query head of each
+ * sequence and the summaries every one of the kv_heads kv heads (the router scores
+ * with all of them, so every shard of a sequence selects the same pages); the
+ * decode covers kv heads [kv_head_begin, kv_head_begin + kv_head_count), which
+ * the layout kv addresses as its kv heads 0 .. kv_head_count-1, and writes out
+ * [B, kv_head_count * q_heads / kv_heads, D] (those kv heads' query heads).
+ * selected [B, top_m] as for spa_sparse_decode_step; workspace for
+ * (B, kv_head_count * q_heads / kv_heads, kv_head_count) heads.
+ * Extends spa_sparse_decode_step (same reference unit) to the multi-GPU split of a
+ * batch; kv_head_begin = 0, kv_head_count = kv_heads is spa_sparse_decode_step.
+ */
+int spa_sparse_decode_step_heads(const void* q, int dtype, int batch, int q_heads,
+                                 int kv_heads, int head_dim, int kv_head_begin,
+                                 int kv_head_count, const spa_kv_layout* kv,
+                                 const int32_t* context_lens, int local_window,
+                                 const float* super_summaries, int n_super,
+                                 const float* summaries, int n_pages,
+                                 int superblock, int top_super, int top_m,
+                                 double router_scale, double attn_scale,
+                                 int64_t* selected, void* out, void* workspace,
+                                 size_t workspace_bytes, spa_stream_t stream);
+
+/*
+ * Step fusion switch for the library (process-wide): 1 (default) runs the steps
+ * that qualify as one launch, 0 always chains the router and decode launches.
+ * Returns the previous mode; other values only query it.  Both modes give the
+ * same pages and the same outputs.  No counterpart in the reference (a tuning
+ * and A/B switch of this library).
+ */
+int spa_set_step_fusion(int mode);
 
 /*
  * Allocation-free spa_paged_decode, for callers that cannot allocate device
