@@ -327,6 +327,56 @@ __device__ __forceinline__ void key_select(const uint64_t* keys, int n, int m, i
   __syncthreads();
 }
 
+// Half-warp scoring: half h of a warp scores one candidate.  Lane hl of the half holds the
+// canonical partial sums of lanes hl and hl + 16 (d = lane + 32k, k ascending, separate
+// multiply and add); their sum is the canonical butterfly's first step (offset 16: fp
+// addition is commutative bit for bit), and offsets 8, 4, 2, 1 stay inside the half, so
+// the score equals accumulate_cand's bit for bit with half the shuffles per candidate.
+template <int NS>
+struct HalfRows {
+  float v[kRouterKvBatch][2 * NS];
+};
+template <int NS>
+__device__ __forceinline__ void load_half_rows(HalfRows<NS>& r, const float* base, int64_t kv_stride, int kv_heads) {
+  const int hl = threadIdx.x & 15;
+#pragma unroll
+  for (int u = 0; u < kRouterKvBatch; ++u) {
+    const bool hv = u < kv_heads;
+    const float* row = base + static_cast<int64_t>(hv ? u : 0) * kv_stride;
+#pragma unroll
+    for (int k = 0; k < NS; ++k) {
+      r.v[u][2 * k] = hv ? __ldg(row + hl + 32 * k) : 0.f;
+      r.v[u][2 * k + 1] = hv ? __ldg(row + hl + 16 + 32 * k) : 0.f;
+    }
+  }
+}
+template <int NS>
+__device__ __forceinline__ float accumulate_half(const HalfRows<NS>& r, const float* qg, int kv_heads) {
+  constexpr int D = NS * 32;
+  const int hl = threadIdx.x & 15;
+  float part[kRouterKvBatch];
+#pragma unroll
+  for (int u = 0; u < kRouterKvBatch; ++u) {
+    const float* qq = qg + (u < kv_heads ? u : 0) * D;
+    float pa = 0.f, pb = 0.f;
+#pragma unroll
+    for (int k = 0; k < NS; ++k) {
+      pa = __fadd_rn(pa, __fmul_rn(qq[hl + 32 * k], r.v[u][2 * k]));
+      pb = __fadd_rn(pb, __fmul_rn(qq[hl + 16 + 32 * k], r.v[u][2 * k + 1]));
+    }
+    part[u] = __fadd_rn(pa, pb);
+  }
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1)
+#pragma unroll
+    for (int u = 0; u < kRouterKvBatch; ++u) part[u] = __fadd_rn(part[u], __shfl_xor_sync(0xffffffffu, part[u], off));
+  float total = 0.f;
+#pragma unroll
+  for (int u = 0; u < kRouterKvBatch; ++u)
+    if (u < kv_heads) total = __fadd_rn(total, part[u]);
+  return total;
+}
+
 // Called by every thread of the CTA.  Ends with the top_m logical pages of sequence b in
 // sel_s (descending score, -1 for slots without a candidate), visible to the whole CTA.
 template <typename T, int NS>
@@ -426,6 +476,40 @@ __device__ __forceinline__ void fused_route(const DecodeArgs& a, int b, int rank
     uint64_t* dst = level == 1 ? k1 : k2;
     nl = n_cand > rank ? (n_cand - 1 - rank) / ns + 1 : 0;
     const int nws = level == 1 ? kConsumerWarps : nw;  // scoring warps of this level
+    if (level == 2 && tree) {
+      // two levels, level 2: half-warps, one candidate pair per warp in flight
+      constexpr int HB = 1;
+      const int half = lane >> 4, hl = lane & 15;
+      const int npairs = (nl + 1) >> 1;
+#pragma unroll 1
+      for (int p0 = warp; p0 < npairs; p0 += nws * HB) {
+        HalfRows<NS> hr[HB];
+#pragma unroll
+        for (int hb = 0; hb < HB; ++hb) {
+          const int pr = p0 + hb * nws, i = 2 * pr + half;
+          if (pr < npairs) {
+            // a half without a candidate (odd count) reads a valid row and discards it
+            int g = i < nl ? page_of(rank + i * ns) : 0;
+            if (g >= r.n_pages) g = r.n_pages - 1;  // empty slot: any valid row, key 0 below
+            load_half_rows(hr[hb], page_tab + static_cast<int64_t>(g) * D, page_stride, hkv);
+          }
+        }
+#pragma unroll
+        for (int hb = 0; hb < HB; ++hb) {
+          const int pr = p0 + hb * nws, i = 2 * pr + half;
+          if (pr < npairs) {
+            const float total = accumulate_half(hr[hb], qg, hkv);
+            if (i < nl && hl < ns) {
+              const int c = rank + i * ns;
+              const int g = page_of(c);
+              const float q = hq_pow2 ? __fmul_rn(total, inv_hq) : __fdiv_rn(total, static_cast<float>(r.q_heads));
+              const uint64_t key = g < r.n_pages ? rank_key(__fmul_rn(q, r.scale), g) : 0ull;
+              st_async_b64(peer_addr(k2 + c, hl), key, peer_addr(&xbar[1], hl));
+            }
+          }
+        }
+      }
+    } else {
 #pragma unroll 1
     for (int i0 = warp; warp < nws && i0 < nl; i0 += nws * CB) {
       if (level != first_level || i0 != warp) {
@@ -453,6 +537,7 @@ __device__ __forceinline__ void fused_route(const DecodeArgs& a, int b, int rank
         }
       }
     }
+    }
     // every candidate's key of this level is in this CTA (a lost store ends the wait with
     // the error word set)
     mbar_wait_bounded(&xbar[level - 1], 0);
@@ -477,7 +562,7 @@ __device__ __forceinline__ void fused_route(const DecodeArgs& a, int b, int rank
 }
 
 template <typename T, int D, int STAGES, bool ROUTE = false>
-__global__ void __launch_bounds__(kDecodeThreads) decode_mma_kernel(const __grid_constant__ CUtensorMap kmap,
+__global__ void __launch_bounds__(kDecodeThreads, ROUTE ? 2 : 0) decode_mma_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                      const __grid_constant__ CUtensorMap vmap,
                                                                      const DecodeArgs a) {
   using S = DecodeSmem<D, STAGES>;
