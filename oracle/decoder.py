@@ -31,6 +31,9 @@ class OracleDecoder:
         self.k = [torch.zeros(batch, h, cfg.max_context, dh) for _ in range(cfg.layers)]
         self.v = [torch.zeros(batch, h, cfg.max_context, dh) for _ in range(cfg.layers)]
         self.ctx = 0
+        # per layer: fp32 summaries of the completed pages so far (a page's keys never change
+        # once it is complete, so each page is summarised once, with summaries_fp64's arithmetic)
+        self.summ = [torch.zeros(batch, h, 0, dh) for _ in range(cfg.layers)]
         self.pages = np.full((cfg.layers * batch, cfg.promo_slots), -1, np.int32)
         self.last = np.zeros((cfg.layers * batch, cfg.promo_slots), np.int32)
         self.step_index = 0
@@ -71,8 +74,11 @@ class OracleDecoder:
             self.v[i][:, :, pos] = v
             m = min(cfg.top_m, n)
             if m > 0:
-                summ, _ = summaries_fp64(self.k[i], p, n)
-                sel = select_blocks(q, summ, m, scale=1.0 / math.sqrt(dh))
+                have = self.summ[i].size(2)
+                if have < n:
+                    new_pages, _ = summaries_fp64(self.k[i][:, :, have * p:n * p], p, n - have)
+                    self.summ[i] = torch.cat((self.summ[i], new_pages), dim=2)
+                sel = select_blocks(q, self.summ[i][:, :, :n], m, scale=1.0 / math.sqrt(dh))
             else:
                 sel = torch.full((b, 1), -1, dtype=torch.int64)
             att = gather_decode(q, self.k[i][:, :, : pos + 1], self.v[i][:, :, : pos + 1], sel, local_window=win,

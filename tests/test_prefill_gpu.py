@@ -8,6 +8,7 @@ import torch
 
 import attention_b200 as spa
 import oracle
+from attention_b200 import workloads
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -69,3 +70,28 @@ def test_prefill_with_halo(dtype, halo):
     if halo >= window - 1:
         full = oracle.local_reference_chunked(q, k, v, window, chunk=512)[:, :, sl]
         assert_close(out, full, dtype)
+
+
+@pytest.mark.parametrize("seq", [4096, 16384, 32768, 131072, 262144])
+def test_prefill_benchmark_shapes_sampled_rows(seq):
+    """The benchmark's prefill shapes: batch 1, 32 heads, head_dim 128, bf16, window 2048,
+    S = 4k .. 256k.  Row blocks at the sequence start, around the window boundary, at a
+    128-row tile boundary in the middle, and the last rows of the sequence (the last work
+    items of the persistent scheduler: the last tile pairs of the last head) are compared
+    on every head with the chunked local_reference (fp64), within the bf16 tolerance."""
+    window, heads, dim = 2048, 32, 128
+    wl = workloads.local_prefill_workload(seq, heads=heads, head_dim=dim, seed=seq % 1000)
+    q, k, v = wl["q"], wl["k"], wl["v"]
+    out = spa.local_causal_prefill(q, k, v, window)
+    mid = (seq // 2) // 128 * 128
+    blocks = [(0, 160), (window - 96, window + 96), (mid - 64, mid + 64), (seq - 192, seq)]
+    for i0, i1 in blocks:
+        h0 = max(0, i0 - window + 1)
+        qc = q[:, :, i0:i1].cpu()
+        kc, vc = k[:, :, i0:i1].cpu(), v[:, :, i0:i1].cpu()
+        kh, vh = (k[:, :, h0:i0].cpu(), v[:, :, h0:i0].cpu()) if i0 > 0 else (None, None)
+        ref = oracle.local_reference_chunked(qc, kc, vc, window, chunk=64, k_halo=kh, v_halo=vh)
+        got = out[:, :, i0:i1].double().cpu()
+        err = (got - ref).abs()
+        assert (err <= 2e-2 + 1e-2 * ref.abs()).all(), (seq, i0, err.max().item())
+    assert spa.device_error_flags() == 0
