@@ -118,10 +118,13 @@ PROTOTYPES = {
     "spa_span_gather_decode": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp, _sz, _vp]),
     "spa_sparse_decode_step": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _d, _d, _vp,
                                     _vp, _vp, _sz, _vp]),
+    "spa_sparse_decode_step_chained": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _d,
+                                            _d, _vp, _vp, _vp, _sz, _vp]),
     "spa_sparse_decode_step_gated": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _d,
                                           _d, _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
     "spa_sparse_decode_step_heads": (_i, [_vp, _i, _i, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i,
                                           _i, _d, _d, _vp, _vp, _vp, _sz, _vp]),
+    "spa_sparse_step_launches": (_i, [_i, _i, _i, _i, _i, _i, _i, _i, _i, ctypes.POINTER(_i)]),
     "spa_set_step_fusion": (_i, [_i]),
     "spa_paged_decode_noalloc": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp]),
     "spa_kv_append": (_i, [_KV, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
@@ -131,8 +134,11 @@ PROTOTYPES = {
     "spa_add_rms_norm": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _d, _i, _vp]),
     "spa_embed_rms_norm": (_i, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i, _i, _d, _i, _vp]),
     "spa_linear": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "spa_linear_chained": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "spa_argmax_advance": (_i, [_vp, _i, _i, _vp, _vp, _i, _vp]),
     "spa_norm_linear": (_i, [_vp, ctypes.POINTER(NormPrologue), _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
+                             ctypes.POINTER(KvAppendEpilogue), _vp]),
+    "spa_norm_linear_chained": (_i, [_vp, ctypes.POINTER(NormPrologue), _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
                              ctypes.POINTER(KvAppendEpilogue), _vp]),
 }
 
@@ -171,6 +177,15 @@ def device_error_flags() -> int:
     v = ctypes.c_uint32(0)
     check(lib.spa_device_error(ctypes.byref(v)), "spa_device_error")
     return int(v.value)
+
+
+def sparse_step_launches(dtype: int, batch: int, q_heads: int, kv_heads: int, head_dim: int, *, kv_head_count: int = 0,
+                         local_window: int, page_size: int, top_m: int) -> int:
+    """Kernels one sparse decode step of this shape launches (1 fused, else 2 or 3)."""
+    n = ctypes.c_int()
+    check(lib.spa_sparse_step_launches(dtype, batch, q_heads, kv_heads, head_dim, kv_head_count, local_window,
+                                       page_size, top_m, ctypes.byref(n)), "spa_sparse_step_launches")
+    return n.value
 
 
 def decode_plan(batch: int, q_heads: int, kv_heads: int, max_candidates: int) -> tuple[int, bool]:

@@ -37,6 +37,9 @@ __global__ void __launch_bounds__(32) promotion_update_kernel(int32_t* __restric
                                                               int step_arg, const int32_t* __restrict__ step_dev,
                                                               int ttl) {
   extern __shared__ int64_t promo_smem[];  // sel [top_m], then pg [slots], lh [slots]
+  // launched as a programmatic dependent of the kernel before it: every read after it completes
+  pdl_trigger();
+  pdl_block();
   const int r = blockIdx.x, lane = threadIdx.x;
   if (r >= rows) return;
   const int step = step_dev ? *step_dev : step_arg;
@@ -149,8 +152,7 @@ extern "C" int spa_promotion_update(int32_t* pages, int32_t* last_hit, int rows,
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const size_t smem = sizeof(int64_t) * static_cast<size_t>(top_m) + sizeof(int32_t) * 2 * static_cast<size_t>(slots);
   SPA_CHECK_CUDA(spa_set_smem_once(spa::promotion_update_kernel, static_cast<int>(smem)));
-  spa::promotion_update_kernel<<<rows, 32, smem, st>>>(pages, last_hit, rows, slots, selected, top_m, step, step_dev,
-                                                      ttl);
-  SPA_CHECK_CUDA(cudaGetLastError());
+  SPA_CHECK_CUDA(spa::launch_ex(spa::promotion_update_kernel, dim3(rows), dim3(32), smem, st, true, 1, pages,
+                                 last_hit, rows, slots, selected, top_m, step, step_dev, ttl));
   return SPA_OK;
 }

@@ -144,22 +144,31 @@ __global__ void __launch_bounds__(kLinearWarps * 32) linear_rows_kernel(const T*
                                                                         const T* __restrict__ bias,
                                                                         void* __restrict__ out, int rows, int K,
                                                                         int N, int gelu, int out_f32, int vec,
-                                                                        const LinearPro pro, const LinearAppend app) {
+                                                                        int chained, const LinearPro pro,
+                                                                        const LinearAppend app) {
   extern __shared__ __align__(16) unsigned char linear_smem[];
   T* xs = reinterpret_cast<T*>(linear_smem);  // [rows][K]
   constexpr int kVec = 16 / sizeof(T);        // elements per 16-byte load
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x * kLinearWarps + warp;
   const T* wr = w + static_cast<int64_t>(n < N ? n : 0) * K;
-  // the first weight batch is requested before x is staged
+  // the first weight batch is requested before x is staged; chained (launched as a
+  // programmatic dependent of the kernel before it), before that kernel has completed too
+  // -- the weights are not its outputs -- and everything else after it has
   uint4 r[kLinearBatch];
-  if (vec && n < N) {
+  auto first_weights = [&] {
+    if (vec && n < N) {
 #pragma unroll
-    for (int u = 0; u < kLinearBatch; ++u) {
-      const int k = (lane + 32 * u) * kVec;
-      if (k < K) r[u] = __ldg(reinterpret_cast<const uint4*>(wr + k));
+      for (int u = 0; u < kLinearBatch; ++u) {
+        const int k = (lane + 32 * u) * kVec;
+        if (k < K) r[u] = __ldg(reinterpret_cast<const uint4*>(wr + k));
+      }
     }
-  }
+  };
+  pdl_trigger();
+  if (chained) first_weights();
+  pdl_block();
+  if (!chained) first_weights();
   const int total = rows * K;
   if (pro.norm_w) {
     __shared__ float part[kLinearMaxRows][kLinearWarps];
@@ -292,7 +301,7 @@ __global__ void __launch_bounds__(kLinearWarps * 32) linear_rows_kernel(const T*
 
 template <typename T>
 int launch_linear(const void* x, const void* w, const void* bias, void* out, int rows, int K, int N, int gelu,
-                  int out_f32, const LinearPro& pro, const LinearAppend& app, cudaStream_t st) {
+                  int out_f32, int chained, const LinearPro& pro, const LinearAppend& app, cudaStream_t st) {
   constexpr int kVec = 16 / sizeof(T);
   const size_t smem = static_cast<size_t>(rows) * K * sizeof(T);
   if (smem > 200 * 1024) return SPA_ERR_UNSUPPORTED;
@@ -301,10 +310,9 @@ int launch_linear(const void* x, const void* w, const void* bias, void* out, int
                   (pro.norm_w || reinterpret_cast<uintptr_t>(x) % 16 == 0);
   auto kern = linear_rows_kernel<T>;
   SPA_CHECK_CUDA(spa_set_smem_once(kern, static_cast<int>(smem)));
-  kern<<<(N + kLinearWarps - 1) / kLinearWarps, kLinearWarps * 32, smem, st>>>(
-      static_cast<const T*>(x), static_cast<const T*>(w), static_cast<const T*>(bias), out, rows, K, N, gelu, out_f32,
-      vec, pro, app);
-  SPA_CHECK_CUDA(cudaGetLastError());
+  SPA_CHECK_CUDA(launch_ex(kern, dim3((N + kLinearWarps - 1) / kLinearWarps), dim3(kLinearWarps * 32), smem, st,
+                           chained != 0, 1, static_cast<const T*>(x), static_cast<const T*>(w),
+                           static_cast<const T*>(bias), out, rows, K, N, gelu, out_f32, vec, chained, pro, app));
   return SPA_OK;
 }
 }  // namespace spa
@@ -347,6 +355,9 @@ __global__ void __launch_bounds__(256) argmax_advance_kernel(const float* __rest
                                                              int n_counters) {
   __shared__ float bv[8];
   __shared__ int bi[8];
+  // launched as a programmatic dependent of the kernel before it: every read after it completes
+  pdl_trigger();
+  pdl_block();
   const int row = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* lr = logits + static_cast<int64_t>(row) * cols;
   float v = -INFINITY;
@@ -390,16 +401,16 @@ extern "C" int spa_argmax_advance(const float* logits, int rows, int cols, int64
   if (rows < 0 || cols <= 0 || n_counters < 0 || (n_counters > 0 && !counters)) return SPA_ERR_INVALID;
   if (rows == 0) return SPA_OK;
   if (!logits || !token) return SPA_ERR_INVALID;
-  spa::argmax_advance_kernel<<<rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(logits, cols, token, counters,
-                                                                                       n_counters);
-  SPA_CHECK_CUDA(cudaGetLastError());
+  SPA_CHECK_CUDA(spa::launch_ex(spa::argmax_advance_kernel, dim3(rows), dim3(256), 0,
+                                 reinterpret_cast<cudaStream_t>(stream), true, 1, logits, cols, token, counters,
+                                 n_counters));
   return SPA_OK;
 }
 
 namespace spa {
 int linear_impl(const void* x, const void* weight, const void* bias, void* out, int rows, int in_features,
                 int out_features, int activation, int out_f32, int dtype, const LinearPro& pro,
-                const LinearAppend& app, spa_stream_t stream) {
+                const LinearAppend& app, spa_stream_t stream, int chained = 0) {
   if (rows < 0 || rows > kLinearMaxRows || in_features <= 0 || out_features <= 0 || !dtype_ok(dtype) ||
       (activation != 0 && activation != 1) || (out_f32 != 0 && out_f32 != 1))
     return SPA_ERR_INVALID;
@@ -407,13 +418,13 @@ int linear_impl(const void* x, const void* weight, const void* bias, void* out, 
   if (!x || !weight || !out) return SPA_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == SPA_F32)
-    return launch_linear<float>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, pro, app,
-                                st);
+    return launch_linear<float>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, chained, pro,
+                                app, st);
   if (dtype == SPA_F16)
-    return launch_linear<__half>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, pro, app,
-                                 st);
-  return launch_linear<__nv_bfloat16>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, pro,
-                                      app, st);
+    return launch_linear<__half>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, chained, pro,
+                                 app, st);
+  return launch_linear<__nv_bfloat16>(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, chained,
+                                      pro, app, st);
 }
 }  // namespace spa
 
@@ -425,9 +436,19 @@ extern "C" int spa_linear(const void* x, const void* weight, const void* bias, v
                           stream);
 }
 
-extern "C" int spa_norm_linear(const void* x, const spa_norm_prologue* norm, const void* weight, const void* bias,
-                               void* out, int rows, int in_features, int out_features, int activation, int out_f32,
-                               int dtype, const spa_kv_append_epilogue* append, spa_stream_t stream) {
+extern "C" int spa_linear_chained(const void* x, const void* weight, const void* bias, void* out, int rows,
+                                  int in_features, int out_features, int activation, int out_f32, int dtype,
+                                  spa_stream_t stream) {
+  const spa::LinearPro pro{};
+  const spa::LinearAppend app{};
+  return spa::linear_impl(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, dtype, pro, app,
+                          stream, 1);
+}
+
+namespace spa {
+int norm_linear_impl(const void* x, const spa_norm_prologue* norm, const void* weight, const void* bias, void* out,
+                     int rows, int in_features, int out_features, int activation, int out_f32, int dtype,
+                     const spa_kv_append_epilogue* append, spa_stream_t stream, int chained) {
   if (!norm || !norm->norm_weight) return SPA_ERR_INVALID;
   spa::LinearAppend app{};
   if (append) {
@@ -458,5 +479,21 @@ extern "C" int spa_norm_linear(const void* x, const spa_norm_prologue* norm, con
   pro.x_out = norm->x_out;
   pro.eps = static_cast<float>(norm->eps);
   return spa::linear_impl(x, weight, bias, out, rows, in_features, out_features, activation, out_f32, dtype, pro, app,
-                          stream);
+                          stream, chained);
+}
+}  // namespace spa
+
+extern "C" int spa_norm_linear(const void* x, const spa_norm_prologue* norm, const void* weight, const void* bias,
+                               void* out, int rows, int in_features, int out_features, int activation, int out_f32,
+                               int dtype, const spa_kv_append_epilogue* append, spa_stream_t stream) {
+  return spa::norm_linear_impl(x, norm, weight, bias, out, rows, in_features, out_features, activation, out_f32, dtype,
+                               append, stream, 0);
+}
+
+extern "C" int spa_norm_linear_chained(const void* x, const spa_norm_prologue* norm, const void* weight,
+                                       const void* bias, void* out, int rows, int in_features, int out_features,
+                                       int activation, int out_f32, int dtype, const spa_kv_append_epilogue* append,
+                                       spa_stream_t stream) {
+  return spa::norm_linear_impl(x, norm, weight, bias, out, rows, in_features, out_features, activation, out_f32, dtype,
+                               append, stream, 1);
 }

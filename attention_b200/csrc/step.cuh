@@ -23,6 +23,22 @@ inline int& step_fusion_mode() {
   return mode;
 }
 
+// Whether a step of this form runs as one launch (the route instantiation of the decode).
+inline bool step_fusable(bool fast, bool gated, bool router_copies_query, int kv_heads, int top_m) {
+  return step_fusion_mode() != 0 && fast && !gated && !router_copies_query && kv_heads <= kRouterKvBatch &&
+         top_m <= DecodeSmem<128, kDecodeStages>::kSelCap;
+}
+
+// The step's split plan: the decode's, except that a fused step whose pairs are too few for
+// the decode's cluster plan still takes clusters of kMaxClusterSplits splits (the routing
+// needs the splits of a pair in one cluster) when they fit on the GPU twice over.
+inline SplitPlan step_plan(int batch, int q_heads, int kv_heads, int max_cand, bool fusable) {
+  SplitPlan plan = decode_plan(batch, q_heads, kv_heads, max_cand);
+  if (fusable && !plan.cluster && static_cast<int64_t>(batch) * kv_heads * kMaxClusterSplits <= 2 * device_sm_count())
+    plan = {kMaxClusterSplits, true};
+  return plan;
+}
+
 // Router-side argument checks of a step (the ones router_tree_impl / router_topm_impl make).
 inline int step_route_checks(const void* q, int dtype, int batch, int q_heads, int kv_heads, int head_dim,
                              const float* super_summaries, int n_super, const float* summaries, int n_pages,
@@ -72,7 +88,13 @@ int sparse_step_impl(const void* q, int dtype, int batch, int q_heads, int kv_he
   a.top_m = top_m;
   a.span_len = 0;
   const int max_cand = local_window + top_m * kv->page_size;
-  const spa::SplitPlan plan = spa::decode_plan(batch, a.Hq, a.Hkv, max_cand);
+  const bool linear_rows = !kv->page_table && kv->page_stride_rows == kv->page_size;
+  const bool fast = dtype != SPA_F32 && (head_dim == 64 || head_dim == 128) && group <= 16 &&
+                    (kv->page_size % spa::kChunk == 0 || linear_rows) && kv->total_rows < (1ll << 31) &&
+                    reinterpret_cast<uintptr_t>(kv->k) % 16 == 0 && reinterpret_cast<uintptr_t>(kv->v) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(q) % 4 == 0;
+  const bool fusable = step_fusable(fast, gate != nullptr, q_copy != nullptr, kv_heads, top_m);
+  const spa::SplitPlan plan = step_plan(batch, a.Hq, a.Hkv, max_cand, fusable);
   a.nsplit = plan.nsplit;
   a.scale = static_cast<float>(attn_scale);
   a.scale_log2 = static_cast<float>(attn_scale * 1.4426950408889634);
@@ -84,18 +106,11 @@ int sparse_step_impl(const void* q, int dtype, int batch, int q_heads, int kv_he
     a.part_o = static_cast<float*>(workspace);
     a.part_lse = need ? a.part_o + static_cast<size_t>(batch) * a.Hq * a.nsplit * head_dim : nullptr;
   }
-  const bool linear_rows = !kv->page_table && kv->page_stride_rows == kv->page_size;
-  const bool fast = dtype != SPA_F32 && (head_dim == 64 || head_dim == 128) && group <= 16 &&
-                    (kv->page_size % spa::kChunk == 0 || linear_rows) && kv->total_rows < (1ll << 31) &&
-                    reinterpret_cast<uintptr_t>(kv->k) % 16 == 0 && reinterpret_cast<uintptr_t>(kv->v) % 16 == 0 &&
-                    reinterpret_cast<uintptr_t>(q) % 4 == 0;
   a.cluster_merge = fast && plan.cluster;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
   // ---- one launch: the decode clusters route their sequence themselves
-  const bool fusable = step_fusion_mode() != 0 && fast && plan.cluster && plan.nsplit >= 2 && !gate && !q_copy &&
-                       kv_heads <= kRouterKvBatch && top_m <= DecodeSmem<128, kDecodeStages>::kSelCap;
-  if (fusable) {
+  if (fusable && plan.cluster && plan.nsplit >= 2) {
     int rc = step_route_checks(q, dtype, batch, q_heads, kv_heads, head_dim, super_summaries, n_super, summaries,
                                n_pages, superblock, top_super, top_m);
     if (rc) return rc;
@@ -113,6 +128,9 @@ int sparse_step_impl(const void* q, int dtype, int batch, int q_heads, int kv_he
     a.route.scale = static_cast<float>(router_scale);
     a.route.selected = selected;
     a.route.selected_copy = selected_copy;
+    // with router_pdl (the session's copy-in precedes it) launched as that kernel's
+    // programmatic dependent; it waits for it before its first read either way.  Not by
+    // default: a step launched early behind a running step only holds SM slots there.
     if (dtype == SPA_F16)
       rc = head_dim == 128 ? launch_decode_mma<__half, 128, true>(*kv, dtype, a, st, router_pdl)
                            : launch_decode_mma<__half, 64, true>(*kv, dtype, a, st, router_pdl);
@@ -161,6 +179,19 @@ extern "C" int spa_sparse_decode_step(const void* q, int dtype, int batch, int q
                                stream);
 }
 
+extern "C" int spa_sparse_decode_step_chained(const void* q, int dtype, int batch, int q_heads, int kv_heads,
+                                              int head_dim, const spa_kv_layout* kv, const int32_t* context_lens,
+                                              int local_window, const float* super_summaries, int n_super,
+                                              const float* summaries, int n_pages, int superblock, int top_super,
+                                              int top_m, double router_scale, double attn_scale, int64_t* selected,
+                                              void* out, void* workspace, size_t workspace_bytes,
+                                              spa_stream_t stream) {
+  return spa::sparse_step_impl(q, dtype, batch, q_heads, kv_heads, head_dim, kv, context_lens, local_window,
+                               super_summaries, n_super, summaries, n_pages, superblock, top_super, top_m,
+                               router_scale, attn_scale, selected, out, workspace, workspace_bytes, nullptr, nullptr,
+                               stream, nullptr, nullptr, /*router_pdl=*/true);
+}
+
 extern "C" int spa_sparse_decode_step_gated(const void* q, int dtype, int batch, int q_heads, int kv_heads,
                                             int head_dim, const spa_kv_layout* kv, const int32_t* context_lens,
                                             int local_window, const float* super_summaries, int n_super,
@@ -187,6 +218,27 @@ extern "C" int spa_sparse_decode_step_heads(const void* q, int dtype, int batch,
                                super_summaries, n_super, summaries, n_pages, superblock, top_super, top_m,
                                router_scale, attn_scale, selected, out, workspace, workspace_bytes, nullptr, nullptr,
                                stream, nullptr, nullptr, false, kv_head_begin, kv_head_count);
+}
+
+extern "C" int spa_sparse_step_launches(int dtype, int batch, int q_heads, int kv_heads, int head_dim,
+                                        int kv_head_count, int local_window, int page_size, int top_m,
+                                        int* launches) {
+  if (!launches || batch <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads || page_size <= 0 ||
+      top_m <= 0 || local_window < 0)
+    return SPA_ERR_INVALID;
+  if (kv_head_count <= 0) kv_head_count = kv_heads;
+  const int group = q_heads / kv_heads;
+  const int hq = kv_head_count * group;
+  const bool fast = dtype != SPA_F32 && (head_dim == 64 || head_dim == 128) && group <= 16 &&
+                    page_size % spa::kChunk == 0;
+  const bool fusable = spa::step_fusable(fast, false, false, kv_heads, top_m);
+  const spa::SplitPlan plan =
+      spa::step_plan(batch, hq, kv_head_count, local_window + top_m * page_size, fusable);
+  if (fusable && plan.cluster && plan.nsplit >= 2)
+    *launches = 1;  // one kernel: routing + decode
+  else
+    *launches = 2 + ((fast && plan.cluster) || plan.nsplit <= 1 ? 0 : 1);  // router, decode (+ split merge)
+  return SPA_OK;
 }
 
 extern "C" int spa_set_step_fusion(int mode) {

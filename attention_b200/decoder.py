@@ -120,10 +120,12 @@ LINEAR_MAX_ROWS = 4
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *, gelu: bool = False,
-           out: torch.Tensor | None = None) -> torch.Tensor:
+           out: torch.Tensor | None = None, chained: bool = False) -> torch.Tensor:
     """``F.linear`` (then exact GELU when ``gelu``) for 1..4 rows in one launch
     (``spa_linear``): fp32 products and sums, rounded to x's dtype.  ``out`` may be an fp32
-    tensor, which then holds the rounded values."""
+    tensor, which then holds the rounded values.  ``chained``: ``spa_linear_chained``, which
+    streams the weight rows while the kernel enqueued before it still runs (the weights
+    must not be that kernel's outputs)."""
     if not (x.is_cuda and weight.is_cuda and (bias is None or bias.is_cuda)):
         raise ValueError("CUDA tensors are required")
     if x.dim() != 2 or not 0 < x.size(0) <= LINEAR_MAX_ROWS:
@@ -137,10 +139,10 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
         out = torch.empty(x.size(0), n, dtype=x.dtype, device=x.device)
     elif out.shape != (x.size(0), n) or out.dtype not in (x.dtype, torch.float32) or not out.is_contiguous():
         raise ValueError("out must be a contiguous [rows, out_features] tensor of x's dtype or fp32")
-    _lib.check(_lib.lib.spa_linear(x.data_ptr(), weight.data_ptr(), bias.data_ptr() if bias is not None else None,
-                                   out.data_ptr(), x.size(0), k, n, 1 if gelu else 0,
-                                   1 if out.dtype != x.dtype else 0, dtype_code(x), stream_ptr(x.device)),
-               "spa_linear")
+    fn = _lib.lib.spa_linear_chained if chained else _lib.lib.spa_linear
+    _lib.check(fn(x.data_ptr(), weight.data_ptr(), bias.data_ptr() if bias is not None else None, out.data_ptr(),
+                  x.size(0), k, n, 1 if gelu else 0, 1 if out.dtype != x.dtype else 0, dtype_code(x),
+                  stream_ptr(x.device)), "spa_linear")
     return out
 
 
@@ -148,7 +150,7 @@ def norm_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
                 norm_weight: torch.Tensor, eps: float, delta: torch.Tensor | None = None,
                 x_out: torch.Tensor | None = None, ids: torch.Tensor | None = None,
                 positions: torch.Tensor | None = None, gelu: bool = False,
-                out: torch.Tensor | None = None, append: tuple | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, append: tuple | None = None, chained: bool = False) -> torch.Tensor:
     """``linear(rms_norm(x (+ delta)), weight, bias)`` for 1..4 rows in one launch
     (``spa_norm_linear``); the normalised rows are bit-identical to ``add_rms_norm`` /
     ``rms_norm``.  With ``ids`` (int64) and ``positions`` (int32), ``x`` and ``delta`` are
@@ -156,7 +158,8 @@ def norm_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
     ``embed_rms_norm``.  ``x_out`` (optional) receives the summed rows and must be a
     separate buffer from ``x`` and ``delta``.  ``append = (k_pool, v_pool, page_table,
     positions, k_col, v_col)`` also stores output columns ``[k_col, k_col + Hkv*D)`` and
-    ``[v_col, ...)`` of row m as batch row m's new K and V, as ``kv_append`` would."""
+    ``[v_col, ...)`` of row m as batch row m's new K and V, as ``kv_append`` would.
+    ``chained``: ``spa_norm_linear_chained`` (see ``linear``)."""
     tensors = [x, weight, norm_weight] + [t for t in (bias, delta, x_out, ids, positions, out) if t is not None]
     if not all(t.is_cuda for t in tensors):
         raise ValueError("CUDA tensors are required")
@@ -208,11 +211,10 @@ def norm_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
     pro.norm_weight = nw.data_ptr()
     pro.eps = float(eps)
     pro.x_out = x_out.data_ptr() if x_out is not None else None
-    _lib.check(_lib.lib.spa_norm_linear(x.data_ptr(), ctypes.byref(pro), weight.data_ptr(),
-                                        bias.data_ptr() if bias is not None else None, out.data_ptr(), rows, k, n,
-                                        1 if gelu else 0, 1 if out.dtype != x.dtype else 0, dtype_code(x),
-                                        ctypes.byref(epi) if epi is not None else None, stream_ptr(x.device)),
-               "spa_norm_linear")
+    fn = _lib.lib.spa_norm_linear_chained if chained else _lib.lib.spa_norm_linear
+    _lib.check(fn(x.data_ptr(), ctypes.byref(pro), weight.data_ptr(), bias.data_ptr() if bias is not None else None,
+                  out.data_ptr(), rows, k, n, 1 if gelu else 0, 1 if out.dtype != x.dtype else 0, dtype_code(x),
+                  ctypes.byref(epi) if epi is not None else None, stream_ptr(x.device)), "spa_norm_linear")
     return out
 
 
@@ -281,10 +283,10 @@ class SparseDecoder:
         self.step_index = 0
 
     # ---------------------------------------------------------------- helpers
-    def _linear(self, x, name, *, gelu=False):
+    def _linear(self, x, name, *, gelu=False, chained=False):
         w, b = self.w[f"{name}.w"], self.w[f"{name}.b"]
         if x.dim() == 2 and x.size(0) <= LINEAR_MAX_ROWS:
-            return linear(x, w, b, gelu=gelu)  # decode: a few rows, one launch
+            return linear(x, w, b, gelu=gelu, chained=chained)  # decode: a few rows, one launch
         y = F.linear(x, w, b)
         return F.gelu(y) if gelu else y
 
@@ -364,21 +366,23 @@ class SparseDecoder:
             self._sel_bufs: dict = {}  # [layers, B, m] selections, per m
             self._graphs: dict = {}
 
-    def _norm_linear(self, x, delta, norm, name, x_out, *, gelu=False, append=None):
+    def _norm_linear(self, x, delta, norm, name, x_out, *, gelu=False, append=None, chained=False):
         """x_out = x + delta; returns the linear layer ``name`` of rms_norm(x_out): one
         launch for a batch of up to four rows (with the K/V append when given), else the
         norm and a library GEMM (the caller then appends)."""
         w, b = self.w[f"{name}.w"], self.w[f"{name}.b"]
         if self.batch <= LINEAR_MAX_ROWS:
             return norm_linear(x, w, b, norm_weight=self.w[norm], eps=self.cfg.eps, delta=delta, x_out=x_out,
-                               gelu=gelu, append=append)
+                               gelu=gelu, append=append, chained=chained)
         return self._linear(add_rms_norm(x, delta, self.w[norm], self.cfg.eps, x_out=x_out), name, gelu=gelu)
 
     def _step_body(self):
         """One decode step on the persistent state (no host synchronisation, capturable).
         Each RMSNorm runs fused into the linear layer after it, together with the residual
         add before it (the embedding lookup for the first); the rounding is that of the
-        separate ops."""
+        separate ops.  Every kernel of the step is launched as a programmatic dependent of
+        the one before it: it starts while its predecessor runs (the linear layers stream
+        their weight rows then) and reads its other inputs after the predecessor completes."""
         cfg = self.cfg
         b = self.batch
         h, dh = cfg.heads, cfg.head_dim
@@ -392,7 +396,7 @@ class SparseDecoder:
         if fused:
             qkv = norm_linear(self.w["emb"], self.w["l0.qkv.w"], self.w["l0.qkv.b"], norm_weight=self.w["l0.norm1"],
                               eps=cfg.eps, delta=self.w["pos"], ids=self._token, positions=self._position, x_out=x,
-                              append=append(0))
+                              append=append(0), chained=True)
         else:
             hid = embed_rms_norm(self.w["emb"], self._token, self.w["pos"], self._position, self.w["l0.norm1"],
                                  cfg.eps, x_out=x)
@@ -407,7 +411,7 @@ class SparseDecoder:
         mlp_out = None
         for i in range(cfg.layers):
             if i > 0:
-                qkv = self._norm_linear(x, mlp_out, f"l{i}.norm1", f"l{i}.qkv", spare, append=append(i))
+                qkv = self._norm_linear(x, mlp_out, f"l{i}.norm1", f"l{i}.qkv", spare, append=append(i), chained=True)
                 x, spare = spare, x
             qkv = qkv.view(b, 3, h, dh)
             q = qkv[:, 0].contiguous()
@@ -419,23 +423,24 @@ class SparseDecoder:
                 att, sel = sparse_decode_step(q, self.k_pool[i], self.v_pool[i], self.summaries[i], top_blocks=m,
                                               local_window=cfg.local_window, block_size=cfg.page_size,
                                               router_scale=scale, page_table=self.page_table,
-                                              context_lens=self._ctx_len, selected=sel_all[i])
+                                              context_lens=self._ctx_len, selected=sel_all[i], chained=True)
             else:
                 sel = torch.full((b, 1), -1, dtype=torch.int64, device=self.device)
                 att = paged_gather_decode_attention(q, self.k_pool[i], self.v_pool[i], sel,
                                                     local_window=cfg.local_window, block_size=cfg.page_size,
                                                     page_table=self.page_table, context_lens=self._ctx_len)
-            o = self._linear(att.reshape(b, cfg.d_model), f"l{i}.out")
-            hid = self._norm_linear(x, o, f"l{i}.norm2", f"l{i}.fc1", spare, gelu=True)
+            o = self._linear(att.reshape(b, cfg.d_model), f"l{i}.out", chained=True)
+            hid = self._norm_linear(x, o, f"l{i}.norm2", f"l{i}.fc1", spare, gelu=True, chained=True)
             x, spare = spare, x
-            mlp_out = self._linear(hid, f"l{i}.fc2")
+            mlp_out = self._linear(hid, f"l{i}.fc2", chained=True)
             selected.append(sel)
         if m == 0:
             sel_all = torch.stack(selected)  # [layers, B, 1]
         self.promotion.update(sel_all.reshape(cfg.layers * b, -1), self._step_dev)
         if b <= LINEAR_MAX_ROWS:
             # fp32 logits of the rounded products
-            norm_linear(x, self.w["head"], norm_weight=self.w["norm_f"], eps=cfg.eps, delta=mlp_out, out=self._logits)
+            norm_linear(x, self.w["head"], norm_weight=self.w["norm_f"], eps=cfg.eps, delta=mlp_out, out=self._logits,
+                        chained=True)
         else:
             hf = add_rms_norm(x, mlp_out, self.w["norm_f"], cfg.eps, x_out=spare)
             self._logits.copy_(F.linear(hf, self.w["head"]))

@@ -129,11 +129,13 @@ def sparse_decode_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Te
                        router_scale: float = 1.0, page_table: torch.Tensor | None = None,
                        context_lens: torch.Tensor | None = None, out: torch.Tensor | None = None,
                        selected: torch.Tensor | None = None, gate=None,
-                       kv_head_range: tuple[int, int] | None = None):
+                       kv_head_range: tuple[int, int] | None = None, chained: bool = False):
     """``kv_head_range=(begin, count)``: one rank's (sequence, kv head) shard -- query and
     summaries hold every head of the sequences, keys/values only kv heads
     [begin, begin + count) of a page pool, and the output those kv heads' query heads.
-    Every shard of a sequence selects the same pages."""
+    Every shard of a sequence selects the same pages.  ``chained``: the step's first
+    kernel launches as a programmatic dependent of the kernel before it
+    (``spa_sparse_decode_step_chained``; a model's decode step)."""
     if not query.is_cuda:
         raise ValueError("CUDA tensors are required")
     if kv_head_range is not None:
@@ -164,7 +166,8 @@ def sparse_decode_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Te
         rc = _lib.lib.spa_sparse_decode_step_gated(*args, gate.flags.data_ptr(), promoted.data_ptr(), stream_ptr(dev))
         _lib.check(rc, "spa_sparse_decode_step_gated")
     else:
-        rc = _lib.lib.spa_sparse_decode_step(*args, stream_ptr(dev))
+        fn = _lib.lib.spa_sparse_decode_step_chained if chained else _lib.lib.spa_sparse_decode_step
+        rc = fn(*args, stream_ptr(dev))
         _lib.check(rc, "spa_sparse_decode_step")
     return out, selected
 

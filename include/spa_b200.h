@@ -246,6 +246,24 @@ int spa_sparse_decode_step(const void* q, int dtype, int batch, int q_heads,
                            spa_stream_t stream);
 
 /*
+ * spa_sparse_decode_step for a chain of dependent launches (a model's decode step): the
+ * first kernel is launched as a programmatic dependent of the kernel enqueued before it
+ * and waits for that kernel to complete before its first read, so it is resident and
+ * ready when its inputs are; kernels enqueued after it as programmatic dependents may
+ * start while it runs.  Same arguments and results as spa_sparse_decode_step.  No
+ * counterpart in the reference.
+ */
+int spa_sparse_decode_step_chained(const void* q, int dtype, int batch, int q_heads,
+                                   int kv_heads, int head_dim, const spa_kv_layout* kv,
+                                   const int32_t* context_lens, int local_window,
+                                   const float* super_summaries, int n_super,
+                                   const float* summaries, int n_pages, int superblock,
+                                   int top_super, int top_m, double router_scale,
+                                   double attn_scale, int64_t* selected, void* out,
+                                   void* workspace, size_t workspace_bytes,
+                                   spa_stream_t stream);
+
+/*
  * spa_sparse_decode_step over a kv-head slice: one rank's (sequence, kv head)
  * shard of a decode batch.  q [B, q_heads, D] holds every query head of each
  * sequence and the summaries every one of the kv_heads kv heads (the router scores
@@ -268,6 +286,17 @@ int spa_sparse_decode_step_heads(const void* q, int dtype, int batch, int q_head
                                  double router_scale, double attn_scale,
                                  int64_t* selected, void* out, void* workspace,
                                  size_t workspace_bytes, spa_stream_t stream);
+
+/*
+ * Kernel launches one spa_sparse_decode_step (or _heads with kv_head_count kv
+ * heads; <= 0: all) of this shape enqueues, with the current fusion mode and a
+ * page-pool layout whose page size is page_size: 1 (the single routing +
+ * decode kernel), 2 (router, decode) or 3 (router, decode, split merge).
+ * No counterpart in the reference (lets a caller count kernels per step).
+ */
+int spa_sparse_step_launches(int dtype, int batch, int q_heads, int kv_heads,
+                             int head_dim, int kv_head_count, int local_window,
+                             int page_size, int top_m, int* launches);
 
 /*
  * Step fusion switch for the library (process-wide): 1 (default) runs the steps
@@ -572,6 +601,23 @@ typedef struct spa_kv_append_epilogue {
 int spa_norm_linear(const void* x, const spa_norm_prologue* norm, const void* weight, const void* bias, void* out,
                     int rows, int in_features, int out_features, int activation, int out_f32, int dtype,
                     const spa_kv_append_epilogue* append, spa_stream_t stream);
+
+/*
+ * spa_linear / spa_norm_linear for a chain of dependent launches (a decode step): the
+ * kernel is launched as a programmatic dependent of the kernel enqueued before it on the
+ * stream and starts streaming its weight rows while that kernel still runs; every other
+ * input is read, and every output written, only after that kernel has completed.  The
+ * caller guarantees that weight, bias and the norm weight are not written by the kernel
+ * enqueued immediately before (model weights during inference).  Same arguments and
+ * results as the unchained forms.  No counterpart in the reference (its decode step is a
+ * sequence of PyTorch calls).
+ */
+int spa_linear_chained(const void* x, const void* weight, const void* bias, void* out, int rows,
+                       int in_features, int out_features, int activation, int out_f32, int dtype,
+                       spa_stream_t stream);
+int spa_norm_linear_chained(const void* x, const spa_norm_prologue* norm, const void* weight, const void* bias,
+                            void* out, int rows, int in_features, int out_features, int activation, int out_f32,
+                            int dtype, const spa_kv_append_epilogue* append, spa_stream_t stream);
 
 /*
  * Diagnostic for the failure path: one kernel waits on an mbarrier that nothing
