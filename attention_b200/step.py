@@ -19,6 +19,7 @@ triton_promotion_cache_benchmark.py:53-60).
 from __future__ import annotations
 
 import ctypes
+import weakref
 
 import torch
 
@@ -67,6 +68,53 @@ def _prepare_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
     ws = workspace(dev, ws_bytes) if ws_bytes else None
     return dict(dev=dev, batch=batch, q_heads=q_heads, kv_heads=kv_heads, head_dim=head_dim, layout=layout,
                 lens=lens, summ=summ, sup=sup, ws=ws, ws_bytes=ws_bytes, dtype=dtype_code(query))
+
+
+# Prepared C arguments of recent step forms, keyed by the identity of the borrowed tensors,
+# the query's shape and dtype, the step parameters and the stream.  An entry is kept only
+# when validation borrowed the caller's tensors as they are (fp32 summaries, int32 table and
+# lengths: nothing converted, so nothing cached can go stale).  It holds weak references, so
+# it keeps no memory alive; a hit requires every referenced tensor to be the same live
+# object with the same storage address (a tensor re-pointed in place is prepared again).
+_STEP_CACHE: dict = {}
+_STEP_CACHE_MAX = 32
+
+
+def _prepared_step(query, keys, values, summaries, *, top_blocks, local_window, block_size, super_summaries,
+                   superblock, top_super, page_table, context_lens, router_scale, stream):
+    """The step's C arguments except the query, selection and output pointers:
+    (head, tail, dtype/batch info), from the cache when the same tensors and parameters
+    were prepared before."""
+    held = (keys, values, summaries, super_summaries, page_table, context_lens)
+    key = (query.shape, query.dtype, query.device, tuple(id(t) for t in held), top_blocks, local_window,
+           block_size, superblock, top_super, float(router_scale), stream)
+    hit = _STEP_CACHE.get(key)
+    if hit is not None and all(
+            (r is None and t is None) or (r is not None and r() is t and t.data_ptr() == ptr)
+            for r, t, ptr in zip(hit["refs"], held, hit["ptrs"])):
+        return hit
+    if not query.is_cuda:
+        raise ValueError("CUDA tensors are required")
+    pr = _prepare_step(query, keys, values, summaries, top_blocks=top_blocks, local_window=local_window,
+                       block_size=block_size, super_summaries=super_summaries, superblock=superblock,
+                       top_super=top_super, page_table=page_table, context_lens=context_lens)
+    sup, ws = pr["sup"], pr["ws"]
+    head = (pr["dtype"], pr["batch"], pr["q_heads"], pr["kv_heads"], pr["head_dim"], ctypes.byref(pr["layout"]),
+            pr["lens"].data_ptr(), local_window, sup.data_ptr() if sup is not None else None,
+            sup.size(2) if sup is not None else 0, pr["summ"].data_ptr(), pr["summ"].size(2), superblock, top_super,
+            top_blocks, float(router_scale), pr["head_dim"] ** -0.5)
+    tail = (ws.data_ptr() if ws is not None else None, pr["ws_bytes"])
+    prep = {"head": head, "tail": tail, "batch": pr["batch"], "dev": pr["dev"], "pr": pr}
+    borrowed = pr["summ"] is summaries and (super_summaries is None or sup is super_summaries) and (
+        page_table is None or (pr["lens"] is context_lens and pr["layout"].page_table == page_table.data_ptr()
+                               and page_table.dtype == torch.int32))
+    if borrowed:
+        prep["refs"] = [weakref.ref(t) if t is not None else None for t in held]
+        prep["ptrs"] = [t.data_ptr() if t is not None else 0 for t in held]
+        if len(_STEP_CACHE) >= _STEP_CACHE_MAX:
+            _STEP_CACHE.pop(next(iter(_STEP_CACHE)))
+        _STEP_CACHE[key] = prep
+    return prep
 
 
 def set_step_fusion(enabled: bool) -> bool:
@@ -147,27 +195,27 @@ def sparse_decode_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Te
                                          top_super=top_super, router_scale=router_scale, page_table=page_table,
                                          context_lens=context_lens, out=out, selected=selected,
                                          kv_head_range=kv_head_range)
-    pr = _prepare_step(query, keys, values, summaries, top_blocks=top_blocks, local_window=local_window,
-                       block_size=block_size, super_summaries=super_summaries, superblock=superblock,
-                       top_super=top_super, page_table=page_table, context_lens=context_lens)
-    dev, sup, ws = pr["dev"], pr["sup"], pr["ws"]
+    if not query.is_contiguous():
+        raise ValueError("contiguous CUDA tensors are required")
+    dev = query.device
+    stream = stream_ptr(dev)
+    prep = _prepared_step(query, keys, values, summaries, top_blocks=top_blocks, local_window=local_window,
+                          block_size=block_size, super_summaries=super_summaries, superblock=superblock,
+                          top_super=top_super, page_table=page_table, context_lens=context_lens,
+                          router_scale=router_scale, stream=stream)
     if out is None:
         out = torch.empty_like(query)
     if selected is None:
-        selected = torch.empty(pr["batch"], top_blocks, dtype=torch.int64, device=dev)
-    args = (query.data_ptr(), pr["dtype"], pr["batch"], pr["q_heads"], pr["kv_heads"], pr["head_dim"],
-            ctypes.byref(pr["layout"]), pr["lens"].data_ptr(), local_window,
-            sup.data_ptr() if sup is not None else None, sup.size(2) if sup is not None else 0,
-            pr["summ"].data_ptr(), pr["summ"].size(2), superblock, top_super, top_blocks, float(router_scale),
-            pr["head_dim"] ** -0.5, selected.data_ptr(), out.data_ptr(), ws.data_ptr() if ws is not None else None,
-            pr["ws_bytes"])
+        selected = torch.empty(prep["batch"], top_blocks, dtype=torch.int64, device=dev)
+    args = (query.data_ptr(),) + prep["head"] + (selected.data_ptr(), out.data_ptr()) + prep["tail"]
     if gate is not None:
+        pr = prep["pr"]
         promoted = gate.promoted_for(pr["batch"], top_blocks)
-        rc = _lib.lib.spa_sparse_decode_step_gated(*args, gate.flags.data_ptr(), promoted.data_ptr(), stream_ptr(dev))
+        rc = _lib.lib.spa_sparse_decode_step_gated(*args, gate.flags.data_ptr(), promoted.data_ptr(), stream)
         _lib.check(rc, "spa_sparse_decode_step_gated")
     else:
         fn = _lib.lib.spa_sparse_decode_step_chained if chained else _lib.lib.spa_sparse_decode_step
-        rc = fn(*args, stream_ptr(dev))
+        rc = fn(*args, stream)
         _lib.check(rc, "spa_sparse_decode_step")
     return out, selected
 

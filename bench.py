@@ -276,20 +276,16 @@ class SparseShardInputs:
 def make_step(spa, cfg, x: SparseShardInputs, g: int, m: int, out, sel):
     """One sparse step of batch group g for this rank (m selected pages)."""
     scale = cfg.head_dim ** -0.5
-    kw = dict(local_window=cfg.local_window, block_size=cfg.page_size, page_table=x.table[g], context_lens=x.ctx)
-    if x.shard.full_heads:
-        def step():
-            spa.sparse_decode_step(x.q_rows[g], x.k_pool, x.v_pool, x.summ[g], super_summaries=x.sup[g],
-                                   superblock=cfg.superblock, top_super=cfg.top_super, top_blocks=m,
-                                   router_scale=scale, out=out, selected=sel, **kw)
-    else:
-        # a kv-head group of one sequence: route over all of the sequence's heads, then
-        # decode this rank's kv heads
-        def step():
-            s = spa.select_blocks_tree(x.q_rows[g], x.sup[g], x.summ[g], superblock=cfg.superblock,
-                                       top_super=cfg.top_super, top_blocks=m, scale=scale)
-            sel.copy_(s)
-            out.copy_(spa.paged_gather_decode_attention(x.q_local[g], x.k_pool, x.v_pool, sel, **kw))
+    # a kv-head group of one sequence: routed over all of the sequence's heads, decoded over
+    # this rank's kv heads (kv_head_range)
+    rng = None if x.shard.full_heads else (x.shard.kv.start, x.shard.kv.stop - x.shard.kv.start)
+
+    def step():
+        spa.sparse_decode_step(x.q_rows[g], x.k_pool, x.v_pool, x.summ[g], super_summaries=x.sup[g],
+                               superblock=cfg.superblock, top_super=cfg.top_super, top_blocks=m,
+                               router_scale=scale, out=out, selected=sel, local_window=cfg.local_window,
+                               block_size=cfg.page_size, page_table=x.table[g], context_lens=x.ctx,
+                               kv_head_range=rng)
     return step
 
 
@@ -408,13 +404,16 @@ def run_ours(args, world, rank, local):
     if not args.skip_dense:
         dense = run_dense(args, world, rank, dev, peaks)
 
-    # kernels per step: the router, then the decode (plus a merge kernel when its splits
-    # do not merge on chip)
+    # kernels per step as the library dispatches this shape: 1 (routing inside the decode
+    # kernel), else the router, the decode and, when its splits do not merge on chip, a merge
+    launches_per_step = spa._lib.sparse_step_launches(
+        spa._lib.SPA_BF16, x.n_rows, cfg.q_heads, cfg.kv_heads, cfg.head_dim,
+        kv_head_count=x.shard.kv.stop - x.shard.kv.start, local_window=cfg.local_window, page_size=cfg.page_size,
+        top_m=m0)
     nsplit, on_chip = spa._lib.decode_plan(x.n_rows, local_q_heads, x.shard.kv.stop - x.shard.kv.start,
                                            cfg.local_window + m0 * cfg.page_size)
     merged = nsplit == 1 or on_chip
     decode_kernels = "decode_mma_kernel" if merged else "decode_mma_kernel + decode_combine_kernel"
-    launches_per_step = 2 + (0 if merged else 1)
     result = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -448,6 +447,8 @@ def run_ours(args, world, rank, local):
         "integrated_decode": integrated,
         "clocks": clocks.summary(),
         "gpu_launches": steps * launches_per_step,
+        "step_kernels": "decode_mma_kernel (route instantiation: routing + gather decode in one launch)"
+                        if launches_per_step == 1 else "router_cluster_kernel + " + decode_kernels,
     }
     if rank == 0:
         print(json.dumps(result))
@@ -492,6 +493,25 @@ def run_e2e(spa, cfg, x, groups, world, bytes_step, steps, args):
                 hq.copy_(host_q[g])
         e_ms = timed(lambda g: sessions[g].step())
         s_ms = timed(lambda g: sessions[g].step(), sync_each=True)
+        # the per-call API: copies and one sparse_decode_step call per step from Python
+        dq = [torch.empty_like(x.q_rows[g]) for g in range(groups)]
+        host_out = [torch.empty_like(host_q[g]).pin_memory() for g in range(groups)]
+        host_sel = [torch.empty(x.n_rows, cfg.top_m, dtype=torch.int64).pin_memory() for g in range(groups)]
+
+        dev_out = [torch.empty_like(x.q_rows[g]) for g in range(groups)]
+        dev_sel = [torch.empty(x.n_rows, cfg.top_m, dtype=torch.int64, device=x.q_rows[g].device)
+                   for g in range(groups)]
+
+        def per_call(g):  # a serving loop's buffers are allocated once
+            dq[g].copy_(host_q[g], non_blocking=True)
+            spa.sparse_decode_step(dq[g], x.k_pool, x.v_pool, x.summ[g], super_summaries=x.sup[g],
+                                   superblock=cfg.superblock, top_super=cfg.top_super, top_blocks=cfg.top_m,
+                                   local_window=cfg.local_window, block_size=cfg.page_size, router_scale=scale,
+                                   page_table=x.table[g], context_lens=x.ctx, out=dev_out[g], selected=dev_sel[g])
+            host_out[g].copy_(dev_out[g], non_blocking=True)
+            host_sel[g].copy_(dev_sel[g], non_blocking=True)
+
+        c_ms = timed(per_call)
         res.update(value=round(bytes_step * e2e_steps / (e_ms * 1e-3) / 1e9, 2),
                    us_per_step=round(e_ms * 1e3 / e2e_steps, 3),
                    path="attention_b200.SparseDecodeSession.step: one call into the native session (C ABI "
@@ -499,6 +519,12 @@ def run_e2e(spa, cfg, x, groups, world, bytes_step, steps, args):
                         "brings the step's query from pinned mapped host memory into device memory, the router "
                         "and the gather decode run, and a copy kernel (spa_copy) writes output + page ids into "
                         "pinned host memory; the host may enqueue one step ahead (two buffer slots)",
+                   per_call_api={"us_per_step": round(c_ms * 1e3 / e2e_steps, 3),
+                                 "value": round(bytes_step * e2e_steps / (c_ms * 1e-3) / 1e9, 2),
+                                 "path": "attention_b200.sparse_decode_step called from Python every step, with a "
+                                         "torch host->device copy of the query and device->host copies of output "
+                                         "and page ids into buffers allocated once (prepared arguments cached per "
+                                         "pool and summaries)"},
                    per_step_sync={"us_per_step": round(s_ms * 1e3 / e2e_steps, 3),
                                   "value": round(bytes_step * e2e_steps / (s_ms * 1e-3) / 1e9, 2),
                                   "path": "the same session step, followed every step by a host "
@@ -514,12 +540,12 @@ def run_e2e(spa, cfg, x, groups, world, bytes_step, steps, args):
 
         def call(g):
             dq[g].copy_(host_q[g], non_blocking=True)
-            sel = spa.select_blocks_tree(dq[g], x.sup[g], x.summ[g], superblock=cfg.superblock,
-                                         top_super=cfg.top_super, top_blocks=cfg.top_m, scale=scale)
-            ql = dq[g][:, x.shard.q_heads]
-            out = spa.paged_gather_decode_attention(ql.contiguous(), x.k_pool, x.v_pool, sel,
-                                                    local_window=cfg.local_window, block_size=cfg.page_size,
-                                                    page_table=x.table[g], context_lens=x.ctx)
+            out, sel = spa.sparse_decode_step(dq[g], x.k_pool, x.v_pool, x.summ[g], super_summaries=x.sup[g],
+                                              superblock=cfg.superblock, top_super=cfg.top_super,
+                                              top_blocks=cfg.top_m, local_window=cfg.local_window,
+                                              block_size=cfg.page_size, router_scale=scale,
+                                              page_table=x.table[g], context_lens=x.ctx,
+                                              kv_head_range=(x.shard.kv.start, x.shard.kv.stop - x.shard.kv.start))
             host_out[g].copy_(out, non_blocking=True)
             host_sel[g].copy_(sel, non_blocking=True)
 
@@ -527,8 +553,8 @@ def run_e2e(spa, cfg, x, groups, world, bytes_step, steps, args):
         res.update(value=round(bytes_step * e2e_steps / (e_ms * 1e-3) / 1e9, 2),
                    us_per_step=round(e_ms * 1e3 / e2e_steps, 3),
                    path="per call from Python: host->device copy of the sequences' query rows, "
-                        "select_blocks_tree over all heads, paged_gather_decode_attention over this rank's "
-                        "kv heads, device->host copies of output and page ids")
+                        "sparse_decode_step over this rank's kv heads (routed over all heads), device->host "
+                        "copies of output and page ids")
     return res
 
 
@@ -827,6 +853,14 @@ def run_reference(args, world, rank, local):
     if rank != 0:
         return
     import oracle
+
+    # every host core for the one rank that runs (torchrun sets one thread per process)
+    try:
+        import psutil
+
+        torch.set_num_threads(psutil.cpu_count(logical=False) or os.cpu_count() or 1)
+    except Exception:
+        torch.set_num_threads(os.cpu_count() or 1)
 
     wk = load_workloads()
     cfg = wk.SparseDecodeConfig(top_m=args.top_m)

@@ -136,12 +136,14 @@ def test_fused_step_decoder_shape():
     assert _close(out_f, oracle.gather_decode(q, k, v, exp, local_window=win, block_size=page))
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_kv_head_shards_assemble_the_full_step(world):
+@pytest.mark.parametrize("world,m,pages", [(2, 4, 128), (4, 4, 128), (8, 4, 128), (2, 8, 512), (8, 2, 512)])
+def test_kv_head_shards_assemble_the_full_step(world, m, pages):
     """The 128k batch split into (sequence, kv head) shards as on `world` GPUs, run here
     one shard after another: each shard's pages equal the full step's for its
-    sequences, and the assembled outputs match the full step within tolerance."""
-    cfg = workloads.SparseDecodeConfig(top_m=4, pages_per_seq=128)
+    sequences, and the assembled outputs match the full step within tolerance.  (Two
+    sequences per shard at m = 8: fewer pairs than the decode's cluster plan wants, so the
+    one-launch step takes clusters of 8 splits anyway.)"""
+    cfg = workloads.SparseDecodeConfig(top_m=m, pages_per_seq=pages)
     wl = workloads.sparse_decode_workload(cfg, groups=1, seed=31)
     table, q, ctx = wl["page_table"][0], wl["query"][0], wl["context_lens"]
     summ, sup = spa.page_summaries(wl["k_pool"], block_size=cfg.page_size, n_pages=cfg.routable_pages,

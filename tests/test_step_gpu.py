@@ -146,3 +146,38 @@ def test_session_rejects_unknown_transfer_mode():
         spa.SparseDecodeSession(wl["k_pool"], wl["v_pool"], summ, q_heads=cfg.q_heads, top_blocks=cfg.top_m,
                                 local_window=cfg.local_window, block_size=cfg.page_size, page_table=table,
                                 context_lens=wl["context_lens"], io_mode=7)
+
+
+def test_step_argument_cache_follows_the_tensors():
+    """Repeated calls reuse the prepared arguments; in-place updates of the summaries are
+    seen (the cache borrows the caller's tensors, it copies nothing); a new pool with the
+    same shapes gets its own entry; non-fp32 summaries are converted per call."""
+    from attention_b200 import step as step_mod
+
+    cfg = workloads.SparseDecodeConfig(top_m=4, pages_per_seq=64)
+    wl = workloads.sparse_decode_workload(cfg, groups=2, seed=41)
+    table, q, ctx = wl["page_table"][0], wl["query"][0], wl["context_lens"]
+    summ, sup = spa.page_summaries(wl["k_pool"], block_size=cfg.page_size, n_pages=cfg.routable_pages,
+                                   page_table=table, superblock=cfg.superblock)
+    kw = dict(super_summaries=sup, superblock=cfg.superblock, top_super=cfg.top_super, top_blocks=cfg.top_m,
+              local_window=cfg.local_window, block_size=cfg.page_size, router_scale=cfg.head_dim ** -0.5,
+              page_table=table, context_lens=ctx)
+    step_mod._STEP_CACHE.clear()
+    o1, s1 = spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ, **kw)
+    o2, s2 = spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ, **kw)
+    assert len(step_mod._STEP_CACHE) == 1
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
+    # boost a page that was not selected: the next call must pick it
+    row = 0
+    cand = [g for g in range(cfg.routable_pages) if g not in s1[row].tolist()
+            and (g // cfg.superblock) in s1[row].div(cfg.superblock, rounding_mode="floor").tolist()][0]
+    summ[row, :, cand] += 10 * q[row].float().view(cfg.kv_heads, -1, cfg.head_dim).mean(1)
+    _, s3 = spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ, **kw)
+    assert cand in s3[row].tolist()
+    exp = oracle.select_blocks_tree(q.cpu(), sup.cpu(), summ.cpu(), superblock=cfg.superblock,
+                                    top_super=cfg.top_super, top_blocks=cfg.top_m, scale=cfg.head_dim ** -0.5)
+    assert torch.equal(s3.cpu(), exp)
+    # bf16 summaries: converted per call, never cached
+    n_before = len(step_mod._STEP_CACHE)
+    spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ.to(torch.bfloat16), **kw)
+    assert len(step_mod._STEP_CACHE) == n_before
