@@ -73,7 +73,8 @@ class KvAppendEpilogue(ctypes.Structure):
     """spa_kv_append_epilogue (include/spa_b200.h)."""
 
     _fields_ = [("kv", KvLayout), ("positions", ctypes.c_void_p), ("k_col", ctypes.c_int), ("v_col", ctypes.c_int),
-                ("kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int)]
+                ("kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("q_out", ctypes.c_void_p),
+                ("q_col", ctypes.c_int), ("q_width", ctypes.c_int)]
 
 
 class SessionParams(ctypes.Structure):
@@ -120,6 +121,8 @@ PROTOTYPES = {
                                     _vp, _vp, _sz, _vp]),
     "spa_sparse_decode_step_chained": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _d,
                                             _d, _vp, _vp, _vp, _sz, _vp]),
+    "spa_sparse_decode_step_host": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i,
+                                         _d, _d, _vp, _vp, _vp, _vp, _sz, _vp]),
     "spa_sparse_decode_step_gated": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _d,
                                           _d, _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
     "spa_sparse_decode_step_heads": (_i, [_vp, _i, _i, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _vp, _i, _i, _i,
@@ -136,6 +139,7 @@ PROTOTYPES = {
     "spa_linear": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "spa_linear_chained": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "spa_argmax_advance": (_i, [_vp, _i, _i, _vp, _vp, _i, _vp]),
+    "spa_argmax_advance_log": (_i, [_vp, _i, _i, _vp, _vp, _i, _vp, _vp, _i, _vp]),
     "spa_norm_linear": (_i, [_vp, ctypes.POINTER(NormPrologue), _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
                              ctypes.POINTER(KvAppendEpilogue), _vp]),
     "spa_norm_linear_chained": (_i, [_vp, ctypes.POINTER(NormPrologue), _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,

@@ -17,8 +17,12 @@ def dtype_code(t: torch.Tensor) -> int:
         raise ValueError(f"unsupported dtype {t.dtype}; expected float32, float16 or bfloat16") from None
 
 
-def stream_ptr(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+def stream_ptr(device: torch.device | int) -> int:
+    """The raw handle of the caller's current stream on ``device`` (a device or its index)."""
+    index = device if isinstance(device, int) else device.index
+    if index is None:
+        index = torch.cuda.current_device()
+    return torch._C._cuda_getCurrentRawStream(index)
 
 
 def require_cuda(*tensors: torch.Tensor, message: str = "CUDA tensors are required") -> None:
@@ -42,7 +46,7 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     stream (one buffer per (device, stream); calls on one stream are ordered, so the
     buffer is never used by two kernels at once).  The decode kernels write every
     partial they read back, so no initial contents are needed."""
-    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    key = (device.index, stream_ptr(device))
     buf = _WORKSPACES.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)

@@ -100,6 +100,7 @@ int rms_norm_impl(const void* x, const int64_t* x_rows, int64_t x_limit, const v
 constexpr int kLinearMaxRows = 4;
 constexpr int kLinearWarps = 8;
 constexpr int kLinearBatch = 8;  // 16-byte weight loads per lane in flight
+constexpr int kNormHeld = 4;     // norm prologue: row elements per thread held in registers
 
 template <typename T>
 __device__ __forceinline__ float dot16(const uint4& wv, const uint4& xv, float acc) {
@@ -136,6 +137,8 @@ struct LinearAppend {
   void* v;
   const int32_t* positions;
   int k_col, v_col, kv_heads, head_dim;
+  void* q_out;  // also receives output columns [q_col, q_col + q_width), [rows, q_width]
+  int q_col, q_width;
 };
 
 template <typename T>
@@ -192,30 +195,76 @@ __global__ void __launch_bounds__(kLinearWarps * 32) linear_rows_kernel(const T*
       const float v = to_f32(xr[m][i]);
       return dr[m] ? to_f32(from_f32<T>(v + to_f32(dr[m][i]))) : v;
     };
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+      for (int m = 0; m < rows; ++m)
+        if (bad[m]) spa_raise(SPA_DEVERR_BAD_INDEX);
+    if (K <= kNormHeld * kLinearWarps * 32) {
+      // every element this thread owns (i = threadIdx.x + u * blockDim.x) and its norm
+      // weight requested at once and held in registers: one memory round trip
+      float held[kLinearMaxRows][kNormHeld];
+      float wn[kNormHeld];
 #pragma unroll
-    for (int m = 0; m < kLinearMaxRows; ++m) {
-      if (m >= rows) break;
-      if (bad[m] && blockIdx.x == 0 && threadIdx.x == 0) spa_raise(SPA_DEVERR_BAD_INDEX);
-      float ss = 0.f;
-      for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        const float v = value(m, i);
-        if (xo) xo[m * K + i] = from_f32<T>(v);
-        ss = fmaf(v, v, ss);
+      for (int u = 0; u < kNormHeld; ++u) {
+        const int i = threadIdx.x + u * blockDim.x;
+        wn[u] = i < K ? to_f32(nw[i]) : 0.f;
+#pragma unroll
+        for (int m = 0; m < kLinearMaxRows; ++m) held[m][u] = m < rows && i < K ? value(m, i) : 0.f;
       }
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      if (lane == 0) part[m][warp] = ss;
-    }
-    __syncthreads();
+      for (int m = 0; m < kLinearMaxRows; ++m) {
+        if (m >= rows) break;
+        float ss = 0.f;
 #pragma unroll
-    for (int m = 0; m < kLinearMaxRows; ++m) {
-      if (m >= rows) break;
-      float tot = 0.f;
+        for (int u = 0; u < kNormHeld; ++u) {
+          const int i = threadIdx.x + u * blockDim.x;
+          if (i < K) {
+            if (xo) xo[m * K + i] = from_f32<T>(held[m][u]);
+            ss = fmaf(held[m][u], held[m][u], ss);
+          }
+        }
 #pragma unroll
-      for (int k = 0; k < kLinearWarps; ++k) tot += part[m][k];
-      const float r = rsqrtf(tot / static_cast<float>(K) + pro.eps);
-      for (int i = threadIdx.x; i < K; i += blockDim.x)
-        xs[m * K + i] = bad[m] ? from_f32<T>(0.f) : from_f32<T>(value(m, i) * r * to_f32(nw[i]));
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        if (lane == 0) part[m][warp] = ss;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int m = 0; m < kLinearMaxRows; ++m) {
+        if (m >= rows) break;
+        float tot = 0.f;
+#pragma unroll
+        for (int k = 0; k < kLinearWarps; ++k) tot += part[m][k];
+        const float r = rsqrtf(tot / static_cast<float>(K) + pro.eps);
+#pragma unroll
+        for (int u = 0; u < kNormHeld; ++u) {
+          const int i = threadIdx.x + u * blockDim.x;
+          if (i < K) xs[m * K + i] = bad[m] ? from_f32<T>(0.f) : from_f32<T>(held[m][u] * r * wn[u]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int m = 0; m < kLinearMaxRows; ++m) {
+        if (m >= rows) break;
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) {
+          const float v = value(m, i);
+          if (xo) xo[m * K + i] = from_f32<T>(v);
+          ss = fmaf(v, v, ss);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        if (lane == 0) part[m][warp] = ss;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int m = 0; m < kLinearMaxRows; ++m) {
+        if (m >= rows) break;
+        float tot = 0.f;
+#pragma unroll
+        for (int k = 0; k < kLinearWarps; ++k) tot += part[m][k];
+        const float r = rsqrtf(tot / static_cast<float>(K) + pro.eps);
+        for (int i = threadIdx.x; i < K; i += blockDim.x)
+          xs[m * K + i] = bad[m] ? from_f32<T>(0.f) : from_f32<T>(value(m, i) * r * to_f32(nw[i]));
+      }
     }
   } else if (vec) {
     for (int i = threadIdx.x; i < total / kVec; i += blockDim.x)
@@ -275,6 +324,8 @@ __global__ void __launch_bounds__(kLinearWarps * 32) linear_rows_kernel(const T*
       static_cast<float*>(out)[o] = to_f32(y);
     else
       static_cast<T*>(out)[o] = y;
+    if (app.q_out && n >= app.q_col && n < app.q_col + app.q_width)
+      static_cast<T*>(app.q_out)[static_cast<int64_t>(lane) * app.q_width + (n - app.q_col)] = y;
     if (app.k) {
       const int width = app.kv_heads * app.head_dim;
       T* pool = nullptr;
@@ -339,10 +390,17 @@ extern "C" int spa_embed_rms_norm(const void* table, int64_t table_rows, const i
 }
 
 namespace spa {
-// Greedy token choice at the end of a decode step, one CTA per row: the index of the
-// largest logit with torch.argmax's rules (NaN counts as the largest value; among equal
-// values the first index).  CTA 0 also adds 1 to each of the step's counters (position,
-// context length, step), which every earlier kernel of the step has already read.
+// Greedy token choice at the end of a decode step: the index of the largest logit with
+// torch.argmax's rules (NaN counts as the largest value; among equal values the first
+// index).  One CTA per row, or with a token log one CTA for every row (it reads each row's
+// position before any counter moves).  CTA 0 then adds 1 to each of the step's counters
+// (position, context length, step), which every earlier kernel of the step has already read.
+// A thread requests kArgmaxBatch logits of a row at once, so a row costs one memory round
+// trip per kArgmaxBatch * blockDim.x columns; the comparison is a total order, so the
+// visiting order does not change the winner.
+constexpr int kArgmaxBatch = 16;
+constexpr int kArgmaxLogRows = 256;
+
 __device__ __forceinline__ bool argmax_beats(float a, int ia, float b, int ib) {
   const bool na = a != a, nb = b != b;
   if (na != nb) return na;
@@ -350,48 +408,68 @@ __device__ __forceinline__ bool argmax_beats(float a, int ia, float b, int ib) {
   return ia < ib;
 }
 
-__global__ void __launch_bounds__(256) argmax_advance_kernel(const float* __restrict__ logits, int cols,
-                                                             int64_t* __restrict__ token, int32_t* __restrict__ counters,
-                                                             int n_counters) {
+__global__ void __launch_bounds__(256) argmax_advance_kernel(const float* __restrict__ logits, int rows, int cols,
+                                                             int64_t* __restrict__ token, int32_t* counters,
+                                                             int n_counters, const int32_t* positions,
+                                                             int64_t* __restrict__ log, int log_len) {
   __shared__ float bv[8];
   __shared__ int bi[8];
+  __shared__ int lpos[kArgmaxLogRows];
   // launched as a programmatic dependent of the kernel before it: every read after it completes
   pdl_trigger();
   pdl_block();
-  const int row = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const float* lr = logits + static_cast<int64_t>(row) * cols;
-  float v = -INFINITY;
-  int i = 0x7fffffff;
-  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-    const float x = lr[c];
-    if (argmax_beats(x, c, v, i)) {
-      v = x;
-      i = c;
-    }
-  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (log)
+    for (int j = threadIdx.x; j < rows; j += blockDim.x) lpos[j] = positions[j];
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* lr = logits + static_cast<int64_t>(row) * cols;
+    float v = -INFINITY;
+    int i = 0x7fffffff;
+    for (int base = 0; base < cols; base += kArgmaxBatch * blockDim.x) {
+      float xv[kArgmaxBatch];
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, v, off);
-    const int oi = __shfl_xor_sync(0xffffffffu, i, off);
-    if (argmax_beats(ov, oi, v, i)) {
-      v = ov;
-      i = oi;
-    }
-  }
-  if (lane == 0) {
-    bv[warp] = v;
-    bi[warp] = i;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < 8; ++w)
-      if (argmax_beats(bv[w], bi[w], v, i)) {
-        v = bv[w];
-        i = bi[w];
+      for (int u = 0; u < kArgmaxBatch; ++u) {
+        const int c = base + threadIdx.x + u * blockDim.x;
+        xv[u] = c < cols ? lr[c] : 0.f;
       }
-    token[row] = i;
+#pragma unroll
+      for (int u = 0; u < kArgmaxBatch; ++u) {
+        const int c = base + threadIdx.x + u * blockDim.x;
+        if (c < cols && argmax_beats(xv[u], c, v, i)) {
+          v = xv[u];
+          i = c;
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, i, off);
+      if (argmax_beats(ov, oi, v, i)) {
+        v = ov;
+        i = oi;
+      }
+    }
+    if (lane == 0) {
+      bv[warp] = v;
+      bi[warp] = i;
+    }
+    __syncthreads();  // also orders every lpos read before the counter updates below
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < 8; ++w)
+        if (argmax_beats(bv[w], bi[w], v, i)) {
+          v = bv[w];
+          i = bi[w];
+        }
+      token[row] = i;
+      if (log) {
+        const int p = lpos[row];
+        if (p >= 0 && p < log_len) log[static_cast<int64_t>(p) * rows + row] = i;
+      }
+    }
+    __syncthreads();  // bv / bi are reused by the next row
   }
-  if (row == 0)
+  if (blockIdx.x == 0)
     for (int c = threadIdx.x; c < n_counters; c += blockDim.x) counters[c] += 1;
 }
 }  // namespace spa
@@ -402,8 +480,22 @@ extern "C" int spa_argmax_advance(const float* logits, int rows, int cols, int64
   if (rows == 0) return SPA_OK;
   if (!logits || !token) return SPA_ERR_INVALID;
   SPA_CHECK_CUDA(spa::launch_ex(spa::argmax_advance_kernel, dim3(rows), dim3(256), 0,
-                                 reinterpret_cast<cudaStream_t>(stream), true, 1, logits, cols, token, counters,
-                                 n_counters));
+                                 reinterpret_cast<cudaStream_t>(stream), true, 1, logits, rows, cols, token, counters,
+                                 n_counters, static_cast<const int32_t*>(nullptr), static_cast<int64_t*>(nullptr), 0));
+  return SPA_OK;
+}
+
+extern "C" int spa_argmax_advance_log(const float* logits, int rows, int cols, int64_t* token, int32_t* counters,
+                                      int n_counters, const int32_t* positions, int64_t* log, int log_len,
+                                      spa_stream_t stream) {
+  if (rows < 0 || cols <= 0 || n_counters < 0 || (n_counters > 0 && !counters) || log_len < 0 ||
+      rows > spa::kArgmaxLogRows)
+    return SPA_ERR_INVALID;
+  if (rows == 0) return SPA_OK;
+  if (!logits || !token || !positions || (log_len > 0 && !log)) return SPA_ERR_INVALID;
+  SPA_CHECK_CUDA(spa::launch_ex(spa::argmax_advance_kernel, dim3(1), dim3(256), 0,
+                                 reinterpret_cast<cudaStream_t>(stream), true, 1, logits, rows, cols, token, counters,
+                                 n_counters, positions, log_len > 0 ? log : static_cast<int64_t*>(nullptr), log_len));
   return SPA_OK;
 }
 
@@ -466,6 +558,14 @@ int norm_linear_impl(const void* x, const spa_norm_prologue* norm, const void* w
     app.v_col = append->v_col;
     app.kv_heads = append->kv_heads;
     app.head_dim = append->head_dim;
+    if (append->q_out) {
+      if (out_f32 || append->q_col < 0 || append->q_width <= 0 ||
+          static_cast<int64_t>(append->q_col) + append->q_width > out_features)
+        return SPA_ERR_INVALID;
+      app.q_out = append->q_out;
+      app.q_col = append->q_col;
+      app.q_width = append->q_width;
+    }
   }
   if (norm->ids && (norm->id_limit <= 0 || !norm->delta || !norm->delta_ids || norm->delta_limit <= 0))
     return SPA_ERR_INVALID;

@@ -71,7 +71,10 @@ __global__ void __launch_bounds__(256) copy_bytes_kernel(unsigned char* __restri
   }
 }
 
-int copy_launch(void* dst, const void* src, size_t bytes, spa_stream_t stream, bool release_early) {
+// pdl: launched as a programmatic dependent of the kernel before it (it waits for that
+// kernel's completion at entry either way); without it the launch itself waits, so the
+// copy's CTAs take no SM slots while that kernel runs.
+int copy_launch(void* dst, const void* src, size_t bytes, spa_stream_t stream, bool release_early, bool pdl = true) {
   if (!dst || !src) return SPA_ERR_INVALID;
   if (bytes == 0) return SPA_OK;
   const int vec16 = (reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | bytes) % 16 == 0;
@@ -83,7 +86,7 @@ int copy_launch(void* dst, const void* src, size_t bytes, spa_stream_t stream, b
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   SPA_CHECK_CUDA(cudaLaunchKernelEx(&cfg, spa::copy_bytes_kernel, static_cast<unsigned char*>(dst),

@@ -131,3 +131,39 @@ extern "C" int spa_session_destroy(spa_session* s) {
   session_release(s);
   return SPA_OK;
 }
+
+// One sparse decode step with host buffers, for a caller that does not hold a session: the
+// query is read from pinned host memory by a copy kernel into query_dev (one PCIe read),
+// the step (one launch where it fuses) starts during that copy and writes its output, and
+// a copy of the page ids, straight into pinned host memory.  No copy engine and one host
+// call per step.  The copy waits for the stream's earlier work before it is launched, so
+// a step enqueued behind another takes no SM slots while that one runs.
+extern "C" int spa_sparse_decode_step_host(const void* query_host, void* query_dev, int dtype, int batch,
+                                           int q_heads, int kv_heads, int head_dim, const spa_kv_layout* kv,
+                                           const int32_t* context_lens, int local_window,
+                                           const float* super_summaries, int n_super, const float* summaries,
+                                           int n_pages, int superblock, int top_super, int top_m,
+                                           double router_scale, double attn_scale, int64_t* selected_dev,
+                                           int64_t* selected_host, void* out_host, void* workspace,
+                                           size_t workspace_bytes, spa_stream_t stream) {
+  if (!query_host || !query_dev || !selected_dev || !selected_host || !out_host) return SPA_ERR_INVALID;
+  if (batch <= 0 || q_heads <= 0 || head_dim <= 0 || top_m <= 0) return SPA_ERR_INVALID;
+  // the three host buffers must be pinned and mapped (their device addresses are used)
+  void* qh = nullptr;
+  void* sh = nullptr;
+  void* oh = nullptr;
+  if (cudaHostGetDevicePointer(&qh, const_cast<void*>(query_host), 0) != cudaSuccess ||
+      cudaHostGetDevicePointer(&sh, selected_host, 0) != cudaSuccess ||
+      cudaHostGetDevicePointer(&oh, out_host, 0) != cudaSuccess) {
+    cudaGetLastError();  // not pinned host memory: clear the error state
+    return SPA_ERR_INVALID;
+  }
+  const size_t elem = dtype == SPA_F32 ? 4 : 2;
+  const size_t q_bytes = static_cast<size_t>(batch) * q_heads * head_dim * elem;
+  int rc = spa::copy_launch(query_dev, qh, q_bytes, stream, /*release_early=*/true, /*pdl=*/false);
+  if (rc) return rc;
+  return spa::sparse_step_impl(query_dev, dtype, batch, q_heads, kv_heads, head_dim, kv, context_lens,
+                               local_window, super_summaries, n_super, summaries, n_pages, superblock, top_super,
+                               top_m, router_scale, attn_scale, selected_dev, oh, workspace, workspace_bytes,
+                               nullptr, nullptr, stream, nullptr, static_cast<int64_t*>(sh), /*router_pdl=*/true);
+}

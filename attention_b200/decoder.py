@@ -12,8 +12,10 @@ RMSNorm in place of LayerNorm.  Its decode step is the reference's page_decode
   (fixed-TTL policy, evaluate_promotion_ttl.py:134-135).
 
 The prompt is prefilled with the causal tensor-core prefill (window = prompt length,
-i.e. full causal attention) and written into the page cache.  GEMMs run on cuBLAS;
-attention, routing, KV append and the promotion table are this library's kernels.
+i.e. full causal attention) and written into the page cache; its GEMMs (16k rows) run on
+the library GEMM.  A decode step runs this library's kernels only: few-row linear layers
+with the norms fused in front, routing + gather decode in one launch per layer, the
+promotion table and the greedy argmax.
 """
 
 from __future__ import annotations
@@ -194,7 +196,8 @@ def norm_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
         raise ValueError("out must be a contiguous [rows, out_features] tensor of x's dtype or fp32")
     epi = None
     if append is not None:
-        k_pool, v_pool, table, pos, k_col, v_col = append
+        k_pool, v_pool, table, pos, k_col, v_col = append[:6]
+        q_out = append[6] if len(append) > 6 else None
         width = k_pool.size(1) * k_pool.size(3)
         if (k_pool.dtype != x.dtype or v_pool.shape != k_pool.shape or pos.dtype != torch.int32
                 or pos.numel() != rows or table.dtype != torch.int32 or not (table.is_contiguous() and pos.is_contiguous())
@@ -202,6 +205,12 @@ def norm_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
             raise ValueError("append needs pools of x's dtype, an int32 page table and [rows] int32 positions")
         epi = _lib.KvAppendEpilogue(pool_layout(k_pool, v_pool, table), pos.data_ptr(), k_col, v_col,
                                     k_pool.size(1), k_pool.size(3))
+        if q_out is not None:
+            # the query columns [0, q_width) also go to their own contiguous [rows, ...] buffer
+            if (not q_out.is_cuda or q_out.dtype != x.dtype or not q_out.is_contiguous() or q_out.dim() < 2
+                    or q_out.size(0) != rows or out.dtype != x.dtype or not 0 < q_out[0].numel() <= n):
+                raise ValueError("q_out must be a contiguous CUDA tensor [rows, ...] of x's dtype")
+            epi.q_out, epi.q_col, epi.q_width = q_out.data_ptr(), 0, q_out[0].numel()
     nw = norm_weight.to(x.dtype).contiguous()
     pro = _lib.NormPrologue()
     pro.delta = delta.data_ptr() if delta is not None else None
@@ -218,9 +227,13 @@ def norm_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
     return out
 
 
-def argmax_advance(logits: torch.Tensor, token: torch.Tensor, counters: torch.Tensor | None = None) -> None:
+def argmax_advance(logits: torch.Tensor, token: torch.Tensor, counters: torch.Tensor | None = None, *,
+                   log: torch.Tensor | None = None, positions: torch.Tensor | None = None) -> None:
     """``token[r] = logits[r].argmax()`` (torch.argmax's rules) and ``counters += 1`` in one
-    launch (``spa_argmax_advance``); logits fp32 [rows, cols], token int64 [rows], counters int32."""
+    launch (``spa_argmax_advance``); logits fp32 [rows, cols], token int64 [rows], counters int32.
+    With ``log`` (int64 [length, rows]) and ``positions`` (int32 [rows], read before the
+    counters advance; may be a view of them): also ``log[positions[r], r] = token[r]``
+    (``spa_argmax_advance_log``)."""
     if not (logits.is_cuda and token.is_cuda and (counters is None or counters.is_cuda)):
         raise ValueError("CUDA tensors are required")
     if (logits.dtype != torch.float32 or logits.dim() != 2 or not logits.is_contiguous() or token.dtype != torch.int64
@@ -228,10 +241,19 @@ def argmax_advance(logits: torch.Tensor, token: torch.Tensor, counters: torch.Te
         raise ValueError("logits must be contiguous fp32 [rows, cols] and token int64 [rows]")
     if counters is not None and (counters.dtype != torch.int32 or not counters.is_contiguous()):
         raise ValueError("counters must be a contiguous int32 tensor")
-    _lib.check(_lib.lib.spa_argmax_advance(logits.data_ptr(), logits.size(0), logits.size(1), token.data_ptr(),
-                                           counters.data_ptr() if counters is not None else None,
-                                           counters.numel() if counters is not None else 0,
-                                           stream_ptr(logits.device)), "spa_argmax_advance")
+    cptr, cn = (counters.data_ptr(), counters.numel()) if counters is not None else (None, 0)
+    if log is None:
+        _lib.check(_lib.lib.spa_argmax_advance(logits.data_ptr(), logits.size(0), logits.size(1), token.data_ptr(),
+                                               cptr, cn, stream_ptr(logits.device)), "spa_argmax_advance")
+        return
+    rows = logits.size(0)
+    if (positions is None or not (log.is_cuda and positions.is_cuda) or log.dtype != torch.int64 or log.dim() != 2
+            or log.size(1) != rows or not log.is_contiguous() or positions.dtype != torch.int32
+            or positions.shape != (rows,) or not positions.is_contiguous()):
+        raise ValueError("log must be a contiguous int64 CUDA tensor [length, rows] and positions int32 [rows]")
+    _lib.check(_lib.lib.spa_argmax_advance_log(logits.data_ptr(), rows, logits.size(1), token.data_ptr(), cptr, cn,
+                                               positions.data_ptr(), log.data_ptr(), log.size(0),
+                                               stream_ptr(logits.device)), "spa_argmax_advance_log")
 
 
 def embed_rms_norm(table: torch.Tensor, ids: torch.Tensor, pos_table: torch.Tensor, positions: torch.Tensor,
@@ -365,6 +387,13 @@ class SparseDecoder:
             self._xb = torch.zeros_like(self._xa)
             self._sel_bufs: dict = {}  # [layers, B, m] selections, per m
             self._graphs: dict = {}
+            # the token chosen at each position, written by the step's last kernel (graph
+            # replays follow one another with no copy in between)
+            self._token_log = torch.zeros(self.cfg.max_context, b, dtype=torch.int64, device=self.device)
+            # the query rows of the current layer, stored by the QKV product's epilogue
+            self._q = torch.zeros(b, self.cfg.heads, self.cfg.head_dim, dtype=self.dtype, device=self.device)
+            # the promotion update runs on a branch forked after the last layer's selection
+            self._side = torch.cuda.Stream(device=self.device)
 
     def _norm_linear(self, x, delta, norm, name, x_out, *, gelu=False, append=None, chained=False):
         """x_out = x + delta; returns the linear layer ``name`` of rms_norm(x_out): one
@@ -390,8 +419,8 @@ class SparseDecoder:
         fused = b <= LINEAR_MAX_ROWS  # norms, products and the K/V append in few-row kernels
         d = cfg.d_model
 
-        def append(i):  # the QKV product's K and V columns go straight into layer i's pools
-            return (self.k_pool[i], self.v_pool[i], self.page_table, self._position, d, 2 * d) if fused else None
+        def append(i):  # the QKV product's K and V columns go straight into layer i's pools, Q into its buffer
+            return (self.k_pool[i], self.v_pool[i], self.page_table, self._position, d, 2 * d, self._q) if fused else None
 
         if fused:
             qkv = norm_linear(self.w["emb"], self.w["l0.qkv.w"], self.w["l0.qkv.b"], norm_weight=self.w["l0.norm1"],
@@ -414,7 +443,7 @@ class SparseDecoder:
                 qkv = self._norm_linear(x, mlp_out, f"l{i}.norm1", f"l{i}.qkv", spare, append=append(i), chained=True)
                 x, spare = spare, x
             qkv = qkv.view(b, 3, h, dh)
-            q = qkv[:, 0].contiguous()
+            q = self._q if fused else qkv[:, 0].contiguous()
             if not fused:
                 kv_append(self.k_pool[i], self.v_pool[i], self.page_table, qkv[:, 1].contiguous(),
                           qkv[:, 2].contiguous(), self._position)
@@ -429,6 +458,14 @@ class SparseDecoder:
                 att = paged_gather_decode_attention(q, self.k_pool[i], self.v_pool[i], sel,
                                                     local_window=cfg.local_window, block_size=cfg.page_size,
                                                     page_table=self.page_table, context_lens=self._ctx_len)
+            if i == cfg.layers - 1:
+                # every layer's selection is written: the promotion update runs beside the rest
+                # of the step (nothing after it reads the promotion table)
+                main = torch.cuda.current_stream(self.device)
+                self._side.wait_stream(main)
+                with torch.cuda.stream(self._side):
+                    sel_rows = (sel_all if m > 0 else torch.stack(selected + [sel])).reshape(cfg.layers * b, -1)
+                    self.promotion.update(sel_rows, self._step_dev)
             o = self._linear(att.reshape(b, cfg.d_model), f"l{i}.out", chained=True)
             hid = self._norm_linear(x, o, f"l{i}.norm2", f"l{i}.fc1", spare, gelu=True, chained=True)
             x, spare = spare, x
@@ -436,7 +473,6 @@ class SparseDecoder:
             selected.append(sel)
         if m == 0:
             sel_all = torch.stack(selected)  # [layers, B, 1]
-        self.promotion.update(sel_all.reshape(cfg.layers * b, -1), self._step_dev)
         if b <= LINEAR_MAX_ROWS:
             # fp32 logits of the rounded products
             norm_linear(x, self.w["head"], norm_weight=self.w["norm_f"], eps=cfg.eps, delta=mlp_out, out=self._logits,
@@ -444,8 +480,12 @@ class SparseDecoder:
         else:
             hf = add_rms_norm(x, mlp_out, self.w["norm_f"], cfg.eps, x_out=spare)
             self._logits.copy_(F.linear(hf, self.w["head"]))
-        # greedy token, then position, context length and step advance (one launch)
-        argmax_advance(self._logits, self._token, self._counters)
+        # the branch (promotion update) joins before the counters advance: it reads the step
+        # counter
+        torch.cuda.current_stream(self.device).wait_stream(self._side)
+        # greedy token (also logged at its position), then position, context length and step
+        # advance (one launch)
+        argmax_advance(self._logits, self._token, self._counters, log=self._token_log, positions=self._position)
         return sel_all
 
     def _check_room(self, steps: int) -> None:
@@ -495,7 +535,7 @@ class SparseDecoder:
         self._position.fill_(self.ctx)
         self._ctx_len.fill_(self.ctx + 1)
         self._step_dev.fill_(self.step_index)
-        out = torch.empty(steps, self.batch, dtype=torch.int64, device=self.device)
+        first = self.ctx
         for t in range(steps):
             self._begin_step()
             if graphed:
@@ -521,7 +561,7 @@ class SparseDecoder:
                 g.replay()
             else:
                 self._step_body()
-            out[t].copy_(self._token)
             self.step_index += 1
             self.ctx += 1
-        return out
+        # the step at position p logged its token at row p
+        return self._token_log[first:first + steps].clone()

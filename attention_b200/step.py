@@ -70,30 +70,54 @@ def _prepare_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
                 lens=lens, summ=summ, sup=sup, ws=ws, ws_bytes=ws_bytes, dtype=dtype_code(query))
 
 
-# Prepared C arguments of recent step forms, keyed by the identity of the borrowed tensors,
-# the query's shape and dtype, the step parameters and the stream.  An entry is kept only
-# when validation borrowed the caller's tensors as they are (fp32 summaries, int32 table and
-# lengths: nothing converted, so nothing cached can go stale).  It holds weak references, so
-# it keeps no memory alive; a hit requires every referenced tensor to be the same live
-# object with the same storage address (a tensor re-pointed in place is prepared again).
+# Prepared C arguments of recent step forms.  An entry is kept only when validation borrowed
+# the caller's tensors as they are (fp32 summaries, int32 table and lengths: nothing
+# converted, so nothing cached can go stale) and holds only integers (pointers, sizes) and
+# the library's workspace, so it keeps none of the caller's memory alive.  Two keys lead to
+# an entry:
+# * the identity of the borrowed tensors (weak references: a hit needs the same live objects
+#   at the same storage addresses) -- the cheap path for a caller that passes the same tensors;
+# * their metadata (address, shape, strides, dtype), which determines every argument the
+#   entry holds -- a caller that passes fresh views of the same storage (``table[g]``) hits
+#   here, and a tensor freed and reallocated with other metadata cannot.
+# Both keys also carry the query's shape and dtype, the step parameters and the stream.
 _STEP_CACHE: dict = {}
+_STEP_META: dict = {}
 _STEP_CACHE_MAX = 32
 
 
+def _meta(t):
+    return None if t is None else (t.data_ptr(), t.shape, t.stride(), t.dtype)
+
+
+def _remember(cache: dict, key, value) -> None:
+    if len(cache) >= _STEP_CACHE_MAX:
+        cache.pop(next(iter(cache)))
+    cache[key] = value
+
+
 def _prepared_step(query, keys, values, summaries, *, top_blocks, local_window, block_size, super_summaries,
-                   superblock, top_super, page_table, context_lens, router_scale, stream):
+                   superblock, top_super, page_table, context_lens, router_scale, stream, host_query=False):
     """The step's C arguments except the query, selection and output pointers:
-    (head, tail, dtype/batch info), from the cache when the same tensors and parameters
-    were prepared before."""
+    (head, tail, batch), from the cache when the same tensors (or tensors with the same
+    storage and metadata) and parameters were prepared before."""
     held = (keys, values, summaries, super_summaries, page_table, context_lens)
-    key = (query.shape, query.dtype, query.device, tuple(id(t) for t in held), top_blocks, local_window,
-           block_size, superblock, top_super, float(router_scale), stream)
+    params = (query.shape, query.dtype, query.get_device(), top_blocks, local_window, block_size, superblock,
+              top_super, float(router_scale), stream)
+    key = (tuple(id(t) for t in held),) + params
     hit = _STEP_CACHE.get(key)
-    if hit is not None and all(
-            (r is None and t is None) or (r is not None and r() is t and t.data_ptr() == ptr)
-            for r, t, ptr in zip(hit["refs"], held, hit["ptrs"])):
-        return hit
-    if not query.is_cuda:
+    if hit is not None:
+        entry, refs, ptrs = hit
+        if all((r is None and t is None) or (r is not None and r() is t and t.data_ptr() == ptr)
+               for r, t, ptr in zip(refs, held, ptrs)):
+            return entry
+    mkey = tuple(_meta(t) for t in held) + params
+    entry = _STEP_META.get(mkey)
+    if entry is not None:
+        # same storage and metadata as a prepared form (a caller passing fresh views): the
+        # identity key stays that of the tensors first prepared
+        return entry
+    if not (query.is_cuda or host_query):
         raise ValueError("CUDA tensors are required")
     pr = _prepare_step(query, keys, values, summaries, top_blocks=top_blocks, local_window=local_window,
                        block_size=block_size, super_summaries=super_summaries, superblock=superblock,
@@ -101,20 +125,30 @@ def _prepared_step(query, keys, values, summaries, *, top_blocks, local_window, 
     sup, ws = pr["sup"], pr["ws"]
     head = (pr["dtype"], pr["batch"], pr["q_heads"], pr["kv_heads"], pr["head_dim"], ctypes.byref(pr["layout"]),
             pr["lens"].data_ptr(), local_window, sup.data_ptr() if sup is not None else None,
-            sup.size(2) if sup is not None else 0, pr["summ"].data_ptr(), pr["summ"].size(2), superblock, top_super,
-            top_blocks, float(router_scale), pr["head_dim"] ** -0.5)
+            sup.size(2) if sup is not None else 0, pr["summ"].data_ptr(), pr["summ"].size(2), superblock,
+            top_super, top_blocks, float(router_scale), pr["head_dim"] ** -0.5)
     tail = (ws.data_ptr() if ws is not None else None, pr["ws_bytes"])
-    prep = {"head": head, "tail": tail, "batch": pr["batch"], "dev": pr["dev"], "pr": pr}
+    entry = {"head": head, "tail": tail, "batch": pr["batch"], "ws": ws}
     borrowed = pr["summ"] is summaries and (super_summaries is None or sup is super_summaries) and (
         page_table is None or (pr["lens"] is context_lens and pr["layout"].page_table == page_table.data_ptr()
                                and page_table.dtype == torch.int32))
-    if borrowed:
-        prep["refs"] = [weakref.ref(t) if t is not None else None for t in held]
-        prep["ptrs"] = [t.data_ptr() if t is not None else 0 for t in held]
-        if len(_STEP_CACHE) >= _STEP_CACHE_MAX:
-            _STEP_CACHE.pop(next(iter(_STEP_CACHE)))
-        _STEP_CACHE[key] = prep
-    return prep
+    if not borrowed:
+        # converted copies: the arguments point into them, so the entry keeps them
+        entry["keep"] = pr
+        return entry
+    _remember(_STEP_META, mkey, entry)
+    refs = [weakref.ref(t) if t is not None else None for t in held]
+    _remember(_STEP_CACHE, key, (entry, refs, [t.data_ptr() if t is not None else 0 for t in held]))
+    return entry
+
+
+def _check_outputs(query, out, selected, batch, top_blocks):
+    if out is not None and (out.shape != query.shape or out.dtype != query.dtype or not out.is_contiguous()
+                            or out.get_device() != query.get_device()):
+        raise ValueError("out must be a contiguous CUDA tensor of the query's shape and dtype")
+    if selected is not None and (selected.shape != (batch, top_blocks) or selected.dtype != torch.int64
+                                 or not selected.is_contiguous() or selected.get_device() != query.get_device()):
+        raise ValueError("selected must be a contiguous int64 CUDA tensor [batch, top_blocks]")
 
 
 def set_step_fusion(enabled: bool) -> bool:
@@ -157,6 +191,11 @@ def _sparse_decode_step_heads(query, keys, values, summaries, *, top_blocks, loc
     max_cand = local_window + top_blocks * block_size
     ws_bytes = _lib.lib.spa_decode_workspace_size(batch, count * group, count, head_dim, max_cand)
     ws = workspace(dev, ws_bytes) if ws_bytes else None
+    if out is not None and (out.shape != (batch, count * group, head_dim) or out.dtype != query.dtype
+                            or not out.is_contiguous() or out.get_device() != query.get_device()):
+        raise ValueError("out must be a contiguous CUDA tensor [batch, the shard's query heads, head_dim] "
+                         "of the query's dtype")
+    _check_outputs(query, None, selected, batch, top_blocks)
     if out is None:
         out = torch.empty(batch, count * group, head_dim, dtype=query.dtype, device=dev)
     if selected is None:
@@ -168,6 +207,43 @@ def _sparse_decode_step_heads(query, keys, values, summaries, *, top_blocks, loc
         float(router_scale), head_dim ** -0.5, selected.data_ptr(), out.data_ptr(),
         ws.data_ptr() if ws is not None else None, ws_bytes, stream_ptr(dev))
     _lib.check(rc, "spa_sparse_decode_step_heads")
+    return out, selected
+
+
+def _sparse_decode_step_host(query, keys, values, summaries, *, top_blocks, local_window, block_size,
+                             super_summaries, superblock, top_super, router_scale, page_table, context_lens, out,
+                             selected):
+    """The step with pinned host buffers (``spa_sparse_decode_step_host``): the query is read
+    from host memory by a copy kernel, output and page ids are written into host memory by
+    the step; they are complete when the caller's stream is."""
+    if query.is_cuda or not query.is_contiguous() or not keys.is_cuda:
+        raise ValueError("host query: a contiguous pinned CPU query with CUDA keys/values/summaries")
+    dev_index = keys.get_device()
+    stream = stream_ptr(dev_index)
+    prep = _prepared_step(query, keys, values, summaries, top_blocks=top_blocks, local_window=local_window,
+                          block_size=block_size, super_summaries=super_summaries, superblock=superblock,
+                          top_super=top_super, page_table=page_table, context_lens=context_lens,
+                          router_scale=router_scale, stream=stream, host_query=True)
+    batch = prep["batch"]
+    if out is None:
+        out = torch.empty(query.shape, dtype=query.dtype, pin_memory=True)
+    elif out.is_cuda or out.shape != query.shape or out.dtype != query.dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous pinned CPU tensor of the query's shape and dtype")
+    if selected is None:
+        selected = torch.empty(batch, top_blocks, dtype=torch.int64, pin_memory=True)
+    elif (selected.is_cuda or selected.shape != (batch, top_blocks) or selected.dtype != torch.int64
+          or not selected.is_contiguous()):
+        raise ValueError("selected must be a contiguous pinned int64 CPU tensor [batch, top_blocks]")
+    q_dev = prep.get("q_dev")
+    if q_dev is None:  # device staging of the query and the page ids, kept with the prepared arguments
+        q_dev = prep["q_dev"] = torch.empty(query.shape, dtype=query.dtype, device=keys.device)
+        prep["sel_dev"] = torch.empty(batch, top_blocks, dtype=torch.int64, device=keys.device)
+    rc = _lib.lib.spa_sparse_decode_step_host(query.data_ptr(), q_dev.data_ptr(), *prep["head"],
+                                              prep["sel_dev"].data_ptr(), selected.data_ptr(), out.data_ptr(),
+                                              *prep["tail"], stream)
+    if rc == _lib.SPA_ERR_INVALID:
+        raise ValueError("spa_sparse_decode_step_host: query, out and selected must be pinned host memory")
+    _lib.check(rc, "spa_sparse_decode_step_host")
     return out, selected
 
 
@@ -183,9 +259,19 @@ def sparse_decode_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Te
     [begin, begin + count) of a page pool, and the output those kv heads' query heads.
     Every shard of a sequence selects the same pages.  ``chained``: the step's first
     kernel launches as a programmatic dependent of the kernel before it
-    (``spa_sparse_decode_step_chained``; a model's decode step)."""
+    (``spa_sparse_decode_step_chained``; a model's decode step).
+
+    A pinned CPU ``query`` (with pinned CPU ``out`` / ``selected``, allocated pinned when
+    omitted) runs the step with host buffers (``spa_sparse_decode_step_host``): no copy
+    engine, results on the host once the current stream has completed."""
     if not query.is_cuda:
-        raise ValueError("CUDA tensors are required")
+        if gate is not None or kv_head_range is not None or chained:
+            raise ValueError("CUDA tensors are required")
+        return _sparse_decode_step_host(query, keys, values, summaries, top_blocks=top_blocks,
+                                        local_window=local_window, block_size=block_size,
+                                        super_summaries=super_summaries, superblock=superblock, top_super=top_super,
+                                        router_scale=router_scale, page_table=page_table,
+                                        context_lens=context_lens, out=out, selected=selected)
     if kv_head_range is not None:
         if gate is not None:
             raise ValueError("a refresh gate is not supported with kv_head_range")
@@ -197,20 +283,19 @@ def sparse_decode_step(query: torch.Tensor, keys: torch.Tensor, values: torch.Te
                                          kv_head_range=kv_head_range)
     if not query.is_contiguous():
         raise ValueError("contiguous CUDA tensors are required")
-    dev = query.device
-    stream = stream_ptr(dev)
+    stream = stream_ptr(query.get_device())
     prep = _prepared_step(query, keys, values, summaries, top_blocks=top_blocks, local_window=local_window,
                           block_size=block_size, super_summaries=super_summaries, superblock=superblock,
                           top_super=top_super, page_table=page_table, context_lens=context_lens,
                           router_scale=router_scale, stream=stream)
+    _check_outputs(query, out, selected, prep["batch"], top_blocks)
     if out is None:
         out = torch.empty_like(query)
     if selected is None:
-        selected = torch.empty(prep["batch"], top_blocks, dtype=torch.int64, device=dev)
+        selected = torch.empty(prep["batch"], top_blocks, dtype=torch.int64, device=query.device)
     args = (query.data_ptr(),) + prep["head"] + (selected.data_ptr(), out.data_ptr()) + prep["tail"]
     if gate is not None:
-        pr = prep["pr"]
-        promoted = gate.promoted_for(pr["batch"], top_blocks)
+        promoted = gate.promoted_for(prep["batch"], top_blocks)
         rc = _lib.lib.spa_sparse_decode_step_gated(*args, gate.flags.data_ptr(), promoted.data_ptr(), stream)
         _lib.check(rc, "spa_sparse_decode_step_gated")
     else:

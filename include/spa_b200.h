@@ -246,6 +246,25 @@ int spa_sparse_decode_step(const void* q, int dtype, int batch, int q_heads,
                            spa_stream_t stream);
 
 /*
+ * spa_sparse_decode_step with host buffers (the per-call form of a serving loop without a
+ * session): query_host, selected_host [batch, top_m] and out_host are pinned, mapped host
+ * memory (cudaHostAlloc / torch pin_memory; anything else returns SPA_ERR_INVALID before a
+ * launch).  A copy kernel reads the query into query_dev (device, batch*q_heads*head_dim
+ * elements), the step starts during that copy and writes the output and a copy of the
+ * page ids into the host buffers (selected_dev, device [batch, top_m], holds the ids the
+ * decode reads).  Nothing goes through a copy engine; the results are complete on the host
+ * when the stream's work is.  The reference's equivalent is the timed call of
+ * triton_paged_gather_decode_benchmark.py:71 with its inputs copied in and outputs read back.
+ */
+int spa_sparse_decode_step_host(const void* query_host, void* query_dev, int dtype, int batch, int q_heads,
+                                int kv_heads, int head_dim, const spa_kv_layout* kv, const int32_t* context_lens,
+                                int local_window, const float* super_summaries, int n_super,
+                                const float* summaries, int n_pages, int superblock, int top_super, int top_m,
+                                double router_scale, double attn_scale, int64_t* selected_dev,
+                                int64_t* selected_host, void* out_host, void* workspace, size_t workspace_bytes,
+                                spa_stream_t stream);
+
+/*
  * spa_sparse_decode_step for a chain of dependent launches (a model's decode step): the
  * first kernel is launched as a programmatic dependent of the kernel enqueued before it
  * and waits for that kernel to complete before its first read, so it is resident and
@@ -588,6 +607,17 @@ typedef struct spa_norm_prologue {
 int spa_argmax_advance(const float* logits, int rows, int cols, int64_t* token, int32_t* counters, int n_counters,
                        spa_stream_t stream);
 
+/*
+ * spa_argmax_advance that also logs the token: log[positions[r] * rows + r] = token[r] for
+ * 0 <= positions[r] < log_len (positions are read before the counters advance; they may be
+ * the first rows entries of counters).  A decoder keeps its generated tokens on the device
+ * this way, with no copy between two graph replays.  rows <= 256 (one CTA serves every row).
+ * No reference counterpart (the reference appends tokens on the host).
+ */
+int spa_argmax_advance_log(const float* logits, int rows, int cols, int64_t* token, int32_t* counters,
+                           int n_counters, const int32_t* positions, int64_t* log, int log_len,
+                           spa_stream_t stream);
+
 /* The new token's K/V append fused into a spa_norm_linear epilogue (the QKV projection). */
 typedef struct spa_kv_append_epilogue {
   spa_kv_layout kv;         /* K/V pools and page table, as for spa_kv_append */
@@ -596,6 +626,11 @@ typedef struct spa_kv_append_epilogue {
   int v_col;                /* first output column of V */
   int kv_heads;
   int head_dim;
+  void* q_out;              /* optional [rows, q_width] of the output dtype: also receives output
+                               columns [q_col, q_col + q_width) (the query, contiguous for the
+                               attention step at any batch size); NULL: none */
+  int q_col;
+  int q_width;
 } spa_kv_append_epilogue;
 
 int spa_norm_linear(const void* x, const spa_norm_prologue* norm, const void* weight, const void* bias, void* out,

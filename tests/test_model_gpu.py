@@ -223,3 +223,28 @@ def test_argmax_advance_matches_torch_argmax():
     assert token.tolist() == [int(logits[0].argmax()), 100, 7, 0]
     assert counters.tolist() == [4, 5, 6, 7, 8]
     assert spa.device_error_flags() == 0
+
+
+@pytest.mark.parametrize("cols", [4096, 5000, 37])
+def test_argmax_advance_log_matches_torch_argmax(cols):
+    """The logged form: one CTA serves every row, reads each row's position before the
+    counters (which hold the positions) advance, and writes the token at that position."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    logits = torch.randn(4, cols, device="cuda", generator=g)
+    logits[1, 3] = logits[1, cols - 1] = 50.0  # a tie: the first index wins
+    logits[2, 5] = float("nan")
+    logits[3] = 0.0
+    token = torch.full((4,), -5, dtype=torch.int64, device="cuda")
+    counters = torch.tensor([3, 4, 9, 6, 7, 8, 9, 10, 11], dtype=torch.int32, device="cuda")
+    log = torch.full((9, 4), -1, dtype=torch.int64, device="cuda")
+    argmax_advance(logits, token, counters, log=log, positions=counters[:4])
+    exp = torch.argmax(logits, dim=-1)
+    assert torch.equal(token, exp)
+    assert token.tolist()[1:] == [3, 5, 0]
+    assert counters.tolist() == [4, 5, 10, 7, 8, 9, 10, 11, 12]
+    want = torch.full((9, 4), -1, dtype=torch.int64)
+    for r, p in enumerate([3, 4, 9, 6]):
+        if p < 9:  # position 9 lies outside the log: not stored
+            want[p, r] = exp[r]
+    assert torch.equal(log.cpu(), want)
+    assert spa.device_error_flags() == 0

@@ -151,7 +151,8 @@ def test_session_rejects_unknown_transfer_mode():
 def test_step_argument_cache_follows_the_tensors():
     """Repeated calls reuse the prepared arguments; in-place updates of the summaries are
     seen (the cache borrows the caller's tensors, it copies nothing); a new pool with the
-    same shapes gets its own entry; non-fp32 summaries are converted per call."""
+    same shapes gets its own entry; fresh views of the same storage reuse the entry;
+    non-fp32 summaries are converted per call; wrong outputs are refused before any launch."""
     from attention_b200 import step as step_mod
 
     cfg = workloads.SparseDecodeConfig(top_m=4, pages_per_seq=64)
@@ -163,10 +164,30 @@ def test_step_argument_cache_follows_the_tensors():
               local_window=cfg.local_window, block_size=cfg.page_size, router_scale=cfg.head_dim ** -0.5,
               page_table=table, context_lens=ctx)
     step_mod._STEP_CACHE.clear()
+    step_mod._STEP_META.clear()
     o1, s1 = spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ, **kw)
     o2, s2 = spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ, **kw)
-    assert len(step_mod._STEP_CACHE) == 1
+    assert len(step_mod._STEP_CACHE) == 1 and len(step_mod._STEP_META) == 1
     assert torch.equal(o1, o2) and torch.equal(s1, s2)
+    # a fresh view of the same table each call: same prepared arguments
+    for _ in range(3):
+        o4, s4 = spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ, **{**kw, "page_table": wl["page_table"][0]})
+        assert torch.equal(o4, o1) and torch.equal(s4, s1)
+    assert len(step_mod._STEP_META) == 1
+    # the other group's table (another storage address): its own entry and its own pages
+    summ_b, sup_b = spa.page_summaries(wl["k_pool"], block_size=cfg.page_size, n_pages=cfg.routable_pages,
+                                       page_table=wl["page_table"][1], superblock=cfg.superblock)
+    _, s5 = spa.sparse_decode_step(wl["query"][1], wl["k_pool"], wl["v_pool"], summ_b,
+                                   **{**kw, "page_table": wl["page_table"][1], "super_summaries": sup_b})
+    assert len(step_mod._STEP_META) == 2
+    exp_b = oracle.select_blocks_tree(wl["query"][1].cpu(), sup_b.cpu(), summ_b.cpu(), superblock=cfg.superblock,
+                                      top_super=cfg.top_super, top_blocks=cfg.top_m, scale=cfg.head_dim ** -0.5)
+    assert torch.equal(s5.cpu(), exp_b)
+    with pytest.raises(ValueError):
+        spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ, out=torch.empty_like(q)[:-1], **kw)
+    with pytest.raises(ValueError):
+        spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ,
+                               selected=torch.empty(q.size(0), cfg.top_m, dtype=torch.int32, device=q.device), **kw)
     # boost a page that was not selected: the next call must pick it
     row = 0
     cand = [g for g in range(cfg.routable_pages) if g not in s1[row].tolist()
@@ -178,6 +199,42 @@ def test_step_argument_cache_follows_the_tensors():
                                     top_super=cfg.top_super, top_blocks=cfg.top_m, scale=cfg.head_dim ** -0.5)
     assert torch.equal(s3.cpu(), exp)
     # bf16 summaries: converted per call, never cached
-    n_before = len(step_mod._STEP_CACHE)
+    n_before = len(step_mod._STEP_CACHE), len(step_mod._STEP_META)
     spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ.to(torch.bfloat16), **kw)
-    assert len(step_mod._STEP_CACHE) == n_before
+    assert (len(step_mod._STEP_CACHE), len(step_mod._STEP_META)) == n_before
+
+
+@pytest.mark.parametrize("top_m", [2, 8])
+def test_host_buffer_step_matches_device_step(top_m):
+    """The per-call step with pinned host buffers (copy kernel in, results written into host
+    memory by the step) equals the device-buffer step bit for bit, on two batches in a row;
+    pageable host memory is refused before any launch."""
+    cfg = workloads.SparseDecodeConfig(top_m=top_m, pages_per_seq=128)
+    wl = workloads.sparse_decode_workload(cfg, groups=2, seed=43)
+    kw = dict(superblock=cfg.superblock, top_super=cfg.top_super, top_blocks=cfg.top_m,
+              local_window=cfg.local_window, block_size=cfg.page_size, router_scale=cfg.head_dim ** -0.5,
+              context_lens=wl["context_lens"])
+    outs = []
+    for g in range(2):
+        table = wl["page_table"][g]
+        summ, sup = spa.page_summaries(wl["k_pool"], block_size=cfg.page_size, n_pages=cfg.routable_pages,
+                                       page_table=table, superblock=cfg.superblock)
+        q = wl["query"][g]
+        o_dev, s_dev = spa.sparse_decode_step(q, wl["k_pool"], wl["v_pool"], summ, super_summaries=sup,
+                                              page_table=table, **kw)
+        q_host = q.cpu().pin_memory()
+        o_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+        s_host = torch.full((cfg.batch, top_m), -7, dtype=torch.int64).pin_memory()
+        r_out, r_sel = spa.sparse_decode_step(q_host, wl["k_pool"], wl["v_pool"], summ, super_summaries=sup,
+                                              page_table=table, out=o_host, selected=s_host, **kw)
+        assert r_out is o_host and r_sel is s_host
+        outs.append((o_dev, s_dev, o_host, s_host))
+        if g == 0:
+            with pytest.raises(ValueError):
+                spa.sparse_decode_step(q.cpu(), wl["k_pool"], wl["v_pool"], summ, super_summaries=sup,
+                                       page_table=table, **kw)
+    torch.cuda.synchronize()
+    for o_dev, s_dev, o_host, s_host in outs:
+        assert torch.equal(s_host, s_dev.cpu())
+        assert torch.equal(o_host, o_dev.cpu())
+    assert spa.device_error_flags() == 0
