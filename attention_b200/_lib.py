@@ -93,6 +93,33 @@ class SessionParams(ctypes.Structure):
                 ("result_sel_offset", ctypes.c_size_t), ("result_bytes", ctypes.c_size_t),
                 ("result_host", ctypes.c_void_p * 2)]
 
+DECODER_MAX_LAYERS = 8
+
+
+class DecoderLayer(ctypes.Structure):
+    """spa_decoder_layer (include/spa_b200.h)."""
+
+    _fields_ = [(name, ctypes.c_void_p) for name in ("norm1", "qkv_w", "qkv_b", "out_w", "out_b", "norm2", "fc1_w",
+                                                     "fc1_b", "fc2_w", "fc2_b", "k_pool", "v_pool", "summaries")]
+
+
+class DecoderStepParams(ctypes.Structure):
+    """spa_decoder_step_params (include/spa_b200.h)."""
+
+    _fields_ = [("dtype", ctypes.c_int), ("batch", ctypes.c_int), ("d_model", ctypes.c_int), ("heads", ctypes.c_int),
+                ("ffn", ctypes.c_int), ("vocab", ctypes.c_int), ("layers", ctypes.c_int),
+                ("local_window", ctypes.c_int), ("top_m", ctypes.c_int), ("n_pages", ctypes.c_int),
+                ("max_pages", ctypes.c_int), ("eps", ctypes.c_double), ("router_scale", ctypes.c_double),
+                ("attn_scale", ctypes.c_double), ("emb", ctypes.c_void_p), ("emb_rows", ctypes.c_int64),
+                ("pos_emb", ctypes.c_void_p), ("pos_rows", ctypes.c_int64), ("norm_f", ctypes.c_void_p),
+                ("head_w", ctypes.c_void_p), ("layer", DecoderLayer * DECODER_MAX_LAYERS), ("kv", KvLayout),
+                ("token", ctypes.c_void_p), ("counters", ctypes.c_void_p), ("logits", ctypes.c_void_p),
+                ("token_log", ctypes.c_void_p), ("log_len", ctypes.c_int), ("selected", ctypes.c_void_p),
+                ("promo_pages", ctypes.c_void_p), ("promo_last_hit", ctypes.c_void_p),
+                ("promo_slots", ctypes.c_int), ("promo_ttl", ctypes.c_int), ("workspace", ctypes.c_void_p),
+                ("workspace_bytes", ctypes.c_size_t)]
+
+
 PROTOTYPES = {
     "spa_version": (ctypes.c_char_p, []),
     "spa_device_error": (_i, [ctypes.POINTER(ctypes.c_uint32)]),
@@ -144,6 +171,8 @@ PROTOTYPES = {
                              ctypes.POINTER(KvAppendEpilogue), _vp]),
     "spa_norm_linear_chained": (_i, [_vp, ctypes.POINTER(NormPrologue), _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
                              ctypes.POINTER(KvAppendEpilogue), _vp]),
+    "spa_decoder_step_workspace_size": (_sz, [ctypes.POINTER(DecoderStepParams)]),
+    "spa_decoder_step": (_i, [ctypes.POINTER(DecoderStepParams), _vp]),
 }
 
 

@@ -31,26 +31,17 @@ __global__ void kv_append_kernel(T* __restrict__ k, T* __restrict__ v, KvAddr ad
 // policy defines them.  Reference policy: fixed-TTL refresh of promoted ids,
 // evaluate_promotion_ttl.py:134-135; promoted-id reuse,
 // triton_promotion_cache_benchmark.py:53-60.
-__global__ void __launch_bounds__(32) promotion_update_kernel(int32_t* __restrict__ pages,
-                                                              int32_t* __restrict__ last_hit, int rows, int slots,
-                                                              const int64_t* __restrict__ selected, int top_m,
-                                                              int step_arg, const int32_t* __restrict__ step_dev,
-                                                              int ttl) {
-  extern __shared__ int64_t promo_smem[];  // sel [top_m], then pg [slots], lh [slots]
-  // launched as a programmatic dependent of the kernel before it: every read after it completes
-  pdl_trigger();
-  pdl_block();
-  const int r = blockIdx.x, lane = threadIdx.x;
-  if (r >= rows) return;
-  const int step = step_dev ? *step_dev : step_arg;
-  int32_t* pg_g = pages + static_cast<int64_t>(r) * slots;
-  int32_t* lh_g = last_hit + static_cast<int64_t>(r) * slots;
+//
+// promotion_row_update: the update of one table row by one (converged) warp.  sel_src is the
+// row's selection [top_m]; sel, pg and lh are the warp's shared-memory staging ([top_m],
+// [slots], [slots]).
+__device__ __forceinline__ void promotion_row_update(int32_t* __restrict__ pg_g, int32_t* __restrict__ lh_g,
+                                                     const int64_t* __restrict__ sel_src, int top_m, int slots,
+                                                     int step, int ttl, int64_t* sel, int32_t* pg, int32_t* lh) {
+  const int lane = threadIdx.x & 31;
   // the row's selection is staged with the table (loads in flight together), so the
   // per-page loops below read shared memory, not one global load per page
-  int64_t* sel = promo_smem;
-  int32_t* pg = reinterpret_cast<int32_t*>(sel + top_m);
-  int32_t* lh = pg + slots;
-  for (int j = lane; j < top_m; j += 32) sel[j] = selected[static_cast<int64_t>(r) * top_m + j];
+  for (int j = lane; j < top_m; j += 32) sel[j] = sel_src[j];
   for (int i = lane; i < slots; i += 32) {
     pg[i] = pg_g[i];
     lh[i] = lh_g[i];
@@ -115,6 +106,24 @@ __global__ void __launch_bounds__(32) promotion_update_kernel(int32_t* __restric
     pg_g[i] = pg[i];
     lh_g[i] = lh[i];
   }
+}
+
+__global__ void __launch_bounds__(32) promotion_update_kernel(int32_t* __restrict__ pages,
+                                                              int32_t* __restrict__ last_hit, int rows, int slots,
+                                                              const int64_t* __restrict__ selected, int top_m,
+                                                              int step_arg, const int32_t* __restrict__ step_dev,
+                                                              int ttl) {
+  extern __shared__ int64_t promo_smem[];  // sel [top_m], then pg [slots], lh [slots]
+  // launched as a programmatic dependent of the kernel before it: every read after it completes
+  pdl_trigger();
+  pdl_block();
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  const int step = step_dev ? *step_dev : step_arg;
+  int64_t* sel = promo_smem;
+  int32_t* pg = reinterpret_cast<int32_t*>(sel + top_m);
+  promotion_row_update(pages + static_cast<int64_t>(r) * slots, last_hit + static_cast<int64_t>(r) * slots,
+                       selected + static_cast<int64_t>(r) * top_m, top_m, slots, step, ttl, sel, pg, pg + slots);
 }
 
 }  // namespace spa

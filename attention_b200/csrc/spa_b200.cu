@@ -10,6 +10,7 @@
 #include "session.cuh"
 #include "model.cuh"
 #include "cache.cuh"
+#include "decoder_step.cuh"
 #include "prefill_generic.cuh"
 #include "prefill_sm100.cuh"
 

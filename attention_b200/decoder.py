@@ -282,12 +282,35 @@ def embed_rms_norm(table: torch.Tensor, ids: torch.Tensor, pos_table: torch.Tens
     return out
 
 
+def persistent_step_supported(cfg: DecoderConfig, batch: int) -> bool:
+    """Whether ``spa_decoder_step`` (the whole decode step as one launch) takes this shape."""
+    return (1 <= batch <= 4 and 1 <= cfg.layers <= _lib.DECODER_MAX_LAYERS and cfg.head_dim in (32, 64, 128)
+            and cfg.d_model <= 512 and cfg.d_model % 8 == 0 and cfg.mlp_mult * cfg.d_model % 8 == 0
+            and cfg.vocab % 8 == 0 and cfg.top_m <= 32 and cfg.max_pages <= 4096 and cfg.promo_slots <= 512)
+
+
 class SparseDecoder:
     """Batch of sequences decoded with paged KV caches (one pool per layer).
 
-    Sequence b owns pages [b * max_pages, (b+1) * max_pages) of every layer's pool."""
+    Sequence b owns pages [b * max_pages, (b+1) * max_pages) of every layer's pool.
 
-    def __init__(self, cfg: DecoderConfig, weights: dict, batch: int, *, dtype=torch.bfloat16, device="cuda"):
+    ``engine``: "kernels" runs a decode step as a chain of the library's few-row kernels
+    (one per linear layer, one routed decode per layer, the promotion update and the
+    argmax), launched as programmatic dependents of one another; "persistent" as one
+    cooperative kernel (``spa_decoder_step``) whose phases exchange data through global
+    memory.  "auto" is "kernels": on B200 the chain's launch boundaries cost less than the
+    one kernel's seven inter-SM exchanges per layer (122 against 130 us per step at the
+    benchmark's shape)."""
+
+    def __init__(self, cfg: DecoderConfig, weights: dict, batch: int, *, dtype=torch.bfloat16, device="cuda",
+                 engine: str = "auto"):
+        if engine not in ("auto", "persistent", "kernels"):
+            raise ValueError("engine must be 'auto', 'persistent' or 'kernels'")
+        if engine == "auto":
+            engine = "kernels"
+        elif engine == "persistent" and not persistent_step_supported(cfg, batch):
+            raise ValueError("this decoder shape is outside the persistent step's limits")
+        self.engine = engine
         self.cfg, self.batch, self.dtype, self.device = cfg, batch, dtype, torch.device(device)
         self.w = {k: t.to(device=self.device, dtype=dtype) for k, t in weights.items()}
         h, p, dh = cfg.heads, cfg.page_size, cfg.head_dim
@@ -405,6 +428,60 @@ class SparseDecoder:
                                gelu=gelu, append=append, chained=chained)
         return self._linear(add_rms_norm(x, delta, self.w[norm], self.cfg.eps, x_out=x_out), name, gelu=gelu)
 
+    def _persistent_params(self, m: int):
+        """spa_decoder_step arguments for ``n_routable`` routable pages (cached per page
+        count: every pointer is a persistent buffer)."""
+        cache = self.__dict__.setdefault("_ds_params", {})
+        p = cache.get(self.n_routable)
+        if p is not None:
+            return p
+        cfg, w = self.cfg, self.w
+        p = _lib.DecoderStepParams()
+        p.dtype, p.batch, p.d_model, p.heads = dtype_code(self._xa), self.batch, cfg.d_model, cfg.heads
+        p.ffn, p.vocab, p.layers = cfg.mlp_mult * cfg.d_model, cfg.vocab, cfg.layers
+        p.local_window, p.top_m, p.n_pages, p.max_pages = cfg.local_window, cfg.top_m, self.n_routable, cfg.max_pages
+        p.eps = cfg.eps
+        p.router_scale = p.attn_scale = 1.0 / math.sqrt(cfg.head_dim)
+        p.emb, p.emb_rows = w["emb"].data_ptr(), w["emb"].size(0)
+        p.pos_emb, p.pos_rows = w["pos"].data_ptr(), w["pos"].size(0)
+        p.norm_f, p.head_w = w["norm_f"].data_ptr(), w["head"].data_ptr()
+        for i in range(cfg.layers):
+            ly = p.layer[i]
+            for field, name in (("norm1", f"l{i}.norm1"), ("qkv_w", f"l{i}.qkv.w"), ("qkv_b", f"l{i}.qkv.b"),
+                                ("out_w", f"l{i}.out.w"), ("out_b", f"l{i}.out.b"), ("norm2", f"l{i}.norm2"),
+                                ("fc1_w", f"l{i}.fc1.w"), ("fc1_b", f"l{i}.fc1.b"), ("fc2_w", f"l{i}.fc2.w"),
+                                ("fc2_b", f"l{i}.fc2.b")):
+                setattr(ly, field, w[name].data_ptr())
+            ly.k_pool, ly.v_pool = self.k_pool[i].data_ptr(), self.v_pool[i].data_ptr()
+            ly.summaries = self.summaries[i].data_ptr() if self.summaries[i] is not None else None
+        p.kv = pool_layout(self.k_pool[0], self.v_pool[0], self.page_table)
+        p.token, p.counters, p.logits = self._token.data_ptr(), self._counters.data_ptr(), self._logits.data_ptr()
+        p.token_log, p.log_len = self._token_log.data_ptr(), self._token_log.size(0)
+        p.selected = self._sel_bufs[max(m, 1)].data_ptr()
+        p.promo_pages, p.promo_last_hit = self.promotion.pages.data_ptr(), self.promotion.last_hit.data_ptr()
+        p.promo_slots, p.promo_ttl = self.promotion.slots, self.promotion.ttl
+        ws = getattr(self, "_ds_workspace", None)
+        need = _lib.lib.spa_decoder_step_workspace_size(ctypes.byref(p))
+        if need == 0:
+            raise ValueError("this decoder shape is outside the persistent step's limits")
+        if ws is None or ws.numel() < need:
+            # zero-filled once: the step's exchange words carry a launch counter kept in it
+            ws = self._ds_workspace = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+        cache[self.n_routable] = p
+        return p
+
+    def _persistent_step_body(self):
+        """One decode step as one launch of ``spa_decoder_step``; returns the [layers, B, m]
+        selections (m >= 1; -1 when no page is routable)."""
+        m = min(self.cfg.top_m, self.n_routable)
+        if max(m, 1) not in self._sel_bufs:
+            self._sel_bufs[max(m, 1)] = torch.full((self.cfg.layers, self.batch, max(m, 1)), -1, dtype=torch.int64,
+                                                   device=self.device)
+        p = self._persistent_params(m)
+        _lib.check(_lib.lib.spa_decoder_step(ctypes.byref(p), stream_ptr(self.device)), "spa_decoder_step")
+        return self._sel_bufs[max(m, 1)]
+
     def _step_body(self):
         """One decode step on the persistent state (no host synchronisation, capturable).
         Each RMSNorm runs fused into the linear layer after it, together with the residual
@@ -412,6 +489,8 @@ class SparseDecoder:
         separate ops.  Every kernel of the step is launched as a programmatic dependent of
         the one before it: it starts while its predecessor runs (the linear layers stream
         their weight rows then) and reads its other inputs after the predecessor completes."""
+        if self.engine == "persistent":
+            return self._persistent_step_body()
         cfg = self.cfg
         b = self.batch
         h, dh = cfg.heads, cfg.head_dim

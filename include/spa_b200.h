@@ -655,6 +655,79 @@ int spa_norm_linear_chained(const void* x, const spa_norm_prologue* norm, const 
                             int dtype, const spa_kv_append_epilogue* append, spa_stream_t stream);
 
 /*
+ * The integrated decoder's whole decode step in ONE launch (the KV-cache model decode of
+ * triton_kvcache_transformer_decode.py:35-66 -- per layer the block of
+ * train_tiny_transformer.py:134-190 with RMSNorm -- re-built around the paged cache, with
+ * the router of triton_paged_gather_decode_benchmark.py:16-17 over the routable pages, the
+ * gather decode of triton_paged_attention.py:139-168 over the local window + selected
+ * pages, and the fixed-TTL promotion table of evaluate_promotion_ttl.py:134-135):
+ *
+ *   x = emb[token] + pos_emb[position];  per layer:  h = RMSNorm(x, norm1);
+ *   qkv = h W_qkv^T + b (the new token's K and V stored at `position` in the layer's pools);
+ *   selected = top-m of the router scores (ties to the lower page) over pages [0, n_pages);
+ *   att = attention over the last local_window tokens then the selected pages;
+ *   x = x + att W_out^T + b;  x = x + fc2(GELU(fc1(RMSNorm(x, norm2))));
+ *   logits = RMSNorm(x, norm_f) head^T (fp32 of the rounded products);
+ *   token = argmax(logits) (torch.argmax's rules), token_log[position, b] = token;
+ *   promotion update of every (layer, b) row with its selection at step counters[2B];
+ *   counters += 1 (positions [B], context lengths [B], step).
+ *
+ * The linear layers, norms and router use the arithmetic of spa_norm_linear / spa_linear /
+ * spa_router_topm (bit-identical for the same inputs); the attention agrees with
+ * spa_paged_gather_decode to rounding.  One cooperative grid of one CTA per SM; the phases
+ * exchange data through the workspace (spa_decoder_step_workspace_size bytes, 256-byte
+ * aligned, zero-filled before the first step and kept between steps).  Limits: batch 1..4,
+ * layers 1..8, head_dim 32/64/128, d_model <= 512, d_model / ffn / vocab multiples of 8,
+ * top_m <= 32, max pages per sequence <= 4096, promotion slots <= 512; weights 16-byte
+ * aligned.  After a step that reported SPA_DEVERR_WAIT_TIMEOUT, zero the workspace again.
+ */
+#define SPA_DECODER_MAX_LAYERS 8
+typedef struct spa_decoder_layer {
+  const void* norm1;         /* [d_model] */
+  const void* qkv_w;         /* [3 d_model, d_model] (q, k, v blocks, head-major) */
+  const void* qkv_b;         /* [3 d_model] or NULL */
+  const void* out_w;         /* [d_model, d_model] */
+  const void* out_b;         /* [d_model] or NULL */
+  const void* norm2;         /* [d_model] */
+  const void* fc1_w;         /* [ffn, d_model] */
+  const void* fc1_b;         /* [ffn] or NULL */
+  const void* fc2_w;         /* [d_model, ffn] */
+  const void* fc2_b;         /* [d_model] or NULL */
+  void* k_pool;              /* the layer's pools, addressed by spa_decoder_step_params.kv */
+  void* v_pool;
+  const float* summaries;    /* [batch, heads, n_pages, head_dim] fp32 page mean keys (n_pages > 0) */
+} spa_decoder_layer;
+
+typedef struct spa_decoder_step_params {
+  int dtype, batch, d_model, heads, ffn, vocab, layers;
+  int local_window, top_m, n_pages;
+  int max_pages;             /* pages per sequence when kv.page_table is NULL */
+  double eps, router_scale, attn_scale;
+  const void* emb;           /* [emb_rows, d_model] */
+  int64_t emb_rows;
+  const void* pos_emb;       /* [pos_rows, d_model] */
+  int64_t pos_rows;
+  const void* norm_f;        /* [d_model] */
+  const void* head_w;        /* [vocab, d_model] */
+  spa_decoder_layer layer[SPA_DECODER_MAX_LAYERS];
+  spa_kv_layout kv;          /* page geometry and table shared by every layer (k, v unused) */
+  int64_t* token;            /* [batch]: this step's tokens in, the greedy next tokens out */
+  int32_t* counters;         /* [2 batch + 1]: positions, context lengths, step */
+  float* logits;             /* [batch, vocab] */
+  int64_t* token_log;        /* [log_len, batch] or NULL */
+  int log_len;
+  int64_t* selected;         /* [layers, batch, max(min(top_m, n_pages), 1)] (-1 when none) */
+  int32_t* promo_pages;      /* [layers * batch, promo_slots] or NULL (no promotion table) */
+  int32_t* promo_last_hit;
+  int promo_slots, promo_ttl;
+  void* workspace;
+  size_t workspace_bytes;
+} spa_decoder_step_params;
+
+size_t spa_decoder_step_workspace_size(const spa_decoder_step_params* params);
+int spa_decoder_step(const spa_decoder_step_params* params, spa_stream_t stream);
+
+/*
  * Diagnostic for the failure path: one kernel waits on an mbarrier that nothing
  * completes, with the library's bounded wait limited to `cycles` (1 .. 4e9 clock
  * cycles).  The wait gives up, the kernel returns, and spa_device_error then reports
