@@ -524,25 +524,27 @@ def run_e2e(spa, cfg, x, groups, world, bytes_step, steps, args):
                                    page_table=tables[g], context_lens=x.ctx, out=host_out[g], selected=host_sel[g])
 
         c_ms = timed(per_call)
-        res.update(value=round(bytes_step * e2e_steps / (e_ms * 1e-3) / 1e9, 2),
-                   us_per_step=round(e_ms * 1e3 / e2e_steps, 3),
-                   path="attention_b200.SparseDecodeSession.step: one call into the native session (C ABI "
-                        "spa_session_step) that launches the CUDA graph of its host-buffer slot: a copy kernel "
-                        "brings the step's query from pinned mapped host memory into device memory, the router "
-                        "and the gather decode run, and a copy kernel (spa_copy) writes output + page ids into "
-                        "pinned host memory; the host may enqueue one step ahead (two buffer slots)",
-                   per_call_api={"us_per_step": round(c_ms * 1e3 / e2e_steps, 3),
-                                 "value": round(bytes_step * e2e_steps / (c_ms * 1e-3) / 1e9, 2),
-                                 "path": "attention_b200.sparse_decode_step called from Python every step with "
-                                         "pinned host query, output and page-id tensors (spa_sparse_decode_step_host: "
-                                         "a copy kernel reads the query from host memory, the one-launch step writes "
-                                         "output and page ids into host memory; prepared arguments cached per pool, "
-                                         "table and summaries)"},
+        # headline: the drop-in call a user of the reference's API makes each step
+        res.update(value=round(bytes_step * e2e_steps / (c_ms * 1e-3) / 1e9, 2),
+                   us_per_step=round(c_ms * 1e3 / e2e_steps, 3),
+                   path="attention_b200.sparse_decode_step called from Python every step with pinned host "
+                        "query, output and page-id tensors (spa_sparse_decode_step_host: a copy kernel reads the "
+                        "query from host memory, the one-launch step writes output and page ids into host memory; "
+                        "prepared arguments cached per pool, table and summaries); the host may run ahead of the "
+                        "device",
+                   session={"us_per_step": round(e_ms * 1e3 / e2e_steps, 3),
+                            "value": round(bytes_step * e2e_steps / (e_ms * 1e-3) / 1e9, 2),
+                            "path": "attention_b200.SparseDecodeSession.step: one call into the native session "
+                                    "(C ABI spa_session_step) that launches the CUDA graph of its host-buffer "
+                                    "slot: a copy kernel brings the step's query from pinned mapped host memory "
+                                    "into device memory, the router and the gather decode run, and a copy kernel "
+                                    "(spa_copy) writes output + page ids into pinned host memory; the host may "
+                                    "enqueue one step ahead (two buffer slots)"},
                    per_step_sync={"us_per_step": round(s_ms * 1e3 / e2e_steps, 3),
                                   "value": round(bytes_step * e2e_steps / (s_ms * 1e-3) / 1e9, 2),
-                                  "path": "the same session step, followed every step by a host "
-                                          "synchronisation before the next step is enqueued (results read "
-                                          "on the host each step)"})
+                                  "path": "the session step, followed every step by a host synchronisation "
+                                          "before the next step is enqueued (results read on the host each "
+                                          "step)"})
         for s in sessions:
             s.close()
         del sessions
