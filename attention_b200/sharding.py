@@ -107,6 +107,7 @@ class PrefillShard:
         self.halo = window
         self.compute = compute or _device_compute
         self._kh = self._vh = None
+        self._side = None
 
     def halo_free_from(self, seq: int) -> int:
         """First row whose window lies inside the chunk (rounded up to the kernel's tile)."""
@@ -133,6 +134,26 @@ class PrefillShard:
         reqs = dist.batch_isend_irecv(ops) if ops else []
         if self.rank == 0:
             self.compute(q, k, v, out, self.window, (0, seq), None, None)
+        elif q.is_cuda:
+            # The rows that need the halo run on a side stream that waits for the inputs and
+            # the halo receive only: their CTAs take the SMs that the interior rows' persistent
+            # CTAs leave as those run out of work (one CTA per SM fits), instead of a second
+            # launch behind the first one's last wave.  The two launches write disjoint rows.
+            split = self.halo_free_from(seq)
+            main = torch.cuda.current_stream(q.device)
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=q.device)
+            inputs_ready = torch.cuda.Event()
+            inputs_ready.record(main)
+            if split < seq:
+                self.compute(q, k, v, out, self.window, (split, seq), None, None)
+            with torch.cuda.stream(self._side):
+                self._side.wait_event(inputs_ready)
+                for r in reqs:
+                    r.wait()
+                reqs = []
+                self.compute(q, k, v, out, self.window, (0, split), self._kh, self._vh)
+            main.wait_stream(self._side)
         else:
             split = self.halo_free_from(seq)
             if split < seq:
