@@ -156,6 +156,7 @@ PROTOTYPES = {
                                           _i, _d, _d, _vp, _vp, _vp, _sz, _vp]),
     "spa_sparse_step_launches": (_i, [_i, _i, _i, _i, _i, _i, _i, _i, _i, ctypes.POINTER(_i)]),
     "spa_set_step_fusion": (_i, [_i]),
+    "spa_set_prefill_sm_reserve": (_i, [_i]),
     "spa_paged_decode_noalloc": (_i, [_vp, _i, _i, _i, _i, _i, _KV, _vp, _i, _vp, _i, _i, _d, _vp, _vp]),
     "spa_kv_append": (_i, [_KV, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "spa_local_prefill": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),

@@ -624,6 +624,12 @@ inline bool prefill_sm100_supported(const PrefillArgs& a, int dtype) {
   return (m & 15) == 0;
 }
 
+// SMs the persistent prefill grid leaves free (process-wide).
+inline int& prefill_sm_reserve() {
+  static int n = 0;
+  return n;
+}
+
 template <typename T>
 int launch_prefill_sm100(const PrefillArgs& a, int dtype, cudaStream_t st) {
   CUtensorMap qm, km, vm, khm, vhm;
@@ -652,8 +658,10 @@ int launch_prefill_sm100(const PrefillArgs& a, int dtype, cudaStream_t st) {
   const int64_t items = static_cast<int64_t>(t.n_pairs) * static_cast<int64_t>(bh);
   if (items > 0x7fffffff) return SPA_ERR_UNSUPPORTED;
   t.n_items = static_cast<int>(items);
-  // persistent: one CTA per SM (the kernel's shared memory and TMEM admit one)
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, device_sm_count()));
+  // persistent: one CTA per SM (the kernel's shared memory and TMEM admit one), minus the
+  // SMs left to a concurrent halo exchange (spa_set_prefill_sm_reserve)
+  const int sms = std::max(1, device_sm_count() - prefill_sm_reserve());
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, sms));
   t.scale_log2 = a.scale * 1.4426950408889634f;
   if (a.D == 128) {
     auto kern = prefill_tc_kernel<T, 128>;
@@ -669,3 +677,9 @@ int launch_prefill_sm100(const PrefillArgs& a, int dtype, cudaStream_t st) {
 }
 
 }  // namespace spa
+
+extern "C" int spa_set_prefill_sm_reserve(int n) {
+  const int prev = spa::prefill_sm_reserve();
+  if (n >= 0) spa::prefill_sm_reserve() = n;
+  return prev;
+}

@@ -25,6 +25,8 @@ from typing import Callable
 import torch
 import torch.distributed as dist
 
+from . import _lib
+
 
 def shard_rows(n: int, world: int, rank: int) -> slice:
     """Contiguous, balanced split of n rows over world ranks."""
@@ -101,6 +103,8 @@ class PrefillShard:
     chunk; ranks exchange halos pairwise (r -> r+1) with one batched send/recv."""
 
     TILE = 128
+    # SMs the prefill leaves to the halo exchange's copy kernels while it is in flight
+    sm_reserve = 8
 
     def __init__(self, rank: int, world: int, window: int, *, group=None, compute: Callable | None = None):
         self.rank, self.world, self.window, self.group = rank, world, window, group
@@ -132,8 +136,14 @@ class PrefillShard:
             ops += [dist.P2POp(dist.irecv, self._kh, self.rank - 1, self.group),
                     dist.P2POp(dist.irecv, self._vh, self.rank - 1, self.group)]
         reqs = dist.batch_isend_irecv(ops) if ops else []
+        # while the exchange is in flight the prefill leaves SMs to its copy kernels (they
+        # would otherwise wait for the persistent prefill's last CTA)
+        reserve = self.sm_reserve if ops and q.is_cuda else 0
+        prev = _lib.lib.spa_set_prefill_sm_reserve(reserve) if reserve else None
         if self.rank == 0:
             self.compute(q, k, v, out, self.window, (0, seq), None, None)
+            if prev is not None:
+                _lib.lib.spa_set_prefill_sm_reserve(prev)
         elif q.is_cuda:
             # The rows that need the halo run on a side stream that waits for the inputs and
             # the halo receive only: their CTAs take the SMs that the interior rows' persistent
@@ -147,6 +157,8 @@ class PrefillShard:
             inputs_ready.record(main)
             if split < seq:
                 self.compute(q, k, v, out, self.window, (split, seq), None, None)
+            if prev is not None:
+                _lib.lib.spa_set_prefill_sm_reserve(prev)
             with torch.cuda.stream(self._side):
                 self._side.wait_event(inputs_ready)
                 for r in reqs:

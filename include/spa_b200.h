@@ -381,6 +381,15 @@ int spa_local_prefill(const void* q, const void* k, const void* v, int dtype,
                       spa_stream_t stream);
 
 /*
+ * SMs the tensor-core prefill leaves free (process-wide, default 0): its persistent
+ * grid is min(work items, SMs - n).  A sequence-parallel rank sets it while its halo
+ * exchange is in flight, so the exchange's copy kernels find SMs to run on beside the
+ * prefill instead of waiting for its last CTA.  Returns the previous value; a negative
+ * n only queries it.  No counterpart in the reference.
+ */
+int spa_set_prefill_sm_reserve(int n);
+
+/*
  * Promotion cache update (one table of `slots` entries per row r < rows):
  * page[r, i] (int32, -1 = free) and last_hit[r, i] (int32).  With the row's
  * selected pages sel[r, 0..top_m) at decode step `step`:
